@@ -1,0 +1,573 @@
+"""bench.py -- throughput of the non-GEMM extension-op path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline workload: the ModernBERT-base-shaped
+non-GEMM layer chain at batch 64 x seq 512 per GPU (32768 tokens, hidden 768,
+12 heads x 64, GeGLU intermediate 1152): LayerNorm -> RoPE on q,k -> masked
+row softmax -> residual add -> LayerNorm -> GeGLU. A step is one pass of the
+chain; the GEMM outputs it consumes (qkv, scores, attention output, MLP input)
+are seeded synthetic tensors. Under torchrun each rank runs its own 64-sequence
+shard (weak scaling, no collective on the data path); `value` is the bytes all
+ranks moved divided by the slowest rank's device time.
+
+Metric: algorithmic HBM bytes per second (each input read once, each output
+written once) -- the per-op GB/s of BASELINE.json. The same line carries the
+per-op numbers of configs[0..3] (rotating buffer sets >= 2x L2 per op), the
+roofline of the dominant kernel, an end-to-end number through host buffers, the
+SM clocks seen during the run, and the CPU oracle timed on the host cores.
+
+`--impl reference` times the reference's CPU algorithm (the oracle restatement
+of crates/cpu-kernels, threaded like its rayon splits) on a bounded sample of
+the same workload and prints the same metric with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "tenferro-decision-rs_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "per-op HBM GB/s (% of 8 TB/s peak) and Gelem/s at 1/2/4/8 B200 vs host CPU"
+CHAIN = dict(batch=64, seq=512, hidden=768, heads=12, head_dim=64, inter=1152, window=64,
+             pad=37, theta_global=160000.0, theta_local=10000.0)
+FALLBACK_HBM_GBS = 6650.0
+SEED = 0x7E4F0000
+
+
+# ---------------------------------------------------------------------------------
+# bytes
+
+def chain_bytes(c=CHAIN, batch=None) -> dict:
+    B = c["batch"] if batch is None else batch
+    T, h, I, H, L = B * c["seq"], c["hidden"], c["inter"], c["heads"], c["seq"]
+    ln = 2 * h * T * 4 + h * 4
+    return {
+        "layernorm": ln,
+        "rope": 2 * (2 * h * T * 4),
+        "softmax": 2 * B * H * L * L * 4,
+        "residual_add": 3 * h * T * 4,
+        "layernorm2": ln,
+        "geglu": (2 * I + I) * T * 4,
+    }
+
+
+# ---------------------------------------------------------------------------------
+# environment
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            v = float(json.load(fh)["hbm_gbs"])
+        return v, "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the GPUs work."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="tfx_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        power = [num(r[3]) for r in rows if num(r[3]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        load = [s for s, p in zip(sm, power) if p is not None and p > 200] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(power) if power else None}
+
+
+# ---------------------------------------------------------------------------------
+# our arm
+
+class Chain:
+    """Device buffers and launch sequence of one chain step on this GPU."""
+
+    def __init__(self, torch, ops, device, rank, batch):
+        c = CHAIN
+        self.torch, self.ops, self.dev = torch, ops, device
+        B, L, h, I, H, hd = batch, c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
+        self.B, self.L, self.h, self.I, self.H, self.hd = B, L, h, I, H, hd
+        T = B * L
+        g = torch.Generator(device=device)
+        g.manual_seed(SEED + 97 * rank)
+
+        def normal(n, std=1.0):
+            return torch.randn(n, generator=g, device=device, dtype=torch.float32) * std
+
+        self.x0 = normal(h * T)                         # residual stream (h, T)
+        self.gamma1 = torch.rand(h, generator=g, device=device) + 0.5
+        self.gamma2 = torch.rand(h, generator=g, device=device) + 0.5
+        self.qkv = normal(3 * h * T)                    # (3h, L, B) feature-first
+        self.scores = normal(B * H * L * L, 2.0)        # [B][H][L][L]
+        self.attn = normal(h * T)                       # attention output (h, T)
+        self.u = normal(2 * I * T, 1.5)                 # MLP input (2I, T)
+        self.h1 = torch.empty_like(self.x0)
+        self.qk = torch.empty_like(self.qkv)
+        self.probs = torch.empty_like(self.scores)
+        self.h2 = torch.empty_like(self.x0)
+        self.h3 = torch.empty_like(self.x0)
+        self.g = torch.empty(I * T, device=device)
+        self.tables = {}
+        for name in ("theta_global", "theta_local"):
+            self.tables[name] = ops.rope_tables(c[name], L, hd, device=device)
+
+    def inputs(self):
+        return [self.x0, self.qkv, self.scores, self.attn, self.u]
+
+    def outputs(self):
+        return [self.h1, self.qk, self.probs, self.h2, self.h3, self.g]
+
+    def step(self, i, sm_events=None):
+        c, ops = CHAIN, self.ops
+        local = i % 2 == 0  # alternate sliding-window (local) and global layers
+        cos_t, sin_t = self.tables["theta_local" if local else "theta_global"]
+        ops.layer_norm_feature_first(self.x0, self.gamma1, None, 1e-5, out=self.h1)
+        ops.rope_pairhalf(self.qkv, cos_t, sin_t, 2 * self.H, self.L, self.B, self.hd, self.hd,
+                          (self.hd, 3 * self.h, 3 * self.h * self.L, 1), out=self.qk)
+        if sm_events is not None:
+            sm_events[0].record()
+        ops.masked_softmax(self.scores, self.B, self.H, self.L, self.L,
+                           window=c["window"] if local else -1, valid_len=self.L - c["pad"],
+                           out=self.probs)
+        if sm_events is not None:
+            sm_events[1].record()
+        ops.add(self.x0, self.attn, out=self.h2)
+        ops.layer_norm_feature_first(self.h2, self.gamma2, None, 1e-5, out=self.h3)
+        ops.geglu(self.u, self.I, out=self.g)
+
+    KERNELS_PER_STEP = 6
+
+
+def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
+    """configs[0..3] per op: rotating buffer sets whose footprint is >= 2x L2;
+    kernel time from an event pair around every launch. `only` restricts the
+    run to one op (used for profiler captures)."""
+    results = {}
+    gen = torch.Generator(device=device)
+    gen.manual_seed(SEED)
+
+    def normal(n, std=1.0, dtype=torch.float32):
+        return (torch.randn(n, generator=gen, device=device, dtype=dtype) * std)
+
+    def measure(name, make, launch, nbytes, elems):
+        if only is not None and name != only:
+            return
+        per_set = nbytes
+        sets = max(2, math.ceil(2 * l2_bytes / per_set) + 1)
+        bufs = [make() for _ in range(sets)]
+        for k in range(2 * sets):
+            launch(bufs[k % sets])
+        torch.cuda.synchronize()
+        torch.cuda._sleep(20_000_000)  # keep the GPU busy while the launches queue up
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for k in range(reps):
+            evs[k][0].record()
+            launch(bufs[k % sets])
+            evs[k][1].record()
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        results[name] = {"bytes": nbytes, "us": round(ms * 1e3, 3), "gbs": round(gbs, 1),
+                         "frac_of_hbm": round(gbs / hbm_peak, 3),
+                         "gelem_s": round(elems / (ms * 1e-3) / 1e9, 2), "buffer_sets": sets}
+        del bufs
+
+    # LayerNorm 768 x 8192 (f32 and the f64 copy)
+    d, cols = 768, 8192
+    for dt, tag, esz in ((torch.float32, "layernorm_f32", 4), (torch.float64, "layernorm_f64", 8)):
+        w = (torch.rand(d, generator=gen, device=device, dtype=dt) + 0.5)
+        measure(tag, lambda: (normal(d * cols, dtype=dt), torch.empty(d * cols, device=device, dtype=dt)),
+                lambda b, w=w: ops.layer_norm_feature_first(b[0], w, None, 1e-5, out=b[1]),
+                2 * d * cols * esz + d * esz, d * cols)
+    # GeGLU 2304 x 8192 -> 1152 x 8192, and GELU on 2304 x 8192
+    I, cols = 1152, 8192
+    measure("geglu", lambda: (normal(2 * I * cols, 1.5), torch.empty(I * cols, device=device)),
+            lambda b: ops.geglu(b[0], I, out=b[1]), 3 * I * cols * 4, I * cols)
+    measure("gelu_erf", lambda: (normal(2 * I * cols, 1.5), torch.empty(2 * I * cols, device=device)),
+            lambda b: ops.gelu_erf(b[0], out=b[1]), 2 * 2 * I * cols * 4, 2 * I * cols)
+    # RMSNorm (16384, 1024) centered, eps 1e-6; gated SiLU 16384 x 3584
+    rows, width = 16384, 1024
+    wr = normal(width, 0.1) + 1.0
+    measure("rmsnorm_last", lambda: (normal(rows * width), torch.empty(rows * width, device=device)),
+            lambda b: ops.rms_norm_last(b[0], wr, True, 1e-6, out=b[1]),
+            2 * rows * width * 4 + width * 4, rows * width)
+    n = 16384 * 3584
+    measure("gated_silu", lambda: (normal(n), normal(n), torch.empty(n, device=device)),
+            lambda b: ops.gated_silu(b[0], b[1], out=b[2]), 3 * n * 4, n)
+    # masked softmax [8,12,512,512], window 64, 37 padded keys; bias [8192, 768]
+    B, H, L = 8, 12, 512
+    ns = B * H * L * L
+    measure("masked_softmax", lambda: (normal(ns, 2.0), torch.empty(ns, device=device)),
+            lambda b: ops.masked_softmax(b[0], B, H, L, L, window=64, valid_len=L - 37, out=b[1]),
+            2 * ns * 4, ns)
+    F, T = 768, 8192
+    bias = normal(F, 0.02)
+    measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
+            lambda b: ops.bias_act(b[0], bias, out=b[1]), 2 * F * T * 4 + F * 4, F * T)
+    return results
+
+
+def cpu_baseline_sample(seconds=10.0, batch=4):
+    """The oracle chain (reference rayon splits, all host threads) on a bounded
+    sample of the workload: `batch` sequences instead of 64."""
+    import numpy as np
+    from oracle import oracle as orc
+    orc.build()
+    c = CHAIN
+    B, L, h, I, H, hd = batch, c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
+    T = B * L
+    rng = np.random.default_rng(1)
+    x0 = rng.standard_normal(h * T).astype(np.float32)
+    g1 = rng.uniform(0.5, 1.5, h).astype(np.float32)
+    qkv = rng.standard_normal(3 * h * T).astype(np.float32)
+    scores = (2 * rng.standard_normal(B * H * L * L)).astype(np.float32)
+    attn = rng.standard_normal(h * T).astype(np.float32)
+    u = (1.5 * rng.standard_normal(2 * I * T)).astype(np.float32)
+    cos_t, sin_t = orc.rope_tables_f32(c["theta_local"], L, hd)
+    nbytes = sum(chain_bytes(batch=B).values())
+
+    def one():
+        orc.layer_norm_feature_first_f32(x0, h, T, g1, None, 1e-5)
+        orc.rope_pairhalf_f32(qkv, cos_t, sin_t, 2 * H, L, B, hd, hd, (hd, 3 * h, 3 * h * L, 1))
+        orc.masked_softmax_f32(scores, B, H, L, L, window=c["window"], valid_len=L - c["pad"])
+        h2 = orc.add_f32(x0, attn)
+        orc.layer_norm_feature_first_f32(h2, h, T, g1, None, 1e-5)
+        orc.geglu_f32(u, I, T)
+
+    one()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": round(nbytes / med / 1e9, 3), "unit": "GB/s", "cores": orc.threads(),
+            "kind": "port",
+            "sample": f"oracle chain at batch {B} x seq {L} ({nbytes} algorithmic bytes), "
+                      f"median of {len(times)} runs over ~{seconds:.0f} s"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import tfx  # noqa: F401  (raises when libtfx.so is missing)
+    from tfx import ops
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    hbm_peak, peak_src = measured_hbm()
+    props = torch.cuda.get_device_properties(device)
+    l2 = props.L2_cache_size
+    chain = Chain(torch, ops, device, rank, CHAIN["batch"])
+    bytes_per_step = sum(chain_bytes().values())
+
+    for i in range(args.warmup):
+        chain.step(i)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    sm_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    t0.record()
+    for i in range(args.steps):
+        chain.step(i, sm_pairs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_local = t0.elapsed_time(t1)
+    clock_info = clocks.stop()
+    ms = max_over_ranks(ms_local)
+    sm_ms = statistics.mean(a.elapsed_time(b) for a, b in sm_pairs)
+    sm_ms = max_over_ranks(sm_ms)
+    value = world * args.steps * bytes_per_step / (ms * 1e-3) / 1e9
+
+    # end to end through the public API: pinned host inputs -> device -> chain ->
+    # host outputs, every step
+    e2e_steps = max(2, min(args.steps, 10))
+    host_in = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in chain.inputs()]
+    for h_t, d_t in zip(host_in, chain.inputs()):
+        h_t.copy_(d_t)
+    host_out = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in chain.outputs()]
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+    def e2e_step(i):
+        for h_t, d_t in zip(host_in, chain.inputs()):
+            d_t.copy_(h_t, non_blocking=True)
+        chain.step(i)
+        for h_t, d_t in zip(host_out, chain.outputs()):
+            h_t.copy_(d_t, non_blocking=True)
+
+    e2e_step(0)
+    torch.cuda.synchronize()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * e2e_steps * bytes_per_step / (e2e_ms * 1e-3) / 1e9
+
+    ops_results = None
+    if not args.no_ops:
+        ops_results = run_ops_configs(torch, ops, device, l2, hbm_peak)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(args.cpu_seconds)
+
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            with open(tpath) as fh:
+                traffic = json.load(fh).get("chain_masked_softmax_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    sm_bytes = chain_bytes()["softmax"]
+    sm_gbs = sm_bytes / (sm_ms * 1e-3) / 1e9
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded normals on device; GEMM outputs of the chain are inputs)",
+        "config": {
+            "workload": "configs[4]: ModernBERT-base non-GEMM chain LN -> RoPE(q,k) -> masked "
+                        "softmax -> residual add -> LN -> GeGLU, batch 64 x seq 512 per GPU",
+            "tokens_per_gpu": CHAIN["batch"] * CHAIN["seq"], "hidden": CHAIN["hidden"],
+            "heads": CHAIN["heads"], "head_dim": CHAIN["head_dim"], "inter": CHAIN["inter"],
+            "window": 2 * CHAIN["window"], "padded_keys": CHAIN["pad"],
+            "rope_theta": "10000 (even steps, sliding) / 160000 (odd steps, global)",
+            "global_batch": CHAIN["batch"] * world, "seq_len": CHAIN["seq"],
+            "parallelism": f"token-row shards x{world}, no collective",
+            "bytes_per_step_per_gpu": bytes_per_step,
+            "l2": "inputs larger than L2 (3.17 GB per step per GPU vs "
+                  f"{l2 / 2**20:.0f} MiB L2); per-op configs rotate >= 2x L2 of buffers",
+        },
+        "roofline": {"kernel": "masked_softmax (chain)", "bound": "hbm",
+                     "achieved": round(sm_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(sm_gbs / hbm_peak, 3), "peak_source": peak_src,
+                     "bytes_per_launch": sm_bytes, "traffic": traffic,
+                     "us_per_launch": round(sm_ms * 1e3, 2)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "path": "pinned host buffers -> cudaMemcpyAsync -> tfx C ABI kernels -> host"},
+        "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,
+        "clocks": clock_info,
+        "cpu_baseline": cpu,
+        "ops": ops_results,
+    }
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------------
+# reference arm
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle import oracle as orc
+    orc.build()
+    import numpy as np
+    c = CHAIN
+    B = 8  # bounded sample: 8 of the 64 sequences per step
+    L, h, I, H, hd = c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
+    T = B * L
+    rng = np.random.default_rng(2)
+    x0 = rng.standard_normal(h * T).astype(np.float32)
+    g1 = rng.uniform(0.5, 1.5, h).astype(np.float32)
+    qkv = rng.standard_normal(3 * h * T).astype(np.float32)
+    scores = (2 * rng.standard_normal(B * H * L * L)).astype(np.float32)
+    attn = rng.standard_normal(h * T).astype(np.float32)
+    u = (1.5 * rng.standard_normal(2 * I * T)).astype(np.float32)
+    tables = {k: orc.rope_tables_f32(c[k], L, hd) for k in ("theta_local", "theta_global")}
+    nbytes = sum(chain_bytes(batch=B).values())
+
+    def step(i):
+        local = i % 2 == 0
+        cos_t, sin_t = tables["theta_local" if local else "theta_global"]
+        orc.layer_norm_feature_first_f32(x0, h, T, g1, None, 1e-5)
+        orc.rope_pairhalf_f32(qkv, cos_t, sin_t, 2 * H, L, B, hd, hd, (hd, 3 * h, 3 * h * L, 1))
+        orc.masked_softmax_f32(scores, B, H, L, L, window=c["window"] if local else -1,
+                               valid_len=L - c["pad"])
+        h2 = orc.add_f32(x0, attn)
+        orc.layer_norm_feature_first_f32(h2, h, T, g1, None, 1e-5)
+        orc.geglu_f32(u, I, T)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(i)
+    dt = time.perf_counter() - t0
+    value = args.steps * nbytes / dt / 1e9
+    sample = (f"oracle restatement of the reference's rayon CPU path, chain at batch {B} x seq "
+              f"{L} per step ({nbytes} algorithmic bytes)")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded normals on the host)", "impl": "reference",
+        "config": {"workload": "configs[4]: ModernBERT-base non-GEMM chain, bounded sample "
+                               f"batch {B} x seq {L}", "global_batch": B, "seq_len": L,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": orc.threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_only_op(args):
+    import torch
+    from tfx import ops
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    hbm_peak, _ = measured_hbm()
+    l2 = torch.cuda.get_device_properties(device).L2_cache_size
+    res = run_ops_configs(torch, ops, device, l2, hbm_peak, only=args.only_op, reps=args.op_reps)
+    if not res:
+        raise SystemExit(f"unknown op {args.only_op}")
+    print(json.dumps(res))
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-ops", action="store_true", help="skip the per-op configs[0..3]")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--only-op", default=None,
+                    help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
+                         "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, bias_add) and "
+                         "print its result; for profiler captures")
+    ap.add_argument("--op-reps", type=int, default=40)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.only_op:
+        run_only_op(args)
+    elif args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

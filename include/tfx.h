@@ -1,0 +1,206 @@
+/*
+ * tfx.h -- C ABI of the B200 (sm_100a) non-GEMM extension ops of
+ * tenferro-decision (feature-first LayerNorm, feature-last RMSNorm, exact-erf
+ * GELU / GeGLU, gated SiLU, the gemm_bias bias-broadcast epilogue, masked row
+ * softmax, RoPE).
+ *
+ * Library: tenferro-decision-rs_b200/lib/libtfx.so (built with nvcc for
+ * sm_100a; links the CUDA runtime statically).
+ *
+ * Conventions, kept from the reference's extension ops
+ * (crates/tenferro-ext/src, crates/tenferro-infer/src):
+ *   - Layouts are the reference's column-major ones (first axis fastest).
+ *     A feature-first activation (d, cols) stores column c at [c*d, (c+1)*d).
+ *   - Inputs are borrowed, outputs are caller-owned; nothing is allocated.
+ *   - Every call is asynchronous on the given stream (NULL = legacy default
+ *     stream) and takes device pointers, except the tfx_session_* calls,
+ *     which take host pointers and return when the host outputs are written.
+ *   - Errors are returned, never hidden: there is no CPU fallback and no
+ *     implicit transfer (crates/tenferro-ext/src/lib.rs:188-189). On failure
+ *     tfx_last_error_string() names the op and field the way the reference's
+ *     invalid_argument(op, field, message) does, e.g.
+ *     "tenferro-ext::layernorm_ff: weight: null pointer".
+ *   - An empty tensor (a zero extent) is a successful no-op, as in the
+ *     cpu-kernels functions (e.g. crates/cpu-kernels/src/lib.rs:410-412).
+ *   - Elementwise ops accept y == x (in place); other overlaps are rejected
+ *     where the op would read what it already wrote.
+ *   - All functions are thread-safe; the only shared state is a per-device
+ *     attribute cache initialised once per device.
+ */
+#ifndef TFX_H
+#define TFX_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define TFX_API __attribute__((visibility("default")))
+#else
+#define TFX_API
+#endif
+
+/* Same object as cudaStream_t / CUstream (driver_types.h). */
+typedef struct CUstream_st* tfx_stream_t;
+
+#define TFX_OK 0
+#define TFX_ERR_INVALID_ARGUMENT (-1) /* bad pointer, size or parameter */
+#define TFX_ERR_UNSUPPORTED (-2)      /* shape/dtype/layout this build does not handle */
+#define TFX_ERR_CUDA (-3)             /* a CUDA runtime call or launch failed */
+
+/* Thread-local description of the last failure on this thread ("" if none). */
+TFX_API const char* tfx_last_error_string(void);
+/* ABI version: major * 10000 + minor * 100 + patch. */
+TFX_API int tfx_version(void);
+
+/* ---- erf / exact GELU ------------------------------------------------------
+ * Replaces ErfOp (crates/tenferro-ext/src/lib.rs:95-170) and
+ * EagerSessionErfExt::{erf, gelu_erf} (lib.rs:201-234).
+ * f32: the MLX erf of crates/cpu-kernels/src/lib.rs:449-505, bit-identical;
+ *      GELU = (0.5 * x) * (1 + erf(x * FRAC_1_SQRT_2)) (lib.rs:509-511).
+ * f64: Abramowitz-Stegun 7.1.26 (lib.rs:273-285); GELU composed as
+ *      (x * 0.5) * (erf(x * FRAC_1_SQRT_2) + 1) (lib.rs:224-234). */
+TFX_API int tfx_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream);
+TFX_API int tfx_gelu_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream);
+TFX_API int tfx_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream);
+TFX_API int tfx_gelu_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream);
+
+/* ---- GeGLU ---------------------------------------------------------------
+ * Replaces GegluOp (crates/tenferro-ext/src/geglu.rs:27,85-121) and
+ * FusedScope::geglu_first (crates/tenferro-ext/src/cuda_fused.rs:669).
+ * u is feature-first (2*inter, cols); y is (inter, cols):
+ *   y[i + inter*c] = gelu_erf(u[i + 2*inter*c]) * u[inter + i + 2*inter*c]
+ * (cpu-kernels lib.rs:516-538). y must not overlap u. */
+TFX_API int tfx_geglu_ff_f32(const float* u, float* y, int64_t inter, int64_t cols,
+                     tfx_stream_t stream);
+
+/* ---- gated SiLU ----------------------------------------------------------
+ * Replaces GatedSiluOp (crates/tenferro-ext/src/gated_silu.rs:26,67-106),
+ * FusedScope::gated_silu (cuda_fused.rs:640): y = (g / (1 + exp(-g))) * u
+ * (cpu-kernels lib.rs:584-607). y may equal gate or up. */
+TFX_API int tfx_gated_silu_f32(const float* gate, const float* up, float* y, int64_t n,
+                       tfx_stream_t stream);
+/* FusedScope::gated_silu_stacked (cuda_fused.rs:995): gu is column-major
+ * (rows, 2*inter) with column blocks gate | up; y is (rows, inter). */
+TFX_API int tfx_gated_silu_stacked_f32(const float* gu, float* y, int64_t rows, int64_t inter,
+                               tfx_stream_t stream);
+
+/* ---- bias broadcast (gemm_bias epilogue) ---------------------------------
+ * The bias step of GemmBiasOp (crates/tenferro-ext/src/gemm_bias.rs:27,76-142;
+ * cpu-kernels lib.rs:274-288) on a finished product, and
+ * FusedScope::bias_act_first (cuda_fused.rs:704): x, y are feature-first
+ * (features, tokens) -- equivalently row-major [tokens][features] --
+ *   y[o + features*t] = act(x[o + features*t] + bias[o])
+ * act: TFX_ACT_IDENTITY, TFX_ACT_GELU_ERF (the f32 GELU above), TFX_ACT_RELU.
+ * bias may be NULL (activation only). y may equal x. */
+#define TFX_ACT_IDENTITY 0
+#define TFX_ACT_GELU_ERF 1
+#define TFX_ACT_RELU 2
+TFX_API int tfx_bias_act_ff_f32(const float* x, const float* bias, float* y, int64_t features,
+                        int64_t tokens, int act, tfx_stream_t stream);
+
+/* Residual add of the encoder layer (laya-infer/src/model.rs add_assign):
+ * y = a + b elementwise. y may equal a or b. */
+TFX_API int tfx_add_f32(const float* a, const float* b, float* y, int64_t n, tfx_stream_t stream);
+
+/* ---- feature-first LayerNorm ---------------------------------------------
+ * Replaces LayerNormFeatureFirstOp (crates/tenferro-ext/src/layernorm.rs:33,
+ * 94-231), EagerSessionLayerNormExt::layer_norm_feature_first (:260) and
+ * FusedScope::layer_norm_first (cuda_fused.rs:603).
+ * x, y are (d, cols), column c contiguous; weight and bias (nullable) are (d).
+ *   mean = sum(x)/d; var = sum((x-mean)^2)/d; inv = 1/sqrt(var + eps);
+ *   y = (x - mean) * inv * w (+ b)              (cpu-kernels lib.rs:397-443)
+ * f64 restates tenferro_infer::norm::layer_norm (norm.rs:11-45) on the same
+ * layout. y may equal x. */
+TFX_API int tfx_layernorm_ff_f32(const float* x, const float* weight, const float* bias, float* y,
+                         int64_t d, int64_t cols, float eps, tfx_stream_t stream);
+TFX_API int tfx_layernorm_ff_f64(const double* x, const double* weight, const double* bias, double* y,
+                         int64_t d, int64_t cols, double eps, tfx_stream_t stream);
+
+/* ---- feature-last RMSNorm -------------------------------------------------
+ * Replaces RmsNormLastOp (crates/tenferro-ext/src/rms_norm.rs:28,84-137),
+ * EagerSessionRmsNormExt::rms_norm_last (:165-203) and
+ * FusedScope::rms_norm_last (cuda_fused.rs:575).
+ * x, y are column-major (rows, width): element (r, d) at r + rows*d.
+ *   scale = 1/sqrt(sum_d x^2 * (1/width) + eps); y = x * scale * (centered ? 1+w : w)
+ * (cpu-kernels lib.rs:545-581; the eps of the ext trait is an f64 truncated
+ * to f32, rms_norm.rs:186 -- pass the truncated value). f64 restates
+ * tenferro_infer::norm::rms_norm (norm.rs:52-103). y may equal x. */
+TFX_API int tfx_rmsnorm_last_f32(const float* x, const float* weight, float* y, int64_t rows,
+                         int64_t width, int centered, float eps, tfx_stream_t stream);
+TFX_API int tfx_rmsnorm_last_f64(const double* x, const double* weight, double* y, int64_t rows,
+                         int64_t width, int centered, double eps, tfx_stream_t stream);
+
+/* ---- masked row softmax ---------------------------------------------------
+ * Replaces tenferro_infer::softmax::{softmax, masked_softmax}
+ * (crates/tenferro-infer/src/softmax.rs:8-34) and the masked softmax rows
+ * inside the attention kernels (cpu-kernels lib.rs:1053-1080, 1111-1153;
+ * fused.cu fused_attention). Scores are row-major
+ * [batch][heads][q_len][k_len], keys contiguous; probabilities have the same
+ * layout (y may equal scores).
+ * For query q of batch b, key k is kept when all enabled conditions hold:
+ *   valid:  k < valid_len (or valid_lens[b] when valid_lens != NULL)
+ *   causal: k <= q
+ *   window: |q - k| <= window  (skipped for q >= the valid length when
+ *           window_skips_invalid_query, as laya-infer/src/model.rs:474-483)
+ *   keep:   keep[b*keep_stride_b + q*keep_stride_q + k*keep_stride_k] != 0
+ * and the score is v = s * scale (+ add_mask[b*sb + q*sq + k*sk]).
+ * semantics TFX_SOFTMAX_EXCLUDE: masked keys are -inf, non-finite values
+ *   contribute 0, p = exp(v - max) / sum; an all-masked row is NaN
+ *   (cpu-kernels attention rows).
+ * semantics TFX_SOFTMAX_FILL: masked keys are filled with -1e30 and a plain
+ *   softmax follows; an all-masked row is uniform (tenferro-infer
+ *   masked_softmax, util.rs:87). */
+#define TFX_SOFTMAX_EXCLUDE 0
+#define TFX_SOFTMAX_FILL 1
+typedef struct tfx_softmax_desc {
+  int64_t batch, heads, q_len, k_len;
+  float scale;                   /* 1.0f = scores used as given */
+  int32_t semantics;             /* TFX_SOFTMAX_EXCLUDE or TFX_SOFTMAX_FILL */
+  int32_t causal;                /* nonzero: keep k <= q */
+  int32_t window_skips_invalid_query;
+  int64_t window;                /* < 0: no window */
+  int64_t valid_len;             /* < 0: all keys valid (ignored when valid_lens != NULL) */
+  const int32_t* valid_lens;     /* nullable device array [batch] */
+  const float* add_mask;         /* nullable device additive mask */
+  int64_t add_stride_b, add_stride_q, add_stride_k;
+  const uint8_t* keep;           /* nullable device boolean mask */
+  int64_t keep_stride_b, keep_stride_q, keep_stride_k;
+} tfx_softmax_desc;
+/* Fills a descriptor for an unmasked softmax over rows of length k_len. */
+TFX_API void tfx_softmax_desc_init(tfx_softmax_desc* desc, int64_t batch, int64_t heads,
+                           int64_t q_len, int64_t k_len);
+TFX_API int tfx_masked_softmax_f32(const float* scores, float* probs, const tfx_softmax_desc* desc,
+                           tfx_stream_t stream);
+
+/* ---- RoPE -----------------------------------------------------------------
+ * Replaces tenferro_infer::rope::{rope_modernbert, rope_qwen_partial}
+ * (crates/tenferro-infer/src/rope.rs:36-66, rotate_pair_half :68-113) and the
+ * RoPE step of FusedScope::laya_attention / jeff_attention.
+ * x, y are strided: element (vec v, position p, batch b, channel j) at
+ * v*stride_vec + p*stride_pos + b*stride_batch + j*stride_feat. Pairs are
+ * (i, i + rotary_dim/2) for i < rotary_dim/2:
+ *   y_i = x_i*cos - x_{i+half}*sin,  y_{i+half} = x_i*sin + x_{i+half}*cos
+ * each product rounded separately; channels j >= rotary_dim are copied.
+ * cos/sin are device tables (seq, rotary_dim/2), row-major, for positions
+ * 0..seq-1, e.g. from tfx_rope_tables_f32. y may equal x. */
+typedef struct tfx_rope_desc {
+  int64_t n_vec, seq, batch, head_dim, rotary_dim;
+  int64_t stride_vec, stride_pos, stride_batch, stride_feat;
+} tfx_rope_desc;
+TFX_API int tfx_rope_pairhalf_f32(const float* x, float* y, const float* cos_table,
+                          const float* sin_table, const tfx_rope_desc* desc,
+                          tfx_stream_t stream);
+/* Host helper (no GPU): the reference's tables, angle p * base^(-2i/rotary_dim)
+ * in f64, cos/sin rounded to f32 (rope.rs:84-92, table() :15-24). Host arrays
+ * of seq * rotary_dim/2 floats. */
+TFX_API int tfx_rope_tables_f32(double base, int64_t seq, int64_t rotary_dim, float* cos_host,
+                        float* sin_host);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFX_H */

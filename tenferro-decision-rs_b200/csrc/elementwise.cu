@@ -1,0 +1,478 @@
+// elementwise.cu -- streaming elementwise ops: erf / exact GELU (f32, f64),
+// GeGLU, gated SiLU (two-input and stacked), bias broadcast + activation and
+// the residual add.
+//
+// All of them are HBM-bound. One grid-stride kernel template moves U x 128-bit
+// vectors per thread per iteration: every load of an iteration is issued
+// before any result is computed, so a 256-thread CTA keeps U*4 KB in flight;
+// the grid is sized to the SM count times the kernel's occupancy. Pointers
+// that are not 16-byte aligned (or sizes that are not multiples of the vector)
+// take the same kernel with a vector width of 1. The f32 erf/GELU arithmetic
+// is the reference's (tfx_math.h), computed two values per instruction with
+// sm_100's paired f32 FMA.
+
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "tfx_math.h"
+
+namespace tfx {
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int N>
+struct Vec {
+  float v[N];
+};
+
+template <int N>
+__device__ __forceinline__ Vec<N> vload(const float* p, uint32_t i) {
+  Vec<N> r;
+  if constexpr (N == 4) {
+    const float4 q = ld_stream(reinterpret_cast<const float4*>(p) + i);
+    r.v[0] = q.x; r.v[1] = q.y; r.v[2] = q.z; r.v[3] = q.w;
+  } else if constexpr (N == 2) {
+    const float2 q = ld_stream(reinterpret_cast<const float2*>(p) + i);
+    r.v[0] = q.x; r.v[1] = q.y;
+  } else {
+    r.v[0] = ld_stream(p + i);
+  }
+  return r;
+}
+
+template <int N>
+__device__ __forceinline__ void vstore(float* p, uint32_t i, const Vec<N>& r) {
+  if constexpr (N == 4) {
+    reinterpret_cast<float4*>(p)[i] = make_float4(r.v[0], r.v[1], r.v[2], r.v[3]);
+  } else if constexpr (N == 2) {
+    reinterpret_cast<float2*>(p)[i] = make_float2(r.v[0], r.v[1]);
+  } else {
+    p[i] = r.v[0];
+  }
+}
+
+// Applies a pairwise (float2) / scalar function to a vector.
+template <int N, class P, class S>
+__device__ __forceinline__ Vec<N> apply(const Vec<N>& a, P pair_fn, S scalar_fn) {
+  Vec<N> r;
+#pragma unroll
+  for (int k = 0; k + 1 < N; k += 2) {
+    const float2 o = pair_fn(make_float2(a.v[k], a.v[k + 1]));
+    r.v[k] = o.x;
+    r.v[k + 1] = o.y;
+  }
+  if constexpr (N % 2 == 1) r.v[N - 1] = scalar_fn(a.v[N - 1]);
+  return r;
+}
+
+// Grid-stride driver: F::In load(i) gathers the inputs of vector i, and
+// F::store(i, in) computes and writes its outputs.
+template <class F, int U>
+__global__ void __launch_bounds__(kThreads) map_kernel(uint32_t n, F f) {
+  const uint32_t step = gridDim.x * (kThreads * U);
+  for (uint32_t base = blockIdx.x * (kThreads * U) + threadIdx.x; base < n; base += step) {
+    typename F::In in[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kThreads;
+      if (i < n) in[u] = f.load(i);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kThreads;
+      if (i < n) f.store(i, in[u]);
+    }
+    if (base > 0xFFFFFFFFu - step) break;  // next base would wrap
+  }
+}
+
+template <class F, int U>
+int launch_map(const char* op, uint32_t n, const F& f, cudaStream_t stream) {
+  if (n == 0) return TFX_OK;
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  static int occupancy = 0;  // per instantiation; identical on every B200
+  if (occupancy == 0) {
+    int blocks = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, map_kernel<F, U>, kThreads, 0) !=
+            cudaSuccess || blocks <= 0)
+      blocks = 1;
+    occupancy = blocks;
+  }
+  const uint64_t need = (uint64_t(n) + kThreads * U - 1) / (kThreads * U);
+  const uint32_t grid = uint32_t(std::min<uint64_t>(need, uint64_t(dev.sms) * occupancy));
+  map_kernel<F, U><<<grid, kThreads, 0, stream>>>(n, f);
+  return check_launch(op);
+}
+
+// ---- functors ------------------------------------------------------------------
+
+template <int N>
+struct ErfF {
+  using In = Vec<N>;
+  const float* x;
+  float* y;
+  __device__ In load(uint32_t i) const { return vload<N>(x, i); }
+  __device__ void store(uint32_t i, const In& a) const {
+    vstore<N>(y, i, apply<N>(a, [](float2 p) { return math::erf_mlx2(p); },
+                                [](float s) { return math::erf_mlx(s); }));
+  }
+};
+
+template <int N>
+struct GeluF {
+  using In = Vec<N>;
+  const float* x;
+  float* y;
+  __device__ In load(uint32_t i) const { return vload<N>(x, i); }
+  __device__ void store(uint32_t i, const In& a) const {
+    vstore<N>(y, i, apply<N>(a, [](float2 p) { return math::gelu_mlx2(p); },
+                                [](float s) { return math::gelu_mlx(s); }));
+  }
+};
+
+// GeGLU over feature-first u (2I, cols): output vector o covers outputs
+// [N*o, N*o + N) of the flattened (I, cols) result.
+template <int N>
+struct GegluF {
+  struct In {
+    Vec<N> v, g;
+  };
+  const float* u;
+  float* y;
+  FastDiv per_col;     // I / N output vectors per column
+  uint32_t inter_vec;  // I / N
+  __device__ In load(uint32_t o) const {
+    const uint32_t c = per_col.div(o);
+    const uint32_t i = o - c * inter_vec;
+    const uint32_t vi = c * 2 * inter_vec + i;  // vector index of the value half
+    In r;
+    r.v = vload<N>(u, vi);
+    r.g = vload<N>(u, vi + inter_vec);
+    return r;
+  }
+  __device__ void store(uint32_t o, const In& a) const {
+    Vec<N> out;
+#pragma unroll
+    for (int k = 0; k + 1 < N; k += 2) {
+      const float2 g = math::gelu_mlx2(make_float2(a.v.v[k], a.v.v[k + 1]));
+      const float2 p = __fmul2_rn(g, make_float2(a.g.v[k], a.g.v[k + 1]));
+      out.v[k] = p.x;
+      out.v[k + 1] = p.y;
+    }
+    if constexpr (N % 2 == 1) out.v[N - 1] = __fmul_rn(math::gelu_mlx(a.v.v[N - 1]), a.g.v[N - 1]);
+    vstore<N>(y, o, out);
+  }
+};
+
+// silu(g) * u = (g / (1 + exp(-g))) * u  (crates/cpu-kernels/src/lib.rs:603)
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+template <int N>
+struct SiluF {
+  struct In {
+    Vec<N> g, u;
+  };
+  const float* gate;
+  const float* up;
+  float* y;
+  __device__ In load(uint32_t i) const { return In{vload<N>(gate, i), vload<N>(up, i)}; }
+  __device__ void store(uint32_t i, const In& a) const {
+    Vec<N> out;
+#pragma unroll
+    for (int k = 0; k < N; ++k) out.v[k] = silu_mul(a.g.v[k], a.u.v[k]);
+    vstore<N>(y, i, out);
+  }
+};
+
+template <int N>
+struct AddF {
+  struct In {
+    Vec<N> a, b;
+  };
+  const float* a;
+  const float* b;
+  float* y;
+  __device__ In load(uint32_t i) const { return In{vload<N>(a, i), vload<N>(b, i)}; }
+  __device__ void store(uint32_t i, const In& v) const {
+    Vec<N> out;
+#pragma unroll
+    for (int k = 0; k + 1 < N; k += 2) {
+      const float2 s = __fadd2_rn(make_float2(v.a.v[k], v.a.v[k + 1]),
+                                  make_float2(v.b.v[k], v.b.v[k + 1]));
+      out.v[k] = s.x;
+      out.v[k + 1] = s.y;
+    }
+    if constexpr (N % 2 == 1) out.v[N - 1] = __fadd_rn(v.a.v[N - 1], v.b.v[N - 1]);
+    vstore<N>(y, i, out);
+  }
+};
+
+// act(x + bias[o]) over feature-first (F, tokens): vector i starts at feature
+// (N*i) mod F. ACT: 0 identity, 1 GELU (reference erf), 2 ReLU.
+template <int N, int ACT, bool BIAS>
+struct BiasActF {
+  using In = Vec<N>;
+  const float* x;
+  const float* bias;
+  float* y;
+  FastDiv per_tok;   // F / N vectors per token
+  uint32_t feat_vec; // F / N
+  __device__ In load(uint32_t i) const { return vload<N>(x, i); }
+  __device__ void store(uint32_t i, const In& a) const {
+    Vec<N> v = a;
+    if constexpr (BIAS) {
+      const uint32_t o = i - per_tok.div(i) * feat_vec;
+      Vec<N> b;
+      if constexpr (N == 4) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(bias) + o);
+        b.v[0] = q.x; b.v[1] = q.y; b.v[2] = q.z; b.v[3] = q.w;
+      } else {
+#pragma unroll
+        for (int k = 0; k < N; ++k) b.v[k] = __ldg(bias + o * N + k);
+      }
+#pragma unroll
+      for (int k = 0; k < N; ++k) v.v[k] = __fadd_rn(v.v[k], b.v[k]);
+    }
+    if constexpr (ACT == TFX_ACT_GELU_ERF) {
+      v = apply<N>(v, [](float2 p) { return math::gelu_mlx2(p); },
+                   [](float s) { return math::gelu_mlx(s); });
+    } else if constexpr (ACT == TFX_ACT_RELU) {
+#pragma unroll
+      for (int k = 0; k < N; ++k) v.v[k] = v.v[k] > 0.0f ? v.v[k] : 0.0f;
+    }
+    vstore<N>(y, i, v);
+  }
+};
+
+// ---- f64 erf / GELU (tenferro-ext/src/lib.rs:273-285, 224-234) ---------------
+
+__device__ __forceinline__ double erf_as(double x) {
+  if (x == 0.0) return 0.0;
+  const double sign = x < 0.0 ? -1.0 : 1.0;
+  x = fabs(x);
+  const double t = __ddiv_rn(1.0, __dadd_rn(1.0, __dmul_rn(0.3275911, x)));
+  double p = __dsub_rn(__dmul_rn(1.061405429, t), 1.453152027);
+  p = __dadd_rn(__dmul_rn(p, t), 1.421413741);
+  p = __dsub_rn(__dmul_rn(p, t), 0.284496736);
+  p = __dadd_rn(__dmul_rn(p, t), 0.254829592);
+  p = __dmul_rn(p, t);
+  return __dmul_rn(sign, __dsub_rn(1.0, __dmul_rn(p, exp(__dmul_rn(-x, x)))));
+}
+
+template <bool GELU>
+__global__ void __launch_bounds__(kThreads) erf_f64_kernel(const double* __restrict__ x,
+                                                           double* __restrict__ y, uint64_t n) {
+  const uint64_t step = uint64_t(gridDim.x) * kThreads;
+  for (uint64_t i = uint64_t(blockIdx.x) * kThreads + threadIdx.x; i < n; i += step) {
+    const double v = ld_stream(x + i);
+    if constexpr (GELU) {
+      const double gate = __dadd_rn(erf_as(__dmul_rn(v, 0.70710678118654752440)), 1.0);
+      y[i] = __dmul_rn(__dmul_rn(v, 0.5), gate);
+    } else {
+      y[i] = erf_as(v);
+    }
+  }
+}
+
+// ---- host-side dispatch ----------------------------------------------------------
+
+// Vector width usable for all pointers and the element count.
+int vec_width(int64_t n, std::initializer_list<const void*> ptrs) {
+  bool a16 = n % 4 == 0, a8 = n % 2 == 0;
+  for (const void* p : ptrs) {
+    a16 = a16 && aligned(p, 16);
+    a8 = a8 && aligned(p, 8);
+  }
+  return a16 ? 4 : (a8 ? 2 : 1);
+}
+
+constexpr int64_t kMaxVectors = int64_t(1) << 31;
+
+template <template <int> class F, class Make>
+int run_flat(const char* op, int64_t n, int width, Make make, cudaStream_t stream) {
+  if (n / width >= kMaxVectors)
+    return fail(TFX_ERR_UNSUPPORTED, op, "n", "more than 2^31 vectors in one call");
+  if (width == 4) return launch_map<F<4>, 4>(op, uint32_t(n / 4), make(F<4>{}), stream);
+  if (width == 2) return launch_map<F<2>, 4>(op, uint32_t(n / 2), make(F<2>{}), stream);
+  return launch_map<F<1>, 8>(op, uint32_t(n), make(F<1>{}), stream);
+}
+
+}  // namespace
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" {
+
+int tfx_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::erf";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
+  TFX_REQUIRE(x == y || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
+  const int w = vec_width(n, {x, y});
+  return run_flat<ErfF>(op, n, w, [&](auto f) { f.x = x; f.y = y; return f; }, stream);
+}
+
+int tfx_gelu_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gelu_erf";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
+  TFX_REQUIRE(x == y || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
+  const int w = vec_width(n, {x, y});
+  return run_flat<GeluF>(op, n, w, [&](auto f) { f.x = x; f.y = y; return f; }, stream);
+}
+
+int tfx_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::erf";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
+  TFX_REQUIRE(x == y || !overlaps(x, n * 8, y, n * 8), op, "y", "partially overlaps x");
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  const uint64_t grid = std::min<uint64_t>((uint64_t(n) + kThreads - 1) / kThreads,
+                                           uint64_t(dev.sms) * 8);
+  erf_f64_kernel<false><<<unsigned(grid), kThreads, 0, stream>>>(x, y, uint64_t(n));
+  return check_launch(op);
+}
+
+int tfx_gelu_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gelu_erf";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
+  TFX_REQUIRE(x == y || !overlaps(x, n * 8, y, n * 8), op, "y", "partially overlaps x");
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  const uint64_t grid = std::min<uint64_t>((uint64_t(n) + kThreads - 1) / kThreads,
+                                           uint64_t(dev.sms) * 8);
+  erf_f64_kernel<true><<<unsigned(grid), kThreads, 0, stream>>>(x, y, uint64_t(n));
+  return check_launch(op);
+}
+
+int tfx_geglu_ff_f32(const float* u, float* y, int64_t inter, int64_t cols, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::geglu";
+  TFX_REQUIRE(inter >= 0 && cols >= 0, op, "shape", "extents must be non-negative");
+  if (inter == 0 || cols == 0) return TFX_OK;
+  TFX_REQUIRE(u && y, op, u ? "y" : "u", "null pointer");
+  const int64_t n_out = inter * cols;
+  TFX_REQUIRE(!overlaps(u, size_t(2 * n_out) * 4, y, size_t(n_out) * 4), op, "y",
+              "output overlaps the input");
+  int w = vec_width(inter, {u, y});
+  if (n_out / w >= kMaxVectors || inter / w > 0xFFFFFFFFll)
+    return fail(TFX_ERR_UNSUPPORTED, op, "shape", "more than 2^31 output vectors in one call");
+  auto make = [&](auto f) {
+    f.u = u;
+    f.y = y;
+    f.inter_vec = uint32_t(inter / w);
+    f.per_col = FastDiv(uint32_t(inter / w));
+    return f;
+  };
+  if (w == 4) return launch_map<GegluF<4>, 2>(op, uint32_t(n_out / 4), make(GegluF<4>{}), stream);
+  if (w == 2) return launch_map<GegluF<2>, 4>(op, uint32_t(n_out / 2), make(GegluF<2>{}), stream);
+  return launch_map<GegluF<1>, 8>(op, uint32_t(n_out), make(GegluF<1>{}), stream);
+}
+
+int tfx_gated_silu_f32(const float* gate, const float* up, float* y, int64_t n,
+                       tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gated_silu";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(gate && up && y, op, !gate ? "gate" : (!up ? "up" : "y"), "null pointer");
+  TFX_REQUIRE(y == gate || !overlaps(gate, n * 4, y, n * 4), op, "y", "partially overlaps gate");
+  TFX_REQUIRE(y == up || !overlaps(up, n * 4, y, n * 4), op, "y", "partially overlaps up");
+  const int w = vec_width(n, {gate, up, y});
+  return run_flat<SiluF>(op, n, w, [&](auto f) { f.gate = gate; f.up = up; f.y = y; return f; },
+                         stream);
+}
+
+int tfx_gated_silu_stacked_f32(const float* gu, float* y, int64_t rows, int64_t inter,
+                               tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gated_silu_stacked";
+  TFX_REQUIRE(rows >= 0 && inter >= 0, op, "shape", "extents must be non-negative");
+  if (rows == 0 || inter == 0) return TFX_OK;
+  TFX_REQUIRE(gu && y, op, gu ? "y" : "gu", "null pointer");
+  const int64_t n = rows * inter;
+  TFX_REQUIRE(y == gu || !overlaps(gu, size_t(2 * n) * 4, y, size_t(n) * 4), op, "y",
+              "output overlaps the up half of gu");
+  const float* g = gu;
+  const float* u = gu + n;  // column blocks gate | up of the column-major (rows, 2I)
+  const int w = vec_width(n, {g, u, y});
+  return run_flat<SiluF>(op, n, w, [&](auto f) { f.gate = g; f.up = u; f.y = y; return f; },
+                         stream);
+}
+
+int tfx_add_f32(const float* a, const float* b, float* y, int64_t n, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::add";
+  TFX_REQUIRE(n >= 0, op, "n", "must be non-negative");
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(a && b && y, op, !a ? "a" : (!b ? "b" : "y"), "null pointer");
+  TFX_REQUIRE(y == a || !overlaps(a, n * 4, y, n * 4), op, "y", "partially overlaps a");
+  TFX_REQUIRE(y == b || !overlaps(b, n * 4, y, n * 4), op, "y", "partially overlaps b");
+  const int w = vec_width(n, {a, b, y});
+  return run_flat<AddF>(op, n, w, [&](auto f) { f.a = a; f.b = b; f.y = y; return f; }, stream);
+}
+
+int tfx_bias_act_ff_f32(const float* x, const float* bias, float* y, int64_t features,
+                        int64_t tokens, int act, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gemm_bias";
+  TFX_REQUIRE(features >= 0 && tokens >= 0, op, "shape", "extents must be non-negative");
+  TFX_REQUIRE(act == TFX_ACT_IDENTITY || act == TFX_ACT_GELU_ERF || act == TFX_ACT_RELU, op,
+              "act", "unknown activation " + std::to_string(act));
+  if (features == 0 || tokens == 0) return TFX_OK;
+  TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
+  const int64_t n = features * tokens;
+  TFX_REQUIRE(y == x || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
+  TFX_REQUIRE(!bias || !overlaps(bias, features * 4, y, n * 4), op, "bias", "overlaps y");
+  const int w = bias ? vec_width(features, {x, y, bias}) : vec_width(n, {x, y});
+  if (n / w >= kMaxVectors || features / w > 0xFFFFFFFFll)
+    return fail(TFX_ERR_UNSUPPORTED, op, "shape", "more than 2^31 vectors in one call");
+  const uint32_t nv = uint32_t(n / w);
+  auto go = [&](auto f, auto unroll) {
+    f.x = x;
+    f.bias = bias;
+    f.y = y;
+    f.feat_vec = uint32_t(features / w);
+    f.per_tok = FastDiv(uint32_t(features / w));
+    return launch_map<decltype(f), decltype(unroll)::value>(op, nv, f, stream);
+  };
+  using U4 = std::integral_constant<int, 4>;
+  using U8 = std::integral_constant<int, 8>;
+#define TFX_BIAS_CASE(A)                                                             \
+  if (act == A) {                                                                    \
+    if (bias) {                                                                      \
+      if (w == 4) return go(BiasActF<4, A, true>{}, U4{});                           \
+      if (w == 2) return go(BiasActF<2, A, true>{}, U4{});                           \
+      return go(BiasActF<1, A, true>{}, U8{});                                       \
+    }                                                                                \
+    if (w == 4) return go(BiasActF<4, A, false>{}, U4{});                            \
+    if (w == 2) return go(BiasActF<2, A, false>{}, U4{});                            \
+    return go(BiasActF<1, A, false>{}, U8{});                                        \
+  }
+  TFX_BIAS_CASE(TFX_ACT_IDENTITY)
+  TFX_BIAS_CASE(TFX_ACT_GELU_ERF)
+  TFX_BIAS_CASE(TFX_ACT_RELU)
+#undef TFX_BIAS_CASE
+  return fail(TFX_ERR_INVALID_ARGUMENT, op, "act", "unknown activation");
+}
+
+}  // extern "C"

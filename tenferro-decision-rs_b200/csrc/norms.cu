@@ -1,0 +1,596 @@
+// norms.cu -- feature-first LayerNorm and feature-last RMSNorm.
+//
+// LayerNorm (x is (d, cols), column c contiguous): one warp owns one column.
+// The whole column is loaded into registers with 128-bit loads (d <= 1024 f32
+// or d <= 1024 f64), so the reference's two passes -- the sum, then the
+// centred sum of squares (crates/cpu-kernels/src/lib.rs:413-433) -- run over
+// registers, and HBM sees exactly one read and one write of the activation.
+// Wider columns use a CTA per column with the column held by 256 threads;
+// anything else (unaligned, very wide) a CTA-per-column kernel that re-reads
+// the column from L2.
+//
+// RMSNorm (x is column-major (rows, width): a token's features are strided by
+// `rows`): a tile of 32*VEC consecutive tokens is read as one contiguous
+// 128*VEC-byte run per feature, and the feature axis of the tile is split
+// over a thread-block cluster of up to 8 CTAs. Each CTA keeps its share of the
+// tile in registers, reduces its partial sums of squares per token in shared
+// memory, and the cluster adds the partials through distributed shared memory
+// before every CTA scales and writes its own share -- one read and one write
+// of the activation, with the per-token reduction spread over up to 8 SMs.
+
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <string>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace tfx {
+namespace {
+
+// ---- arithmetic in the reference's operation order ------------------------------
+
+template <typename T>
+__device__ __forceinline__ T add_rn(T a, T b) {
+  if constexpr (std::is_same_v<T, float>) return __fadd_rn(a, b);
+  else return __dadd_rn(a, b);
+}
+template <typename T>
+__device__ __forceinline__ T sub_rn(T a, T b) {
+  if constexpr (std::is_same_v<T, float>) return __fsub_rn(a, b);
+  else return __dsub_rn(a, b);
+}
+template <typename T>
+__device__ __forceinline__ T mul_rn(T a, T b) {
+  if constexpr (std::is_same_v<T, float>) return __fmul_rn(a, b);
+  else return __dmul_rn(a, b);
+}
+template <typename T>
+__device__ __forceinline__ T div_rn(T a, T b) {
+  if constexpr (std::is_same_v<T, float>) return __fdiv_rn(a, b);
+  else return __ddiv_rn(a, b);
+}
+template <typename T>
+__device__ __forceinline__ T sqrt_rn(T a) {
+  if constexpr (std::is_same_v<T, float>) return __fsqrt_rn(a);
+  else return __dsqrt_rn(a);
+}
+
+// f32 (cpu-kernels lib.rs:413-424) divides the sums by d; the f64 composite
+// (tenferro-infer norm.rs:23-30) multiplies them by 1/width.
+template <typename T>
+__device__ __forceinline__ T scale_by_width(T sum, T d, T inv_d) {
+  if constexpr (std::is_same_v<T, float>) return div_rn(sum, d);
+  else return mul_rn(sum, inv_d);
+}
+
+// 16-byte vector of T.
+template <typename T>
+struct V16;
+template <>
+struct V16<float> {
+  static constexpr int N = 4;
+  float v[4];
+};
+template <>
+struct V16<double> {
+  static constexpr int N = 2;
+  double v[2];
+};
+
+template <typename T>
+__device__ __forceinline__ V16<T> load16(const T* p) {
+  V16<T> r;
+  if constexpr (std::is_same_v<T, float>) {
+    const float4 q = ld_stream(reinterpret_cast<const float4*>(p));
+    r.v[0] = q.x; r.v[1] = q.y; r.v[2] = q.z; r.v[3] = q.w;
+  } else {
+    const double2 q = ld_stream(reinterpret_cast<const double2*>(p));
+    r.v[0] = q.x; r.v[1] = q.y;
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ V16<T> ldg16(const T* p) {
+  V16<T> r;
+  if constexpr (std::is_same_v<T, float>) {
+    const float4 q = __ldg(reinterpret_cast<const float4*>(p));
+    r.v[0] = q.x; r.v[1] = q.y; r.v[2] = q.z; r.v[3] = q.w;
+  } else {
+    const double2 q = __ldg(reinterpret_cast<const double2*>(p));
+    r.v[0] = q.x; r.v[1] = q.y;
+  }
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void store16(T* p, const V16<T>& r) {
+  if constexpr (std::is_same_v<T, float>)
+    *reinterpret_cast<float4*>(p) = make_float4(r.v[0], r.v[1], r.v[2], r.v[3]);
+  else
+    *reinterpret_cast<double2*>(p) = make_double2(r.v[0], r.v[1]);
+}
+
+template <typename T>
+__device__ __forceinline__ T warp_sum_t(T v) {
+  return warp_sum(v);
+}
+
+// ---- LayerNorm: one warp per column, column in registers --------------------------
+
+// NV = 16-byte vectors per lane; d <= 32 * NV * V16<T>::N and d % V16<T>::N == 0.
+template <typename T, int NV, bool BIAS>
+__global__ void __launch_bounds__(256) ln_warp_kernel(const T* __restrict__ x,
+                                                      const T* __restrict__ w,
+                                                      const T* __restrict__ b, T* __restrict__ y,
+                                                      uint32_t d, uint64_t cols, T eps) {
+  constexpr int VN = V16<T>::N;
+  const int lane = threadIdx.x & 31;
+  const uint64_t col = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (col >= cols) return;  // the whole warp leaves together
+  const uint32_t dv = d / VN;
+  const T* xc = x + col * d;
+  V16<T> v[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) v[j] = load16(xc + q * VN);
+  }
+  T s = T(0);
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 32 + lane < dv)
+#pragma unroll
+      for (int k = 0; k < VN; ++k) s = add_rn(s, v[j].v[k]);
+  s = warp_sum_t(s);
+  const T dd = T(d), inv_d = T(1) / T(d);
+  const T mean = scale_by_width(s, dd, inv_d);
+  T ss = T(0);
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 32 + lane < dv)
+#pragma unroll
+      for (int k = 0; k < VN; ++k) {
+        const T c = sub_rn(v[j].v[k], mean);
+        ss = add_rn(ss, mul_rn(c, c));
+      }
+  ss = warp_sum_t(ss);
+  const T var = scale_by_width(ss, dd, inv_d);
+  const T inv = div_rn(T(1), sqrt_rn(add_rn(var, eps)));
+  T* yc = y + col * d;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const V16<T> wv = ldg16(w + q * VN);
+      V16<T> o;
+#pragma unroll
+      for (int k = 0; k < VN; ++k) o.v[k] = mul_rn(mul_rn(sub_rn(v[j].v[k], mean), inv), wv.v[k]);
+      if constexpr (BIAS) {
+        const V16<T> bv = ldg16(b + q * VN);
+#pragma unroll
+        for (int k = 0; k < VN; ++k) o.v[k] = add_rn(o.v[k], bv.v[k]);
+      }
+      store16(yc + q * VN, o);
+    }
+  }
+}
+
+// ---- LayerNorm: one CTA (256 threads) per column, column in registers --------------
+
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T* red /* [8] */) {
+  v = warp_sum_t(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();  // red may still be read from a previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  T s = T(0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = add_rn(s, red[i]);
+  return s;
+}
+
+template <typename T, int NV, bool BIAS>
+__global__ void __launch_bounds__(256) ln_cta_kernel(const T* __restrict__ x,
+                                                     const T* __restrict__ w,
+                                                     const T* __restrict__ b, T* __restrict__ y,
+                                                     uint32_t d, T eps) {
+  constexpr int VN = V16<T>::N;
+  __shared__ T red[8];
+  const uint64_t col = blockIdx.x;
+  const uint32_t dv = d / VN;
+  const T* xc = x + col * d;
+  V16<T> v[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 256 + threadIdx.x;
+    if (q < dv) v[j] = load16(xc + q * VN);
+  }
+  T s = T(0);
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 256 + threadIdx.x < dv)
+#pragma unroll
+      for (int k = 0; k < VN; ++k) s = add_rn(s, v[j].v[k]);
+  s = block_sum(s, red);
+  const T dd = T(d), inv_d = T(1) / T(d);
+  const T mean = scale_by_width(s, dd, inv_d);
+  T ss = T(0);
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (j * 256 + threadIdx.x < dv)
+#pragma unroll
+      for (int k = 0; k < VN; ++k) {
+        const T c = sub_rn(v[j].v[k], mean);
+        ss = add_rn(ss, mul_rn(c, c));
+      }
+  ss = block_sum(ss, red);
+  const T var = scale_by_width(ss, dd, inv_d);
+  const T inv = div_rn(T(1), sqrt_rn(add_rn(var, eps)));
+  T* yc = y + col * d;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 256 + threadIdx.x;
+    if (q < dv) {
+      const V16<T> wv = ldg16(w + q * VN);
+      V16<T> o;
+#pragma unroll
+      for (int k = 0; k < VN; ++k) o.v[k] = mul_rn(mul_rn(sub_rn(v[j].v[k], mean), inv), wv.v[k]);
+      if constexpr (BIAS) {
+        const V16<T> bv = ldg16(b + q * VN);
+#pragma unroll
+        for (int k = 0; k < VN; ++k) o.v[k] = add_rn(o.v[k], bv.v[k]);
+      }
+      store16(yc + q * VN, o);
+    }
+  }
+}
+
+// ---- LayerNorm: any d, any alignment (three passes over the column, L2-resident) --
+
+template <typename T>
+__global__ void __launch_bounds__(256) ln_generic_kernel(const T* x, const T* __restrict__ w,
+                                                         const T* __restrict__ b, T* y,
+                                                         uint64_t d, T eps) {
+  __shared__ T red[8];
+  const T* xc = x + uint64_t(blockIdx.x) * d;
+  T* yc = y + uint64_t(blockIdx.x) * d;
+  T s = T(0);
+  for (uint64_t i = threadIdx.x; i < d; i += 256) s = add_rn(s, xc[i]);
+  s = block_sum(s, red);
+  const T dd = T(d), inv_d = T(1) / T(d);
+  const T mean = scale_by_width(s, dd, inv_d);
+  T ss = T(0);
+  for (uint64_t i = threadIdx.x; i < d; i += 256) {
+    const T c = sub_rn(xc[i], mean);
+    ss = add_rn(ss, mul_rn(c, c));
+  }
+  ss = block_sum(ss, red);
+  const T var = scale_by_width(ss, dd, inv_d);
+  const T inv = div_rn(T(1), sqrt_rn(add_rn(var, eps)));
+  for (uint64_t i = threadIdx.x; i < d; i += 256) {
+    T o = mul_rn(mul_rn(sub_rn(xc[i], mean), inv), w[i]);
+    if (b) o = add_rn(o, b[i]);
+    yc[i] = o;
+  }
+}
+
+template <typename T>
+int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64_t d,
+                 int64_t cols, T eps, cudaStream_t stream) {
+  clear_error();
+  TFX_REQUIRE(d >= 0 && cols >= 0, op, "shape", "extents must be non-negative");
+  if (d == 0 || cols == 0) return TFX_OK;
+  TFX_REQUIRE(x, op, "x", "null pointer");
+  TFX_REQUIRE(w, op, "weight", "null pointer");
+  TFX_REQUIRE(y, op, "y", "null pointer");
+  const size_t bytes = size_t(d) * size_t(cols) * sizeof(T);
+  TFX_REQUIRE(y == x || !overlaps(x, bytes, y, bytes), op, "y", "partially overlaps x");
+  TFX_REQUIRE(!overlaps(w, size_t(d) * sizeof(T), y, bytes), op, "weight", "overlaps y");
+  TFX_REQUIRE(!b || !overlaps(b, size_t(d) * sizeof(T), y, bytes), op, "bias", "overlaps y");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  constexpr int VN = V16<T>::N;
+  const bool vec = d % VN == 0 && aligned(x, 16) && aligned(y, 16) && aligned(w, 16) &&
+                   (!b || aligned(b, 16));
+  const int64_t dv = d / VN;
+  const bool bias = b != nullptr;
+  if (vec && dv <= 32 * 16) {
+    TFX_REQUIRE(cols / 8 < (int64_t(1) << 31), op, "cols", "too many columns for one call");
+    const unsigned grid = unsigned((cols + 7) / 8);
+    const uint32_t du = uint32_t(d);
+#define TFX_LN_WARP(NVV)                                                                 \
+  if (dv <= 32 * NVV) {                                                                   \
+    if (bias) ln_warp_kernel<T, NVV, true><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);  \
+    else ln_warp_kernel<T, NVV, false><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);      \
+    return check_launch(op);                                                              \
+  }
+    TFX_LN_WARP(1)
+    TFX_LN_WARP(2)
+    TFX_LN_WARP(3)
+    TFX_LN_WARP(4)
+    TFX_LN_WARP(6)
+    TFX_LN_WARP(8)
+    TFX_LN_WARP(12)
+    TFX_LN_WARP(16)
+#undef TFX_LN_WARP
+  }
+  TFX_REQUIRE(cols < (int64_t(1) << 31), op, "cols", "too many columns for one call");
+  if (vec && dv <= 256 * 8) {
+    const unsigned grid = unsigned(cols);
+    const uint32_t du = uint32_t(d);
+#define TFX_LN_CTA(NVV)                                                                   \
+  if (dv <= 256 * NVV) {                                                                   \
+    if (bias) ln_cta_kernel<T, NVV, true><<<grid, 256, 0, stream>>>(x, w, b, y, du, eps);  \
+    else ln_cta_kernel<T, NVV, false><<<grid, 256, 0, stream>>>(x, w, b, y, du, eps);      \
+    return check_launch(op);                                                               \
+  }
+    TFX_LN_CTA(2)
+    TFX_LN_CTA(4)
+    TFX_LN_CTA(8)
+#undef TFX_LN_CTA
+  }
+  ln_generic_kernel<T><<<unsigned(cols), 256, 0, stream>>>(x, w, b, y, uint64_t(d), eps);
+  return check_launch(op);
+}
+
+// ---- RMSNorm feature-last: cluster-split register tiles ---------------------------
+
+template <typename T, int VEC>
+struct RowVec {
+  T v[VEC];
+};
+
+template <typename T, int VEC>
+__device__ __forceinline__ RowVec<T, VEC> load_rows(const T* p) {
+  RowVec<T, VEC> r;
+  if constexpr (sizeof(T) * VEC == 16) {
+    const V16<T> q = load16(p);
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) r.v[k] = q.v[k];
+  } else if constexpr (std::is_same_v<T, float> && VEC == 2) {
+    const float2 q = ld_stream(reinterpret_cast<const float2*>(p));
+    r.v[0] = q.x;
+    r.v[1] = q.y;
+  } else {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) r.v[k] = ld_stream(p + k);
+  }
+  return r;
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void store_rows(T* p, const RowVec<T, VEC>& r) {
+  if constexpr (sizeof(T) * VEC == 16) {
+    V16<T> q;
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) q.v[k] = r.v[k];
+    store16(p, q);
+  } else if constexpr (std::is_same_v<T, float> && VEC == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(r.v[0], r.v[1]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) p[k] = r.v[k];
+  }
+}
+
+constexpr int kRmsWarps = 8;
+
+// One cluster of C CTAs owns tokens [tile*32*VEC, (tile+1)*32*VEC); CTA `rank`
+// owns features [rank*fpc, min(width, (rank+1)*fpc)); warp w of it owns the
+// features f0 + w + 8k, k < FPT; lane l owns tokens tile*32*VEC + l*VEC + [0, VEC).
+template <typename T, int VEC, int FPT>
+__global__ void __launch_bounds__(kRmsWarps * 32) rms_cluster_kernel(
+    const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, uint32_t rows,
+    uint32_t width, uint32_t fpc, T eps, T inv_width, int centered) {
+  constexpr int TR = 32 * VEC;  // tokens per tile
+  __shared__ T red[kRmsWarps][TR];
+  __shared__ T part[TR];
+  __shared__ T scale_s[TR];
+  cg::cluster_group cluster = cg::this_cluster();
+  const uint32_t rank = cluster.block_rank();
+  const uint32_t csize = cluster.num_blocks();
+  const uint32_t tile = blockIdx.x / csize;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t r0 = tile * TR + lane * VEC;
+  const bool row_ok = r0 < rows;  // rows % VEC == 0: a vector is all in or all out
+  const uint32_t f0 = rank * fpc;
+  const uint32_t f1 = min(width, f0 + fpc);
+
+  RowVec<T, VEC> v[FPT];
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + kRmsWarps * k;
+    if (row_ok && f < f1) v[k] = load_rows<T, VEC>(x + uint64_t(f) * rows + r0);
+  }
+  T ss[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) ss[j] = T(0);
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + kRmsWarps * k;
+    if (row_ok && f < f1)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) ss[j] = add_rn(ss[j], mul_rn(v[k].v[j], v[k].v[j]));
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) red[warp][lane * VEC + j] = ss[j];
+  __syncthreads();
+  if (threadIdx.x < TR) {
+    T s = T(0);
+#pragma unroll
+    for (int i = 0; i < kRmsWarps; ++i) s = add_rn(s, red[i][threadIdx.x]);
+    part[threadIdx.x] = s;
+  }
+  cluster.sync();  // every CTA's partial sums are visible cluster-wide
+  if (threadIdx.x < TR) {
+    T tot = T(0);
+    for (uint32_t c = 0; c < csize; ++c) tot = add_rn(tot, *cluster.map_shared_rank(&part[threadIdx.x], c));
+    // scale = 1 / sqrt(mean_sq * (1/width) + eps)  (cpu-kernels lib.rs:571)
+    scale_s[threadIdx.x] = div_rn(T(1), sqrt_rn(add_rn(mul_rn(tot, inv_width), eps)));
+  }
+  cluster.sync();  // no CTA leaves while a peer may still read its partials
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + kRmsWarps * k;
+    if (row_ok && f < f1) {
+      const T wf = __ldg(w + f);
+      const T wt = centered ? add_rn(T(1), wf) : wf;
+      RowVec<T, VEC> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o.v[j] = mul_rn(mul_rn(v[k].v[j], scale_s[lane * VEC + j]), wt);
+      store_rows<T, VEC>(y + uint64_t(f) * rows + r0, o);
+    }
+  }
+}
+
+// Any width / alignment: a CTA per 32-token tile, two passes over the features
+// (the second read mostly hits L2).
+template <typename T>
+__global__ void __launch_bounds__(256) rms_generic_kernel(const T* x, const T* __restrict__ w,
+                                                          T* y, uint64_t rows,
+                                                          uint64_t width, T eps, T inv_width,
+                                                          int centered) {
+  __shared__ T red[8][32];
+  __shared__ T scale_s[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t r = uint64_t(blockIdx.x) * 32 + lane;
+  T ss = T(0);
+  if (r < rows)
+    for (uint64_t f = warp; f < width; f += 8) {
+      const T v = x[f * rows + r];
+      ss = add_rn(ss, mul_rn(v, v));
+    }
+  red[warp][lane] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    T s = T(0);
+    for (int i = 0; i < 8; ++i) s = add_rn(s, red[i][threadIdx.x]);
+    scale_s[threadIdx.x] = div_rn(T(1), sqrt_rn(add_rn(mul_rn(s, inv_width), eps)));
+  }
+  __syncthreads();
+  if (r < rows)
+    for (uint64_t f = warp; f < width; f += 8) {
+      const T wt = centered ? add_rn(T(1), w[f]) : w[f];
+      y[f * rows + r] = mul_rn(mul_rn(x[f * rows + r], scale_s[lane]), wt);
+    }
+}
+
+template <typename T, int VEC, int FPT>
+cudaError_t launch_rms_cluster(const T* x, const T* w, T* y, uint32_t rows, uint32_t width,
+                               int csize, uint32_t fpc, T eps, T inv_width, int centered,
+                               cudaStream_t stream) {
+  const uint32_t tiles = (rows + 32 * VEC - 1) / (32 * VEC);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles * csize, 1, 1);
+  cfg.blockDim = dim3(kRmsWarps * 32, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rms_cluster_kernel<T, VEC, FPT>, x, w, y, rows, width, fpc, eps,
+                            inv_width, centered);
+}
+
+// Picks (VEC, FPT, cluster size) for the shape; returns false if no cluster
+// configuration covers the width (then the generic kernel runs).
+template <typename T>
+int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int64_t width,
+                 int centered, T eps, cudaStream_t stream) {
+  clear_error();
+  TFX_REQUIRE(rows >= 0 && width >= 0, op, "shape", "extents must be non-negative");
+  if (rows == 0 || width == 0) return TFX_OK;
+  TFX_REQUIRE(x, op, "x", "null pointer");
+  TFX_REQUIRE(w, op, "weight", "null pointer");
+  TFX_REQUIRE(y, op, "y", "null pointer");
+  const size_t bytes = size_t(rows) * size_t(width) * sizeof(T);
+  TFX_REQUIRE(y == x || !overlaps(x, bytes, y, bytes), op, "y", "partially overlaps x");
+  TFX_REQUIRE(!overlaps(w, size_t(width) * sizeof(T), y, bytes), op, "weight", "overlaps y");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  // f32: 1/width as the f32 reciprocal (lib.rs:560); f64: 1.0 / width.
+  const T inv_width = T(1) / T(width);
+  const bool small = rows < (int64_t(1) << 31) && width < (int64_t(1) << 31) &&
+                     uint64_t(rows) * uint64_t(width) < (uint64_t(1) << 40);
+  int vec = 1;
+  constexpr int V16N = 16 / int(sizeof(T));
+  if (rows % V16N == 0 && aligned(x, 16) && aligned(y, 16)) vec = V16N;
+  else if (std::is_same_v<T, float> && rows % 2 == 0 && aligned(x, 8) && aligned(y, 8)) vec = 2;
+  if (small) {
+    const uint32_t r = uint32_t(rows), wd = uint32_t(width);
+    // Features per CTA = 8 warps * FPT; the cluster holds up to 8 CTAs.
+    auto try_cfg = [&](int fpt, auto launch) -> int {
+      const int64_t per_cta = int64_t(kRmsWarps) * fpt;
+      const int64_t csize = (width + per_cta - 1) / per_cta;
+      if (csize > 8) return 1;  // not covered
+      const uint32_t fpc = uint32_t((width + csize - 1) / csize);
+      const cudaError_t err = launch(int(csize), fpc);
+      if (err != cudaSuccess)
+        return fail(TFX_ERR_CUDA, op, "launch", std::string(cudaGetErrorName(err)) + ": " +
+                                                     cudaGetErrorString(err));
+      return TFX_OK;
+    };
+#define TFX_RMS_TRY(V, FPT)                                                                 \
+  {                                                                                         \
+    const int rc = try_cfg(FPT, [&](int cs, uint32_t fpc) {                                 \
+      return launch_rms_cluster<T, V, FPT>(x, w, y, r, wd, cs, fpc, eps, inv_width, centered, \
+                                           stream);                                         \
+    });                                                                                     \
+    if (rc != 1) return rc;                                                                 \
+  }
+    if constexpr (std::is_same_v<T, float>) {
+      if (vec == 4) { TFX_RMS_TRY(4, 4) TFX_RMS_TRY(4, 8) TFX_RMS_TRY(4, 16) }
+      else if (vec == 2) { TFX_RMS_TRY(2, 8) TFX_RMS_TRY(2, 16) TFX_RMS_TRY(2, 32) }
+      else { TFX_RMS_TRY(1, 16) TFX_RMS_TRY(1, 32) TFX_RMS_TRY(1, 64) }
+    } else {
+      if (vec == 2) { TFX_RMS_TRY(2, 4) TFX_RMS_TRY(2, 8) TFX_RMS_TRY(2, 16) }
+      else { TFX_RMS_TRY(1, 8) TFX_RMS_TRY(1, 16) TFX_RMS_TRY(1, 32) }
+    }
+#undef TFX_RMS_TRY
+  }
+  TFX_REQUIRE((rows + 31) / 32 < (int64_t(1) << 31), op, "rows", "too many rows for one call");
+  rms_generic_kernel<T><<<unsigned((rows + 31) / 32), 256, 0, stream>>>(
+      x, w, y, uint64_t(rows), uint64_t(width), eps, inv_width, centered);
+  return check_launch(op);
+}
+
+}  // namespace
+}  // namespace tfx
+
+extern "C" {
+
+int tfx_layernorm_ff_f32(const float* x, const float* weight, const float* bias, float* y,
+                         int64_t d, int64_t cols, float eps, tfx_stream_t stream) {
+  return tfx::layernorm_ff<float>("tenferro-ext::layernorm_ff", x, weight, bias, y, d, cols, eps,
+                                  stream);
+}
+
+int tfx_layernorm_ff_f64(const double* x, const double* weight, const double* bias, double* y,
+                         int64_t d, int64_t cols, double eps, tfx_stream_t stream) {
+  return tfx::layernorm_ff<double>("tenferro-infer::layer_norm", x, weight, bias, y, d, cols,
+                                   eps, stream);
+}
+
+int tfx_rmsnorm_last_f32(const float* x, const float* weight, float* y, int64_t rows,
+                         int64_t width, int centered, float eps, tfx_stream_t stream) {
+  return tfx::rmsnorm_last<float>("tenferro-ext::rms_norm_last", x, weight, y, rows, width,
+                                  centered ? 1 : 0, eps, stream);
+}
+
+int tfx_rmsnorm_last_f64(const double* x, const double* weight, double* y, int64_t rows,
+                         int64_t width, int centered, double eps, tfx_stream_t stream) {
+  return tfx::rmsnorm_last<double>("tenferro-infer::rms_norm", x, weight, y, rows, width,
+                                   centered ? 1 : 0, eps, stream);
+}
+
+}  // extern "C"

@@ -1,4 +1,4 @@
-"""pytest configuration: the `gpu` marker and import paths.
+"""pytest configuration: the `gpu` marker, import paths, and the in-tree builds.
 
 `-m "not gpu"` runs the oracle checks, host logic, C-ABI load/export checks and
 the gloo multi-process tests on CPU. `-m gpu` runs the parity tests proper,
@@ -12,9 +12,19 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "tenferro-decision-rs_b200")
-for path in (ROOT, PKG):
+for path in (ROOT, PKG, os.path.dirname(os.path.abspath(__file__))):
     if path not in sys.path:
         sys.path.insert(0, path)
+
+# libtfx.so is normally built by __graft_entry__.build(); build it here when a
+# checkout runs the tests first (nvcc cross-compiles without a GPU).
+if not os.path.exists(os.path.join(PKG, "lib", "libtfx.so")):
+    import importlib.util
+
+    _spec = importlib.util.spec_from_file_location("tfx_build", os.path.join(PKG, "build.py"))
+    _mod = importlib.util.module_from_spec(_spec)
+    _spec.loader.exec_module(_mod)
+    _mod.build()
 
 
 def pytest_configure(config):

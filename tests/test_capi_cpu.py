@@ -1,0 +1,111 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol the header
+declares, validates arguments before any CUDA call, and its host helpers agree
+with the oracle. No kernel is launched here."""
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import tfx
+from tfx import _lib
+from helpers import assert_bitwise
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_library_exports_every_header_symbol():
+    names = _lib.header_symbols()
+    assert len(names) >= 19
+    for name in names:
+        assert hasattr(_lib.lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert set(names) <= exported
+    # Everything else stays hidden (-fvisibility=hidden).
+    assert not [s for s in exported if s.startswith("tfx_") and s not in names]
+
+
+def test_version():
+    assert _lib.lib.tfx_version() == 10000
+
+
+@pytest.mark.parametrize("call,expect", [
+    (lambda L: L.tfx_layernorm_ff_f32(None, None, None, None, 8, 2, ctypes.c_float(1e-5), None),
+     "tenferro-ext::layernorm_ff: x: null pointer"),
+    (lambda L: L.tfx_layernorm_ff_f32(None, None, None, None, -1, 2, ctypes.c_float(1e-5), None),
+     "tenferro-ext::layernorm_ff: shape: extents must be non-negative"),
+    (lambda L: L.tfx_rmsnorm_last_f32(None, None, None, 4, 4, 1, ctypes.c_float(1e-6), None),
+     "tenferro-ext::rms_norm_last: x: null pointer"),
+    (lambda L: L.tfx_geglu_ff_f32(None, None, 3, 2, None), "tenferro-ext::geglu: u: null pointer"),
+    (lambda L: L.tfx_gated_silu_f32(None, None, None, -5, None),
+     "tenferro-ext::gated_silu: n: must be non-negative"),
+    (lambda L: L.tfx_bias_act_ff_f32(None, None, None, 4, 4, 7, None),
+     "tenferro-ext::gemm_bias: act: unknown activation 7"),
+    (lambda L: L.tfx_masked_softmax_f32(None, None, None, None),
+     "tenferro-infer::masked_softmax: desc: null pointer"),
+])
+def test_argument_errors_without_gpu(call, expect):
+    rc = call(_lib.lib)
+    assert rc == _lib.TFX_ERR_INVALID_ARGUMENT
+    assert tfx.last_error() == expect
+
+
+def test_empty_tensors_are_noops_without_gpu():
+    L = _lib.lib
+    assert L.tfx_layernorm_ff_f32(None, None, None, None, 0, 5, ctypes.c_float(1e-5), None) == 0
+    assert L.tfx_rmsnorm_last_f32(None, None, None, 0, 5, 1, ctypes.c_float(1e-6), None) == 0
+    assert L.tfx_erf_f32(None, None, 0, None) == 0
+    assert L.tfx_geglu_ff_f32(None, None, 0, 5, None) == 0
+    d = _lib.SoftmaxDesc()
+    L.tfx_softmax_desc_init(ctypes.byref(d), 0, 4, 8, 8)
+    assert L.tfx_masked_softmax_f32(None, None, ctypes.byref(d), None) == 0
+    assert tfx.last_error() == ""
+
+
+def test_softmax_desc_defaults():
+    d = _lib.SoftmaxDesc()
+    _lib.lib.tfx_softmax_desc_init(ctypes.byref(d), 2, 3, 4, 5)
+    assert (d.batch, d.heads, d.q_len, d.k_len) == (2, 3, 4, 5)
+    assert d.scale == 1.0 and d.window == -1 and d.valid_len == -1
+    assert d.semantics == _lib.TFX_SOFTMAX_EXCLUDE and not d.keep and not d.add_mask
+
+
+@pytest.mark.parametrize("base,seq,rot", [(160000.0, 512, 64), (10000.0, 512, 64),
+                                          (10000.0, 33, 6)])
+def test_rope_tables_match_oracle(orc, base, seq, rot):
+    half = rot // 2
+    c = np.empty(seq * half, np.float32)
+    s = np.empty(seq * half, np.float32)
+    assert _lib.lib.tfx_rope_tables_f32(ctypes.c_double(base), seq, rot,
+                                        c.ctypes.data_as(ctypes.c_void_p),
+                                        s.ctypes.data_as(ctypes.c_void_p)) == 0
+    oc, os_ = orc.rope_tables_f32(base, seq, rot)
+    assert_bitwise(c, oc, "cos")
+    assert_bitwise(s, os_, "sin")
+
+
+def test_rope_tables_reject_odd_width():
+    assert _lib.lib.tfx_rope_tables_f32(ctypes.c_double(1e4), 4, 3, None, None) == -1
+    assert "positive even number" in tfx.last_error()
+
+
+def test_product_erf_matches_oracle_over_bit_patterns(tmp_path):
+    """The product's branch-free erf / GELU (tfx_math.h, host-compiled) equal the
+    oracle's literal restatement bit for bit. Every 31st f32 bit pattern by
+    default; TFX_EXHAUSTIVE=1 checks all 2^32."""
+    exe = tmp_path / "erf_exhaustive"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-fno-fast-math",
+                    "-I", os.path.join(ROOT, "oracle"),
+                    "-I", os.path.join(ROOT, "tenferro-decision-rs_b200", "csrc"),
+                    os.path.join(ROOT, "tests", "native", "erf_exhaustive.cpp"),
+                    os.path.join(ROOT, "oracle", "oracle.cpp"), "-o", str(exe), "-lpthread"],
+                   check=True)
+    stride = "1" if os.environ.get("TFX_EXHAUSTIVE") == "1" else "31"
+    res = subprocess.run([str(exe), stride], capture_output=True, text=True, timeout=1800)
+    assert res.returncode == 0, res.stdout + res.stderr
+    assert "erf_mismatch=0 gelu_mismatch=0" in res.stdout
