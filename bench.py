@@ -233,10 +233,24 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
             evs[k][1].record()
         torch.cuda.synchronize()
         ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        # back-to-back launches with events only around the batch: the rate a
+        # stream of these launches sustains (launch overlap included)
+        b0 = torch.cuda.Event(enable_timing=True)
+        b1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(20_000_000)
+        b0.record()
+        for k in range(reps):
+            launch(bufs[k % sets])
+        b1.record()
+        torch.cuda.synchronize()
+        ms_b = b0.elapsed_time(b1) / reps
         gbs = nbytes / (ms * 1e-3) / 1e9
         results[name] = {"bytes": nbytes, "us": round(ms * 1e3, 3), "gbs": round(gbs, 1),
                          "frac_of_hbm": round(gbs / hbm_peak, 3),
-                         "gelem_s": round(elems / (ms * 1e-3) / 1e9, 2), "buffer_sets": sets}
+                         "gelem_s": round(elems / (ms * 1e-3) / 1e9, 2),
+                         "us_batched": round(ms_b * 1e3, 3),
+                         "gbs_batched": round(nbytes / (ms_b * 1e-3) / 1e9, 1),
+                         "buffer_sets": sets}
         del bufs
 
     # LayerNorm 768 x 8192 (f32 and the f64 copy)
@@ -375,35 +389,44 @@ def run_ours(args):
     sm_ms = max_over_ranks(sm_ms)
     value = world * args.steps * bytes_per_step / (ms * 1e-3) / 1e9
 
-    # end to end through the public API: pinned host inputs -> device -> chain ->
-    # host outputs, every step
+    # end to end through the public host-buffer API (tfx_session_*): every step
+    # copies its inputs from pinned host memory and its results back, pipelined
+    # inside each call; the calls block, so this leg is timed on the host clock.
+    from tfx.session import Session
     e2e_steps = max(2, min(args.steps, 10))
-    host_in = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in chain.inputs()]
-    for h_t, d_t in zip(host_in, chain.inputs()):
-        h_t.copy_(d_t)
-    host_out = [torch.empty(t.numel(), dtype=t.dtype, pin_memory=True) for t in chain.outputs()]
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+    hx0, hqkv, hsc, hattn, hu = (pin(t) for t in chain.inputs())
+    hg1, hg2 = pin(chain.gamma1), pin(chain.gamma2)
+    hh1, hqk, hpr, hh2, hh3, hg = (torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+                                   for t in chain.outputs())
+    c = CHAIN
+    sess = Session(local)
 
     def e2e_step(i):
-        for h_t, d_t in zip(host_in, chain.inputs()):
-            d_t.copy_(h_t, non_blocking=True)
-        chain.step(i)
-        for h_t, d_t in zip(host_out, chain.outputs()):
-            h_t.copy_(d_t, non_blocking=True)
+        local_layer = i % 2 == 0
+        theta = c["theta_local" if local_layer else "theta_global"]
+        sess.layer_norm_feature_first(hx0, hg1, None, 1e-5, out=hh1)
+        sess.rope_pairhalf(hqkv, theta, 2 * chain.H, chain.L, chain.B, chain.hd, chain.hd,
+                           (chain.hd, 3 * chain.h, 3 * chain.h * chain.L, 1), out=hqk)
+        sess.masked_softmax(hsc, chain.B, chain.H, chain.L, chain.L,
+                            window=c["window"] if local_layer else -1,
+                            valid_len=chain.L - c["pad"], out=hpr)
+        sess.add(hx0, hattn, out=hh2)
+        sess.layer_norm_feature_first(hh2, hg2, None, 1e-5, out=hh3)
+        sess.geglu(hu, chain.I, out=hg)
 
+    nb = lambda *ts: sum(t.numel() * t.element_size() for t in ts)  # noqa: E731
+    h2d = nb(hx0, hg1, hqkv, hsc, hx0, hattn, hh2, hg2, hu)
+    d2h = nb(hh1, hqk, hpr, hh2, hh3, hg)
     e2e_step(0)
-    torch.cuda.synchronize()
     barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
+    w0 = time.perf_counter()
     for i in range(e2e_steps):
         e2e_step(i)
-    e1.record()
-    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - w0) * 1e3
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    sess.close()
+    e2e_ms = max_over_ranks(e2e_ms)
     e2e_value = world * e2e_steps * bytes_per_step / (e2e_ms * 1e-3) / 1e9
 
     ops_results = None
@@ -462,7 +485,8 @@ def run_ours(args):
                      "us_per_launch": round(sm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "path": "pinned host buffers -> cudaMemcpyAsync -> tfx C ABI kernels -> host"},
+                "path": "tfx_session_* host-buffer calls (pinned host memory, chunked "
+                        "copy-in / kernel / copy-out pipelined over 3 streams), host clock"},
         "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,
         "clocks": clock_info,
         "cpu_baseline": cpu,

@@ -199,6 +199,52 @@ TFX_API int tfx_rope_pairhalf_f32(const float* x, float* y, const float* cos_tab
 TFX_API int tfx_rope_tables_f32(double base, int64_t seq, int64_t rotary_dim, float* cos_host,
                         float* sin_host);
 
+/* ---- host-buffer sessions ---------------------------------------------------
+ * The reference executes these ext ops on host tensors of a CPU session
+ * (execute_*_in_session over TensorRead slices, e.g.
+ * crates/tenferro-ext/src/layernorm.rs:94-231, rms_norm.rs:84-137,
+ * geglu.rs:85-121, gated_silu.rs:67-106, gemm_bias.rs:76-142). A session is
+ * the drop-in for that executor: same arguments as the device entry points
+ * above, but x / y / weights / masks are HOST pointers, and the call returns
+ * once the host outputs are written. Work is split into chunks along the
+ * token axis and pipelined (copy in, kernel, copy out) over three streams of
+ * the session's GPU. Pinned host memory makes the copies fully asynchronous.
+ * A session serialises its own calls; use one session per host thread for
+ * concurrency, or one per GPU. */
+typedef struct tfx_session tfx_session;
+TFX_API int tfx_session_create(int device, tfx_session** out);
+TFX_API int tfx_session_destroy(tfx_session* session);
+/* Target staging bytes (inputs + outputs) per pipelined chunk; default 32 MiB. */
+TFX_API int tfx_session_set_chunk_bytes(tfx_session* session, int64_t bytes);
+TFX_API int tfx_session_layernorm_ff_f32(tfx_session* session, const float* x,
+                                         const float* weight, const float* bias, float* y,
+                                         int64_t d, int64_t cols, float eps);
+TFX_API int tfx_session_layernorm_ff_f64(tfx_session* session, const double* x,
+                                         const double* weight, const double* bias, double* y,
+                                         int64_t d, int64_t cols, double eps);
+TFX_API int tfx_session_rmsnorm_last_f32(tfx_session* session, const float* x,
+                                         const float* weight, float* y, int64_t rows,
+                                         int64_t width, int centered, float eps);
+TFX_API int tfx_session_erf_f32(tfx_session* session, const float* x, float* y, int64_t n);
+TFX_API int tfx_session_gelu_erf_f32(tfx_session* session, const float* x, float* y, int64_t n);
+TFX_API int tfx_session_geglu_ff_f32(tfx_session* session, const float* u, float* y,
+                                     int64_t inter, int64_t cols);
+TFX_API int tfx_session_gated_silu_f32(tfx_session* session, const float* gate,
+                                       const float* up, float* y, int64_t n);
+TFX_API int tfx_session_bias_act_ff_f32(tfx_session* session, const float* x,
+                                        const float* bias, float* y, int64_t features,
+                                        int64_t tokens, int act);
+TFX_API int tfx_session_add_f32(tfx_session* session, const float* a, const float* b, float* y,
+                                int64_t n);
+/* desc->valid_lens / add_mask / keep are host pointers here. */
+TFX_API int tfx_session_masked_softmax_f32(tfx_session* session, const float* scores,
+                                           float* probs, const tfx_softmax_desc* desc);
+/* Tables are built from base as tfx_rope_tables_f32 does (and cached). y is x
+ * with the described vectors rotated: every element of x's extent that is not
+ * rotated is copied unchanged. */
+TFX_API int tfx_session_rope_pairhalf_f32(tfx_session* session, const float* x, float* y,
+                                          double base, const tfx_rope_desc* desc);
+
 #ifdef __cplusplus
 }
 #endif

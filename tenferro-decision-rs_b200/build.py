@@ -25,7 +25,7 @@ LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libtfx.so")
 INCLUDE = os.path.join(ROOT, "include")
 
-SOURCES = ["runtime.cu", "elementwise.cu", "norms.cu", "softmax.cu", "rope.cu"]
+SOURCES = ["runtime.cu", "elementwise.cu", "norms.cu", "softmax.cu", "rope.cu", "session.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [

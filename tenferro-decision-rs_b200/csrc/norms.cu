@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <string>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -480,6 +481,70 @@ __global__ void __launch_bounds__(256) rms_generic_kernel(const T* x, const T* _
     }
 }
 
+// Cluster-free alternative for f32: a CTA per 32-token tile; pass 1 streams
+// the tile's features (U loads in flight per thread) into per-token sums of
+// squares, pass 2 re-reads the tile -- from L2, which holds it since pass 1 --
+// and writes the scaled values.
+template <int U>
+__global__ void __launch_bounds__(256) rms_tile_kernel(const float* x,
+                                                       const float* __restrict__ w, float* y,
+                                                       uint32_t rows, uint32_t width, float eps,
+                                                       float inv_width, int centered) {
+  __shared__ float red[8][32];
+  __shared__ float scale_s[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t r = blockIdx.x * 32 + lane;
+  const bool ok = r < rows;
+  float ss = 0.0f;
+  for (uint32_t f0 = warp; f0 < width; f0 += 8 * U) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t f = f0 + 8 * u;
+      v[u] = (ok && f < width) ? ld_stream(x + uint64_t(f) * rows + r) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) ss = __fadd_rn(ss, __fmul_rn(v[u], v[u]));
+  }
+  red[warp][lane] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s = __fadd_rn(s, red[i][threadIdx.x]);
+    scale_s[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(s, inv_width), eps)));
+  }
+  __syncthreads();
+  const float sc = scale_s[lane];
+  for (uint32_t f0 = warp; f0 < width; f0 += 8 * U) {
+    float v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t f = f0 + 8 * u;
+      v[u] = (ok && f < width) ? __ldcg(x + uint64_t(f) * rows + r) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t f = f0 + 8 * u;
+      if (ok && f < width) {
+        const float wf = __ldg(w + f);
+        const float wt = centered ? __fadd_rn(1.0f, wf) : wf;
+        y[uint64_t(f) * rows + r] = __fmul_rn(__fmul_rn(v[u], sc), wt);
+      }
+    }
+  }
+}
+
+// Kernel choice for the f32 feature-last RMSNorm: "cluster" (default) or
+// "tile"; TFX_RMS_KERNEL overrides it for tuning runs.
+bool rms_use_tile() {
+  static const int choice = [] {
+    const char* e = getenv("TFX_RMS_KERNEL");
+    return (e && std::string(e) == "tile") ? 1 : 0;
+  }();
+  return choice == 1;
+}
+
 template <typename T, int VEC, int FPT>
 cudaError_t launch_rms_cluster(const T* x, const T* w, T* y, uint32_t rows, uint32_t width,
                                int csize, uint32_t fpc, T eps, T inv_width, int centered,
@@ -526,6 +591,13 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
   constexpr int V16N = 16 / int(sizeof(T));
   if (rows % V16N == 0 && aligned(x, 16) && aligned(y, 16)) vec = V16N;
   else if (std::is_same_v<T, float> && rows % 2 == 0 && aligned(x, 8) && aligned(y, 8)) vec = 2;
+  if constexpr (std::is_same_v<T, float>) {
+    if (small && rms_use_tile()) {
+      rms_tile_kernel<8><<<unsigned((rows + 31) / 32), 256, 0, stream>>>(
+          x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width, centered);
+      return check_launch(op);
+    }
+  }
   if (small) {
     const uint32_t r = uint32_t(rows), wd = uint32_t(width);
     // Features per CTA = 8 warps * FPT; the cluster holds up to 8 CTAs.

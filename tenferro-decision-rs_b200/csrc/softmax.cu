@@ -2,25 +2,33 @@
 // scores (keys contiguous).
 //
 // One warp owns one row of up to 1024 keys: the row is read once with 128-bit
-// loads into registers, the mask is evaluated from (q, k) arithmetic (window,
-// valid length, causality) plus the optional additive / boolean mask tensors,
-// the max and the sum are warp-shuffle reductions over registers, and the
-// probabilities are written once. Longer rows use a CTA per row (up to 8192
-// keys in registers); anything else a CTA-per-row kernel that re-reads the row
-// from L2. Semantics follow the reference (see tfx.h): EXCLUDE restates the
-// f32 attention rows of crates/cpu-kernels/src/lib.rs:1053-1080, FILL the
-// tenferro-infer masked_softmax (softmax.rs:26-34, util.rs:87).
+// loads into registers, the max and the sum are warp-shuffle reductions over
+// registers, and the probabilities are written once. Longer rows use a CTA per
+// row (up to 8192 keys in registers); anything else a CTA-per-row kernel that
+// re-reads the row from L2. Semantics follow the reference (see tfx.h):
+// EXCLUDE restates the f32 attention rows of crates/cpu-kernels/src/lib.rs:
+// 1053-1080, FILL the tenferro-infer masked_softmax (softmax.rs:26-34,
+// util.rs:87).
+//
+// The analytic mask conditions (valid length, causality, sliding window) all
+// keep one interval of keys per row, so each row computes [lo, hi) once and
+// every key is tested with one unsigned compare. The division p = e / sum is
+// done as e * (1/sum) followed by one FMA correction step (Markstein), which
+// returns the correctly rounded quotient for normal results; numerators that
+// could produce a subnormal quotient take the IEEE division instead.
 
 #include <cmath>
 #include <string>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace tfx {
 namespace {
 
 struct MaskArgs {
   int64_t heads, q_len, k_len;
+  int64_t row_offset;  // global index of the first row handed to the kernel
   int64_t window, valid_len;
   const int32_t* valid_lens;
   const float* add;
@@ -28,59 +36,76 @@ struct MaskArgs {
   const uint8_t* keep;
   int64_t keep_sb, keep_sq, keep_sk;
   float scale;
-  int causal, skip_invalid_q, semantics;
+  int causal, skip_invalid_q;
 };
 
+// Keys [lo, lo + span) of a row pass the analytic conditions.
 struct RowCtx {
-  int64_t b, q, vlen;
-  bool window_on;
+  int64_t b, q;
+  uint32_t lo, span;  // kept iff (uint32)(k - lo) < span
 };
 
-__device__ __forceinline__ RowCtx row_ctx(const MaskArgs& m, uint64_t row) {
+__device__ __forceinline__ RowCtx row_ctx(const MaskArgs& m, uint64_t local_row) {
   RowCtx c;
+  const uint64_t row = local_row + uint64_t(m.row_offset);
   c.q = int64_t(row % uint64_t(m.q_len));
   c.b = int64_t(row / uint64_t(m.heads * m.q_len));
-  c.vlen = m.valid_lens ? int64_t(m.valid_lens[c.b]) : m.valid_len;
-  c.window_on = m.window >= 0 && !(m.skip_invalid_q && c.vlen >= 0 && c.q >= c.vlen);
+  const int64_t vlen = m.valid_lens ? int64_t(m.valid_lens[c.b]) : m.valid_len;
+  int64_t lo = 0, hi = m.k_len;
+  if (vlen >= 0) hi = min(hi, vlen);
+  if (m.causal) hi = min(hi, c.q + 1);
+  if (m.window >= 0 && !(m.skip_invalid_q && vlen >= 0 && c.q >= vlen)) {
+    lo = max(lo, c.q - m.window);
+    hi = min(hi, c.q + m.window + 1);
+  }
+  if (hi < lo) hi = lo;
+  c.lo = uint32_t(lo);
+  c.span = uint32_t(hi - lo);
   return c;
 }
 
-template <bool TENSORS>
-__device__ __forceinline__ bool kept(const MaskArgs& m, const RowCtx& c, int64_t k) {
-  if (c.vlen >= 0 && k >= c.vlen) return false;
-  if (m.causal && k > c.q) return false;
-  if (c.window_on) {
-    const int64_t diff = c.q > k ? c.q - k : k - c.q;
-    if (diff > m.window) return false;
-  }
-  if constexpr (TENSORS) {
-    if (m.keep && m.keep[c.b * m.keep_sb + c.q * m.keep_sq + k * m.keep_sk] == 0) return false;
-  }
-  return true;
-}
+constexpr int kExclude = TFX_SOFTMAX_EXCLUDE;
 
-// The masked, scaled score of key k (EXCLUDE: -inf when masked; FILL: -1e30).
-template <bool TENSORS>
-__device__ __forceinline__ float score(const MaskArgs& m, const RowCtx& c, int64_t k, float s) {
-  const bool keep = kept<TENSORS>(m, c, k);
-  if (m.semantics == TFX_SOFTMAX_EXCLUDE && !keep) return -INFINITY;
+// Masked, scaled score of key k (in range). EXCLUDE: -inf when masked;
+// FILL: -1e30 when masked (util.rs:87).
+template <int SEM, bool TENSORS>
+__device__ __forceinline__ float score(const MaskArgs& m, const RowCtx& c, uint32_t k, float s) {
+  bool keep = k - c.lo < c.span;
+  if constexpr (TENSORS) {
+    if (m.keep && m.keep[c.b * m.keep_sb + c.q * m.keep_sq + int64_t(k) * m.keep_sk] == 0)
+      keep = false;
+  }
   float v = __fmul_rn(s, m.scale);
   if constexpr (TENSORS) {
-    if (m.add) v = __fadd_rn(v, __ldg(m.add + c.b * m.add_sb + c.q * m.add_sq + k * m.add_sk));
+    if (m.add && keep)
+      v = __fadd_rn(v, __ldg(m.add + c.b * m.add_sb + c.q * m.add_sq + int64_t(k) * m.add_sk));
   }
-  if (!keep) v = -1.0e30f;
-  return v;
+  return keep ? v : (SEM == kExclude ? -INFINITY : -1.0e30f);
 }
 
-// p = exp(v - max), EXCLUDE: non-finite v contributes 0.
-__device__ __forceinline__ float expo(const MaskArgs& m, float v, float mx) {
-  if (m.semantics == TFX_SOFTMAX_EXCLUDE && !isfinite(v)) return 0.0f;
-  return expf(__fsub_rn(v, mx));
+// exp(v - max); EXCLUDE: non-finite v (masked, NaN, inf) contributes 0.
+template <int SEM>
+__device__ __forceinline__ float expo(float v, float mx) {
+  const float e = expf(__fsub_rn(v, mx));
+  if constexpr (SEM == kExclude) return fabsf(v) < INFINITY ? e : 0.0f;
+  return e;
+}
+
+// e / sum, correctly rounded (see the file comment); r = 1/sum rounded.
+__device__ __forceinline__ float quotient(float e, float sum, float r, bool fast) {
+  float q = __fmul_rn(e, r);
+  if (fast && e >= 0x1p-100f) {
+    const float res = __fmaf_rn(-q, sum, e);
+    q = __fmaf_rn(res, r, q);
+  } else if (e != 0.0f) {
+    q = __fdiv_rn(e, sum);
+  }
+  return q;
 }
 
 // ---- warp per row, NV float4 per lane ------------------------------------------
 
-template <int NV, bool TENSORS>
+template <int NV, int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ s,
                                                            float* __restrict__ p, uint64_t rows,
                                                            MaskArgs m) {
@@ -105,7 +130,7 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
     const uint32_t q4 = j * 32 + lane;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? score<TENSORS>(m, c, int64_t(q4) * 4 + e, v[j][e]) : -INFINITY;
+      v[j][e] = q4 < kv ? score<SEM, TENSORS>(m, c, q4 * 4 + e, v[j][e]) : -INFINITY;
       mx = fmaxf(mx, v[j][e]);
     }
   }
@@ -113,21 +138,22 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
   float sum = 0.0f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 32 + lane;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? expo(m, v[j][e], mx) : 0.0f;
+      v[j][e] = expo<SEM>(v[j][e], mx);
       sum = __fadd_rn(sum, v[j][e]);
     }
   }
   sum = warp_sum(sum);
+  const float r = __frcp_rn(sum);
+  const bool fast = sum < 0x1p24f;
   float4* dst = reinterpret_cast<float4*>(p + row * uint64_t(m.k_len));
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const uint32_t q4 = j * 32 + lane;
     if (q4 < kv)
-      dst[q4] = make_float4(__fdiv_rn(v[j][0], sum), __fdiv_rn(v[j][1], sum),
-                            __fdiv_rn(v[j][2], sum), __fdiv_rn(v[j][3], sum));
+      dst[q4] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
+                            quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
   }
 }
 
@@ -145,7 +171,7 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
   return r;
 }
 
-template <int NV, bool TENSORS>
+template <int NV, int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restrict__ s,
                                                           float* __restrict__ p, MaskArgs m) {
   __shared__ float red[8];
@@ -168,7 +194,7 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
     const uint32_t q4 = j * 256 + threadIdx.x;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? score<TENSORS>(m, c, int64_t(q4) * 4 + e, v[j][e]) : -INFINITY;
+      v[j][e] = q4 < kv ? score<SEM, TENSORS>(m, c, q4 * 4 + e, v[j][e]) : -INFINITY;
       mx = fmaxf(mx, v[j][e]);
     }
   }
@@ -176,27 +202,28 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
   float sum = 0.0f;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 256 + threadIdx.x;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? expo(m, v[j][e], mx) : 0.0f;
+      v[j][e] = expo<SEM>(v[j][e], mx);
       sum = __fadd_rn(sum, v[j][e]);
     }
   }
   sum = block_reduce(sum, red, false);
+  const float r = __frcp_rn(sum);
+  const bool fast = sum < 0x1p24f;
   float4* dst = reinterpret_cast<float4*>(p + row * uint64_t(m.k_len));
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const uint32_t q4 = j * 256 + threadIdx.x;
     if (q4 < kv)
-      dst[q4] = make_float4(__fdiv_rn(v[j][0], sum), __fdiv_rn(v[j][1], sum),
-                            __fdiv_rn(v[j][2], sum), __fdiv_rn(v[j][3], sum));
+      dst[q4] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
+                            quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
   }
 }
 
 // ---- any length / alignment: CTA per row, three passes (row re-read from L2) ----
 
-template <bool TENSORS>
+template <int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* s, float* p,
                                                               MaskArgs m) {
   __shared__ float red[8];
@@ -204,45 +231,70 @@ __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* s, fl
   const RowCtx c = row_ctx(m, row);
   const float* src = s + row * uint64_t(m.k_len);
   float* dst = p + row * uint64_t(m.k_len);
+  const uint32_t n = uint32_t(m.k_len);
   float mx = -INFINITY;
-  for (int64_t k = threadIdx.x; k < m.k_len; k += 256) mx = fmaxf(mx, score<TENSORS>(m, c, k, src[k]));
+  for (uint32_t k = threadIdx.x; k < n; k += 256)
+    mx = fmaxf(mx, score<SEM, TENSORS>(m, c, k, src[k]));
   mx = block_reduce(mx, red, true);
   float sum = 0.0f;
-  for (int64_t k = threadIdx.x; k < m.k_len; k += 256)
-    sum = __fadd_rn(sum, expo(m, score<TENSORS>(m, c, k, src[k]), mx));
+  for (uint32_t k = threadIdx.x; k < n; k += 256)
+    sum = __fadd_rn(sum, expo<SEM>(score<SEM, TENSORS>(m, c, k, src[k]), mx));
   sum = block_reduce(sum, red, false);
-  __syncthreads();  // every read of src precedes any write of dst (in-place calls)
-  // In place, dst == src: each thread reads then writes only its own keys.
-  for (int64_t k = threadIdx.x; k < m.k_len; k += 256)
-    dst[k] = __fdiv_rn(expo(m, score<TENSORS>(m, c, k, src[k]), mx), sum);
+  const float r = __frcp_rn(sum);
+  const bool fast = sum < 0x1p24f;
+  // In place (dst == src) each thread reads, then writes, only its own keys.
+  for (uint32_t k = threadIdx.x; k < n; k += 256)
+    dst[k] = quotient(expo<SEM>(score<SEM, TENSORS>(m, c, k, src[k]), mx), sum, r, fast);
+}
+
+template <int SEM, bool TENSORS>
+int launch_softmax(const char* op, const float* scores, float* probs, int64_t rows, int64_t kl,
+                   const MaskArgs& m, cudaStream_t stream) {
+  const bool vec = kl % 4 == 0 && aligned(scores, 16) && aligned(probs, 16);
+  const int64_t kv = kl / 4;
+  if (vec && kv <= 32 * 8) {
+    TFX_REQUIRE(rows / 8 < (int64_t(1) << 31), op, "shape", "too many rows for one call");
+    const unsigned grid = unsigned((rows + 7) / 8);
+#define TFX_SM_WARP(NV)                                                                    \
+  if (kv <= 32 * NV) {                                                                     \
+    softmax_warp_kernel<NV, SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, rows, m); \
+    return check_launch(op);                                                               \
+  }
+    TFX_SM_WARP(1)
+    TFX_SM_WARP(2)
+    TFX_SM_WARP(3)
+    TFX_SM_WARP(4)
+    TFX_SM_WARP(6)
+    TFX_SM_WARP(8)
+#undef TFX_SM_WARP
+  }
+  TFX_REQUIRE(rows < (int64_t(1) << 31), op, "shape", "too many rows for one call");
+  const unsigned grid = unsigned(rows);
+  if (vec && kv <= 256 * 8) {
+#define TFX_SM_CTA(NV)                                                              \
+  if (kv <= 256 * NV) {                                                             \
+    softmax_cta_kernel<NV, SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, m); \
+    return check_launch(op);                                                        \
+  }
+    TFX_SM_CTA(2)
+    TFX_SM_CTA(4)
+    TFX_SM_CTA(8)
+#undef TFX_SM_CTA
+  }
+  softmax_generic_kernel<SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, m);
+  return check_launch(op);
 }
 
 }  // namespace
-}  // namespace tfx
 
-using namespace tfx;
-
-extern "C" int tfx_masked_softmax_f32(const float* scores, float* probs,
-                                      const tfx_softmax_desc* d, tfx_stream_t stream) {
-  clear_error();
+// Rows [row_begin, row_begin + row_count) of the softmax described by d;
+// scores / probs point at row row_begin. Arguments are validated by the caller.
+int masked_softmax_rows(const float* scores, float* probs, const tfx_softmax_desc* d,
+                        int64_t row_begin, int64_t row_count, cudaStream_t stream) {
   const char* op = "tenferro-infer::masked_softmax";
-  TFX_REQUIRE(d, op, "desc", "null pointer");
-  TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->q_len >= 0 && d->k_len >= 0, op, "shape",
-              "extents must be non-negative");
-  TFX_REQUIRE(d->semantics == TFX_SOFTMAX_EXCLUDE || d->semantics == TFX_SOFTMAX_FILL, op,
-              "semantics", "unknown semantics " + std::to_string(d->semantics));
-  const int64_t rows = d->batch * d->heads * d->q_len;
-  if (rows == 0 || d->k_len == 0) return TFX_OK;
-  TFX_REQUIRE(scores && probs, op, scores ? "probs" : "scores", "null pointer");
-  const size_t bytes = size_t(rows) * size_t(d->k_len) * 4;
-  TFX_REQUIRE(probs == scores || !overlaps(scores, bytes, probs, bytes), op, "probs",
-              "partially overlaps scores");
-  TFX_REQUIRE(rows < (int64_t(1) << 40), op, "shape", "too many rows");
-  int st = TFX_OK;
-  device_info(&st);
-  if (st != TFX_OK) return st;
-
+  if (row_count == 0) return TFX_OK;
   MaskArgs m;
+  m.row_offset = row_begin;
   m.heads = d->heads;
   m.q_len = d->q_len;
   m.k_len = d->k_len;
@@ -260,43 +312,47 @@ extern "C" int tfx_masked_softmax_f32(const float* scores, float* probs,
   m.scale = d->scale;
   m.causal = d->causal ? 1 : 0;
   m.skip_invalid_q = d->window_skips_invalid_query ? 1 : 0;
-  m.semantics = d->semantics;
   const bool tensors = m.add != nullptr || m.keep != nullptr;
+  const int64_t kl = d->k_len;
+  if (d->semantics == TFX_SOFTMAX_EXCLUDE) {
+    if (tensors) return launch_softmax<TFX_SOFTMAX_EXCLUDE, true>(op, scores, probs, row_count, kl, m, stream);
+    return launch_softmax<TFX_SOFTMAX_EXCLUDE, false>(op, scores, probs, row_count, kl, m, stream);
+  }
+  if (tensors) return launch_softmax<TFX_SOFTMAX_FILL, true>(op, scores, probs, row_count, kl, m, stream);
+  return launch_softmax<TFX_SOFTMAX_FILL, false>(op, scores, probs, row_count, kl, m, stream);
+}
 
-  const bool vec = d->k_len % 4 == 0 && aligned(scores, 16) && aligned(probs, 16);
-  const int64_t kv = d->k_len / 4;
-  if (vec && kv <= 32 * 8) {
-    TFX_REQUIRE(rows / 8 < (int64_t(1) << 31), op, "shape", "too many rows for one call");
-    const unsigned grid = unsigned((rows + 7) / 8);
-#define TFX_SM_WARP(NV)                                                                       \
-  if (kv <= 32 * NV) {                                                                        \
-    if (tensors) softmax_warp_kernel<NV, true><<<grid, 256, 0, stream>>>(scores, probs, rows, m); \
-    else softmax_warp_kernel<NV, false><<<grid, 256, 0, stream>>>(scores, probs, rows, m);   \
-    return check_launch(op);                                                                  \
-  }
-    TFX_SM_WARP(1)
-    TFX_SM_WARP(2)
-    TFX_SM_WARP(3)
-    TFX_SM_WARP(4)
-    TFX_SM_WARP(6)
-    TFX_SM_WARP(8)
-#undef TFX_SM_WARP
-  }
-  TFX_REQUIRE(rows < (int64_t(1) << 31), op, "shape", "too many rows for one call");
-  const unsigned grid = unsigned(rows);
-  if (vec && kv <= 256 * 8) {
-#define TFX_SM_CTA(NV)                                                                   \
-  if (kv <= 256 * NV) {                                                                  \
-    if (tensors) softmax_cta_kernel<NV, true><<<grid, 256, 0, stream>>>(scores, probs, m); \
-    else softmax_cta_kernel<NV, false><<<grid, 256, 0, stream>>>(scores, probs, m);     \
-    return check_launch(op);                                                             \
-  }
-    TFX_SM_CTA(2)
-    TFX_SM_CTA(4)
-    TFX_SM_CTA(8)
-#undef TFX_SM_CTA
-  }
-  if (tensors) softmax_generic_kernel<true><<<grid, 256, 0, stream>>>(scores, probs, m);
-  else softmax_generic_kernel<false><<<grid, 256, 0, stream>>>(scores, probs, m);
-  return check_launch(op);
+int validate_softmax(const float* scores, const float* probs, const tfx_softmax_desc* d,
+                     int64_t* rows_out) {
+  const char* op = "tenferro-infer::masked_softmax";
+  TFX_REQUIRE(d, op, "desc", "null pointer");
+  TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->q_len >= 0 && d->k_len >= 0, op, "shape",
+              "extents must be non-negative");
+  TFX_REQUIRE(d->semantics == TFX_SOFTMAX_EXCLUDE || d->semantics == TFX_SOFTMAX_FILL, op,
+              "semantics", "unknown semantics " + std::to_string(d->semantics));
+  TFX_REQUIRE(d->k_len < (int64_t(1) << 31), op, "k_len", "rows longer than 2^31 keys");
+  const int64_t rows = d->batch * d->heads * d->q_len;
+  *rows_out = d->k_len == 0 ? 0 : rows;
+  if (rows == 0 || d->k_len == 0) return TFX_OK;
+  TFX_REQUIRE(scores && probs, op, scores ? "probs" : "scores", "null pointer");
+  const size_t bytes = size_t(rows) * size_t(d->k_len) * 4;
+  TFX_REQUIRE(probs == scores || !overlaps(scores, bytes, probs, bytes), op, "probs",
+              "partially overlaps scores");
+  TFX_REQUIRE(rows < (int64_t(1) << 40), op, "shape", "too many rows");
+  return TFX_OK;
+}
+
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" int tfx_masked_softmax_f32(const float* scores, float* probs,
+                                      const tfx_softmax_desc* d, tfx_stream_t stream) {
+  clear_error();
+  int64_t rows = 0;
+  int rc = validate_softmax(scores, probs, d, &rows);
+  if (rc != TFX_OK || rows == 0) return rc;
+  device_info(&rc);
+  if (rc != TFX_OK) return rc;
+  return masked_softmax_rows(scores, probs, d, 0, rows, stream);
 }

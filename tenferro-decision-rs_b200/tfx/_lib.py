@@ -82,6 +82,21 @@ SIGNATURES = {
     "tfx_masked_softmax_f32": (_int, [_p, _p, ctypes.POINTER(SoftmaxDesc), _p]),
     "tfx_rope_pairhalf_f32": (_int, [_p, _p, _p, _p, ctypes.POINTER(RopeDesc), _p]),
     "tfx_rope_tables_f32": (_int, [ctypes.c_double, _i64, _i64, _p, _p]),
+    "tfx_session_create": (_int, [_int, ctypes.POINTER(ctypes.c_void_p)]),
+    "tfx_session_destroy": (_int, [_p]),
+    "tfx_session_set_chunk_bytes": (_int, [_p, _i64]),
+    "tfx_session_layernorm_ff_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, ctypes.c_float]),
+    "tfx_session_layernorm_ff_f64": (_int, [_p, _p, _p, _p, _p, _i64, _i64, ctypes.c_double]),
+    "tfx_session_rmsnorm_last_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _int, ctypes.c_float]),
+    "tfx_session_erf_f32": (_int, [_p, _p, _p, _i64]),
+    "tfx_session_gelu_erf_f32": (_int, [_p, _p, _p, _i64]),
+    "tfx_session_geglu_ff_f32": (_int, [_p, _p, _p, _i64, _i64]),
+    "tfx_session_gated_silu_f32": (_int, [_p, _p, _p, _p, _i64]),
+    "tfx_session_bias_act_ff_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _int]),
+    "tfx_session_add_f32": (_int, [_p, _p, _p, _p, _i64]),
+    "tfx_session_masked_softmax_f32": (_int, [_p, _p, _p, ctypes.POINTER(SoftmaxDesc)]),
+    "tfx_session_rope_pairhalf_f32": (_int, [_p, _p, _p, ctypes.c_double,
+                                             ctypes.POINTER(RopeDesc)]),
 }
 
 

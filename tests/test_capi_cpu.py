@@ -109,3 +109,16 @@ def test_product_erf_matches_oracle_over_bit_patterns(tmp_path):
     res = subprocess.run([str(exe), stride], capture_output=True, text=True, timeout=1800)
     assert res.returncode == 0, res.stdout + res.stderr
     assert "erf_mismatch=0 gelu_mismatch=0" in res.stdout
+
+
+def test_session_create_without_gpu_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present; covered by the GPU session tests")
+    h = ctypes.c_void_p()
+    rc = _lib.lib.tfx_session_create(0, ctypes.byref(h))
+    assert rc == _lib.TFX_ERR_CUDA and not h.value
+    assert tfx.last_error().startswith("tfx_session: device:")
+    assert _lib.lib.tfx_session_destroy(None) == 0
+    assert _lib.lib.tfx_session_gelu_erf_f32(None, None, None, 4) == _lib.TFX_ERR_INVALID_ARGUMENT
+    assert tfx.last_error() == "tenferro-ext::gelu_erf: session: null session"

@@ -1,0 +1,96 @@
+"""GPU parity of the host-buffer session (tfx_session_*): every op on host
+arrays, split into many pipelined chunks (small chunk size), against the
+oracle -- the ext-op executor form of the reference (CPU TensorRead in, owned
+host tensor out)."""
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import (assert_bitwise, assert_close, splitmix_normal, splitmix_uniform, F32_RTOL,
+                     F32_ATOL_REL, F64_RTOL, F64_ATOL_REL)
+from tfx.session import Session
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def sess():
+    s = Session(0, chunk_bytes=1 << 20)  # 1 MiB chunks: dozens of chunks per call
+    yield s
+    s.close()
+
+
+def test_session_layernorm(orc, sess):
+    d, cols = 768, 3001
+    x = splitmix_normal(d * cols, 0x7E4F0800)
+    w = splitmix_uniform(d, 0x7E4F0801, 0.5, 1.5)
+    b = splitmix_normal(d, 0x7E4F0802, std=0.1)
+    y = sess.layer_norm_feature_first(x, w, b, 1e-5)
+    assert_close(y, orc.layer_norm_feature_first_f32(x, d, cols, w, b, 1e-5), F32_RTOL,
+                 F32_ATOL_REL, "session layernorm")
+    x64, w64 = x.astype(np.float64), w.astype(np.float64)
+    y64 = sess.layer_norm_feature_first(x64, w64, None, 1e-5)
+    assert_close(y64, orc.layer_norm_feature_first_f64(x64, d, cols, w64, None, 1e-5), F64_RTOL,
+                 F64_ATOL_REL, "session layernorm f64")
+
+
+def test_session_rmsnorm_strided_row_chunks(orc, sess):
+    rows, width = 5003, 1024
+    x = splitmix_normal(rows * width, 0x7E4F0810)
+    w = splitmix_normal(width, 0x7E4F0811, mean=1.0, std=0.1)
+    y = sess.rms_norm_last(x, w, True, 1e-6)
+    assert_close(y, orc.rms_norm_last_f32(x, rows, width, w, True, 1e-6), F32_RTOL, F32_ATOL_REL,
+                 "session rmsnorm")
+
+
+def test_session_elementwise_bitwise(orc, sess):
+    n = 3_000_001
+    x = splitmix_normal(n, 0x7E4F0820, std=1.5)
+    assert_bitwise(sess.erf(x), orc.erf_f32(x), "session erf")
+    assert_bitwise(sess.gelu_erf(x), orc.gelu_erf_f32(x), "session gelu")
+    b = splitmix_normal(n, 0x7E4F0821)
+    assert_bitwise(sess.add(x, b), orc.add_f32(x, b), "session add")
+    assert_close(sess.gated_silu(x, b), orc.gated_silu_f32(x, b), F32_RTOL, F32_ATOL_REL,
+                 "session silu")
+    inter, cols = 1152, 777
+    u = splitmix_normal(2 * inter * cols, 0x7E4F0822, std=1.5)
+    assert_bitwise(sess.geglu(u, inter), orc.geglu_f32(u, inter, cols), "session geglu")
+    F, T = 768, 2049
+    xb = splitmix_normal(F * T, 0x7E4F0823)
+    bias = splitmix_normal(F, 0x7E4F0824, std=0.02)
+    assert_bitwise(sess.bias_act(xb, bias), orc.bias_add_f32(xb, bias, F, T), "session bias")
+    assert_bitwise(sess.bias_act(xb, bias, act=1), orc.bias_act_f32(xb, bias, F, T, 1),
+                   "session bias gelu")
+
+
+def test_session_softmax_with_host_masks(orc, sess):
+    B, H, L = 3, 4, 128
+    s = splitmix_normal(B * H * L * L, 0x7E4F0830, std=2.0)
+    vl = np.array([128, 90, 17], dtype=np.int32)
+    kw = dict(window=16, valid_lens=vl, window_skips_invalid_query=True)
+    assert_close(sess.masked_softmax(s, B, H, L, L, **kw),
+                 orc.masked_softmax_f32(s, B, H, L, L, **kw), F32_RTOL, F32_ATOL_REL,
+                 "session softmax")
+    keep = (np.arange(L)[None, :] <= np.arange(L)[:, None]).astype(np.uint8).ravel()  # [q][k]
+    kw = dict(keep=keep, keep_strides=(0, L, 1), semantics=1)
+    assert_close(sess.masked_softmax(s, B, H, L, L, **kw),
+                 orc.masked_softmax_f32(s, B, H, L, L, **kw), F32_RTOL, F32_ATOL_REL,
+                 "session softmax keep")
+
+
+def test_session_rope_chain_layout(orc, sess):
+    hidden, hd, L, B = 768, 64, 512, 5
+    x = splitmix_normal(3 * hidden * L * B, 0x7E4F0840)
+    strides = (hd, 3 * hidden, 3 * hidden * L, 1)
+    y = sess.rope_pairhalf(x, 160000.0, 24, L, B, hd, hd, strides)
+    c, s = orc.rope_tables_f32(160000.0, L, hd)
+    assert_bitwise(y, orc.rope_pairhalf_f32(x, c, s, 24, L, B, hd, hd, strides), "session rope")
+
+
+def test_session_pinned_torch_tensors(orc, sess):
+    n = 1 << 22
+    x = torch.from_numpy(splitmix_normal(n, 0x7E4F0850, std=1.5)).pin_memory()
+    y = torch.empty(n, dtype=torch.float32).pin_memory()
+    sess.gelu_erf(x, out=y)
+    assert_bitwise(y.numpy(), orc.gelu_erf_f32(x.numpy()), "session pinned gelu")
