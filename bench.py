@@ -64,6 +64,22 @@ def chain_bytes(c=CHAIN, batch=None) -> dict:
     }
 
 
+def softmax_touched_bytes(batch, heads, L, window, valid_len):
+    """HBM bytes the masked softmax must move: the 16-byte score chunks that
+    intersect each row's kept key interval (masked scores never reach the
+    result and are not read) plus every probability written."""
+    import numpy as np
+    q = np.arange(L)
+    lo = np.zeros(L, dtype=np.int64)
+    hi = np.full(L, L if valid_len < 0 else valid_len, dtype=np.int64)
+    if window >= 0:
+        lo = np.maximum(lo, q - window)
+        hi = np.minimum(hi, q + window + 1)
+    hi = np.maximum(hi, lo)
+    chunks = np.where(hi > lo, (hi - 1) // 4 - lo // 4 + 1, 0)
+    return int(batch * heads * (chunks.sum() * 16 + L * L * 4))
+
+
 # ---------------------------------------------------------------------------------
 # environment
 
@@ -215,7 +231,7 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     def normal(n, std=1.0, dtype=torch.float32):
         return (torch.randn(n, generator=gen, device=device, dtype=dtype) * std)
 
-    def measure(name, make, launch, nbytes, elems):
+    def measure(name, make, launch, nbytes, elems, touched=None):
         if only is not None and name != only:
             return
         per_set = nbytes
@@ -251,6 +267,10 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
                          "us_batched": round(ms_b * 1e3, 3),
                          "gbs_batched": round(nbytes / (ms_b * 1e-3) / 1e9, 1),
                          "buffer_sets": sets}
+        if touched is not None:
+            g = touched / (ms * 1e-3) / 1e9
+            results[name].update({"touched_bytes": touched, "gbs_touched": round(g, 1),
+                                  "frac_touched_of_hbm": round(g / hbm_peak, 3)})
         del bufs
 
     # LayerNorm 768 x 8192 (f32 and the f64 copy)
@@ -280,7 +300,7 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     ns = B * H * L * L
     measure("masked_softmax", lambda: (normal(ns, 2.0), torch.empty(ns, device=device)),
             lambda b: ops.masked_softmax(b[0], B, H, L, L, window=64, valid_len=L - 37, out=b[1]),
-            2 * ns * 4, ns)
+            2 * ns * 4, ns, touched=softmax_touched_bytes(B, H, L, 64, L - 37))
     F, T = 768, 8192
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
@@ -446,7 +466,16 @@ def run_ours(args):
         except Exception:
             traffic = None
 
-    sm_bytes = chain_bytes()["softmax"]
+    # The softmax reads only the score chunks its mask keeps: its algorithmic
+    # bytes per launch are those plus every probability written, averaged over
+    # the timed steps (even steps sliding-window, odd steps global).
+    c = CHAIN
+    t_local = softmax_touched_bytes(c["batch"], c["heads"], c["seq"], c["window"],
+                                    c["seq"] - c["pad"])
+    t_global = softmax_touched_bytes(c["batch"], c["heads"], c["seq"], -1, c["seq"] - c["pad"])
+    n_local = (args.steps + 1) // 2
+    sm_bytes = (n_local * t_local + (args.steps - n_local) * t_global) / args.steps
+    sm_dense = chain_bytes()["softmax"]
     sm_gbs = sm_bytes / (sm_ms * 1e-3) / 1e9
     if world > 1:
         dist.destroy_process_group()
@@ -481,7 +510,9 @@ def run_ours(args):
         "roofline": {"kernel": "masked_softmax (chain)", "bound": "hbm",
                      "achieved": round(sm_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(sm_gbs / hbm_peak, 3), "peak_source": peak_src,
-                     "bytes_per_launch": sm_bytes, "traffic": traffic,
+                     "bytes_per_launch": int(sm_bytes), "traffic": traffic,
+                     "bytes_per_launch_dense": sm_dense,
+                     "dense_equivalent_gbs": round(sm_dense / (sm_ms * 1e-3) / 1e9, 1),
                      "us_per_launch": round(sm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,

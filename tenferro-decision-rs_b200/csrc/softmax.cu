@@ -66,6 +66,15 @@ __device__ __forceinline__ RowCtx row_ctx(const MaskArgs& m, uint64_t local_row)
 
 constexpr int kExclude = TFX_SOFTMAX_EXCLUDE;
 
+// Whether any of keys [k, k + 4) passes the analytic conditions. A score that
+// fails them never reaches the result (EXCLUDE replaces it by -inf, FILL by
+// -1e30), so a float4 of scores outside [lo, lo + span) is not read -- the
+// same skipping of masked key spans as the reference's attention rows
+// (crates/cpu-kernels/src/lib.rs:900-936, key_ranges).
+__device__ __forceinline__ bool any_kept4(const RowCtx& c, uint32_t k) {
+  return c.span != 0 && k + 3 >= c.lo && k < c.lo + c.span;
+}
+
 // Masked, scaled score of key k (in range). EXCLUDE: -inf when masked;
 // FILL: -1e30 when masked (util.rs:87).
 template <int SEM, bool TENSORS>
@@ -119,10 +128,9 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const uint32_t q4 = j * 32 + lane;
-    if (q4 < kv) {
-      const float4 t = ld_stream(src + q4);
-      v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
-    }
+    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (q4 < kv && any_kept4(c, q4 * 4)) t = ld_stream(src + q4);
+    v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
   }
   float mx = -INFINITY;
 #pragma unroll
@@ -183,10 +191,9 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     const uint32_t q4 = j * 256 + threadIdx.x;
-    if (q4 < kv) {
-      const float4 t = ld_stream(src + q4);
-      v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
-    }
+    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (q4 < kv && any_kept4(c, q4 * 4)) t = ld_stream(src + q4);
+    v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
   }
   float mx = -INFINITY;
 #pragma unroll
@@ -232,19 +239,21 @@ __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* s, fl
   const float* src = s + row * uint64_t(m.k_len);
   float* dst = p + row * uint64_t(m.k_len);
   const uint32_t n = uint32_t(m.k_len);
+  // Scores outside the row's analytic interval are never read (see any_kept4).
+  auto at = [&](uint32_t k) { return k - c.lo < c.span ? src[k] : 0.0f; };
   float mx = -INFINITY;
   for (uint32_t k = threadIdx.x; k < n; k += 256)
-    mx = fmaxf(mx, score<SEM, TENSORS>(m, c, k, src[k]));
+    mx = fmaxf(mx, score<SEM, TENSORS>(m, c, k, at(k)));
   mx = block_reduce(mx, red, true);
   float sum = 0.0f;
   for (uint32_t k = threadIdx.x; k < n; k += 256)
-    sum = __fadd_rn(sum, expo<SEM>(score<SEM, TENSORS>(m, c, k, src[k]), mx));
+    sum = __fadd_rn(sum, expo<SEM>(score<SEM, TENSORS>(m, c, k, at(k)), mx));
   sum = block_reduce(sum, red, false);
   const float r = __frcp_rn(sum);
   const bool fast = sum < 0x1p24f;
   // In place (dst == src) each thread reads, then writes, only its own keys.
   for (uint32_t k = threadIdx.x; k < n; k += 256)
-    dst[k] = quotient(expo<SEM>(score<SEM, TENSORS>(m, c, k, src[k]), mx), sum, r, fast);
+    dst[k] = quotient(expo<SEM>(score<SEM, TENSORS>(m, c, k, at(k)), mx), sum, r, fast);
 }
 
 template <int SEM, bool TENSORS>
