@@ -260,12 +260,33 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
         b1.record()
         torch.cuda.synchronize()
         ms_b = b0.elapsed_time(b1) / reps
+        # the same launches captured once in a CUDA graph and replayed
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                for k in range(reps):
+                    launch(bufs[k % sets])
+        torch.cuda.current_stream().wait_stream(side)
+        graph.replay()
+        torch.cuda.synchronize()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record()
+        graph.replay()
+        g1.record()
+        torch.cuda.synchronize()
+        ms_g = g0.elapsed_time(g1) / reps
+        del graph
         gbs = nbytes / (ms * 1e-3) / 1e9
         results[name] = {"bytes": nbytes, "us": round(ms * 1e3, 3), "gbs": round(gbs, 1),
                          "frac_of_hbm": round(gbs / hbm_peak, 3),
                          "gelem_s": round(elems / (ms * 1e-3) / 1e9, 2),
                          "us_batched": round(ms_b * 1e3, 3),
                          "gbs_batched": round(nbytes / (ms_b * 1e-3) / 1e9, 1),
+                         "us_graph": round(ms_g * 1e3, 3),
+                         "gbs_graph": round(nbytes / (ms_g * 1e-3) / 1e9, 1),
                          "buffer_sets": sets}
         if touched is not None:
             g = touched / (ms * 1e-3) / 1e9

@@ -240,8 +240,10 @@ TFX_API int tfx_session_add_f32(tfx_session* session, const float* a, const floa
 TFX_API int tfx_session_masked_softmax_f32(tfx_session* session, const float* scores,
                                            float* probs, const tfx_softmax_desc* desc);
 /* Tables are built from base as tfx_rope_tables_f32 does (and cached). y is x
- * with the described vectors rotated: every element of x's extent that is not
- * rotated is copied unchanged. */
+ * with the described vectors rotated: within the extent the descriptor spans
+ * (from element 0 to the last element of the last vector), elements that are
+ * not rotated are copied from x; elements of y beyond that extent (e.g. the v
+ * block after the last token of a qkv tensor) are not written. */
 TFX_API int tfx_session_rope_pairhalf_f32(tfx_session* session, const float* x, float* y,
                                           double base, const tfx_rope_desc* desc);
 

@@ -535,14 +535,104 @@ __global__ void __launch_bounds__(256) rms_tile_kernel(const float* x,
   }
 }
 
-// Kernel choice for the f32 feature-last RMSNorm: "cluster" (default) or
-// "tile"; TFX_RMS_KERNEL overrides it for tuning runs.
-bool rms_use_tile() {
+// Split variant, pass A: CTA (tile, chunk) reduces tokens [tile*32*VEC, +32*VEC)
+// over features [chunk*fpc, +fpc) (warp w owns features f0 + w + 8k) and writes
+// one partial sum of squares per token to partial[chunk * rows + token].
+template <int VEC, int FPT>
+__global__ void __launch_bounds__(256) rms_partial_kernel(const float* __restrict__ x,
+                                                          float* __restrict__ partial,
+                                                          uint32_t rows, uint32_t width,
+                                                          uint32_t fpc) {
+  constexpr int TR = 32 * VEC;
+  __shared__ float red[8][TR];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t r0 = blockIdx.x * TR + lane * VEC;
+  const bool row_ok = r0 < rows;
+  const uint32_t f0 = blockIdx.y * fpc;
+  const uint32_t f1 = min(width, f0 + fpc);
+  RowVec<float, VEC> v[FPT];
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + 8 * k;
+    if (row_ok && f < f1) v[k] = load_rows<float, VEC>(x + uint64_t(f) * rows + r0);
+  }
+  float ss[VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) ss[j] = 0.0f;
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + 8 * k;
+    if (row_ok && f < f1)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) ss[j] = __fadd_rn(ss[j], __fmul_rn(v[k].v[j], v[k].v[j]));
+  }
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) red[warp][lane * VEC + j] = ss[j];
+  __syncthreads();
+  if (threadIdx.x < TR) {
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s = __fadd_rn(s, red[i][threadIdx.x]);
+    const uint32_t r = blockIdx.x * TR + threadIdx.x;
+    if (r < rows) partial[uint64_t(blockIdx.y) * rows + r] = s;
+  }
+}
+
+// Split variant, pass B: sums the token's partials in chunk order, then scales
+// the CTA's (tile, chunk) block, re-reading x (from L2 when x fits there).
+template <int VEC, int FPT>
+__global__ void __launch_bounds__(256) rms_apply_kernel(const float* x,
+                                                        const float* __restrict__ w,
+                                                        const float* __restrict__ partial,
+                                                        float* y, uint32_t rows, uint32_t width,
+                                                        uint32_t fpc, uint32_t chunks, float eps,
+                                                        float inv_width, int centered) {
+  constexpr int TR = 32 * VEC;
+  __shared__ float scale_s[TR];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (threadIdx.x < TR) {
+    const uint32_t r = blockIdx.x * TR + threadIdx.x;
+    float tot = 0.0f;
+    if (r < rows)
+      for (uint32_t c = 0; c < chunks; ++c) tot = __fadd_rn(tot, __ldcg(partial + uint64_t(c) * rows + r));
+    scale_s[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, inv_width), eps)));
+  }
+  const uint32_t r0 = blockIdx.x * TR + lane * VEC;
+  const bool row_ok = r0 < rows;
+  const uint32_t f0 = blockIdx.y * fpc;
+  const uint32_t f1 = min(width, f0 + fpc);
+  RowVec<float, VEC> v[FPT];
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + 8 * k;
+    if (row_ok && f < f1) v[k] = load_rows<float, VEC>(x + uint64_t(f) * rows + r0);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < FPT; ++k) {
+    const uint32_t f = f0 + warp + 8 * k;
+    if (row_ok && f < f1) {
+      const float wf = __ldg(w + f);
+      const float wt = centered ? __fadd_rn(1.0f, wf) : wf;
+      RowVec<float, VEC> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) o.v[j] = __fmul_rn(__fmul_rn(v[k].v[j], scale_s[lane * VEC + j]), wt);
+      store_rows<float, VEC>(y + uint64_t(f) * rows + r0, o);
+    }
+  }
+}
+
+// Kernel choice for the f32 feature-last RMSNorm: 0 = automatic, 1 = cluster,
+// 2 = tile, 3 = split, 4 = 16-CTA cluster; TFX_RMS_KERNEL overrides it for
+// tuning runs.
+int rms_kernel_choice() {
   static const int choice = [] {
     const char* e = getenv("TFX_RMS_KERNEL");
-    return (e && std::string(e) == "tile") ? 1 : 0;
+    if (!e) return 0;
+    const std::string s(e);
+    return s == "cluster" ? 1 : s == "tile" ? 2 : s == "split" ? 3 : s == "cluster16" ? 4 : 0;
   }();
-  return choice == 1;
+  return choice;
 }
 
 template <typename T, int VEC, int FPT>
@@ -562,12 +652,55 @@ cudaError_t launch_rms_cluster(const T* x, const T* w, T* y, uint32_t rows, uint
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (csize > 8) {
+    const cudaError_t err = cudaFuncSetAttribute(
+        rms_cluster_kernel<T, VEC, FPT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err != cudaSuccess) return err;
+  }
   return cudaLaunchKernelEx(&cfg, rms_cluster_kernel<T, VEC, FPT>, x, w, y, rows, width, fpc, eps,
                             inv_width, centered);
 }
 
-// Picks (VEC, FPT, cluster size) for the shape; returns false if no cluster
-// configuration covers the width (then the generic kernel runs).
+// Split variant: pass A (partials) and pass B (scale + write) over a grid of
+// (token tiles, 64-feature chunks). The partial sums live in a stream-ordered
+// scratch allocation of chunks * rows floats, released on the same stream.
+// Returns 1 (nothing launched) when the scratch cannot be had.
+int rms_split(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+              uint32_t width, int vec, int centered, float eps, float inv_width,
+              cudaStream_t stream) {
+  constexpr int FPT = 8;
+  const uint32_t fpc = 8 * FPT;
+  const uint32_t chunks = (width + fpc - 1) / fpc;
+  const uint32_t tr = 32 * uint32_t(vec);
+  const uint32_t tiles = (rows + tr - 1) / tr;
+  if (chunks > 65535) return 1;
+  float* partial = nullptr;
+  if (cudaMallocAsync(reinterpret_cast<void**>(&partial), size_t(chunks) * rows * 4, stream) !=
+      cudaSuccess) {
+    cudaGetLastError();  // clear the allocation failure; the caller falls back
+    return 1;
+  }
+  const dim3 grid(tiles, chunks);
+  if (vec == 4) {
+    rms_partial_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
+    rms_apply_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
+                                                       chunks, eps, inv_width, centered);
+  } else if (vec == 2) {
+    rms_partial_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
+    rms_apply_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
+                                                       chunks, eps, inv_width, centered);
+  } else {
+    rms_partial_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
+    rms_apply_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
+                                                       chunks, eps, inv_width, centered);
+  }
+  const int rc = check_launch(op);
+  cudaFreeAsync(partial, stream);
+  return rc;
+}
+
+// Picks the kernel and its (VEC, FPT, cluster size) for the shape; the generic
+// kernel runs when nothing else covers it.
 template <typename T>
 int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int64_t width,
                  int centered, T eps, cudaStream_t stream) {
@@ -581,7 +714,7 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
   TFX_REQUIRE(y == x || !overlaps(x, bytes, y, bytes), op, "y", "partially overlaps x");
   TFX_REQUIRE(!overlaps(w, size_t(width) * sizeof(T), y, bytes), op, "weight", "overlaps y");
   int st = TFX_OK;
-  device_info(&st);
+  const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
   // f32: 1/width as the f32 reciprocal (lib.rs:560); f64: 1.0 / width.
   const T inv_width = T(1) / T(width);
@@ -591,20 +724,31 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
   constexpr int V16N = 16 / int(sizeof(T));
   if (rows % V16N == 0 && aligned(x, 16) && aligned(y, 16)) vec = V16N;
   else if (std::is_same_v<T, float> && rows % 2 == 0 && aligned(x, 8) && aligned(y, 8)) vec = 2;
+  int max_cluster = 8;
   if constexpr (std::is_same_v<T, float>) {
-    if (small && rms_use_tile()) {
+    const int choice = rms_kernel_choice();
+    if (small && choice == 2) {
       rms_tile_kernel<8><<<unsigned((rows + 31) / 32), 256, 0, stream>>>(
           x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width, centered);
       return check_launch(op);
     }
+    // The split variant re-reads x once; it wins when x stays in L2 between
+    // its two passes.
+    const bool fits_l2 = double(bytes) <= 0.75 * double(dev.l2_bytes);
+    if (small && (choice == 3 || (choice == 0 && fits_l2)) && (rows + 127) / 128 < 65536 * 64) {
+      const int rc = rms_split(op, x, w, y, uint32_t(rows), uint32_t(width), vec, centered, eps,
+                               inv_width, stream);
+      if (rc != 1) return rc;  // 1: scratch unavailable, take the cluster kernel
+    }
+    if (choice == 4) max_cluster = 16;
   }
   if (small) {
     const uint32_t r = uint32_t(rows), wd = uint32_t(width);
-    // Features per CTA = 8 warps * FPT; the cluster holds up to 8 CTAs.
+    // Features per CTA = 8 warps * FPT; the cluster holds up to max_cluster CTAs.
     auto try_cfg = [&](int fpt, auto launch) -> int {
       const int64_t per_cta = int64_t(kRmsWarps) * fpt;
       const int64_t csize = (width + per_cta - 1) / per_cta;
-      if (csize > 8) return 1;  // not covered
+      if (csize > max_cluster) return 1;  // not covered
       const uint32_t fpc = uint32_t((width + csize - 1) / csize);
       const cudaError_t err = launch(int(csize), fpc);
       if (err != cudaSuccess)

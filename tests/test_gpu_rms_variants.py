@@ -1,0 +1,41 @@
+"""GPU parity of every feature-last RMSNorm kernel variant. The variant is
+picked once per process (TFX_RMS_KERNEL), so each runs in a fresh interpreter
+that compares a few shapes against the oracle and prints one verdict line."""
+
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+SCRIPT = r"""
+import sys
+sys.path.insert(0, {root!r}); sys.path.insert(0, {pkg!r}); sys.path.insert(0, {tests!r})
+import numpy as np, torch
+from oracle import oracle as orc
+from tfx import ops
+from helpers import assert_close, splitmix_normal, F32_RTOL, F32_ATOL_REL
+for rows, width in [(16384, 1024), (4096, 2048), (258, 1025), (63, 31), (1000, 4096), (7, 9)]:
+    x = splitmix_normal(rows * width, 0x7E4F0900 + rows)
+    w = splitmix_normal(width, 0x7E4F0901 + width, mean=1.0, std=0.1)
+    for centered in (True, False):
+        y = ops.rms_norm_last(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(), centered,
+                              1e-6).cpu().numpy()
+        assert_close(y, orc.rms_norm_last_f32(x, rows, width, w, centered, 1e-6), F32_RTOL,
+                     F32_ATOL_REL, f"rms {{rows}}x{{width}}")
+print("variant ok")
+"""
+
+
+@pytest.mark.parametrize("variant", ["cluster", "cluster16", "tile", "split"])
+def test_rms_variant(variant):
+    code = SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
+                         tests=os.path.join(ROOT, "tests"))
+    env = dict(os.environ, TFX_RMS_KERNEL=variant)
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert res.returncode == 0 and "variant ok" in res.stdout, res.stdout + res.stderr
