@@ -179,6 +179,95 @@ __global__ void __launch_bounds__(256) ln_warp_kernel(const T* __restrict__ x,
   }
 }
 
+// ---- LayerNorm f32: one warp per column, column staged in shared memory ------------
+//
+// Same arithmetic as ln_warp_kernel, but the column is copied into the warp's
+// slice of shared memory with cp.async (16 bytes per lane per step) instead of
+// being held in registers. At 32 registers per thread 64 warps fit on an SM,
+// so 148 SMs keep 9472 columns in flight at once -- config-sized tensors
+// (8192 columns of 768) run in a single wave instead of 1.4.
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+template <int NV, bool BIAS>
+__global__ void __launch_bounds__(256, 8) ln_smem_kernel(const float* __restrict__ x,
+                                                         const float* __restrict__ w,
+                                                         const float* __restrict__ b,
+                                                         float* __restrict__ y, uint32_t d,
+                                                         uint64_t cols, float eps) {
+  extern __shared__ float4 stage[];  // 8 warps x d floats
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t col = uint64_t(blockIdx.x) * 8 + warp;
+  if (col >= cols) return;  // the whole warp leaves together
+  const uint32_t dv = d / 4;
+  float4* sx = stage + warp * dv;
+  const float4* xc = reinterpret_cast<const float4*>(x + col * d);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) cp_async16(sx + q, xc + q);
+  }
+  cp_async_wait_all();
+  __syncwarp();
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 v = sx[q];
+      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+    }
+  }
+  s = warp_sum(s);
+  const float dd = float(d);
+  const float mean = __fdiv_rn(s, dd);
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 v = sx[q];
+      const float cx = __fsub_rn(v.x, mean), cy = __fsub_rn(v.y, mean);
+      const float cz = __fsub_rn(v.z, mean), cw = __fsub_rn(v.w, mean);
+      ss = __fadd_rn(ss, __fmul_rn(cx, cx));
+      ss = __fadd_rn(ss, __fmul_rn(cy, cy));
+      ss = __fadd_rn(ss, __fmul_rn(cz, cz));
+      ss = __fadd_rn(ss, __fmul_rn(cw, cw));
+    }
+  }
+  ss = warp_sum(ss);
+  const float var = __fdiv_rn(ss, dd);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  float4* yc = reinterpret_cast<float4*>(y + col * d);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 v = sx[q];
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+      float4 o;
+      o.x = __fmul_rn(__fmul_rn(__fsub_rn(v.x, mean), inv), wv.x);
+      o.y = __fmul_rn(__fmul_rn(__fsub_rn(v.y, mean), inv), wv.y);
+      o.z = __fmul_rn(__fmul_rn(__fsub_rn(v.z, mean), inv), wv.z);
+      o.w = __fmul_rn(__fmul_rn(__fsub_rn(v.w, mean), inv), wv.w);
+      if constexpr (BIAS) {
+        const float4 bv = __ldg(reinterpret_cast<const float4*>(b) + q);
+        o.x = __fadd_rn(o.x, bv.x);
+        o.y = __fadd_rn(o.y, bv.y);
+        o.z = __fadd_rn(o.z, bv.z);
+        o.w = __fadd_rn(o.w, bv.w);
+      }
+      yc[q] = o;
+    }
+  }
+}
+
 // ---- LayerNorm: one CTA (256 threads) per column, column in registers --------------
 
 template <typename T>
@@ -300,11 +389,38 @@ int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64
                    (!b || aligned(b, 16));
   const int64_t dv = d / VN;
   const bool bias = b != nullptr;
+  if constexpr (std::is_same_v<T, float>) {
+    // Shared-memory staged warp-per-column kernel (f32, d <= 1024); the
+    // register-resident one stays selectable for tuning (TFX_LN_KERNEL=regs).
+    static const bool use_regs = [] {
+      const char* e = getenv("TFX_LN_KERNEL");
+      return e && std::string(e) == "regs";
+    }();
+    if (vec && dv <= 32 * 8 && !use_regs) {
+      TFX_REQUIRE(cols / 8 < (int64_t(1) << 31), op, "cols", "too many columns for one call");
+      const unsigned grid = unsigned((cols + 7) / 8);
+      const uint32_t du = uint32_t(d);
+      const size_t smem = size_t(8) * size_t(d) * 4;
+#define TFX_LN_SMEM(NVV)                                                                       \
+  if (dv <= 32 * NVV) {                                                                         \
+    if (bias) ln_smem_kernel<NVV, true><<<grid, 256, smem, stream>>>(x, w, b, y, du, cols, eps);  \
+    else ln_smem_kernel<NVV, false><<<grid, 256, smem, stream>>>(x, w, b, y, du, cols, eps);      \
+    return check_launch(op);                                                                    \
+  }
+      TFX_LN_SMEM(1)
+      TFX_LN_SMEM(2)
+      TFX_LN_SMEM(3)
+      TFX_LN_SMEM(4)
+      TFX_LN_SMEM(6)
+      TFX_LN_SMEM(8)
+#undef TFX_LN_SMEM
+    }
+  }
   if (vec && dv <= 32 * 16) {
     TFX_REQUIRE(cols / 8 < (int64_t(1) << 31), op, "cols", "too many columns for one call");
     const unsigned grid = unsigned((cols + 7) / 8);
     const uint32_t du = uint32_t(d);
-#define TFX_LN_WARP(NVV)                                                                 \
+#define TFX_LN_WARP(NVV)                                                                \
   if (dv <= 32 * NVV) {                                                                   \
     if (bias) ln_warp_kernel<T, NVV, true><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);  \
     else ln_warp_kernel<T, NVV, false><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);      \

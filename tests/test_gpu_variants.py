@@ -39,3 +39,33 @@ def test_rms_variant(variant):
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                          timeout=600)
     assert res.returncode == 0 and "variant ok" in res.stdout, res.stdout + res.stderr
+
+
+LN_SCRIPT = r"""
+import sys
+sys.path.insert(0, {root!r}); sys.path.insert(0, {pkg!r}); sys.path.insert(0, {tests!r})
+import numpy as np, torch
+from oracle import oracle as orc
+from tfx import ops
+from helpers import assert_close, splitmix_normal, splitmix_uniform, F32_RTOL, F32_ATOL_REL
+for d, cols in [(768, 8192), (1024, 100), (512, 33), (4, 9), (132, 17)]:
+    x = splitmix_normal(d * cols, 0x7E4F0A00 + d)
+    w = splitmix_uniform(d, 0x7E4F0A01 + d, 0.5, 1.5)
+    for b in (None, splitmix_normal(d, 0x7E4F0A02 + d, std=0.1)):
+        y = ops.layer_norm_feature_first(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(),
+                                         None if b is None else torch.from_numpy(b).cuda(),
+                                         1e-5).cpu().numpy()
+        assert_close(y, orc.layer_norm_feature_first_f32(x, d, cols, w, b, 1e-5), F32_RTOL,
+                     F32_ATOL_REL, f"ln {{d}}x{{cols}}")
+print("variant ok")
+"""
+
+
+@pytest.mark.parametrize("variant", ["regs", "smem"])
+def test_layernorm_variant(variant):
+    code = LN_SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
+                            tests=os.path.join(ROOT, "tests"))
+    env = dict(os.environ, TFX_LN_KERNEL=variant)
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                         timeout=600)
+    assert res.returncode == 0 and "variant ok" in res.stdout, res.stdout + res.stderr
