@@ -132,6 +132,23 @@ TFX_API int tfx_rmsnorm_last_f32(const float* x, const float* weight, float* y, 
                          int64_t width, int centered, float eps, tfx_stream_t stream);
 TFX_API int tfx_rmsnorm_last_f64(const double* x, const double* weight, double* y, int64_t rows,
                          int64_t width, int centered, double eps, tfx_stream_t stream);
+/* Same result as tfx_rmsnorm_last_f32, for callers that cannot let a library
+ * allocate device memory during a call -- e.g. a serving process whose HBM is
+ * reserved up front by its own allocator, or a latency-critical loop that must
+ * not touch an allocator or risk an allocation's implicit synchronisation.
+ * No counterpart in the reference. It allocates and frees nothing: the
+ * kernels' partial sums live in a fixed 4 MiB array inside libtfx's device
+ * image, reserved on every GPU that loads the library until the process
+ * exits. Limit: rows * ceil(width / 64) <= 1048576 (e.g. width 1024: up to
+ * 65536 rows; width 4096: up to 16384); larger calls return
+ * TFX_ERR_UNSUPPORTED. The first call on a device looks the array up for that
+ * device (make it before any stream capture). All calls share the array, so
+ * calls that can overlap on the GPU (other streams, other threads) race and
+ * must be serialised by the caller; nothing in it needs clearing between
+ * calls. */
+TFX_API int tfx_rmsnorm_last_f32_noalloc(const float* x, const float* weight, float* y,
+                                         int64_t rows, int64_t width, int centered, float eps,
+                                         tfx_stream_t stream);
 
 /* ---- masked row softmax ---------------------------------------------------
  * Replaces tenferro_infer::softmax::{softmax, masked_softmax}

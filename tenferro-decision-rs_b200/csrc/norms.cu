@@ -21,6 +21,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <mutex>
 #include <string>
 #include <cstdlib>
 #include <type_traits>
@@ -926,3 +927,105 @@ int tfx_rmsnorm_last_f64(const double* x, const double* weight, double* y, int64
 }
 
 }  // extern "C"
+
+// ---- RMSNorm without any allocation ------------------------------------------------
+//
+// tfx_rmsnorm_last_f32 takes the split kernels' partial sums from a
+// stream-ordered allocation. Some callers cannot let a library allocate device
+// memory at call time: a serving process whose HBM is reserved up front by its
+// own allocator (a cudaMallocAsync there can fail or fragment the pool), or a
+// latency-critical loop that must not take the allocator's locks, grow a pool
+// or risk the implicit synchronisation of an allocation. For them this entry
+// point runs the same two kernels on a fixed scratch array that is part of the
+// library's device image: it is reserved on every GPU that loads libtfx, for as
+// long as the process lives, and no call allocates or frees anything.
+
+// Partial sums of squares of the split kernels: (width / 64 rounded up) * rows
+// floats per call, at most 2^20 (4 MiB).
+constexpr size_t kStaticScratchFloats = size_t(1) << 20;
+static __device__ __align__(256) float g_rms_static_scratch[kStaticScratchFloats];
+
+namespace tfx {
+namespace {
+
+// Device address of g_rms_static_scratch on the current device. Host code only
+// sees a host-side stand-in for the array, so the address is looked up with
+// cudaGetSymbolAddress once per device (with that device current) and cached.
+float* static_scratch(const char* op, int* status) {
+  constexpr int kMaxDev = 64;
+  static std::once_flag once[kMaxDev];
+  static float* addr[kMaxDev];
+  static cudaError_t err[kMaxDev];
+  int dev = -1;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    *status = fail(TFX_ERR_CUDA, op, "scratch", "cannot read the current device");
+    return nullptr;
+  }
+  std::call_once(once[dev], [dev] {
+    err[dev] = cudaGetSymbolAddress(reinterpret_cast<void**>(&addr[dev]), g_rms_static_scratch);
+  });
+  if (err[dev] != cudaSuccess || addr[dev] == nullptr) {
+    *status = fail(TFX_ERR_CUDA, op, "scratch",
+                   std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(err[dev]));
+    return nullptr;
+  }
+  *status = TFX_OK;
+  return addr[dev];
+}
+
+}  // namespace
+}  // namespace tfx
+
+extern "C" int tfx_rmsnorm_last_f32_noalloc(const float* x, const float* weight, float* y,
+                                            int64_t rows, int64_t width, int centered,
+                                            float eps, tfx_stream_t stream) {
+  using namespace tfx;
+  clear_error();
+  const char* op = "tenferro-ext::rms_norm_last";
+  TFX_REQUIRE(rows >= 0 && width >= 0, op, "shape", "extents must be non-negative");
+  if (rows == 0 || width == 0) return TFX_OK;
+  TFX_REQUIRE(x, op, "x", "null pointer");
+  TFX_REQUIRE(weight, op, "weight", "null pointer");
+  TFX_REQUIRE(y, op, "y", "null pointer");
+  const size_t bytes = size_t(rows) * size_t(width) * 4;
+  TFX_REQUIRE(y == x || !overlaps(x, bytes, y, bytes), op, "y", "partially overlaps x");
+  TFX_REQUIRE(!overlaps(weight, size_t(width) * 4, y, bytes), op, "weight", "overlaps y");
+  const int64_t chunks = (width + 63) / 64;
+  if (rows >= (int64_t(1) << 31) || chunks > 65535 ||
+      uint64_t(chunks) * uint64_t(rows) > kStaticScratchFloats)
+    return fail(TFX_ERR_UNSUPPORTED, op, "shape",
+                "rows x ceil(width/64) = " + std::to_string(chunks) + " x " +
+                    std::to_string(rows) + " partial sums exceed the fixed scratch of " +
+                    std::to_string(kStaticScratchFloats) +
+                    " floats; split the rows over several calls or use tfx_rmsnorm_last_f32");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  float* partial = static_scratch(op, &st);
+  if (st != TFX_OK) return st;
+  int vec = 1;
+  if (rows % 4 == 0 && aligned(x, 16) && aligned(y, 16)) vec = 4;
+  else if (rows % 2 == 0 && aligned(x, 8) && aligned(y, 8)) vec = 2;
+  // Pass A writes every partial that pass B reads, so nothing in the scratch
+  // needs clearing between calls.
+  constexpr int FPT = 8;
+  const uint32_t r = uint32_t(rows), wd = uint32_t(width);
+  const uint32_t fpc = 8 * FPT, nch = uint32_t(chunks);
+  const float inv_width = 1.0f / float(width);
+  const dim3 grid((r + 32 * vec - 1) / (32 * vec), nch);
+  if (vec == 4) {
+    rms_partial_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, partial, r, wd, fpc);
+    rms_apply_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, weight, partial, y, r, wd, fpc, nch,
+                                                       eps, inv_width, centered ? 1 : 0);
+  } else if (vec == 2) {
+    rms_partial_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, partial, r, wd, fpc);
+    rms_apply_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, weight, partial, y, r, wd, fpc, nch,
+                                                       eps, inv_width, centered ? 1 : 0);
+  } else {
+    rms_partial_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, partial, r, wd, fpc);
+    rms_apply_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, weight, partial, y, r, wd, fpc, nch,
+                                                       eps, inv_width, centered ? 1 : 0);
+  }
+  return check_launch(op);
+}

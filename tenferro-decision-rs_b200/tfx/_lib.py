@@ -78,6 +78,7 @@ SIGNATURES = {
     "tfx_layernorm_ff_f64": (_int, [_p, _p, _p, _p, _i64, _i64, ctypes.c_double, _p]),
     "tfx_rmsnorm_last_f32": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_float, _p]),
     "tfx_rmsnorm_last_f64": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_double, _p]),
+    "tfx_rmsnorm_last_f32_noalloc": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_float, _p]),
     "tfx_softmax_desc_init": (None, [ctypes.POINTER(SoftmaxDesc), _i64, _i64, _i64, _i64]),
     "tfx_masked_softmax_f32": (_int, [_p, _p, ctypes.POINTER(SoftmaxDesc), _p]),
     "tfx_rope_pairhalf_f32": (_int, [_p, _p, _p, _p, ctypes.POINTER(RopeDesc), _p]),
