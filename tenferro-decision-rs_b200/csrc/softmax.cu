@@ -66,15 +66,6 @@ __device__ __forceinline__ RowCtx row_ctx(const MaskArgs& m, uint64_t local_row)
 
 constexpr int kExclude = TFX_SOFTMAX_EXCLUDE;
 
-// Whether any of keys [k, k + 4) passes the analytic conditions. A score that
-// fails them never reaches the result (EXCLUDE replaces it by -inf, FILL by
-// -1e30), so a float4 of scores outside [lo, lo + span) is not read -- the
-// same skipping of masked key spans as the reference's attention rows
-// (crates/cpu-kernels/src/lib.rs:900-936, key_ranges).
-__device__ __forceinline__ bool any_kept4(const RowCtx& c, uint32_t k) {
-  return c.span != 0 && k + 3 >= c.lo && k < c.lo + c.span;
-}
-
 // Masked, scaled score of key k (in range). EXCLUDE: -inf when masked;
 // FILL: -1e30 when masked (util.rs:87).
 template <int SEM, bool TENSORS>
@@ -112,60 +103,14 @@ __device__ __forceinline__ float quotient(float e, float sum, float r, bool fast
   return q;
 }
 
-// ---- warp per row, NV float4 per lane ------------------------------------------
-
-template <int NV, int SEM, bool TENSORS>
-__global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ s,
-                                                           float* __restrict__ p, uint64_t rows,
-                                                           MaskArgs m) {
-  const int lane = threadIdx.x & 31;
-  const uint64_t row = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;  // the whole warp leaves together
-  const RowCtx c = row_ctx(m, row);
-  const uint32_t kv = uint32_t(m.k_len / 4);
-  const float4* src = reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len));
-  float v[NV][4];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 32 + lane;
-    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (q4 < kv && any_kept4(c, q4 * 4)) t = ld_stream(src + q4);
-    v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
-  }
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 32 + lane;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? score<SEM, TENSORS>(m, c, q4 * 4 + e, v[j][e]) : -INFINITY;
-      mx = fmaxf(mx, v[j][e]);
-    }
-  }
-  mx = warp_max(mx);
-  float sum = 0.0f;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[j][e] = expo<SEM>(v[j][e], mx);
-      sum = __fadd_rn(sum, v[j][e]);
-    }
-  }
-  sum = warp_sum(sum);
-  const float r = __frcp_rn(sum);
-  const bool fast = sum < 0x1p24f;
-  float4* dst = reinterpret_cast<float4*>(p + row * uint64_t(m.k_len));
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 32 + lane;
-    if (q4 < kv)
-      dst[q4] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
-                            quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
-  }
-}
-
-// ---- CTA (256 threads) per row, NV float4 per thread ----------------------------
+// ---- one row, compacted onto the keys its mask can keep ---------------------------
+//
+// The threads of a row (a warp, or a CTA for long rows) take the float4 chunks
+// that meet the row's kept interval [lo, lo + span) -- chunk c0 + t + STRIDE*j
+// for thread t -- so reading, exp and division scale with the kept keys, not
+// with k_len. Every key outside those chunks is masked: its probability is one
+// per-row value p_out (0; NaN for an all-masked EXCLUDE row, 1/k_len for an
+// all-masked FILL row), written without reading its score.
 
 __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
   v = is_max ? warp_max(v) : warp_sum(v);
@@ -179,6 +124,92 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
   return r;
 }
 
+template <int NV, int STRIDE, int SEM, bool TENSORS, class RMax, class RSum>
+__device__ __forceinline__ void softmax_row(const float4* __restrict__ src, float4* dst,
+                                            const MaskArgs& m, const RowCtx& c, uint32_t kv,
+                                            uint32_t tid, RMax rmax, RSum rsum) {
+  const uint32_t c0 = c.lo >> 2;
+  const uint32_t nch = c.span ? ((c.lo + c.span - 1) >> 2) - c0 + 1 : 0;
+  float v[NV][4];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t idx = j * STRIDE + tid;
+    if (idx < nch) {
+      const float4 t = ld_stream(src + c0 + idx);
+      v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
+    }
+  }
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * STRIDE < nch) {  // uniform over the row's threads
+      const uint32_t idx = j * STRIDE + tid;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[j][e] = idx < nch ? score<SEM, TENSORS>(m, c, (c0 + idx) * 4 + e, v[j][e]) : -INFINITY;
+        mx = fmaxf(mx, v[j][e]);
+      }
+    }
+  }
+  // FILL: the keys outside the processed chunks hold -1e30 as well.
+  if (SEM != kExclude && nch < kv) mx = fmaxf(mx, -1.0e30f);
+  mx = rmax(mx);
+  float sum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * STRIDE < nch) {
+      const uint32_t idx = j * STRIDE + tid;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        v[j][e] = idx < nch ? expo<SEM>(v[j][e], mx) : 0.0f;
+        sum = __fadd_rn(sum, v[j][e]);
+      }
+    }
+  }
+  sum = rsum(sum);
+  // exp of a key outside the processed chunks: 0, or 1 when the whole FILL row
+  // is masked (then every one of them adds 1, as the dense sum would).
+  float e_out = 0.0f;
+  if (SEM != kExclude && nch < kv) {
+    e_out = expf(__fsub_rn(-1.0e30f, mx));
+    sum = __fadd_rn(sum, __fmul_rn(float(4 * (kv - nch)), e_out));
+  }
+  const float r = __frcp_rn(sum);
+  const bool fast = sum < 0x1p24f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    if (j * STRIDE < nch) {
+      const uint32_t idx = j * STRIDE + tid;
+      if (idx < nch)
+        dst[c0 + idx] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
+                                    quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
+    }
+  }
+  const float p_out = quotient(e_out, sum, r, fast);
+  const float4 fill = make_float4(p_out, p_out, p_out, p_out);
+  for (uint32_t q4 = tid; q4 < kv; q4 += STRIDE)
+    if (q4 - c0 >= nch) dst[q4] = fill;
+}
+
+// ---- warp per row (k_len <= 1024) -------------------------------------------------
+
+template <int NV, int SEM, bool TENSORS>
+__global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ s,
+                                                           float* __restrict__ p, uint64_t rows,
+                                                           MaskArgs m) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t row = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;  // the whole warp leaves together
+  const RowCtx c = row_ctx(m, row);
+  const uint32_t kv = uint32_t(m.k_len / 4);
+  softmax_row<NV, 32, SEM, TENSORS>(
+      reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
+      reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, lane,
+      [](float x) { return warp_max(x); }, [](float x) { return warp_sum(x); });
+}
+
+// ---- CTA (256 threads) per row (k_len <= 8192) -------------------------------------
+
 template <int NV, int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restrict__ s,
                                                           float* __restrict__ p, MaskArgs m) {
@@ -186,46 +217,11 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
   const uint64_t row = blockIdx.x;
   const RowCtx c = row_ctx(m, row);
   const uint32_t kv = uint32_t(m.k_len / 4);
-  const float4* src = reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len));
-  float v[NV][4];
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 256 + threadIdx.x;
-    float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (q4 < kv && any_kept4(c, q4 * 4)) t = ld_stream(src + q4);
-    v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
-  }
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 256 + threadIdx.x;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[j][e] = q4 < kv ? score<SEM, TENSORS>(m, c, q4 * 4 + e, v[j][e]) : -INFINITY;
-      mx = fmaxf(mx, v[j][e]);
-    }
-  }
-  mx = block_reduce(mx, red, true);
-  float sum = 0.0f;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[j][e] = expo<SEM>(v[j][e], mx);
-      sum = __fadd_rn(sum, v[j][e]);
-    }
-  }
-  sum = block_reduce(sum, red, false);
-  const float r = __frcp_rn(sum);
-  const bool fast = sum < 0x1p24f;
-  float4* dst = reinterpret_cast<float4*>(p + row * uint64_t(m.k_len));
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const uint32_t q4 = j * 256 + threadIdx.x;
-    if (q4 < kv)
-      dst[q4] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
-                            quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
-  }
+  softmax_row<NV, 256, SEM, TENSORS>(
+      reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
+      reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, threadIdx.x,
+      [&](float x) { return block_reduce(x, red, true); },
+      [&](float x) { return block_reduce(x, red, false); });
 }
 
 // ---- any length / alignment: CTA per row, three passes (row re-read from L2) ----
@@ -239,7 +235,8 @@ __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* s, fl
   const float* src = s + row * uint64_t(m.k_len);
   float* dst = p + row * uint64_t(m.k_len);
   const uint32_t n = uint32_t(m.k_len);
-  // Scores outside the row's analytic interval are never read (see any_kept4).
+  // Scores outside the row's analytic interval are never read: they cannot
+  // reach the result (masked keys are -inf / -1e30 whatever they hold).
   auto at = [&](uint32_t k) { return k - c.lo < c.span ? src[k] : 0.0f; };
   float mx = -INFINITY;
   for (uint32_t k = threadIdx.x; k < n; k += 256)
