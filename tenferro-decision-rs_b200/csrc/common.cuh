@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <string>
+#include <utility>
 
 #include "tfx.h"
 
@@ -84,6 +85,23 @@ __device__ __forceinline__ double ld_stream(const double* p) {
   return v;
 }
 
+// Programmatic dependent launch. Every kernel here is launched with
+// programmatic stream serialisation (launch_kernel below), so it may start
+// while the previous kernel on the stream is still finishing. It must call
+// pdl_wait() before touching global memory: that returns once the previous
+// grid has completed and its writes are visible (and guards against
+// overwriting what the previous grid still reads). pdl_launch_dependents()
+// lets the next kernel's CTAs be scheduled as soon as this grid's last CTA has
+// started; they in turn wait in their own pdl_wait().
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_enter() {
+  pdl_wait();
+  pdl_launch_dependents();
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int m = 16; m >= 1; m >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, m));
@@ -122,6 +140,40 @@ struct FastDiv {
     return (t + ((n - t) >> 1)) >> (s - 1);
   }
 };
+
+// Launches kernel<<<grid, block, smem, stream>>>(args...) with programmatic
+// stream serialisation allowed (see pdl_wait) and, when cluster > 1, a
+// (cluster, 1, 1) thread-block cluster; then reports failures as check_launch
+// does.
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* op, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t stream, unsigned cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  unsigned n = 1;
+  if (cluster > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "launch",
+                std::string(cudaGetErrorName(err)) + ": " + cudaGetErrorString(err));
+  }
+  return check_launch(op);
+}
 
 }  // namespace tfx
 

@@ -71,6 +71,7 @@ __device__ __forceinline__ Vec<N> apply(const Vec<N>& a, P pair_fn, S scalar_fn)
 // F::store(i, in) computes and writes its outputs.
 template <class F, int U>
 __global__ void __launch_bounds__(kThreads) map_kernel(uint32_t n, F f) {
+  pdl_enter();
   const uint32_t step = gridDim.x * (kThreads * U);
   for (uint32_t base = blockIdx.x * (kThreads * U) + threadIdx.x; base < n; base += step) {
     typename F::In in[U];
@@ -104,8 +105,7 @@ int launch_map(const char* op, uint32_t n, const F& f, cudaStream_t stream) {
   }
   const uint64_t need = (uint64_t(n) + kThreads * U - 1) / (kThreads * U);
   const uint32_t grid = uint32_t(std::min<uint64_t>(need, uint64_t(dev.sms) * occupancy));
-  map_kernel<F, U><<<grid, kThreads, 0, stream>>>(n, f);
-  return check_launch(op);
+  return launch_kernel(op, map_kernel<F, U>, dim3(grid), dim3(kThreads), 0, stream, 1, n, f);
 }
 
 // ---- functors ------------------------------------------------------------------
@@ -268,6 +268,7 @@ __device__ __forceinline__ double erf_as(double x) {
 template <bool GELU>
 __global__ void __launch_bounds__(kThreads) erf_f64_kernel(const double* __restrict__ x,
                                                            double* __restrict__ y, uint64_t n) {
+  pdl_enter();
   const uint64_t step = uint64_t(gridDim.x) * kThreads;
   for (uint64_t i = uint64_t(blockIdx.x) * kThreads + threadIdx.x; i < n; i += step) {
     const double v = ld_stream(x + i);
@@ -344,8 +345,8 @@ int tfx_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream) {
   if (st != TFX_OK) return st;
   const uint64_t grid = std::min<uint64_t>((uint64_t(n) + kThreads - 1) / kThreads,
                                            uint64_t(dev.sms) * 8);
-  erf_f64_kernel<false><<<unsigned(grid), kThreads, 0, stream>>>(x, y, uint64_t(n));
-  return check_launch(op);
+  return launch_kernel(op, erf_f64_kernel<false>, dim3(unsigned(grid)), dim3(kThreads), 0, stream,
+                       1, x, y, uint64_t(n));
 }
 
 int tfx_gelu_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream) {
@@ -360,8 +361,8 @@ int tfx_gelu_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream)
   if (st != TFX_OK) return st;
   const uint64_t grid = std::min<uint64_t>((uint64_t(n) + kThreads - 1) / kThreads,
                                            uint64_t(dev.sms) * 8);
-  erf_f64_kernel<true><<<unsigned(grid), kThreads, 0, stream>>>(x, y, uint64_t(n));
-  return check_launch(op);
+  return launch_kernel(op, erf_f64_kernel<true>, dim3(unsigned(grid)), dim3(kThreads), 0, stream,
+                       1, x, y, uint64_t(n));
 }
 
 int tfx_geglu_ff_f32(const float* u, float* y, int64_t inter, int64_t cols, tfx_stream_t stream) {

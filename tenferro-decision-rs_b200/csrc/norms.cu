@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(256) ln_warp_kernel(const T* __restrict__ x,
                                                       const T* __restrict__ w,
                                                       const T* __restrict__ b, T* __restrict__ y,
                                                       uint32_t d, uint64_t cols, T eps) {
+  pdl_enter();
   constexpr int VN = V16<T>::N;
   const int lane = threadIdx.x & 31;
   const uint64_t col = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
@@ -202,6 +203,7 @@ __global__ void __launch_bounds__(256, 8) ln_smem_kernel(const float* __restrict
                                                          const float* __restrict__ b,
                                                          float* __restrict__ y, uint32_t d,
                                                          uint64_t cols, float eps) {
+  pdl_enter();
   extern __shared__ float4 stage[];  // 8 warps x d floats
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint64_t col = uint64_t(blockIdx.x) * 8 + warp;
@@ -289,6 +291,7 @@ __global__ void __launch_bounds__(256) ln_cta_kernel(const T* __restrict__ x,
                                                      const T* __restrict__ w,
                                                      const T* __restrict__ b, T* __restrict__ y,
                                                      uint32_t d, T eps) {
+  pdl_enter();
   constexpr int VN = V16<T>::N;
   __shared__ T red[8];
   const uint64_t col = blockIdx.x;
@@ -346,6 +349,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) ln_generic_kernel(const T* x, const T* __restrict__ w,
                                                          const T* __restrict__ b, T* y,
                                                          uint64_t d, T eps) {
+  pdl_enter();
   __shared__ T red[8];
   const T* xc = x + uint64_t(blockIdx.x) * d;
   T* yc = y + uint64_t(blockIdx.x) * d;
@@ -404,9 +408,10 @@ int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64
       const size_t smem = size_t(8) * size_t(d) * 4;
 #define TFX_LN_SMEM(NVV)                                                                       \
   if (dv <= 32 * NVV) {                                                                         \
-    if (bias) ln_smem_kernel<NVV, true><<<grid, 256, smem, stream>>>(x, w, b, y, du, cols, eps);  \
-    else ln_smem_kernel<NVV, false><<<grid, 256, smem, stream>>>(x, w, b, y, du, cols, eps);      \
-    return check_launch(op);                                                                    \
+    return bias ? launch_kernel(op, ln_smem_kernel<NVV, true>, dim3(grid), dim3(256), smem,      \
+                                stream, 1, x, w, b, y, du, uint64_t(cols), eps)                  \
+                : launch_kernel(op, ln_smem_kernel<NVV, false>, dim3(grid), dim3(256), smem,     \
+                                stream, 1, x, w, b, y, du, uint64_t(cols), eps);                 \
   }
       TFX_LN_SMEM(1)
       TFX_LN_SMEM(2)
@@ -423,9 +428,10 @@ int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64
     const uint32_t du = uint32_t(d);
 #define TFX_LN_WARP(NVV)                                                                \
   if (dv <= 32 * NVV) {                                                                   \
-    if (bias) ln_warp_kernel<T, NVV, true><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);  \
-    else ln_warp_kernel<T, NVV, false><<<grid, 256, 0, stream>>>(x, w, b, y, du, cols, eps);      \
-    return check_launch(op);                                                              \
+    return bias ? launch_kernel(op, ln_warp_kernel<T, NVV, true>, dim3(grid), dim3(256), 0,     \
+                                stream, 1, x, w, b, y, du, uint64_t(cols), eps)                  \
+                : launch_kernel(op, ln_warp_kernel<T, NVV, false>, dim3(grid), dim3(256), 0,    \
+                                stream, 1, x, w, b, y, du, uint64_t(cols), eps);                 \
   }
     TFX_LN_WARP(1)
     TFX_LN_WARP(2)
@@ -443,17 +449,18 @@ int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64
     const uint32_t du = uint32_t(d);
 #define TFX_LN_CTA(NVV)                                                                   \
   if (dv <= 256 * NVV) {                                                                   \
-    if (bias) ln_cta_kernel<T, NVV, true><<<grid, 256, 0, stream>>>(x, w, b, y, du, eps);  \
-    else ln_cta_kernel<T, NVV, false><<<grid, 256, 0, stream>>>(x, w, b, y, du, eps);      \
-    return check_launch(op);                                                               \
+    return bias ? launch_kernel(op, ln_cta_kernel<T, NVV, true>, dim3(grid), dim3(256), 0,  \
+                                stream, 1, x, w, b, y, du, eps)                             \
+                : launch_kernel(op, ln_cta_kernel<T, NVV, false>, dim3(grid), dim3(256), 0, \
+                                stream, 1, x, w, b, y, du, eps);                            \
   }
     TFX_LN_CTA(2)
     TFX_LN_CTA(4)
     TFX_LN_CTA(8)
 #undef TFX_LN_CTA
   }
-  ln_generic_kernel<T><<<unsigned(cols), 256, 0, stream>>>(x, w, b, y, uint64_t(d), eps);
-  return check_launch(op);
+  return launch_kernel(op, ln_generic_kernel<T>, dim3(unsigned(cols)), dim3(256), 0, stream, 1, x,
+                       w, b, y, uint64_t(d), eps);
 }
 
 // ---- RMSNorm feature-last: cluster-split register tiles ---------------------------
@@ -505,6 +512,7 @@ template <typename T, int VEC, int FPT>
 __global__ void __launch_bounds__(kRmsWarps * 32) rms_cluster_kernel(
     const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, uint32_t rows,
     uint32_t width, uint32_t fpc, T eps, T inv_width, int centered) {
+  pdl_enter();
   constexpr int TR = 32 * VEC;  // tokens per tile
   __shared__ T red[kRmsWarps][TR];
   __shared__ T part[TR];
@@ -573,6 +581,7 @@ __global__ void __launch_bounds__(256) rms_generic_kernel(const T* x, const T* _
                                                           T* y, uint64_t rows,
                                                           uint64_t width, T eps, T inv_width,
                                                           int centered) {
+  pdl_enter();
   __shared__ T red[8][32];
   __shared__ T scale_s[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -607,6 +616,7 @@ __global__ void __launch_bounds__(256) rms_tile_kernel(const float* x,
                                                        const float* __restrict__ w, float* y,
                                                        uint32_t rows, uint32_t width, float eps,
                                                        float inv_width, int centered) {
+  pdl_enter();
   __shared__ float red[8][32];
   __shared__ float scale_s[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -660,6 +670,7 @@ __global__ void __launch_bounds__(256) rms_partial_kernel(const float* __restric
                                                           float* __restrict__ partial,
                                                           uint32_t rows, uint32_t width,
                                                           uint32_t fpc) {
+  pdl_enter();
   constexpr int TR = 32 * VEC;
   __shared__ float red[8][TR];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -704,6 +715,7 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const float* x,
                                                         float* y, uint32_t rows, uint32_t width,
                                                         uint32_t fpc, uint32_t chunks, float eps,
                                                         float inv_width, int centered) {
+  pdl_enter();
   constexpr int TR = 32 * VEC;
   __shared__ float scale_s[TR];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -762,13 +774,15 @@ cudaError_t launch_rms_cluster(const T* x, const T* w, T* y, uint32_t rows, uint
   cfg.blockDim = dim3(kRmsWarps * 32, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = unsigned(csize);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see pdl_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (csize > 8) {
     const cudaError_t err = cudaFuncSetAttribute(
         rms_cluster_kernel<T, VEC, FPT>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -798,20 +812,19 @@ int rms_split(const char* op, const float* x, const float* w, float* y, uint32_t
     return 1;
   }
   const dim3 grid(tiles, chunks);
-  if (vec == 4) {
-    rms_partial_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
-    rms_apply_kernel<4, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
-                                                       chunks, eps, inv_width, centered);
-  } else if (vec == 2) {
-    rms_partial_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
-    rms_apply_kernel<2, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
-                                                       chunks, eps, inv_width, centered);
-  } else {
-    rms_partial_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, partial, rows, width, fpc);
-    rms_apply_kernel<1, FPT><<<grid, 256, 0, stream>>>(x, w, partial, y, rows, width, fpc,
-                                                       chunks, eps, inv_width, centered);
-  }
-  const int rc = check_launch(op);
+  auto run = [&](auto partial_k, auto apply_k) {
+    int rc = launch_kernel(op, partial_k, grid, dim3(256), 0, stream, 1, x, partial, rows, width,
+                           fpc);
+    if (rc == TFX_OK)
+      rc = launch_kernel(op, apply_k, grid, dim3(256), 0, stream, 1, x, w,
+                         static_cast<const float*>(partial), y, rows, width, fpc, chunks, eps,
+                         inv_width, centered);
+    return rc;
+  };
+  int rc;
+  if (vec == 4) rc = run(rms_partial_kernel<4, FPT>, rms_apply_kernel<4, FPT>);
+  else if (vec == 2) rc = run(rms_partial_kernel<2, FPT>, rms_apply_kernel<2, FPT>);
+  else rc = run(rms_partial_kernel<1, FPT>, rms_apply_kernel<1, FPT>);
   cudaFreeAsync(partial, stream);
   return rc;
 }
@@ -845,9 +858,9 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
   if constexpr (std::is_same_v<T, float>) {
     const int choice = rms_kernel_choice();
     if (small && choice == 2) {
-      rms_tile_kernel<8><<<unsigned((rows + 31) / 32), 256, 0, stream>>>(
-          x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width, centered);
-      return check_launch(op);
+      return launch_kernel(op, rms_tile_kernel<8>, dim3(unsigned((rows + 31) / 32)), dim3(256), 0,
+                           stream, 1, x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width,
+                           centered);
     }
     // The split variant re-reads x once; it wins when x stays in L2 between
     // its two passes.
@@ -892,9 +905,9 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
 #undef TFX_RMS_TRY
   }
   TFX_REQUIRE((rows + 31) / 32 < (int64_t(1) << 31), op, "rows", "too many rows for one call");
-  rms_generic_kernel<T><<<unsigned((rows + 31) / 32), 256, 0, stream>>>(
-      x, w, y, uint64_t(rows), uint64_t(width), eps, inv_width, centered);
-  return check_launch(op);
+  return launch_kernel(op, rms_generic_kernel<T>, dim3(unsigned((rows + 31) / 32)), dim3(256), 0,
+                       stream, 1, x, w, y, uint64_t(rows), uint64_t(width), eps, inv_width,
+                       centered);
 }
 
 }  // namespace

@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(256) rope_vec_kernel(const float* x, float* y,
                                                        RopeArgs a, uint64_t total,
                                                        FastDiv units_div, FastDiv vec_div,
                                                        FastDiv seq_div, uint32_t rot_units) {
+  pdl_enter();
   const uint64_t step = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += step) {
     const uint32_t tt = uint32_t(t);
@@ -74,6 +75,7 @@ __global__ void __launch_bounds__(256) rope_scalar_kernel(const float* x, float*
                                                           const float* __restrict__ sin_t,
                                                           RopeArgs a, int64_t work_per_vec,
                                                           int vec_fastest, uint64_t total) {
+  pdl_enter();
   const uint64_t step = uint64_t(gridDim.x) * blockDim.x;
   for (uint64_t t = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += step) {
     uint64_t r = t;
@@ -158,17 +160,16 @@ extern "C" int tfx_rope_pairhalf_f32(const float* x, float* y, const float* cos_
     if (total < (int64_t(1) << 32) && vectors < (int64_t(1) << 32)) {
       const uint64_t grid =
           std::min<uint64_t>((uint64_t(total) + 255) / 256, uint64_t(dev.sms) * 8);
-      rope_vec_kernel<<<unsigned(grid), 256, 0, stream>>>(
-          x, y, cos_table, sin_table, a, uint64_t(total), FastDiv(uint32_t(units)),
-          FastDiv(uint32_t(a.n_vec)), FastDiv(uint32_t(a.seq)), uint32_t(a.half / 4));
-      return check_launch(op);
+      return launch_kernel(op, rope_vec_kernel, dim3(unsigned(grid)), dim3(256), 0, stream, 1, x,
+                           y, cos_table, sin_table, a, uint64_t(total), FastDiv(uint32_t(units)),
+                           FastDiv(uint32_t(a.n_vec)), FastDiv(uint32_t(a.seq)),
+                           uint32_t(a.half / 4));
     }
   }
   const int64_t work = a.half + tail;
   const uint64_t total = uint64_t(vectors) * uint64_t(work);
   const int vec_fastest = a.s_vec < a.s_feat ? 1 : 0;
   const uint64_t grid = std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 8);
-  rope_scalar_kernel<<<unsigned(grid), 256, 0, stream>>>(x, y, cos_table, sin_table, a, work,
-                                                         vec_fastest, total);
-  return check_launch(op);
+  return launch_kernel(op, rope_scalar_kernel, dim3(unsigned(grid)), dim3(256), 0, stream, 1, x, y,
+                       cos_table, sin_table, a, work, vec_fastest, total);
 }

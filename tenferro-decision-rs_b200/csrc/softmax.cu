@@ -37,6 +37,10 @@ struct MaskArgs {
   int64_t keep_sb, keep_sq, keep_sk;
   float scale;
   int causal, skip_invalid_q;
+  // Rows < 2^32 (always, below): q = row mod q_len and b = row / (heads*q_len)
+  // by 32-bit multiply-shift division instead of 64-bit division.
+  bool rows32;
+  FastDiv div_q, div_bq;
 };
 
 // Keys [lo, lo + span) of a row pass the analytic conditions.
@@ -48,8 +52,14 @@ struct RowCtx {
 __device__ __forceinline__ RowCtx row_ctx(const MaskArgs& m, uint64_t local_row) {
   RowCtx c;
   const uint64_t row = local_row + uint64_t(m.row_offset);
-  c.q = int64_t(row % uint64_t(m.q_len));
-  c.b = int64_t(row / uint64_t(m.heads * m.q_len));
+  if (m.rows32) {
+    const uint32_t r32 = uint32_t(row);
+    c.q = int64_t(r32 - m.div_q.div(r32) * m.div_q.d);
+    c.b = int64_t(m.div_bq.div(r32));
+  } else {
+    c.q = int64_t(row % uint64_t(m.q_len));
+    c.b = int64_t(row / uint64_t(m.heads * m.q_len));
+  }
   const int64_t vlen = m.valid_lens ? int64_t(m.valid_lens[c.b]) : m.valid_len;
   int64_t lo = 0, hi = m.k_len;
   if (vlen >= 0) hi = min(hi, vlen);
@@ -197,6 +207,7 @@ template <int NV, int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ s,
                                                            float* __restrict__ p, uint64_t rows,
                                                            MaskArgs m) {
+  pdl_enter();
   const int lane = threadIdx.x & 31;
   const uint64_t row = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;  // the whole warp leaves together
@@ -213,6 +224,7 @@ __global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restri
 template <int NV, int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restrict__ s,
                                                           float* __restrict__ p, MaskArgs m) {
+  pdl_enter();
   __shared__ float red[8];
   const uint64_t row = blockIdx.x;
   const RowCtx c = row_ctx(m, row);
@@ -229,6 +241,7 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
 template <int SEM, bool TENSORS>
 __global__ void __launch_bounds__(256) softmax_generic_kernel(const float* s, float* p,
                                                               MaskArgs m) {
+  pdl_enter();
   __shared__ float red[8];
   const uint64_t row = blockIdx.x;
   const RowCtx c = row_ctx(m, row);
@@ -263,8 +276,8 @@ int launch_softmax(const char* op, const float* scores, float* probs, int64_t ro
     const unsigned grid = unsigned((rows + 7) / 8);
 #define TFX_SM_WARP(NV)                                                                    \
   if (kv <= 32 * NV) {                                                                     \
-    softmax_warp_kernel<NV, SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, rows, m); \
-    return check_launch(op);                                                               \
+    return launch_kernel(op, softmax_warp_kernel<NV, SEM, TENSORS>, dim3(grid), dim3(256), 0, \
+                         stream, 1, scores, probs, uint64_t(rows), m);                          \
   }
     TFX_SM_WARP(1)
     TFX_SM_WARP(2)
@@ -279,16 +292,16 @@ int launch_softmax(const char* op, const float* scores, float* probs, int64_t ro
   if (vec && kv <= 256 * 8) {
 #define TFX_SM_CTA(NV)                                                              \
   if (kv <= 256 * NV) {                                                             \
-    softmax_cta_kernel<NV, SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, m); \
-    return check_launch(op);                                                        \
+    return launch_kernel(op, softmax_cta_kernel<NV, SEM, TENSORS>, dim3(grid), dim3(256), 0, \
+                         stream, 1, scores, probs, m);                                         \
   }
     TFX_SM_CTA(2)
     TFX_SM_CTA(4)
     TFX_SM_CTA(8)
 #undef TFX_SM_CTA
   }
-  softmax_generic_kernel<SEM, TENSORS><<<grid, 256, 0, stream>>>(scores, probs, m);
-  return check_launch(op);
+  return launch_kernel(op, softmax_generic_kernel<SEM, TENSORS>, dim3(grid), dim3(256), 0, stream,
+                       1, scores, probs, m);
 }
 
 }  // namespace
@@ -301,6 +314,12 @@ int masked_softmax_rows(const float* scores, float* probs, const tfx_softmax_des
   if (row_count == 0) return TFX_OK;
   MaskArgs m;
   m.row_offset = row_begin;
+  const int64_t total_rows = d->batch * d->heads * d->q_len;
+  m.rows32 = total_rows < (int64_t(1) << 31) && d->heads * d->q_len < (int64_t(1) << 31);
+  if (m.rows32) {
+    m.div_q = FastDiv(uint32_t(d->q_len));
+    m.div_bq = FastDiv(uint32_t(d->heads * d->q_len));
+  }
   m.heads = d->heads;
   m.q_len = d->q_len;
   m.k_len = d->k_len;
