@@ -322,6 +322,10 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     measure("masked_softmax", lambda: (normal(ns, 2.0), torch.empty(ns, device=device)),
             lambda b: ops.masked_softmax(b[0], B, H, L, L, window=64, valid_len=L - 37, out=b[1]),
             2 * ns * 4, ns, touched=softmax_touched_bytes(B, H, L, 64, L - 37))
+    # the chain's global-attention layers: the same rows without the window
+    measure("masked_softmax_global", lambda: (normal(ns, 2.0), torch.empty(ns, device=device)),
+            lambda b: ops.masked_softmax(b[0], B, H, L, L, window=-1, valid_len=L - 37, out=b[1]),
+            2 * ns * 4, ns, touched=softmax_touched_bytes(B, H, L, -1, L - 37))
     F, T = 768, 8192
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
@@ -631,7 +635,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--only-op", default=None,
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
-                         "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, bias_add) and "
+                         "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
+                         "masked_softmax_global, bias_add) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
     args = ap.parse_args()

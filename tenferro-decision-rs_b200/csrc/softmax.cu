@@ -1,9 +1,9 @@
 // softmax.cu -- masked row softmax over row-major [batch][heads][q_len][k_len]
 // scores (keys contiguous).
 //
-// One warp owns one row of up to 1024 keys: the row is read once with 128-bit
-// loads into registers, the max and the sum are warp-shuffle reductions over
-// registers, and the probabilities are written once. Longer rows use a CTA per
+// A group of 8, 16 or 32 lanes owns one row of up to 1024 keys: the row is read
+// once with 128-bit loads into registers, the max and the sum are shuffle
+// reductions over registers, and the probabilities are written once. Longer rows use a CTA per
 // row (up to 8192 keys in registers); anything else a CTA-per-row kernel that
 // re-reads the row from L2. Semantics follow the reference (see tfx.h):
 // EXCLUDE restates the f32 attention rows of crates/cpu-kernels/src/lib.rs:
@@ -14,8 +14,8 @@
 // keep one interval of keys per row, so each row computes [lo, hi) once and
 // every key is tested with one unsigned compare. The division p = e / sum is
 // done as e * (1/sum) followed by one FMA correction step (Markstein), which
-// returns the correctly rounded quotient for normal results; numerators that
-// could produce a subnormal quotient take the IEEE division instead.
+// returns the correctly rounded quotient for normal results; a row with a
+// numerator that could produce a subnormal quotient takes the IEEE division.
 
 #include <cmath>
 #include <string>
@@ -134,12 +134,16 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
   return r;
 }
 
-template <int NV, int STRIDE, int SEM, bool TENSORS, class RMax, class RSum>
+template <int NV, int STRIDE, int SEM, bool TENSORS, class RMax, class RSum, class RAny>
 __device__ __forceinline__ void softmax_row(const float4* __restrict__ src, float4* dst,
                                             const MaskArgs& m, const RowCtx& c, uint32_t kv,
-                                            uint32_t tid, RMax rmax, RSum rsum) {
+                                            uint32_t tid, RMax rmax, RSum rsum, RAny rany) {
+  // Precondition: kv <= NV * STRIDE.
+  constexpr float kMasked = SEM == kExclude ? -INFINITY : -1.0e30f;
   const uint32_t c0 = c.lo >> 2;
-  const uint32_t nch = c.span ? ((c.lo + c.span - 1) >> 2) - c0 + 1 : 0;
+  const uint32_t hi = c.lo + c.span;
+  const uint32_t nch = c.span ? ((hi - 1) >> 2) - c0 + 1 : 0;
+  const bool scaled = m.scale != 1.0f;
   float v[NV][4];
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
@@ -149,34 +153,66 @@ __device__ __forceinline__ void softmax_row(const float4* __restrict__ src, floa
       v[j][0] = t.x; v[j][1] = t.y; v[j][2] = t.z; v[j][3] = t.w;
     }
   }
+  // Scale and mask. Chunks inside [lo, hi) need no per-key test.
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     if (j * STRIDE < nch) {  // uniform over the row's threads
       const uint32_t idx = j * STRIDE + tid;
+      if (idx < nch) {
+        const uint32_t k0 = (c0 + idx) << 2;
+        if constexpr (TENSORS) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        v[j][e] = idx < nch ? score<SEM, TENSORS>(m, c, (c0 + idx) * 4 + e, v[j][e]) : -INFINITY;
-        mx = fmaxf(mx, v[j][e]);
+          for (int e = 0; e < 4; ++e) v[j][e] = score<SEM, true>(m, c, k0 + e, v[j][e]);
+        } else {
+          if (scaled) {
+            const float2 sc = make_float2(m.scale, m.scale);
+            const float2 a = __fmul2_rn(make_float2(v[j][0], v[j][1]), sc);
+            const float2 b = __fmul2_rn(make_float2(v[j][2], v[j][3]), sc);
+            v[j][0] = a.x; v[j][1] = a.y; v[j][2] = b.x; v[j][3] = b.y;
+          }
+          if (k0 < c.lo || k0 + 4 > hi) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (k0 + e - c.lo >= c.span) v[j][e] = kMasked;
+          }
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(v[j][0], v[j][1]), fmaxf(v[j][2], v[j][3])));
       }
     }
   }
   // FILL: the keys outside the processed chunks hold -1e30 as well.
   if (SEM != kExclude && nch < kv) mx = fmaxf(mx, -1.0e30f);
   mx = rmax(mx);
-  float sum = 0.0f;
+  // exp(v - max). EXCLUDE: a non-finite score (masked -inf, NaN, +inf) must
+  // contribute 0; every such case makes exp return NaN or 0 here, and
+  // fmaxf(e, 0) maps NaN to 0 and leaves every other e >= 0 unchanged.
+  float2 acc = make_float2(0.0f, 0.0f);
+  bool tiny = false;  // a nonzero e < 2^-100: its quotient could be subnormal
+  const float2 nmx = make_float2(-mx, -mx);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     if (j * STRIDE < nch) {
       const uint32_t idx = j * STRIDE + tid;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        v[j][e] = idx < nch ? expo<SEM>(v[j][e], mx) : 0.0f;
-        sum = __fadd_rn(sum, v[j][e]);
+      if (idx < nch) {
+        const float2 d0 = __fadd2_rn(make_float2(v[j][0], v[j][1]), nmx);
+        const float2 d1 = __fadd2_rn(make_float2(v[j][2], v[j][3]), nmx);
+        float e0 = expf(d0.x), e1 = expf(d0.y), e2 = expf(d1.x), e3 = expf(d1.y);
+        if constexpr (SEM == kExclude) {
+          e0 = fmaxf(e0, 0.0f); e1 = fmaxf(e1, 0.0f); e2 = fmaxf(e2, 0.0f); e3 = fmaxf(e3, 0.0f);
+        }
+        v[j][0] = e0; v[j][1] = e1; v[j][2] = e2; v[j][3] = e3;
+        acc = __fadd2_rn(acc, make_float2(e0, e1));
+        acc = __fadd2_rn(acc, make_float2(e2, e3));
+        // bits(e) - 1 < bits(2^-100) - 1 (unsigned)  <=>  0 < e < 2^-100
+        const uint32_t lim = 0x0D800000u - 1u;
+        const uint32_t b = min(min(__float_as_uint(e0) - 1u, __float_as_uint(e1) - 1u),
+                               min(__float_as_uint(e2) - 1u, __float_as_uint(e3) - 1u));
+        tiny |= b < lim;
       }
     }
   }
-  sum = rsum(sum);
+  float sum = rsum(__fadd_rn(acc.x, acc.y));
   // exp of a key outside the processed chunks: 0, or 1 when the whole FILL row
   // is masked (then every one of them adds 1, as the dense sum would).
   float e_out = 0.0f;
@@ -185,38 +221,81 @@ __device__ __forceinline__ void softmax_row(const float4* __restrict__ src, floa
     sum = __fadd_rn(sum, __fmul_rn(float(4 * (kv - nch)), e_out));
   }
   const float r = __frcp_rn(sum);
-  const bool fast = sum < 0x1p24f;
+  // Quotients e * (1/sum) + one FMA correction: correctly rounded when the
+  // result is normal (sum < 2^24, e == 0 or e >= 2^-100); otherwise every
+  // element of the row takes the IEEE division.
+  const bool slow = rany(tiny || !(sum < 0x1p24f));
+  const float2 r2 = make_float2(r, r), ns2 = make_float2(-sum, -sum);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
     if (j * STRIDE < nch) {
       const uint32_t idx = j * STRIDE + tid;
-      if (idx < nch)
-        dst[c0 + idx] = make_float4(quotient(v[j][0], sum, r, fast), quotient(v[j][1], sum, r, fast),
-                                    quotient(v[j][2], sum, r, fast), quotient(v[j][3], sum, r, fast));
+      if (idx < nch) {
+        float4 o;
+        if (!slow) {
+          const float2 a = make_float2(v[j][0], v[j][1]), b = make_float2(v[j][2], v[j][3]);
+          float2 qa = __fmul2_rn(a, r2), qb = __fmul2_rn(b, r2);
+          qa = __ffma2_rn(__ffma2_rn(qa, ns2, a), r2, qa);
+          qb = __ffma2_rn(__ffma2_rn(qb, ns2, b), r2, qb);
+          o = make_float4(qa.x, qa.y, qb.x, qb.y);
+        } else {
+          o = make_float4(__fdiv_rn(v[j][0], sum), __fdiv_rn(v[j][1], sum),
+                          __fdiv_rn(v[j][2], sum), __fdiv_rn(v[j][3], sum));
+        }
+        dst[c0 + idx] = o;
+      }
     }
   }
-  const float p_out = quotient(e_out, sum, r, fast);
-  const float4 fill = make_float4(p_out, p_out, p_out, p_out);
-  for (uint32_t q4 = tid; q4 < kv; q4 += STRIDE)
-    if (q4 - c0 >= nch) dst[q4] = fill;
+  if (nch < kv) {  // uniform over the row's threads
+    const float p_out = __fdiv_rn(e_out, sum);
+    const float4 fill = make_float4(p_out, p_out, p_out, p_out);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const uint32_t q4 = j * STRIDE + tid;
+      if (q4 < kv && q4 - c0 >= nch) dst[q4] = fill;
+    }
+  }
 }
 
-// ---- warp per row (k_len <= 1024) -------------------------------------------------
+// ---- LANES (8, 16 or 32) threads per row (k_len <= 1024) ---------------------------
+//
+// Short rows are shared by fewer threads so that each thread holds up to 32
+// keys: the per-row work (index decomposition, interval, reductions, the
+// reciprocal) is then spread over more keys. 256 / LANES rows per CTA; the
+// shuffles of a row stay inside its aligned group of LANES lanes.
 
-template <int NV, int SEM, bool TENSORS>
-__global__ void __launch_bounds__(256) softmax_warp_kernel(const float* __restrict__ s,
-                                                           float* __restrict__ p, uint64_t rows,
-                                                           MaskArgs m) {
+template <int LANES>
+__device__ __forceinline__ float group_max(float v, unsigned mask) {
+#pragma unroll
+  for (int d = LANES / 2; d >= 1; d >>= 1) v = fmaxf(v, __shfl_xor_sync(mask, v, d));
+  return v;
+}
+template <int LANES>
+__device__ __forceinline__ float group_sum(float v, unsigned mask) {
+#pragma unroll
+  for (int d = LANES / 2; d >= 1; d >>= 1) v = __fadd_rn(v, __shfl_xor_sync(mask, v, d));
+  return v;
+}
+
+template <int NV, int LANES, int SEM, bool TENSORS>
+__global__ void __launch_bounds__(256) softmax_lanes_kernel(const float* __restrict__ s,
+                                                            float* __restrict__ p, uint64_t rows,
+                                                            MaskArgs m) {
+  static_assert(LANES == 8 || LANES == 16 || LANES == 32, "LANES");
   pdl_enter();
-  const int lane = threadIdx.x & 31;
-  const uint64_t row = uint64_t(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (row >= rows) return;  // the whole warp leaves together
+  const uint32_t lane = threadIdx.x & (LANES - 1);
+  const uint64_t row = uint64_t(blockIdx.x) * (256 / LANES) + threadIdx.x / LANES;
+  if (row >= rows) return;  // the row's whole group leaves together
+  const unsigned mask =
+      LANES == 32 ? 0xffffffffu : ((1u << LANES) - 1u) << (threadIdx.x & 31 & ~(LANES - 1));
   const RowCtx c = row_ctx(m, row);
   const uint32_t kv = uint32_t(m.k_len / 4);
-  softmax_row<NV, 32, SEM, TENSORS>(
+  softmax_row<NV, LANES, SEM, TENSORS>(
       reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
       reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, lane,
-      [](float x) { return warp_max(x); }, [](float x) { return warp_sum(x); });
+      [mask](float x) { return group_max<LANES>(x, mask); },
+      [mask](float x) { return group_sum<LANES>(x, mask); },
+      [mask](bool b) { return __any_sync(mask, b) != 0; });
 }
 
 // ---- CTA (256 threads) per row (k_len <= 8192) -------------------------------------
@@ -233,7 +312,8 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
       reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
       reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, threadIdx.x,
       [&](float x) { return block_reduce(x, red, true); },
-      [&](float x) { return block_reduce(x, red, false); });
+      [&](float x) { return block_reduce(x, red, false); },
+      [](bool b) { return __syncthreads_or(b) != 0; });
 }
 
 // ---- any length / alignment: CTA per row, three passes (row re-read from L2) ----
@@ -272,20 +352,25 @@ int launch_softmax(const char* op, const float* scores, float* probs, int64_t ro
   const bool vec = kl % 4 == 0 && aligned(scores, 16) && aligned(probs, 16);
   const int64_t kv = kl / 4;
   if (vec && kv <= 32 * 8) {
-    TFX_REQUIRE(rows / 8 < (int64_t(1) << 31), op, "shape", "too many rows for one call");
-    const unsigned grid = unsigned((rows + 7) / 8);
-#define TFX_SM_WARP(NV)                                                                    \
-  if (kv <= 32 * NV) {                                                                     \
-    return launch_kernel(op, softmax_warp_kernel<NV, SEM, TENSORS>, dim3(grid), dim3(256), 0, \
-                         stream, 1, scores, probs, uint64_t(rows), m);                          \
+    // Up to 32 keys per thread: 8 lanes per row up to 256 keys, 16 up to
+    // 512, a warp up to 1024.
+#define TFX_SM_LANES(NV, LANES)                                                           \
+  if (kv <= LANES * NV) {                                                                 \
+    const int64_t per = 256 / LANES;                                                      \
+    TFX_REQUIRE(rows / per < (int64_t(1) << 31), op, "shape", "too many rows for one call"); \
+    return launch_kernel(op, softmax_lanes_kernel<NV, LANES, SEM, TENSORS>,                 \
+                         dim3(unsigned((rows + per - 1) / per)), dim3(256), 0, stream, 1,   \
+                         scores, probs, uint64_t(rows), m);                                 \
   }
-    TFX_SM_WARP(1)
-    TFX_SM_WARP(2)
-    TFX_SM_WARP(3)
-    TFX_SM_WARP(4)
-    TFX_SM_WARP(6)
-    TFX_SM_WARP(8)
-#undef TFX_SM_WARP
+    TFX_SM_LANES(1, 8)
+    TFX_SM_LANES(2, 8)
+    TFX_SM_LANES(4, 8)
+    TFX_SM_LANES(8, 8)
+    TFX_SM_LANES(6, 16)
+    TFX_SM_LANES(8, 16)
+    TFX_SM_LANES(6, 32)
+    TFX_SM_LANES(8, 32)
+#undef TFX_SM_LANES
   }
   TFX_REQUIRE(rows < (int64_t(1) << 31), op, "shape", "too many rows for one call");
   const unsigned grid = unsigned(rows);

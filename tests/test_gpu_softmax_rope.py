@@ -11,7 +11,7 @@ import torch
 
 from gpu_util import P, S, call, dev, empty, host
 from helpers import (golden_case, golden_tensor, assert_bitwise, assert_close, decode_value,
-                     splitmix_normal, F32_RTOL, F32_ATOL_REL)
+                     splitmix_normal, ulp_distance_f32, F32_RTOL, F32_ATOL_REL)
 import tfx
 from tfx import _lib
 import ctypes
@@ -134,7 +134,8 @@ def test_softmax_empty_rows_and_masked_nonfinite(orc):
 
 
 @pytest.mark.parametrize("Lk,offset,semantics", [
-    (1, 0, 0), (3, 0, 0), (65, 0, 1), (128, 1, 0), (512, 0, 1), (1000, 0, 0), (1024, 0, 0),
+    (1, 0, 0), (3, 0, 0), (20, 0, 0), (32, 0, 1), (65, 0, 1), (128, 1, 0), (320, 0, 0),
+    (512, 0, 1), (640, 0, 1), (768, 0, 0), (1000, 0, 0), (1024, 0, 0),
     (2049, 0, 0), (4096, 0, 1), (8192, 0, 0), (9000, 0, 0), (9000, 0, 1)])
 def test_softmax_row_lengths(orc, Lk, offset, semantics):
     B, H, Lq = 1, 2, 5
@@ -143,6 +144,32 @@ def test_softmax_row_lengths(orc, Lk, offset, semantics):
     got = gpu_softmax(s, B, H, Lq, Lk, offset=offset, **kw)
     want = orc.masked_softmax_f32(s, B, H, Lq, Lk, **kw)
     assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"softmax Lk={Lk}")
+
+
+@pytest.mark.parametrize("Lk", [16, 64, 256, 384, 512, 704, 1024])
+@pytest.mark.parametrize("semantics", [0, 1])
+def test_softmax_row_lengths_valid_len(orc, Lk, semantics):
+    """Every lane-group width of the short-row kernel, rows not a multiple of
+    the rows per CTA, a padded key tail (valid_len) instead of causality."""
+    B, H, Lq = 3, 1, 7
+    s = splitmix_normal(B * H * Lq * Lk, 0x7E4F0680 + Lk, std=3.0)
+    kw = dict(valid_len=Lk - 3, semantics=semantics, scale=0.5)
+    got = gpu_softmax(s, B, H, Lq, Lk, **kw)
+    want = orc.masked_softmax_f32(s, B, H, Lq, Lk, **kw)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"softmax Lk={Lk}")
+
+
+@pytest.mark.parametrize("semantics", [0, 1])
+def test_softmax_wide_dynamic_range(orc, semantics):
+    """Scores ~ N(0, 20): probabilities down to ~1e-40 (subnormal quotients,
+    the row-wide IEEE division fallback) against glibc expf in the oracle."""
+    B, H, L = 2, 4, 512
+    s = splitmix_normal(B * H * L * L, 0x7E4F0670 + semantics, std=20.0)
+    got = gpu_softmax(s, B, H, L, L, semantics=semantics, causal=1)
+    want = orc.masked_softmax_f32(s, B, H, L, L, semantics=semantics, causal=1)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, "softmax wide range")
+    big = want > 1e-30
+    assert int(ulp_distance_f32(got[big], want[big]).max()) <= 64
 
 
 def test_softmax_in_place_and_scale(orc):
