@@ -101,36 +101,98 @@ def measured_hbm():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled while the GPUs work."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, read (never
+    set) through NVML every 10 ms by a background thread. `mark()` brackets the
+    timed region: the summary's median SM clock and reasons come from the
+    samples taken inside it, so a short timed region still has samples. Falls
+    back to `nvidia-smi -lms 100` when NVML cannot be loaded."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40),
+               ("sw_thermal_slowdown", 0x20), ("sw_power_cap", 0x4),
+               ("hw_power_brake_slowdown", 0x80))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    def __init__(self, torch, device):
+        self.samples = []  # (host time, sm MHz, max sm MHz, power W, reason bits)
+        self.window = [None, None]
+        self.stop_flag = False
+        self.thread = None
+        self.nvml = None
+        self.handle = None
+        self.smi = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            props = torch.cuda.get_device_properties(device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            try:
+                self.handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(device.index or 0)
+            self.nvml = pynvml
+            self.reason_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.max_sm = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+            self.index = device.index or 0
+
+    def _run(self):
+        nv, h = self.nvml, self.handle
+        while not self.stop_flag:
+            try:
+                self.samples.append((time.perf_counter(),
+                                     nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                     self.max_sm, nv.nvmlDeviceGetPowerUsage(h) / 1000.0,
+                                     int(self.reason_fn(h))))
+            except Exception:
+                pass
+            time.sleep(0.01)
 
     def start(self):
+        if self.nvml is not None:
+            import threading
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+            return
+        fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         fd, self.path = tempfile.mkstemp(prefix="tfx_clocks_", suffix=".csv")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+            self.smi = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={fields}",
                  "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
-            self.proc = None
+            self.smi = None
+
+    def mark(self, which: int):
+        self.window[which] = time.perf_counter()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
+        if self.thread is not None:
+            self.stop_flag = True
+            self.thread.join(timeout=5)
+            lo, hi = self.window
+            inside = [x for x in self.samples
+                      if lo is not None and hi is not None and lo <= x[0] <= hi] or self.samples
+            if not inside:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_sm, "reasons": [], "samples": 0,
+                        "source": "nvml"}
+            reasons = sorted({n for x in inside for n, bit in self.REASONS if x[4] & bit})
+            return {"sm_mhz": statistics.median(x[1] for x in inside),
+                    "sm_min_mhz": min(x[1] for x in inside), "sm_max_mhz": self.max_sm,
+                    "reasons": reasons, "samples": len(inside),
+                    "power_w_max": max(x[3] for x in inside),
+                    "source": "nvml, 10 ms, timed region only"}
+        if self.smi is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+        self.smi.terminate()
         try:
-            self.proc.wait(timeout=5)
+            self.smi.wait(timeout=5)
         except Exception:
-            self.proc.kill()
+            self.smi.kill()
         rows = []
         with open(self.path) as fh:
             for line in fh:
@@ -141,9 +203,9 @@ class ClockSampler:
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
 
-        def num(s):
+        def num(v):
             try:
-                return float(s)
+                return float(v)
             except ValueError:
                 return None
 
@@ -152,10 +214,11 @@ class ClockSampler:
         power = [num(r[3]) for r in rows if num(r[3]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        load = [s for s, p in zip(sm, power) if p is not None and p > 200] or sm
+        load = [v for v, pw in zip(sm, power) if pw is not None and pw > 200] or sm
         return {"sm_mhz": statistics.median(load) if load else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(power) if power else None}
+                "samples": len(rows), "power_w_max": max(power) if power else None,
+                "source": "nvidia-smi, 100 ms"}
 
 
 # ---------------------------------------------------------------------------------
@@ -326,6 +389,15 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     measure("masked_softmax_global", lambda: (normal(ns, 2.0), torch.empty(ns, device=device)),
             lambda b: ops.masked_softmax(b[0], B, H, L, L, window=-1, valid_len=L - 37, out=b[1]),
             2 * ns * 4, ns, touched=softmax_touched_bytes(B, H, L, -1, L - 37))
+    # the chain's RoPE on q and k of a feature-first qkv (3h, L, B), full chain shape
+    c = CHAIN
+    h, hd, Lc, Bc = c["hidden"], c["head_dim"], c["seq"], c["batch"]
+    cos_t, sin_t = ops.rope_tables(c["theta_local"], Lc, hd, device=device)
+    nq = 3 * h * Lc * Bc
+    measure("rope_qk", lambda: (normal(nq), torch.empty(nq, device=device)),
+            lambda b: ops.rope_pairhalf(b[0], cos_t, sin_t, 2 * c["heads"], Lc, Bc, hd, hd,
+                                        (hd, 3 * h, 3 * h * Lc, 1), out=b[1]),
+            2 * (2 * h * Lc * Bc * 4), 2 * h * Lc * Bc)
     F, T = 768, 8192
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
@@ -412,9 +484,8 @@ def run_ours(args):
         chain.step(i)
     torch.cuda.synchronize()
 
-    clocks = ClockSampler(local)
+    clocks = ClockSampler(torch, device)
     clocks.start()
-    time.sleep(0.3)
     sm_pairs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
@@ -422,10 +493,12 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     t0.record()
+    clocks.mark(0)
     for i in range(args.steps):
         chain.step(i, sm_pairs[i])
     t1.record()
     torch.cuda.synchronize()
+    clocks.mark(1)
     barrier()
     ms_local = t0.elapsed_time(t1)
     clock_info = clocks.stop()
@@ -636,7 +709,7 @@ def main():
     ap.add_argument("--only-op", default=None,
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
-                         "masked_softmax_global, bias_add) and "
+                         "masked_softmax_global, rope_qk, bias_add) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
     args = ap.parse_args()
