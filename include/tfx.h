@@ -54,6 +54,13 @@ typedef struct CUstream_st* tfx_stream_t;
 TFX_API const char* tfx_last_error_string(void);
 /* ABI version: major * 10000 + minor * 100 + patch. */
 TFX_API int tfx_version(void);
+/* Diagnostic, no counterpart in the reference: the number of bounded waits
+ * inside libtfx kernels on the current device that gave up since the library
+ * was loaded (a kernel that gives up leaves its output incomplete). Every wait
+ * of a kernel on an asynchronous copy is bounded (about one second), so a lost
+ * copy ends the kernel instead of hanging the GPU. Synchronous (reads device
+ * memory). */
+TFX_API int tfx_wait_timeouts(uint32_t* count);
 
 /* ---- erf / exact GELU ------------------------------------------------------
  * Replaces ErfOp (crates/tenferro-ext/src/lib.rs:95-170) and

@@ -30,6 +30,7 @@ struct DeviceInfo {
   int sms = 0;
   int max_threads_per_sm = 0;
   int l2_bytes = 0;
+  int smem_optin = 0;  // largest dynamic shared memory one CTA may opt in to
   int cc_major = 0, cc_minor = 0;
 };
 // The current device's attributes, read once per device.

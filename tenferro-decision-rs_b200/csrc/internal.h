@@ -14,4 +14,9 @@ int validate_softmax(const float* scores, const float* probs, const tfx_softmax_
 int masked_softmax_rows(const float* scores, float* probs, const tfx_softmax_desc* d,
                         int64_t row_begin, int64_t row_count, cudaStream_t stream);
 
+// rms_stream.cu: the TMA-pipelined feature-last RMSNorm; 1 when the shape or
+// alignment is not covered (nothing launched), else a status.
+int rms_stream(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+               uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
+
 }  // namespace tfx

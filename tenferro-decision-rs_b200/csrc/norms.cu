@@ -27,6 +27,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "internal.h"
 
 namespace cg = cooperative_groups;
 
@@ -752,14 +753,19 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const float* x,
 }
 
 // Kernel choice for the f32 feature-last RMSNorm: 0 = automatic, 1 = cluster,
-// 2 = tile, 3 = split, 4 = 16-CTA cluster; TFX_RMS_KERNEL overrides it for
-// tuning runs.
+// 2 = tile, 3 = split, 4 = 16-CTA cluster, 5 = TMA-pipelined stream;
+// TFX_RMS_KERNEL overrides it for tuning runs.
 int rms_kernel_choice() {
   static const int choice = [] {
     const char* e = getenv("TFX_RMS_KERNEL");
     if (!e) return 0;
     const std::string s(e);
-    return s == "cluster" ? 1 : s == "tile" ? 2 : s == "split" ? 3 : s == "cluster16" ? 4 : 0;
+    return s == "cluster" ? 1
+           : s == "tile"    ? 2
+           : s == "split"   ? 3
+           : s == "cluster16" ? 4
+           : s == "stream"  ? 5
+                            : 0;
   }();
   return choice;
 }
@@ -861,6 +867,13 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
       return launch_kernel(op, rms_tile_kernel<8>, dim3(unsigned((rows + 31) / 32)), dim3(256), 0,
                            stream, 1, x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width,
                            centered);
+    }
+    // The streaming kernel reads x once with its loads always in flight; it
+    // covers aligned shapes with rows % 4 == 0 and width up to ~1700.
+    if (small && (choice == 0 || choice == 5)) {
+      const int rc = rms_stream(op, x, w, y, uint32_t(rows), uint32_t(width), centered, eps,
+                                inv_width, stream);
+      if (rc != 1) return rc;
     }
     // The split variant re-reads x once; it wins when x stays in L2 between
     // its two passes.

@@ -51,6 +51,8 @@ const DeviceInfo& device_info(int* status) {
         cudaDeviceGetAttribute(&d.max_threads_per_sm, cudaDevAttrMaxThreadsPerMultiProcessor,
                                dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&d.l2_bytes, cudaDevAttrL2CacheSize, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+            cudaSuccess ||
         cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) !=
             cudaSuccess ||
         cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) !=

@@ -65,6 +65,7 @@ _int = ctypes.c_int
 SIGNATURES = {
     "tfx_last_error_string": (ctypes.c_char_p, []),
     "tfx_version": (_int, []),
+    "tfx_wait_timeouts": (_int, [_p]),
     "tfx_erf_f32": (_int, [_p, _p, _i64, _p]),
     "tfx_gelu_erf_f32": (_int, [_p, _p, _i64, _p]),
     "tfx_erf_f64": (_int, [_p, _p, _i64, _p]),

@@ -138,7 +138,9 @@ def test_rmsnorm_config3_full_size(orc, centered):
 
 @pytest.mark.parametrize("rows,width,offset", [
     (1, 1, 0), (3, 4, 0), (63, 31, 0), (64, 1024, 1), (257, 100, 0), (130, 1025, 0),
-    (128, 2048, 0), (100, 4096, 0), (96, 4100, 0), (64, 8192, 0), (10, 9000, 0), (4, 3, 1)])
+    (128, 2048, 0), (100, 4096, 0), (96, 4100, 0), (64, 8192, 0), (10, 9000, 0), (4, 3, 1),
+    (4, 3, 0), (100, 200, 0), (1000, 1000, 0), (1600, 1400, 0), (20000, 64, 0), (16, 768, 0),
+    (300, 3000, 0), (64, 2500, 0), (3000, 520, 0)])
 def test_rmsnorm_shapes(orc, rows, width, offset):
     x = splitmix_normal(rows * width, 0x7E4F0500 + rows + width)
     w = splitmix_normal(width, 0x7E4F0501 + width, mean=1.0, std=0.1)
@@ -159,6 +161,15 @@ def test_rmsnorm_in_place(orc):
     got = gpu_rms(x, w, rows, width, True, 1e-6, in_place=True)
     assert_close(got, orc.rms_norm_last_f32(x, rows, width, w, True, 1e-6), F32_RTOL,
                  F32_ATOL_REL, "rmsnorm in place")
+
+
+def test_no_wait_gave_up():
+    """Every bounded wait of the TMA-pipelined kernels completed in the runs above."""
+    import ctypes
+    from tfx import _lib
+    n = ctypes.c_uint32(99)
+    call("tfx_wait_timeouts", ctypes.byref(n))
+    assert n.value == 0
 
 
 def test_rmsnorm_f64_primitives(orc):
