@@ -294,7 +294,7 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     def normal(n, std=1.0, dtype=torch.float32):
         return (torch.randn(n, generator=gen, device=device, dtype=dtype) * std)
 
-    def measure(name, make, launch, nbytes, elems, touched=None):
+    def measure(name, make, launch, nbytes, elems, touched=None, flops=None):
         if only is not None and name != only:
             return
         per_set = nbytes
@@ -355,6 +355,9 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
             g = touched / (ms * 1e-3) / 1e9
             results[name].update({"touched_bytes": touched, "gbs_touched": round(g, 1),
                                   "frac_touched_of_hbm": round(g / hbm_peak, 3)})
+        if flops is not None:
+            results[name].update({"flops": flops,
+                                  "tflops_graph": round(flops / (ms_g * 1e-3) / 1e12, 2)})
         del bufs
 
     # LayerNorm 768 x 8192 (f32 and the f64 copy)
@@ -398,6 +401,24 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
             lambda b: ops.rope_pairhalf(b[0], cos_t, sin_t, 2 * c["heads"], Lc, Bc, hd, hd,
                                         (hd, 3 * h, 3 * h * Lc, 1), out=b[1]),
             2 * (2 * h * Lc * Bc * 4), 2 * h * Lc * Bc)
+    # the Laya attention block (split + RoPE + masked attention) on configs[3]'s
+    # attention shape: batch 8, 12 heads, 512 tokens, head_dim 64; keep mask of
+    # the sliding-window (128) layers and of the global layers, 37 padded keys
+    Ba, Ha, La, hda = 8, 12, 512, 64
+    da = Ha * hda
+    cos_a, sin_a = ops.rope_tables_powf(CHAIN["theta_local"], La, hda, device=device)
+    qa = torch.arange(La, device=device)
+    for tag, win in (("laya_attention_window", 64), ("laya_attention_global", La)):
+        kk = qa[:, None]
+        qq = qa[None, :]
+        m2 = ((kk - qq).abs() <= win) & (kk < La - 37)  # [k][q]
+        keep_a = m2.to(torch.uint8).unsqueeze(0).expand(Ba, La, La).contiguous().reshape(-1)
+        kept = int(m2.sum().item())
+        nbytes_a = 3 * da * La * Ba * 4 + La * La * Ba + da * La * Ba * 4
+        measure(tag, lambda: (normal(3 * da * La * Ba), torch.empty(da * La * Ba, device=device)),
+                lambda b, keep_a=keep_a: ops.laya_attention_block(b[0], keep_a, da, Ha, La, Ba,
+                                                                  cos_a, sin_a, out=b[1]),
+                nbytes_a, da * La * Ba, flops=4 * Ba * Ha * kept * hda)
     F, T = 768, 8192
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
@@ -709,7 +730,8 @@ def main():
     ap.add_argument("--only-op", default=None,
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
-                         "masked_softmax_global, rope_qk, bias_add) and "
+                         "masked_softmax_global, rope_qk, laya_attention_window, "
+                         "laya_attention_global, bias_add) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
     args = ap.parse_args()

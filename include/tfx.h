@@ -223,6 +223,99 @@ TFX_API int tfx_rope_pairhalf_f32(const float* x, float* y, const float* cos_tab
 TFX_API int tfx_rope_tables_f32(double base, int64_t seq, int64_t rotary_dim, float* cos_host,
                         float* sin_host);
 
+/* ---- attention blocks -------------------------------------------------------
+ * The attention cores of the two forwards, mirroring the reference's CUDA
+ * path (FusedScope::laya_attention / jeff_attention, crates/tenferro-ext/src/
+ * cuda_fused.rs:911-993, 1029-1103: a prep kernel writes head-major q, k, v,
+ * then one attention kernel, fused.cu:157-306) with the arithmetic of its CPU
+ * ops (crates/cpu-kernels/src/lib.rs:618-760 jeff_full_attention_into,
+ * :819-1150 laya_attention_block_into, behind LayaAttentionBlockOp,
+ * crates/tenferro-ext/src/laya_attention.rs:27-176). Head-major tensors are
+ * (batch, heads, length, head_dim) with head_dim contiguous. */
+
+/* Host helper (no GPU): RoPE tables as cpu-kernels builds them, in f32:
+ * angle = (p as f32) * base.powf(-2 i / rotary_dim) with the C library's
+ * powf, cos/sin by cosf/sinf (lib.rs:938-946, :696-699). Row-major
+ * (seq, rotary_dim/2). */
+TFX_API int tfx_rope_tables_powf_f32(float base, int64_t seq, int64_t rotary_dim, float* cos_host,
+                                     float* sin_host);
+
+/* Laya split + RoPE (lib.rs:972-1009; CUDA twin fused_laya_qkv_prep,
+ * fused.cu:199-229): qkv feature-first (3*hidden, length, batch) -> head-major
+ * qh, kh, vh; q and k rotated over the full head (pairs i, i + head_dim/2)
+ * with device tables (length, head_dim/2), or copied when cos_table is NULL.
+ * Results are bit-identical to the reference arithmetic. */
+TFX_API int tfx_laya_qkv_prep_f32(const float* qkv, const float* cos_table,
+                                  const float* sin_table, float* qh, float* kh, float* vh,
+                                  int64_t hidden, int64_t heads, int64_t length, int64_t batch,
+                                  tfx_stream_t stream);
+
+/* Jeff prep (lib.rs:660-709; CUDA twin fused_jeff_qkv_prep, fused.cu:150-197):
+ * q, k, v (length, heads*head_dim) column-major (time-first) -> head-major
+ * (1, heads, length, head_dim). q and k: centred RMSNorm per head over
+ * head_dim (mean of squares / head_dim, x * (1/sqrt(m + eps) * (1 + norm))),
+ * then RoPE on the first rotary_dim channels (pairs i, i + rotary_dim/2;
+ * tables (length, rotary_dim/2), may be NULL when rotary_dim == 0). v copied.
+ * Bit-identical to the reference arithmetic (sequential sums per token). */
+TFX_API int tfx_jeff_qkv_prep_f32(const float* q, const float* k, const float* v,
+                                  const float* q_norm, const float* k_norm,
+                                  const float* cos_table, const float* sin_table, float* qh,
+                                  float* kh, float* vh, int64_t length, int64_t heads,
+                                  int64_t head_dim, int64_t rotary_dim, float eps,
+                                  tfx_stream_t stream);
+
+#define TFX_ATTN_EMPTY_NAN 0  /* a row without kept keys is NaN (cpu-kernels Laya) */
+#define TFX_ATTN_EMPTY_ZERO 1 /* ... is 0 (fused_attention, cpu-kernels Jeff) */
+
+/* Masked scaled dot-product attention over head-major q, k, v (fused.cu:
+ * 231-306 / lib.rs:711-752, 1106-1147). score = (q . k) * scale (+ bias);
+ * a key is dropped when causal and key > query, when |query - key| > window
+ * (window >= 0), when key >= valid_len (valid_len >= 0), when keep is given
+ * and keep[q + L*(k + L*b)] == 0, or when active is given and
+ * active[b*L + k] == 0. Scores that are not finite contribute nothing (as
+ * the reference's isfinite test); a row without a kept key, or with a +inf
+ * score, is NaN or 0 per empty_rows. Output element (token t, feature
+ * f = head*head_dim + d, batch b) at t*out_tok + f*out_feat + b*out_batch; with
+ * gate it is multiplied by 1/(1 + exp(-gate[gate_offset + that index])). */
+typedef struct tfx_attention_desc {
+  int64_t batch, heads, length, head_dim;
+  float scale;         /* default 1/sqrt(head_dim) */
+  int32_t empty_rows;  /* TFX_ATTN_EMPTY_NAN (default) or TFX_ATTN_EMPTY_ZERO */
+  int32_t causal;      /* default 0 */
+  int64_t window;      /* default -1 (none) */
+  int64_t valid_len;   /* default -1 (none) */
+  const uint8_t* keep; /* nullable, (length, length, batch), query fastest */
+  const float* bias;   /* nullable, same layout, added to the scaled score */
+  const float* active; /* nullable, (batch, length) key mask */
+  const float* gate;   /* nullable */
+  int64_t gate_offset;
+  int64_t out_tok, out_feat, out_batch; /* default (heads*head_dim, 1, heads*head_dim*length) */
+} tfx_attention_desc;
+TFX_API int tfx_attention_desc_init(tfx_attention_desc* desc, int64_t batch, int64_t heads,
+                                    int64_t length, int64_t head_dim);
+TFX_API int tfx_attention_f32(const float* qh, const float* kh, const float* vh, float* out,
+                              const tfx_attention_desc* desc, tfx_stream_t stream);
+
+/* The fused Laya attention block (LayaAttentionBlockOp): prep + attention with
+ * cpu-kernels semantics (keep mask, all-masked rows NaN), out (hidden, length,
+ * batch). Head-major q, k, v live in a stream-ordered scratch allocation
+ * (3 * hidden * length * batch floats) released on the stream. */
+TFX_API int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep,
+                                         const float* cos_table, const float* sin_table,
+                                         float* out, int64_t hidden, int64_t heads,
+                                         int64_t length, int64_t batch, tfx_stream_t stream);
+
+/* Jeff full attention (jeff_full_attention_into / FusedScope::jeff_attention):
+ * prep, causal attention over keys with mask[key] != 0, sigmoid gate (gate
+ * (length, width) like q); all-masked rows are 0. out (length, heads*head_dim)
+ * column-major. Scratch as above (3 * length * heads * head_dim floats). */
+TFX_API int tfx_jeff_attention_f32(const float* q, const float* k, const float* v,
+                                   const float* gate, const float* q_norm, const float* k_norm,
+                                   const float* mask, const float* cos_table,
+                                   const float* sin_table, float* out, int64_t length,
+                                   int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                                   float eps, tfx_stream_t stream);
+
 /* ---- host-buffer sessions ---------------------------------------------------
  * The reference executes these ext ops on host tensors of a CPU session
  * (execute_*_in_session over TensorRead slices, e.g.

@@ -543,6 +543,197 @@ void orc_rope_pairhalf_f64(const double* x, double* y, const double* cos_t,
 }
 
 // ---------------------------------------------------------------------------
+// Attention blocks, crates/cpu-kernels/src/lib.rs:618-760 (Jeff) and :819-1150
+// (Laya). Products and sums are rounded one by one (no contraction), sums run
+// in key / channel order, exp is glibc expf, as the Rust code compiles.
+// ---------------------------------------------------------------------------
+void orc_rope_tables_powf_f32(float base, int64_t seq, int64_t rotary_dim, float* cos_t,
+                              float* sin_t) {
+  const int64_t half = rotary_dim / 2;
+  for (int64_t p = 0; p < seq; ++p)
+    for (int64_t i = 0; i < half; ++i) {
+      const float e = (-2.0f * float(i)) / float(rotary_dim);
+      const float theta = float(p) * powf(base, e);
+      cos_t[p * half + i] = cosf(theta);
+      sin_t[p * half + i] = sinf(theta);
+    }
+}
+
+}  // extern "C"
+
+namespace {
+// a*c - b*s and a*s + b*c for the pair (x[i], x[i + half]) of one row.
+void rotate_row(float* x, const float* c, const float* s, int64_t half) {
+  for (int64_t i = 0; i < half; ++i) {
+    const float a = x[i], b = x[i + half];
+    x[i] = a * c[i] - b * s[i];
+    x[i + half] = a * s[i] + b * c[i];
+  }
+}
+
+// Masked scaled dot-product attention of one head, scalar path of
+// lib.rs:1106-1147 / :711-752. q, k, v (L, hd) row-major; keep(query, key);
+// out_row(query) receives hd values (accumulated from 0, keys with p == 0
+// skipped). divide: p = e / sum per key (Laya); else p computed the same way
+// but an empty row leaves zeros (Jeff checks sum > 0 first).
+template <class Keep, class OutRow>
+void head_attention(const float* q, const float* k, const float* v, int64_t L, int64_t hd,
+                    float scale, bool jeff, Keep keep, OutRow out_row) {
+  std::vector<float> probs(static_cast<size_t>(L)), acc(static_cast<size_t>(hd));
+  for (int64_t query = 0; query < L; ++query) {
+    const float* qo = q + query * hd;
+    float mx = -INFINITY;
+    for (int64_t key = 0; key < L; ++key) {
+      if (!keep(query, key)) {
+        probs[size_t(key)] = -INFINITY;
+        continue;
+      }
+      const float* ko = k + key * hd;
+      float a = 0.0f;
+      for (int64_t i = 0; i < hd; ++i) a += qo[i] * ko[i];
+      const float score = a * scale;
+      probs[size_t(key)] = score;
+      if (score > mx) mx = score;
+    }
+    float sum = 0.0f;
+    for (int64_t key = 0; key < L; ++key) {
+      const float val = probs[size_t(key)];
+      probs[size_t(key)] = std::isfinite(val) ? expf(val - mx) : 0.0f;
+      sum += probs[size_t(key)];
+    }
+    for (int64_t i = 0; i < hd; ++i) acc[size_t(i)] = 0.0f;
+    if (!jeff || sum > 0.0f) {
+      for (int64_t key = 0; key < L; ++key) {
+        const float p = probs[size_t(key)] / sum;
+        if (p == 0.0f) continue;
+        const float* vo = v + key * hd;
+        for (int64_t i = 0; i < hd; ++i) acc[size_t(i)] += vo[i] * p;
+      }
+    }
+    out_row(query, acc.data());
+  }
+}
+}  // namespace
+
+extern "C" {
+
+void orc_laya_qkv_prep_f32(const float* qkv, const float* cos_t, const float* sin_t,
+                           int64_t hidden, int64_t heads, int64_t length, int64_t batch,
+                           float* qh, float* kh, float* vh) {
+  const int64_t hd = hidden / heads, half = hd / 2;
+  parallel_for(batch * heads, [&](int64_t h0, int64_t h1) {
+    for (int64_t bh = h0; bh < h1; ++bh) {
+      const int64_t b = bh / heads, head = bh % heads, feat = head * hd;
+      for (int64_t l = 0; l < length; ++l) {
+        const float* src = qkv + 3 * hidden * (l + length * b) + feat;
+        const int64_t dst = (bh * length + l) * hd;
+        for (int64_t i = 0; i < hd; ++i) {
+          qh[dst + i] = src[i];
+          kh[dst + i] = src[hidden + i];
+          vh[dst + i] = src[2 * hidden + i];
+        }
+        if (cos_t) {
+          rotate_row(qh + dst, cos_t + l * half, sin_t + l * half, half);
+          rotate_row(kh + dst, cos_t + l * half, sin_t + l * half, half);
+        }
+      }
+    }
+  });
+}
+
+void orc_laya_attention_block_f32(const float* qkv, const uint8_t* keep, int64_t hidden,
+                                  int64_t heads, int64_t length, int64_t batch,
+                                  const float* cos_t, const float* sin_t, float* out) {
+  const int64_t hd = hidden / heads, L = length;
+  const float scale = 1.0f / sqrtf(float(hd));
+  parallel_for(batch * heads, [&](int64_t h0, int64_t h1) {
+    const size_t n = static_cast<size_t>(L * hd);
+    std::vector<float> q(n), k(n), v(n);
+    for (int64_t bh = h0; bh < h1; ++bh) {
+      const int64_t b = bh / heads, head = bh % heads, feat = head * hd;
+      for (int64_t l = 0; l < L; ++l) {
+        const float* src = qkv + 3 * hidden * (l + L * b) + feat;
+        for (int64_t i = 0; i < hd; ++i) {
+          q[size_t(l * hd + i)] = src[i];
+          k[size_t(l * hd + i)] = src[hidden + i];
+          v[size_t(l * hd + i)] = src[2 * hidden + i];
+        }
+        if (cos_t) {
+          rotate_row(q.data() + l * hd, cos_t + l * (hd / 2), sin_t + l * (hd / 2), hd / 2);
+          rotate_row(k.data() + l * hd, cos_t + l * (hd / 2), sin_t + l * (hd / 2), hd / 2);
+        }
+      }
+      head_attention(
+          q.data(), k.data(), v.data(), L, hd, scale, false,
+          [&](int64_t qi, int64_t ki) { return keep[qi + L * (ki + L * b)] != 0; },
+          [&](int64_t qi, const float* acc) {
+            float* o = out + feat + hidden * (qi + L * b);
+            for (int64_t i = 0; i < hd; ++i) o[i] = acc[i];
+          });
+    }
+  });
+}
+
+void orc_jeff_qkv_prep_f32(const float* q, const float* k, const float* v, const float* q_norm,
+                           const float* k_norm, const float* cos_t, const float* sin_t,
+                           int64_t length, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                           float eps, float* qh, float* kh, float* vh) {
+  const int64_t L = length, hd = head_dim, half = rotary_dim / 2;
+  parallel_for(heads, [&](int64_t h0, int64_t h1) {
+    for (int64_t head = h0; head < h1; ++head) {
+      const int64_t feat = head * hd;
+      for (int64_t t = 0; t < L; ++t) {
+        const int64_t dst = (head * L + t) * hd;
+        for (int64_t i = 0; i < hd; ++i) {
+          qh[dst + i] = q[t + L * (feat + i)];
+          kh[dst + i] = k[t + L * (feat + i)];
+          vh[dst + i] = v[t + L * (feat + i)];
+        }
+        for (int which = 0; which < 2; ++which) {
+          float* row = (which == 0 ? qh : kh) + dst;
+          const float* w = which == 0 ? q_norm : k_norm;
+          float mean_sq = 0.0f;
+          for (int64_t i = 0; i < hd; ++i) mean_sq += row[i] * row[i];
+          mean_sq /= float(hd);
+          const float scale = 1.0f / sqrtf(mean_sq + eps);
+          for (int64_t i = 0; i < hd; ++i) row[i] *= scale * (1.0f + w[i]);
+          if (half > 0) rotate_row(row, cos_t + t * half, sin_t + t * half, half);
+        }
+      }
+    }
+  });
+}
+
+void orc_jeff_full_attention_f32(const float* q, const float* k, const float* v,
+                                 const float* gate, const float* q_norm, const float* k_norm,
+                                 const float* mask, int64_t length, int64_t heads,
+                                 int64_t head_dim, int64_t rotary_dim, float theta, float eps,
+                                 float* out) {
+  const int64_t L = length, hd = head_dim, half = rotary_dim / 2;
+  std::vector<float> c(size_t(std::max<int64_t>(1, L * half))), s(c.size());
+  if (half > 0) orc_rope_tables_powf_f32(theta, L, rotary_dim, c.data(), s.data());
+  std::vector<float> qh(static_cast<size_t>(heads * L * hd)), kh(qh.size()), vh(qh.size());
+  orc_jeff_qkv_prep_f32(q, k, v, q_norm, k_norm, c.data(), s.data(), L, heads, hd, rotary_dim,
+                        eps, qh.data(), kh.data(), vh.data());
+  const float scale = 1.0f / sqrtf(float(hd));
+  parallel_for(heads, [&](int64_t h0, int64_t h1) {
+    for (int64_t head = h0; head < h1; ++head) {
+      const int64_t feat = head * hd, base = head * L * hd;
+      head_attention(
+          qh.data() + base, kh.data() + base, vh.data() + base, L, hd, scale, true,
+          [&](int64_t qi, int64_t ki) { return ki <= qi && mask[ki] != 0.0f; },
+          [&](int64_t qi, const float* acc) {
+            for (int64_t i = 0; i < hd; ++i) {
+              const float g = gate[qi + L * (feat + i)];
+              const float sig = 1.0f / (1.0f + expf(-g));
+              out[qi + L * (feat + i)] = acc[i] * sig;
+            }
+          });
+    }
+  });
+}
+
+// ---------------------------------------------------------------------------
 // crates/tenferro-ext/src/lib.rs:273-285 -- erf_f64, Abramowitz-Stegun 7.1.26.
 // ---------------------------------------------------------------------------
 double orc_erf_f64(double x) {

@@ -91,6 +91,40 @@ void orc_rope_pairhalf_f64(const double* x, double* y, const double* cos_t, cons
                            int64_t rotary_dim, int64_t s_vec, int64_t s_pos, int64_t s_batch,
                            int64_t s_feat);
 
+/* ---- attention blocks (crates/cpu-kernels/src/lib.rs) ------------------ */
+/* RoPE tables as cpu-kernels builds them, in f32: angle = (p as f32) *
+ * base.powf(-2 i / rotary_dim) with glibc powf, then cosf / sinf
+ * (lib.rs:938-946 Laya, :696-699 Jeff). Row-major (seq, rotary_dim/2). */
+void orc_rope_tables_powf_f32(float base, int64_t seq, int64_t rotary_dim, float* cos_t,
+                              float* sin_t);
+/* Laya split + RoPE (lib.rs:972-1009): qkv feature-first (3d, L, B) -> head-major
+ * (B, heads, L, hd) q/k/v; cos_t/sin_t (L, hd/2) or null for no RoPE. */
+void orc_laya_qkv_prep_f32(const float* qkv, const float* cos_t, const float* sin_t,
+                           int64_t hidden, int64_t heads, int64_t length, int64_t batch,
+                           float* qh, float* kh, float* vh);
+/* The fused Laya attention block (laya_attention_block_into, lib.rs:819-1150,
+ * scalar path): split, RoPE, masked scaled dot-product attention, out (d, L, B).
+ * keep (L, L, B) with element query + L*(key + L*b); an all-masked row is NaN. */
+void orc_laya_attention_block_f32(const float* qkv, const uint8_t* keep, int64_t hidden,
+                                  int64_t heads, int64_t length, int64_t batch,
+                                  const float* cos_t, const float* sin_t, float* out);
+/* Jeff prep (lib.rs:660-709): per head centred RMSNorm of q and k over head_dim
+ * (mean of squares divided by head_dim, x * (scale * (1 + w))), partial RoPE on
+ * the first rotary_dim channels; v copied. q, k, v (length, heads*head_dim)
+ * column-major; outputs head-major (heads, length, head_dim). */
+void orc_jeff_qkv_prep_f32(const float* q, const float* k, const float* v, const float* q_norm,
+                           const float* k_norm, const float* cos_t, const float* sin_t,
+                           int64_t length, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                           float eps, float* qh, float* kh, float* vh);
+/* jeff_full_attention_into (lib.rs:618-760): prep, causal attention over keys
+ * with mask[key] != 0, sigmoid gate; out (length, width); an all-masked row is 0.
+ * Tables are built inside with powf (theta, rotary_dim). */
+void orc_jeff_full_attention_f32(const float* q, const float* k, const float* v,
+                                 const float* gate, const float* q_norm, const float* k_norm,
+                                 const float* mask, int64_t length, int64_t heads,
+                                 int64_t head_dim, int64_t rotary_dim, float theta, float eps,
+                                 float* out);
+
 /* ---- f64 composites (tenferro-infer, tenferro-ext lib.rs) ---------- */
 double orc_erf_f64(double x);                                   /* tenferro-ext lib.rs:273-285 */
 void orc_erf_f64_n(const double* x, double* y, int64_t n);

@@ -78,6 +78,17 @@ def _declare(L: ctypes.CDLL) -> None:
             _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
         "orc_rope_pairhalf_f64": (None, [
             _f64p, _f64p, _f64p, _f64p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64]),
+        "orc_rope_tables_powf_f32": (None, [ctypes.c_float, _i64, _i64, _f32p, _f32p]),
+        "orc_laya_qkv_prep_f32": (None, [
+            _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _f32p, _f32p, _f32p]),
+        "orc_laya_attention_block_f32": (None, [
+            _f32p, _u8p, _i64, _i64, _i64, _i64, _f32p, _f32p, _f32p]),
+        "orc_jeff_qkv_prep_f32": (None, [
+            _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
+            ctypes.c_float, _f32p, _f32p, _f32p]),
+        "orc_jeff_full_attention_f32": (None, [
+            _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
+            ctypes.c_float, ctypes.c_float, _f32p]),
         "orc_erf_f64": (ctypes.c_double, [ctypes.c_double]),
         "orc_erf_f64_n": (None, [_f64p, _f64p, _i64]),
         "orc_gelu_erf_f64_n": (None, [_f64p, _f64p, _i64]),
@@ -235,6 +246,54 @@ def rope_pairhalf_f64(x, cos_t, sin_t, n_vec, seq, batch, head_dim, rotary_dim, 
     lib().orc_rope_pairhalf_f64(_p64(x), _p64(y), _p64(cos_t), _p64(sin_t), n_vec, seq, batch,
                                 head_dim, rotary_dim, *[int(s) for s in strides])
     return y
+
+
+# ---- attention blocks (cpu-kernels lib.rs:618-760, :819-1150) -----------------
+
+def rope_tables_powf_f32(base, seq, rotary_dim):
+    half = rotary_dim // 2
+    c = np.empty(max(1, seq * half), dtype=np.float32)
+    s = np.empty(max(1, seq * half), dtype=np.float32)
+    lib().orc_rope_tables_powf_f32(ctypes.c_float(base), seq, rotary_dim, _p32(c), _p32(s))
+    return c[:seq * half], s[:seq * half]
+
+
+def laya_qkv_prep_f32(qkv, hidden, heads, length, batch, cos_t=None, sin_t=None):
+    n = hidden * length * batch
+    qh, kh, vh = (np.empty(n, np.float32) for _ in range(3))
+    lib().orc_laya_qkv_prep_f32(_p32(qkv), _p32(cos_t), _p32(sin_t), hidden, heads, length, batch,
+                                _p32(qh), _p32(kh), _p32(vh))
+    return qh, kh, vh
+
+
+def laya_attention_block_f32(qkv, keep, hidden, heads, length, batch, cos_t=None, sin_t=None):
+    assert keep.dtype == np.uint8 and keep.size == length * length * batch
+    out = np.empty(hidden * length * batch, np.float32)
+    lib().orc_laya_attention_block_f32(_p32(qkv), keep.ctypes.data_as(_u8p), hidden, heads,
+                                       length, batch, _p32(cos_t), _p32(sin_t), _p32(out))
+    return out
+
+
+def jeff_qkv_prep_f32(q, k, v, q_norm, k_norm, cos_t, sin_t, length, heads, head_dim,
+                      rotary_dim, eps):
+    n = length * heads * head_dim
+    qh, kh, vh = (np.empty(n, np.float32) for _ in range(3))
+    dummy = np.zeros(1, np.float32)
+    lib().orc_jeff_qkv_prep_f32(
+        _p32(q), _p32(k), _p32(v), _p32(q_norm), _p32(k_norm),
+        _p32(cos_t if cos_t is not None and cos_t.size else dummy),
+        _p32(sin_t if sin_t is not None and sin_t.size else dummy),
+        length, heads, head_dim, rotary_dim, ctypes.c_float(eps), _p32(qh), _p32(kh), _p32(vh))
+    return qh, kh, vh
+
+
+def jeff_full_attention_f32(q, k, v, gate, q_norm, k_norm, mask, length, heads, head_dim,
+                            rotary_dim, theta, eps):
+    out = np.empty(length * heads * head_dim, np.float32)
+    lib().orc_jeff_full_attention_f32(
+        _p32(q), _p32(k), _p32(v), _p32(gate), _p32(q_norm), _p32(k_norm), _p32(mask), length,
+        heads, head_dim, rotary_dim, ctypes.c_float(theta), ctypes.c_float(eps), _p32(out))
+    return out
 
 
 # ---- f64 composites ----------------------------------------------------------

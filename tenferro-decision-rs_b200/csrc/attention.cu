@@ -1,0 +1,796 @@
+// attention.cu -- the attention cores of the Laya (ModernBERT) and Jeff
+// (Qwen3.5) forwards: the prep kernels that bring q, k, v into head-major
+// (batch, heads, length, head_dim) form, and masked scaled dot-product
+// attention over head-major tensors.
+//
+// The reference's CUDA path has the same two stages (fused_laya_qkv_prep /
+// fused_jeff_qkv_prep, then fused_attention, crates/tenferro-ext/src/cuda/
+// fused.cu:150-306, driven by FusedScope, cuda_fused.rs:751-1103); its CPU ops
+// fix the arithmetic (crates/cpu-kernels/src/lib.rs:618-760 Jeff,
+// :819-1150 Laya). The prep kernels reproduce that arithmetic bit for bit
+// (rounded products, sequential per-token sums). The attention kernel is a
+// tiled online-softmax ("flash") kernel on the f32 pipes: a CTA owns 64
+// queries of one head, streams 64-key blocks of K and V through shared
+// memory, keeps the running max, sum and the 64 x head_dim output tile in
+// registers, and skips key blocks that the mask excludes entirely.
+
+#include <algorithm>
+#include <cmath>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace tfx {
+namespace {
+
+// ---- Laya prep: split + full-width RoPE ------------------------------------------------
+
+// One thread per (token row, head, VEC pairs): q and k pairs (i, i + half)
+// rotated as a*c - b*s, a*s + b*c with every product rounded (lib.rs:
+// 996-1008); v copied.
+template <int VEC>
+__global__ void __launch_bounds__(256) laya_prep_kernel(
+    const float* __restrict__ qkv, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, float* __restrict__ qh, float* __restrict__ kh,
+    float* __restrict__ vh, uint32_t hidden, uint32_t heads, uint32_t length, uint32_t hd,
+    uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len) {
+  pdl_enter();
+  const uint32_t half = hd / 2;
+  for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
+       n += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t n32 = uint32_t(n);  // total < 2^32 (checked on the host)
+    const uint32_t rest = div_chunks.div(n32);
+    const uint32_t i0 = (n32 - rest * div_chunks.d) * VEC;
+    const uint32_t row = div_heads.div(rest);  // b * length + l
+    const uint32_t head = rest - row * div_heads.d;
+    const uint32_t b = div_len.div(row), l = row - b * div_len.d;
+    const float* src = qkv + uint64_t(3) * hidden * row + uint64_t(head) * hd;
+    const uint64_t dst = ((uint64_t(b) * heads + head) * length + l) * hd;
+    float qa[VEC], qb[VEC], ka[VEC], kb[VEC], va[VEC], vb[VEC], c[VEC], s[VEC];
+    if constexpr (VEC == 4) {
+      auto ld4 = [](const float* p, float* o) {
+        const float4 t = ld_stream(reinterpret_cast<const float4*>(p));
+        o[0] = t.x; o[1] = t.y; o[2] = t.z; o[3] = t.w;
+      };
+      ld4(src + i0, qa); ld4(src + half + i0, qb);
+      ld4(src + hidden + i0, ka); ld4(src + hidden + half + i0, kb);
+      ld4(src + 2 * hidden + i0, va); ld4(src + 2 * hidden + half + i0, vb);
+      if (cos_t) {
+        const float4 tc = __ldg(reinterpret_cast<const float4*>(cos_t + uint64_t(l) * half + i0));
+        const float4 ts = __ldg(reinterpret_cast<const float4*>(sin_t + uint64_t(l) * half + i0));
+        c[0] = tc.x; c[1] = tc.y; c[2] = tc.z; c[3] = tc.w;
+        s[0] = ts.x; s[1] = ts.y; s[2] = ts.z; s[3] = ts.w;
+      }
+    } else {
+      qa[0] = src[i0]; qb[0] = src[half + i0];
+      ka[0] = src[hidden + i0]; kb[0] = src[hidden + half + i0];
+      va[0] = src[2 * hidden + i0]; vb[0] = src[2 * hidden + half + i0];
+      if (cos_t) {
+        c[0] = __ldg(cos_t + uint64_t(l) * half + i0);
+        s[0] = __ldg(sin_t + uint64_t(l) * half + i0);
+      }
+    }
+    if (cos_t) {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float a0 = qa[j], b0 = qb[j];
+        qa[j] = __fsub_rn(__fmul_rn(a0, c[j]), __fmul_rn(b0, s[j]));
+        qb[j] = __fadd_rn(__fmul_rn(a0, s[j]), __fmul_rn(b0, c[j]));
+        const float a1 = ka[j], b1 = kb[j];
+        ka[j] = __fsub_rn(__fmul_rn(a1, c[j]), __fmul_rn(b1, s[j]));
+        kb[j] = __fadd_rn(__fmul_rn(a1, s[j]), __fmul_rn(b1, c[j]));
+      }
+    }
+    if constexpr (VEC == 4) {
+      auto st4 = [](float* p, const float* v) {
+        *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+      };
+      st4(qh + dst + i0, qa); st4(qh + dst + half + i0, qb);
+      st4(kh + dst + i0, ka); st4(kh + dst + half + i0, kb);
+      st4(vh + dst + i0, va); st4(vh + dst + half + i0, vb);
+    } else {
+      qh[dst + i0] = qa[0]; qh[dst + half + i0] = qb[0];
+      kh[dst + i0] = ka[0]; kh[dst + half + i0] = kb[0];
+      vh[dst + i0] = va[0]; vh[dst + half + i0] = vb[0];
+    }
+  }
+}
+
+// ---- Jeff prep: centred per-head RMSNorm + partial RoPE --------------------------------
+
+// CTA per (32-token tile, head). The time-first inputs are read as [head_dim]
+// x 32-token runs into shared memory; 32 threads each sum one token's squares
+// sequentially (lib.rs:676-683), every element is scaled as
+// x * (scale * (1 + w)) (:684-686), the first rotary_dim channels rotated
+// (:690-707), and the tile written head-major.
+__global__ void __launch_bounds__(256) jeff_prep_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ qh,
+    float* __restrict__ kh, float* __restrict__ vh, uint32_t length, uint32_t hd,
+    uint32_t rotary, float eps) {
+  pdl_enter();
+  extern __shared__ float tile[];  // [hd][33]
+  __shared__ float scale_s[32];
+  const uint32_t tid = threadIdx.x, head = blockIdx.y, t0 = blockIdx.x * 32;
+  const uint32_t half = rotary / 2;
+  const uint64_t feat = uint64_t(head) * hd;
+  const float hd_f = float(hd);
+  for (int which = 0; which < 3; ++which) {
+    const float* src = which == 0 ? q : which == 1 ? k : v;
+    float* dst = which == 0 ? qh : which == 1 ? kh : vh;
+    for (uint32_t idx = tid; idx < hd * 32; idx += 256) {
+      const uint32_t i = idx >> 5, t = idx & 31;
+      tile[i * 33 + t] = t0 + t < length ? src[t0 + t + uint64_t(length) * (feat + i)] : 0.0f;
+    }
+    __syncthreads();
+    if (which < 2) {
+      const float* w = which == 0 ? q_norm : k_norm;
+      if (tid < 32) {
+        float ms = 0.0f;
+        for (uint32_t i = 0; i < hd; ++i) {
+          const float x = tile[i * 33 + tid];
+          ms = __fadd_rn(ms, __fmul_rn(x, x));
+        }
+        ms = __fdiv_rn(ms, hd_f);
+        scale_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+      }
+      __syncthreads();
+      for (uint32_t idx = tid; idx < hd * 32; idx += 256) {
+        const uint32_t i = idx >> 5, t = idx & 31;
+        tile[i * 33 + t] =
+            __fmul_rn(tile[i * 33 + t], __fmul_rn(scale_s[t], __fadd_rn(1.0f, __ldg(w + i))));
+      }
+      __syncthreads();
+      for (uint32_t idx = tid; idx < half * 32; idx += 256) {
+        const uint32_t i = idx >> 5, t = idx & 31;
+        if (t0 + t < length) {
+          const float c = __ldg(cos_t + uint64_t(t0 + t) * half + i);
+          const float s = __ldg(sin_t + uint64_t(t0 + t) * half + i);
+          const float a = tile[i * 33 + t], b = tile[(i + half) * 33 + t];
+          tile[i * 33 + t] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+          tile[(i + half) * 33 + t] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+        }
+      }
+      __syncthreads();
+    }
+    for (uint32_t idx = tid; idx < hd * 32; idx += 256) {
+      const uint32_t t = idx / hd, i = idx - t * hd;
+      if (t0 + t < length) dst[(uint64_t(head) * length + t0 + t) * hd + i] = tile[i * 33 + t];
+    }
+    __syncthreads();
+  }
+}
+
+// ---- attention -----------------------------------------------------------------------
+
+struct AttnArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* out;
+  const uint8_t* keep;
+  const float* bias;
+  const float* active;
+  const float* gate;
+  int64_t gate_offset, out_tok, out_feat, out_batch;
+  uint32_t heads, length, hd;
+  float scale;
+  int empty_nan, causal;
+  int64_t window, valid_len;
+};
+
+// Keys [lo, hi) that the analytic conditions allow for queries [q0, q1].
+__device__ __forceinline__ void analytic_range(const AttnArgs& a, int64_t q0, int64_t q1,
+                                               int64_t* lo, int64_t* hi) {
+  int64_t l = 0, h = a.length;
+  if (a.causal) h = min(h, q1 + 1);
+  if (a.window >= 0) {
+    l = max(l, q0 - a.window);
+    h = min(h, q1 + a.window + 1);
+  }
+  if (a.valid_len >= 0) h = min(h, a.valid_len);
+  *lo = l;
+  *hi = max(l, h);
+}
+
+__device__ __forceinline__ bool key_kept(const AttnArgs& a, uint32_t b, int64_t qi, int64_t kj) {
+  if (a.causal && kj > qi) return false;
+  if (a.window >= 0 && (kj < qi - a.window || kj > qi + a.window)) return false;
+  if (a.valid_len >= 0 && kj >= a.valid_len) return false;
+  const uint64_t L = a.length;
+  if (a.keep && a.keep[uint64_t(qi) + L * (uint64_t(kj) + L * b)] == 0) return false;
+  if (a.active && a.active[uint64_t(b) * L + kj] == 0.0f) return false;
+  return true;
+}
+
+// out element for (token qi, feature f, batch b); empty / +inf rows take
+// the empty value; the gate multiplies every written value.
+__device__ __forceinline__ void store_out(const AttnArgs& a, uint32_t b, uint32_t qi,
+                                          uint64_t f, float val) {
+  const int64_t idx = int64_t(qi) * a.out_tok + int64_t(f) * a.out_feat + int64_t(b) * a.out_batch;
+  if (a.gate) {
+    const float g = a.gate[a.gate_offset + idx];
+    val = __fmul_rn(val, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g))));
+  }
+  a.out[idx] = val;
+}
+
+// Narrows [lo, hi) to the keys the keep mask allows for some query of
+// [q0, q0 + nq); every thread of the CTA gets the result.
+__device__ void keep_narrow(const AttnArgs& a, uint32_t b, uint32_t q0, uint32_t nq, int64_t* lo,
+                            int64_t* hi, int* red) {
+  if (threadIdx.x == 0) {
+    red[0] = int(*hi);
+    red[1] = int(*lo) - 1;
+  }
+  __syncthreads();
+  const uint64_t L = a.length;
+  for (int64_t kj = *lo + threadIdx.x; kj < *hi; kj += blockDim.x) {
+    const uint8_t* row = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
+    bool any = false;
+    for (uint32_t i = 0; i < nq && !any; ++i) any = row[i] != 0;
+    if (any) {
+      atomicMin(&red[0], int(kj));
+      atomicMax(&red[1], int(kj));
+    }
+  }
+  __syncthreads();
+  const int first = red[0], last = red[1];
+  __syncthreads();
+  if (first > last) {
+    *hi = *lo;
+  } else {
+    *lo = first;
+    *hi = int64_t(last) + 1;
+  }
+}
+
+constexpr int kQT = 64;  // queries per CTA
+
+// Flash kernel: 256 threads as 16 x 16; thread (ty, tx) owns queries
+// 4ty..4ty+3, keys KT*tx.. of each block and output channels
+// 64*j + 4tx..4tx+3. Shared memory: Q^T [HD][64], K^T [HD][KB], V [KB][HD],
+// P [64][KB + 4].
+template <int HD, int KB>
+__global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
+  constexpr int KT = KB / 16;
+  constexpr int DJ = HD / 64;
+  constexpr int PS = KB + 4;
+  extern __shared__ __align__(16) float sm[];
+  float* Qt = sm;
+  float* Kt = Qt + HD * kQT;
+  float* Vs = Kt + HD * KB;
+  float* Ps = Vs + KB * HD;
+  __shared__ int red[2];
+  __shared__ int vbad;
+  pdl_enter();
+  const uint32_t tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const uint32_t q0 = blockIdx.x * kQT, head = blockIdx.y, b = blockIdx.z;
+  const uint32_t L = a.length;
+  const uint32_t nq = min(uint32_t(kQT), L - q0);
+  const uint64_t base = (uint64_t(b) * a.heads + head) * L * HD;
+  int64_t lo, hi;
+  analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
+  if (a.keep && lo < hi) keep_narrow(a, b, q0, nq, &lo, &hi, red);
+
+  for (uint32_t idx = tid; idx < kQT * HD / 4; idx += 256) {
+    const uint32_t qq = idx % kQT, h4 = idx / kQT;
+    float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (qq < nq) val = ld_stream(reinterpret_cast<const float4*>(a.q + base + uint64_t(q0 + qq) * HD + 4 * h4));
+    Qt[(4 * h4 + 0) * kQT + qq] = val.x;
+    Qt[(4 * h4 + 1) * kQT + qq] = val.y;
+    Qt[(4 * h4 + 2) * kQT + qq] = val.z;
+    Qt[(4 * h4 + 3) * kQT + qq] = val.w;
+  }
+
+  float o[4][DJ][4];
+  float m[4], l[4];
+  bool inf_row[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.0f;
+    inf_row[i] = false;
+#pragma unroll
+    for (int j = 0; j < DJ; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[i][j][e] = 0.0f;
+  }
+
+  const int64_t kb_first = lo / KB * KB;
+  for (int64_t kb0 = kb_first; kb0 < hi; kb0 += KB) {
+    if (tid == 0) vbad = 0;
+    __syncthreads();  // the previous block's reads of K, V, P are done
+    for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
+      const uint32_t kk = idx % KB, h4 = idx / KB;
+      float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (kb0 + kk < L)
+        val = ld_stream(reinterpret_cast<const float4*>(a.k + base + uint64_t(kb0 + kk) * HD + 4 * h4));
+      Kt[(4 * h4 + 0) * KB + kk] = val.x;
+      Kt[(4 * h4 + 1) * KB + kk] = val.y;
+      Kt[(4 * h4 + 2) * KB + kk] = val.z;
+      Kt[(4 * h4 + 3) * KB + kk] = val.w;
+    }
+    bool bad = false;
+    for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
+      const uint32_t kk = idx / (HD / 4), h4 = idx % (HD / 4);
+      float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (kb0 + kk < L)
+        val = ld_stream(reinterpret_cast<const float4*>(a.v + base + uint64_t(kb0 + kk) * HD + 4 * h4));
+      bad |= !(fabsf(val.x) < INFINITY && fabsf(val.y) < INFINITY && fabsf(val.z) < INFINITY &&
+               fabsf(val.w) < INFINITY);
+      *reinterpret_cast<float4*>(Vs + kk * HD + 4 * h4) = val;
+    }
+    if (bad) vbad = 1;
+    __syncthreads();
+
+    // scores of queries 4ty+i against keys KT*tx+j
+    float s[4][KT];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
+#pragma unroll 8
+    for (int h = 0; h < HD; ++h) {
+      const float4 q4 = *reinterpret_cast<const float4*>(Qt + h * kQT + 4 * ty);
+      float kv[KT];
+      if constexpr (KT == 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(Kt + h * KB + 4 * tx);
+        kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
+      } else {
+        const float2 k2 = *reinterpret_cast<const float2*>(Kt + h * KB + 2 * tx);
+        kv[0] = k2.x; kv[1] = k2.y;
+      }
+      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < KT; ++j) s[i][j] = __fmaf_rn(qv[i], kv[j], s[i][j]);
+    }
+
+    // mask, scale, online softmax
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t qi = int64_t(q0) + 4 * ty + i;
+      float mb = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KT; ++j) {
+        const int64_t kj = kb0 + KT * tx + j;
+        float sc = -INFINITY;
+        if (qi < L && kj >= lo && kj < hi && key_kept(a, b, qi, kj)) {
+          sc = __fmul_rn(s[i][j], a.scale);
+          if (a.bias) sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kj) + uint64_t(L) * b)]);
+          if (sc == INFINITY) inf_row[i] = true;
+          if (!(fabsf(sc) < INFINITY)) sc = -INFINITY;  // NaN / inf: contributes nothing
+        }
+        s[i][j] = sc;
+        mb = fmaxf(mb, sc);
+      }
+#pragma unroll
+      for (int d = 1; d < 16; d <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, d));
+      const float mn = fmaxf(m[i], mb);
+      float corr = 1.0f, ps = 0.0f;
+      if (mn != -INFINITY) {
+        corr = expf(__fsub_rn(m[i], mn));
+#pragma unroll
+        for (int j = 0; j < KT; ++j) {
+          const float p = s[i][j] == -INFINITY ? 0.0f : expf(__fsub_rn(s[i][j], mn));
+          s[i][j] = p;
+          ps = __fadd_rn(ps, p);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
+      }
+#pragma unroll
+      for (int d = 1; d < 16; d <<= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, d));
+      m[i] = mn;
+      l[i] = __fmaf_rn(l[i], corr, ps);
+#pragma unroll
+      for (int j = 0; j < DJ; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[i][j][e] = __fmul_rn(o[i][j][e], corr);
+      if constexpr (KT == 4) {
+        *reinterpret_cast<float4*>(Ps + (4 * ty + i) * PS + 4 * tx) =
+            make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+      } else {
+        *reinterpret_cast<float2*>(Ps + (4 * ty + i) * PS + 2 * tx) = make_float2(s[i][0], s[i][1]);
+      }
+    }
+    __syncthreads();
+
+    // O += P V (keys whose p is 0 are skipped when V holds a non-finite value)
+    const bool guard = vbad != 0;
+#pragma unroll 2
+    for (int k4 = 0; k4 < KB; k4 += 4) {
+      float p[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 t = *reinterpret_cast<const float4*>(Ps + (4 * ty + i) * PS + k4);
+        p[i][0] = t.x; p[i][1] = t.y; p[i][2] = t.z; p[i][3] = t.w;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int j = 0; j < DJ; ++j) {
+          const float4 vv = *reinterpret_cast<const float4*>(Vs + (k4 + kk) * HD + 64 * j + 4 * tx);
+          const float ve[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            if (guard && p[i][kk] == 0.0f) continue;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[i][j][e] = __fmaf_rn(p[i][kk], ve[e], o[i][j][e]);
+          }
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t qi = q0 + 4 * ty + i;
+    if (qi >= L) continue;
+    const bool empty = l[i] == 0.0f || inf_row[i];
+    const float ev = a.empty_nan ? NAN : 0.0f;
+#pragma unroll
+    for (int j = 0; j < DJ; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t d = 64 * j + 4 * tx + e;
+        const float val = empty ? ev : __fdiv_rn(o[i][j][e], l[i]);
+        store_out(a, b, qi, uint64_t(head) * HD + d, val);
+      }
+  }
+}
+
+// Any head_dim: CTA per (query, head, batch), scores of the whole row in
+// shared memory (length floats), the reference's fused_attention structure.
+__global__ void __launch_bounds__(128) attn_row_kernel(AttnArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  float* scores = sm;                // [length]
+  float* query = sm + a.length;      // [hd]
+  __shared__ float scratch[4];
+  __shared__ int inf_flag;
+  pdl_enter();
+  const uint32_t qi = blockIdx.x, head = blockIdx.y, b = blockIdx.z;
+  const uint32_t L = a.length, hd = a.hd;
+  const uint32_t lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t base = (uint64_t(b) * a.heads + head) * L * hd;
+  if (threadIdx.x == 0) inf_flag = 0;
+  for (uint32_t d = threadIdx.x; d < hd; d += 128) query[d] = a.q[base + uint64_t(qi) * hd + d];
+  __syncthreads();
+  int64_t lo, hi;
+  analytic_range(a, qi, qi, &lo, &hi);
+  for (uint32_t kj = warp; kj < L; kj += 4) {
+    const bool kept = kj >= lo && kj < hi && key_kept(a, b, qi, kj);
+    float dot = 0.0f;
+    if (kept) {
+      const float* kr = a.k + base + uint64_t(kj) * hd;
+      for (uint32_t d = lane; d < hd; d += 32) dot = __fmaf_rn(query[d], kr[d], dot);
+      dot = warp_sum(dot);
+    }
+    if (lane == 0) {
+      float sc = -INFINITY;
+      if (kept) {
+        sc = __fmul_rn(dot, a.scale);
+        if (a.bias) sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kj) + uint64_t(L) * b)]);
+        if (sc == INFINITY) inf_flag = 1;
+        if (!(fabsf(sc) < INFINITY)) sc = -INFINITY;
+      }
+      scores[kj] = sc;
+    }
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (uint32_t kj = threadIdx.x; kj < L; kj += 128) mx = fmaxf(mx, scores[kj]);
+  mx = warp_max(mx);
+  if (lane == 0) scratch[warp] = mx;
+  __syncthreads();
+  mx = fmaxf(fmaxf(scratch[0], scratch[1]), fmaxf(scratch[2], scratch[3]));
+  __syncthreads();
+  float sum = 0.0f;
+  for (uint32_t kj = threadIdx.x; kj < L; kj += 128) {
+    const float sc = scores[kj];
+    const float p = sc == -INFINITY ? 0.0f : expf(__fsub_rn(sc, mx));
+    scores[kj] = p;
+    sum = __fadd_rn(sum, p);
+  }
+  sum = warp_sum(sum);
+  if (lane == 0) scratch[warp] = sum;
+  __syncthreads();
+  sum = __fadd_rn(__fadd_rn(scratch[0], scratch[1]), __fadd_rn(scratch[2], scratch[3]));
+  const bool empty = sum == 0.0f || inf_flag;
+  for (uint32_t d = threadIdx.x; d < hd; d += 128) {
+    float acc = 0.0f;
+    if (!empty) {
+      const float* vc = a.v + base + d;
+      for (uint32_t kj = 0; kj < L; ++kj) {
+        const float p = scores[kj];
+        if (p != 0.0f) acc = __fmaf_rn(p, vc[uint64_t(kj) * hd], acc);
+      }
+    }
+    const float val = empty ? (a.empty_nan ? NAN : 0.0f) : __fdiv_rn(acc, sum);
+    store_out(a, b, qi, uint64_t(head) * hd + d, val);
+  }
+}
+
+int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t stream) {
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  const bool vec = aligned(a.q, 16) && aligned(a.k, 16) && aligned(a.v, 16);
+  const dim3 grid((a.length + kQT - 1) / kQT, a.heads, batch);
+  auto flash = [&](auto kernel, int hd, int kb) -> int {
+    const size_t smem = size_t(hd * kQT + hd * kb + kb * hd + kQT * (kb + 4)) * 4;
+    if (smem > size_t(dev.smem_optin)) return 1;
+    const cudaError_t e =
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e));
+    return launch_kernel(op, kernel, grid, dim3(256), smem, stream, 1, a);
+  };
+  if (vec && a.hd == 64) return flash(attn_flash_kernel<64, 64>, 64, 64);
+  if (vec && a.hd == 128) return flash(attn_flash_kernel<128, 64>, 128, 64);
+  if (vec && a.hd == 256) {
+    const int rc = flash(attn_flash_kernel<256, 32>, 256, 32);
+    if (rc != 1) return rc;
+  }
+  const size_t smem = size_t(a.length + a.hd) * 4;
+  if (smem > size_t(dev.smem_optin))
+    return fail(TFX_ERR_UNSUPPORTED, op, "length",
+                "rows longer than the shared-memory score buffer for head_dim " +
+                    std::to_string(a.hd));
+  const cudaError_t e = cudaFuncSetAttribute(
+      attn_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  if (e != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e));
+  return launch_kernel(op, attn_row_kernel, dim3(a.length, a.heads, batch), dim3(128), smem,
+                       stream, 1, a);
+}
+
+}  // namespace
+
+// ---- host entry points ---------------------------------------------------------------
+
+int laya_prep(const char* op, const float* qkv, const float* cos_t, const float* sin_t,
+              float* qh, float* kh, float* vh, int64_t hidden, int64_t heads, int64_t length,
+              int64_t batch, cudaStream_t stream) {
+  TFX_REQUIRE(hidden >= 0 && heads > 0 && length >= 0 && batch >= 0, op, "shape",
+              "extents must be non-negative (heads positive)");
+  TFX_REQUIRE(hidden % heads == 0, op, "hidden", "hidden must be a multiple of heads");
+  const int64_t hd = hidden / heads;
+  TFX_REQUIRE(hd % 2 == 0, op, "head_dim", "head_dim must be even");
+  if (hidden == 0 || length == 0 || batch == 0) return TFX_OK;
+  TFX_REQUIRE(qkv && qh && kh && vh, op, "tensors", "null pointer");
+  TFX_REQUIRE((cos_t == nullptr) == (sin_t == nullptr), op, "tables",
+              "cos and sin tables must both be given or both be null");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  const int64_t half = hd / 2;
+  const bool v4 = half % 4 == 0 && hidden % 4 == 0 && aligned(qkv, 16) && aligned(qh, 16) &&
+                  aligned(kh, 16) && aligned(vh, 16) &&
+                  (!cos_t || (aligned(cos_t, 16) && aligned(sin_t, 16)));
+  const int64_t vec = v4 ? 4 : 1;
+  const int64_t chunks = half / vec;
+  const int64_t total = batch * length * heads * chunks;
+  TFX_REQUIRE(total < (int64_t(1) << 32) && batch * length < (int64_t(1) << 32), op, "shape",
+              "too many elements for one call");
+  const unsigned grid = unsigned(std::min<int64_t>((total + 255) / 256, 148 * 16));
+  const FastDiv dc{uint32_t(chunks)}, dh{uint32_t(heads)}, dl{uint32_t(length)};
+  if (v4)
+    return launch_kernel(op, laya_prep_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
+                         sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
+                         uint32_t(hd), uint64_t(total), dc, dh, dl);
+  return launch_kernel(op, laya_prep_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
+                       sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
+                       uint32_t(hd), uint64_t(total), dc, dh, dl);
+}
+
+int jeff_prep(const char* op, const float* q, const float* k, const float* v,
+              const float* q_norm, const float* k_norm, const float* cos_t, const float* sin_t,
+              float* qh, float* kh, float* vh, int64_t length, int64_t heads, int64_t head_dim,
+              int64_t rotary_dim, float eps, cudaStream_t stream) {
+  TFX_REQUIRE(length >= 0 && heads >= 0 && head_dim >= 0, op, "shape",
+              "extents must be non-negative");
+  TFX_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0, op,
+              "rotary_dim", "rotary_dim must be even and at most head_dim");
+  TFX_REQUIRE(head_dim <= 1024, op, "head_dim", "head_dim above 1024");
+  if (length == 0 || heads == 0 || head_dim == 0) return TFX_OK;
+  TFX_REQUIRE(q && k && v && qh && kh && vh && q_norm && k_norm, op, "tensors", "null pointer");
+  TFX_REQUIRE(rotary_dim == 0 || (cos_t && sin_t), op, "tables", "null pointer");
+  TFX_REQUIRE(length < (int64_t(1) << 31) && heads < 65536, op, "shape", "too large");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  const size_t smem = size_t(head_dim) * 33 * 4;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        jeff_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    if (e != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e));
+  }
+  return launch_kernel(op, jeff_prep_kernel, dim3(unsigned((length + 31) / 32), unsigned(heads)),
+                       dim3(256), smem, stream, 1, q, k, v, q_norm, k_norm, cos_t, sin_t, qh, kh,
+                       vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps);
+}
+
+int attention(const char* op, const float* qh, const float* kh, const float* vh, float* out,
+              const tfx_attention_desc* d, cudaStream_t stream) {
+  TFX_REQUIRE(d, op, "desc", "null pointer");
+  TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->length >= 0 && d->head_dim >= 0, op, "shape",
+              "extents must be non-negative");
+  TFX_REQUIRE(d->empty_rows == TFX_ATTN_EMPTY_NAN || d->empty_rows == TFX_ATTN_EMPTY_ZERO, op,
+              "empty_rows", "unknown value " + std::to_string(d->empty_rows));
+  if (d->batch == 0 || d->heads == 0 || d->length == 0 || d->head_dim == 0) return TFX_OK;
+  TFX_REQUIRE(qh && kh && vh && out, op, "tensors", "null pointer");
+  TFX_REQUIRE(d->length < (int64_t(1) << 31) && d->heads < 65536 && d->batch < 65536, op,
+              "shape", "too large");
+  TFX_REQUIRE(d->head_dim <= 1024, op, "head_dim", "head_dim above 1024");
+  AttnArgs a;
+  a.q = qh;
+  a.k = kh;
+  a.v = vh;
+  a.out = out;
+  a.keep = d->keep;
+  a.bias = d->bias;
+  a.active = d->active;
+  a.gate = d->gate;
+  a.gate_offset = d->gate_offset;
+  a.out_tok = d->out_tok;
+  a.out_feat = d->out_feat;
+  a.out_batch = d->out_batch;
+  a.heads = uint32_t(d->heads);
+  a.length = uint32_t(d->length);
+  a.hd = uint32_t(d->head_dim);
+  a.scale = d->scale;
+  a.empty_nan = d->empty_rows == TFX_ATTN_EMPTY_NAN;
+  a.causal = d->causal ? 1 : 0;
+  a.window = d->window;
+  a.valid_len = d->valid_len;
+  return attn_launch(op, a, uint32_t(d->batch), stream);
+}
+
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" {
+
+int tfx_rope_tables_powf_f32(float base, int64_t seq, int64_t rotary_dim, float* cos_host,
+                             float* sin_host) {
+  clear_error();
+  const char* op = "cpu-kernels::rope_tables";
+  TFX_REQUIRE(seq >= 0, op, "seq", "must be non-negative");
+  TFX_REQUIRE(rotary_dim > 0 && rotary_dim % 2 == 0, op, "rotary_dim",
+              "rotary width must be a positive even number, got " + std::to_string(rotary_dim));
+  TFX_REQUIRE(seq == 0 || (cos_host && sin_host), op, "tables", "null pointer");
+  const int64_t half = rotary_dim / 2;
+  for (int64_t p = 0; p < seq; ++p)
+    for (int64_t i = 0; i < half; ++i) {
+      const float e = (-2.0f * float(i)) / float(rotary_dim);
+      const float theta = float(p) * powf(base, e);
+      cos_host[p * half + i] = cosf(theta);
+      sin_host[p * half + i] = sinf(theta);
+    }
+  return TFX_OK;
+}
+
+int tfx_laya_qkv_prep_f32(const float* qkv, const float* cos_table, const float* sin_table,
+                          float* qh, float* kh, float* vh, int64_t hidden, int64_t heads,
+                          int64_t length, int64_t batch, tfx_stream_t stream) {
+  clear_error();
+  return laya_prep("tenferro-ext::laya_qkv_prep", qkv, cos_table, sin_table, qh, kh, vh, hidden,
+                   heads, length, batch, static_cast<cudaStream_t>(stream));
+}
+
+int tfx_jeff_qkv_prep_f32(const float* q, const float* k, const float* v, const float* q_norm,
+                          const float* k_norm, const float* cos_table, const float* sin_table,
+                          float* qh, float* kh, float* vh, int64_t length, int64_t heads,
+                          int64_t head_dim, int64_t rotary_dim, float eps, tfx_stream_t stream) {
+  clear_error();
+  return jeff_prep("tenferro-ext::jeff_qkv_prep", q, k, v, q_norm, k_norm, cos_table, sin_table,
+                   qh, kh, vh, length, heads, head_dim, rotary_dim, eps,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tfx_attention_desc_init(tfx_attention_desc* d, int64_t batch, int64_t heads, int64_t length,
+                            int64_t head_dim) {
+  clear_error();
+  TFX_REQUIRE(d, "tenferro-ext::attention", "desc", "null pointer");
+  *d = tfx_attention_desc{};
+  d->batch = batch;
+  d->heads = heads;
+  d->length = length;
+  d->head_dim = head_dim;
+  d->scale = head_dim > 0 ? 1.0f / sqrtf(float(head_dim)) : 1.0f;
+  d->empty_rows = TFX_ATTN_EMPTY_NAN;
+  d->window = -1;
+  d->valid_len = -1;
+  d->out_tok = heads * head_dim;
+  d->out_feat = 1;
+  d->out_batch = heads * head_dim * length;
+  return TFX_OK;
+}
+
+int tfx_attention_f32(const float* qh, const float* kh, const float* vh, float* out,
+                      const tfx_attention_desc* desc, tfx_stream_t stream) {
+  clear_error();
+  return attention("tenferro-ext::attention", qh, kh, vh, out, desc,
+                   static_cast<cudaStream_t>(stream));
+}
+
+int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const float* cos_table,
+                                 const float* sin_table, float* out, int64_t hidden,
+                                 int64_t heads, int64_t length, int64_t batch,
+                                 tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::laya_attention_block";
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TFX_REQUIRE(heads > 0 && hidden >= 0 && length >= 0 && batch >= 0, op, "shape",
+              "extents must be non-negative (heads positive)");
+  TFX_REQUIRE(hidden % heads == 0, op, "hidden", "hidden must be a multiple of heads");
+  const int64_t n = hidden * length * batch;
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(qkv && keep && out, op, "tensors", "null pointer");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  float* scratch = nullptr;
+  const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  }
+  int rc = laya_prep(op, qkv, cos_table, sin_table, scratch, scratch + n, scratch + 2 * n, hidden,
+                     heads, length, batch, s);
+  if (rc == TFX_OK) {
+    tfx_attention_desc d;
+    tfx_attention_desc_init(&d, batch, heads, length, hidden / heads);
+    d.keep = keep;
+    rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s);
+  }
+  cudaFreeAsync(scratch, s);
+  return rc;
+}
+
+int tfx_jeff_attention_f32(const float* q, const float* k, const float* v, const float* gate,
+                           const float* q_norm, const float* k_norm, const float* mask,
+                           const float* cos_table, const float* sin_table, float* out,
+                           int64_t length, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                           float eps, tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::jeff_attention";
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TFX_REQUIRE(length >= 0 && heads >= 0 && head_dim >= 0, op, "shape",
+              "extents must be non-negative");
+  const int64_t n = length * heads * head_dim;
+  if (n == 0) return TFX_OK;
+  TFX_REQUIRE(gate && mask && out, op, "tensors", "null pointer");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  float* scratch = nullptr;
+  const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  }
+  int rc = jeff_prep(op, q, k, v, q_norm, k_norm, cos_table, sin_table, scratch, scratch + n,
+                     scratch + 2 * n, length, heads, head_dim, rotary_dim, eps, s);
+  if (rc == TFX_OK) {
+    tfx_attention_desc d;
+    tfx_attention_desc_init(&d, 1, heads, length, head_dim);
+    d.empty_rows = TFX_ATTN_EMPTY_ZERO;
+    d.causal = 1;
+    d.active = mask;
+    d.gate = gate;
+    d.out_tok = 1;
+    d.out_feat = length;
+    d.out_batch = 0;
+    rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s);
+  }
+  cudaFreeAsync(scratch, s);
+  return rc;
+}
+
+}  // extern "C"

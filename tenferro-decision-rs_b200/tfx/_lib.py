@@ -58,9 +58,21 @@ class RopeDesc(ctypes.Structure):
         "stride_batch", "stride_feat")]
 
 
+class AttentionDesc(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("length", ctypes.c_int64),
+        ("head_dim", ctypes.c_int64), ("scale", ctypes.c_float), ("empty_rows", ctypes.c_int32),
+        ("causal", ctypes.c_int32), ("window", ctypes.c_int64), ("valid_len", ctypes.c_int64),
+        ("keep", ctypes.c_void_p), ("bias", ctypes.c_void_p), ("active", ctypes.c_void_p),
+        ("gate", ctypes.c_void_p), ("gate_offset", ctypes.c_int64), ("out_tok", ctypes.c_int64),
+        ("out_feat", ctypes.c_int64), ("out_batch", ctypes.c_int64),
+    ]
+
+
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
+_f32 = ctypes.c_float
 
 SIGNATURES = {
     "tfx_last_error_string": (ctypes.c_char_p, []),
@@ -84,6 +96,15 @@ SIGNATURES = {
     "tfx_masked_softmax_f32": (_int, [_p, _p, ctypes.POINTER(SoftmaxDesc), _p]),
     "tfx_rope_pairhalf_f32": (_int, [_p, _p, _p, _p, ctypes.POINTER(RopeDesc), _p]),
     "tfx_rope_tables_f32": (_int, [ctypes.c_double, _i64, _i64, _p, _p]),
+    "tfx_rope_tables_powf_f32": (_int, [_f32, _i64, _i64, _p, _p]),
+    "tfx_laya_qkv_prep_f32": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
+    "tfx_jeff_qkv_prep_f32": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                                     _i64, _f32, _p]),
+    "tfx_attention_desc_init": (_int, [ctypes.POINTER(AttentionDesc), _i64, _i64, _i64, _i64]),
+    "tfx_attention_f32": (_int, [_p, _p, _p, _p, ctypes.POINTER(AttentionDesc), _p]),
+    "tfx_laya_attention_block_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
+    "tfx_jeff_attention_f32": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
+                                      _i64, _f32, _p]),
     "tfx_session_create": (_int, [_int, ctypes.POINTER(ctypes.c_void_p)]),
     "tfx_session_destroy": (_int, [_p]),
     "tfx_session_set_chunk_bytes": (_int, [_p, _i64]),

@@ -187,3 +187,39 @@ def rope_pairhalf(x, cos_t, sin_t, n_vec, seq, batch, head_dim, rotary_dim, stri
     check(lib.tfx_rope_pairhalf_f32(_ptr(x), _ptr(y), _ptr(cos_t), _ptr(sin_t), ctypes.byref(d),
                                     _stream(x)))
     return y
+
+
+def rope_tables_powf(base, seq, rotary_dim, device="cuda"):
+    """cpu-kernels' f32 tables (powf, cosf, sinf), (seq, rotary_dim/2)."""
+    half = rotary_dim // 2
+    c = torch.empty((seq, half), dtype=torch.float32)
+    s = torch.empty((seq, half), dtype=torch.float32)
+    check(lib.tfx_rope_tables_powf_f32(ctypes.c_float(base), seq, rotary_dim, _ptr(c), _ptr(s)))
+    if device == "cpu":
+        return c, s
+    return c.to(device), s.to(device)
+
+
+def laya_attention_block(qkv, keep, hidden, heads, length, batch, cos_t=None, sin_t=None,
+                         out=None):
+    """LayaAttentionBlockOp: qkv (3*hidden, length, batch) feature-first, keep
+    (length, length, batch) uint8 (query fastest) -> (hidden, length, batch)."""
+    _cuda(qkv, torch.float32, "qkv")
+    _cuda(keep, torch.uint8, "keep")
+    y = torch.empty(hidden * length * batch, device=qkv.device) if out is None else out
+    check(lib.tfx_laya_attention_block_f32(_ptr(qkv), _ptr(keep), _ptr(cos_t), _ptr(sin_t),
+                                           _ptr(y), hidden, heads, length, batch, _stream(qkv)))
+    return y
+
+
+def jeff_attention(q, k, v, gate, q_norm, k_norm, mask, cos_t, sin_t, length, heads, head_dim,
+                   rotary_dim, eps, out=None):
+    """jeff_full_attention_into: q, k, v, gate (length, heads*head_dim) time-first."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v"), (gate, "gate")):
+        _cuda(t, torch.float32, n)
+    y = torch.empty_like(q) if out is None else out
+    check(lib.tfx_jeff_attention_f32(_ptr(q), _ptr(k), _ptr(v), _ptr(gate), _ptr(q_norm),
+                                     _ptr(k_norm), _ptr(mask), _ptr(cos_t), _ptr(sin_t), _ptr(y),
+                                     length, heads, head_dim, rotary_dim, ctypes.c_float(eps),
+                                     _stream(q)))
+    return y

@@ -131,6 +131,22 @@ CASES = [
         "excluded_values": [1.0, "nan", "inf"],
     },
     {
+        "name": "laya_attention_block_masked_nonfinite_and_empty_rows",
+        "source": "crates/cpu-kernels/src/lib.rs",
+        "lines": [1212, 1250],
+        "literals": ["let length = 65;", "let d = 4;",
+                     "qkv[3 * d * key + 2 * d + feature] = (feature + 1) as f32;",
+                     "keep[query + length * 32] = false;", "keep[length * key] = false;",
+                     "keep[length - 1 + length * key] = false;",
+                     "[1.0f32, f32::NAN, f32::INFINITY]",
+                     "laya_attention_block_into(&qkv, &keep, d, 1, length, 1, 0.0, &mut output);",
+                     "query == 0 || query == length - 1", "<= 1e-6"],
+        "length": 65, "hidden": 4, "heads": 1, "batch": 1, "rope_base": 0.0,
+        "masked_key": 32, "empty_queries": [0, 64],
+        "excluded_values": [1.0, "nan", "inf"],
+        "tolerance": {"abs": 1e-6},
+    },
+    {
         "name": "layer_norm_f64_primitive",
         "source": "crates/tenferro-infer/tests/primitives.rs",
         "lines": [33, 72],

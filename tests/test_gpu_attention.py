@@ -1,0 +1,195 @@
+"""GPU parity: attention prep (bitwise) and masked scaled dot-product attention.
+
+The prep kernels reproduce the cpu-kernels arithmetic exactly (rounded products,
+sequential per-token sums) and are compared bit for bit. The attention kernels
+use a different summation order (tiled dot products, online softmax, one
+division at the end) and are compared within the f32 tolerance."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from gpu_util import P, S, call, dev, empty, host
+from helpers import (assert_bitwise, assert_close, decode_value, golden_case, splitmix_normal,
+                     splitmix_uniform, F32_RTOL, F32_ATOL_REL)
+from tfx import _lib
+
+pytestmark = pytest.mark.gpu
+
+
+def keep_window(L, B, window, valid):
+    """keep[q + L*(k + L*b)] for |q - k| <= window and k < valid[b]."""
+    q = np.arange(L)[None, None, :]
+    k = np.arange(L)[None, :, None]
+    v = np.asarray(valid)[:, None, None]
+    m = (np.abs(q - k) <= window) & (k < v)
+    return np.ascontiguousarray(m.astype(np.uint8)).ravel()
+
+
+def gpu_laya_block(qkv, keep, hidden, heads, L, B, tables=None):
+    # Every device tensor stays referenced until the kernels have run: a
+    # temporary passed as P(dev(x)) would be freed (and its memory reused)
+    # before the call.
+    out = empty(hidden * L * B)
+    qd, kd = dev(qkv), dev(keep)
+    c = s = None
+    if tables is not None:
+        c, s = dev(tables[0]), dev(tables[1])
+    call("tfx_laya_attention_block_f32", P(qd), P(kd), P(c), P(s), P(out), hidden, heads, L, B,
+         S())
+    return host(out)
+
+
+@pytest.mark.parametrize("hd,heads,L,B,window,rope", [
+    (64, 4, 128, 2, 16, 10000.0), (64, 3, 200, 2, -1, 160000.0), (128, 2, 96, 2, 32, 10000.0),
+    (256, 1, 80, 2, -1, 10000.0), (48, 2, 70, 1, 8, 10000.0), (4, 2, 33, 2, -1, 0.0)])
+def test_laya_attention_block(orc, hd, heads, L, B, window, rope):
+    d = hd * heads
+    qkv = splitmix_normal(3 * d * L * B, 0x7E4F0A00 + hd + L)
+    valid = [L - 5 * b for b in range(B)]
+    keep = keep_window(L, B, window if window >= 0 else L, valid)
+    tables = orc.rope_tables_powf_f32(rope, L, hd) if rope else None
+    got = gpu_laya_block(qkv, keep, d, heads, L, B, tables)
+    want = orc.laya_attention_block_f32(qkv, keep, d, heads, L, B,
+                                         *(tables if tables is not None else (None, None)))
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"laya attention hd={hd} L={L}")
+
+
+@pytest.mark.parametrize("hd", [4, 64])
+def test_laya_attention_block_known_answer(orc, hd):
+    """crates/cpu-kernels/src/lib.rs:1212-1250 through the GPU (hd 4: the row
+    kernel; hd 64: the tiled kernel with its non-finite V guard): masked NaN /
+    inf never leak, rows without keys are NaN, the rest average v exactly."""
+    case = golden_case("laya_attention_block_masked_nonfinite_and_empty_rows")
+    L, key = case["length"], case["masked_key"]
+    keep = np.ones(L * L, np.uint8)
+    keep[np.arange(L) + L * key] = 0
+    keep[L * np.arange(L)] = 0
+    keep[L - 1 + L * np.arange(L)] = 0
+    for excluded in case["excluded_values"]:
+        qkv = np.zeros(3 * hd * L, np.float32)
+        for k in range(L):
+            qkv[3 * hd * k + 2 * hd:3 * hd * k + 3 * hd] = np.arange(1, hd + 1)
+        qkv[3 * hd * key + 2 * hd:3 * hd * key + 3 * hd] = decode_value(excluded)
+        out = gpu_laya_block(qkv, keep, hd, 1, L, 1).reshape(L, hd)
+        for q in range(L):
+            if q in case["empty_queries"]:
+                assert np.all(np.isnan(out[q])), q
+            else:
+                assert np.max(np.abs(out[q] - np.arange(1, hd + 1))) <= 1e-6 * hd, q
+        if hd == case["hidden"]:
+            want = orc.laya_attention_block_f32(qkv, keep, hd, 1, L, 1)
+            assert_close(out.ravel(), want, F32_RTOL, F32_ATOL_REL, "known answer vs oracle")
+
+
+@pytest.mark.parametrize("hd,heads,L,rope", [(64, 4, 96, 10000.0), (128, 2, 50, 0.0), (6, 3, 17, 10000.0)])
+def test_laya_qkv_prep_bitwise(orc, hd, heads, L, rope):
+    B = 3
+    d = hd * heads
+    qkv = splitmix_normal(3 * d * L * B, 0x7E4F0A10 + hd)
+    n = d * L * B
+    qh, kh, vh = empty(n), empty(n), empty(n)
+    if rope:
+        c, s = orc.rope_tables_powf_f32(rope, L, hd)
+        cd, sd = dev(c), dev(s)
+        cp, sp = P(cd), P(sd)
+    else:
+        c = s = None
+        cp = sp = None
+    xd = dev(qkv)
+    call("tfx_laya_qkv_prep_f32", P(xd), cp, sp, P(qh), P(kh), P(vh), d, heads, L, B, S())
+    want = orc.laya_qkv_prep_f32(qkv, d, heads, L, B, c, s)
+    for got, w, name in zip((qh, kh, vh), want, "qkv"):
+        assert_bitwise(host(got), w, f"laya prep {name}")
+
+
+@pytest.mark.parametrize("hd,rot,heads,L", [(64, 16, 4, 70), (256, 64, 2, 40), (20, 6, 3, 33),
+                                            (128, 0, 2, 32)])
+def test_jeff_qkv_prep_bitwise(orc, hd, rot, heads, L):
+    w = heads * hd
+    q, k, v = (splitmix_normal(L * w, 0x7E4F0A20 + i + hd) for i in range(3))
+    qn = splitmix_normal(hd, 0x7E4F0A28, std=0.1)
+    kn = splitmix_normal(hd, 0x7E4F0A29, std=0.1)
+    c, s = orc.rope_tables_powf_f32(1e6, L, rot) if rot else (np.zeros(1, np.float32),) * 2
+    n = L * w
+    qh, kh, vh = empty(n), empty(n), empty(n)
+    ins = [dev(t) for t in (q, k, v, qn, kn, c, s)]
+    call("tfx_jeff_qkv_prep_f32", *[P(t) for t in ins], P(qh), P(kh), P(vh), L, heads, hd, rot,
+         ctypes.c_float(1e-6), S())
+    want = orc.jeff_qkv_prep_f32(q, k, v, qn, kn, c if rot else None, s if rot else None, L, heads,
+                                 hd, rot, 1e-6)
+    for got, wv, name in zip((qh, kh, vh), want, "qkv"):
+        assert_bitwise(host(got), wv, f"jeff prep {name}")
+
+
+@pytest.mark.parametrize("hd,rot,heads,L", [(64, 16, 4, 130), (256, 64, 2, 72), (20, 6, 2, 31)])
+def test_jeff_attention(orc, hd, rot, heads, L):
+    w = heads * hd
+    theta, eps = 1e7, 1e-6
+    q, k, v, g = (splitmix_normal(L * w, 0x7E4F0A30 + i + hd) for i in range(4))
+    qn = splitmix_normal(hd, 0x7E4F0A38, std=0.1)
+    kn = splitmix_normal(hd, 0x7E4F0A39, std=0.1)
+    mask = (splitmix_uniform(L, 0x7E4F0A3A, 0.0, 1.0) > 0.2).astype(np.float32)
+    mask[0] = 0.0  # query 0 sees no key: its row is 0
+    c, s = orc.rope_tables_powf_f32(theta, L, rot)
+    out = empty(L * w)
+    ins = [dev(t) for t in (q, k, v, g, qn, kn, mask, c, s)]
+    call("tfx_jeff_attention_f32", *[P(t) for t in ins], P(out), L, heads, hd, rot,
+         ctypes.c_float(eps), S())
+    got = host(out)
+    want = orc.jeff_full_attention_f32(q, k, v, g, qn, kn, mask, L, heads, hd, rot, theta, eps)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"jeff attention hd={hd}")
+    assert np.all(got.reshape(w, L)[:, 0] == 0.0)
+
+
+def attention_f64(qh, kh, vh, B, H, L, hd, scale, bias=None, causal=False, active=None):
+    """Double-precision restatement of the additive-bias path (fused.cu:239-306)."""
+    q = qh.reshape(B, H, L, hd).astype(np.float64)
+    k = kh.reshape(B, H, L, hd).astype(np.float64)
+    v = vh.reshape(B, H, L, hd).astype(np.float64)
+    s = np.einsum("bhqd,bhkd->bhqk", q, k) * scale
+    keep = np.ones((B, 1, L, L), bool)
+    if bias is not None:
+        s = s + bias.reshape(B, L, L).transpose(0, 2, 1)[:, None]  # [b][k][q] -> [b][q][k]
+    if causal:
+        keep &= np.tril(np.ones((L, L), bool))[None, None]
+    if active is not None:
+        keep &= (active.reshape(B, 1, 1, L) != 0)
+    s = np.where(keep, s, -np.inf)
+    m = s.max(-1, keepdims=True)
+    p = np.exp(s - m)
+    p = p / p.sum(-1, keepdims=True)
+    return np.einsum("bhqk,bhkd->bhqd", p, v)
+
+
+@pytest.mark.parametrize("hd", [64, 128, 40])
+def test_attention_core_bias_active_causal(hd):
+    """The CUDA twin's form: additive (L, L, B) bias, active key mask, causal,
+    output (d, L, B) -- against a float64 restatement."""
+    B, H, L = 2, 3, 100
+    n = B * H * L * hd
+    qh, kh, vh = (splitmix_normal(n, 0x7E4F0A40 + i) for i in range(3))
+    bias = splitmix_normal(L * L * B, 0x7E4F0A44, std=0.5)
+    active = (splitmix_uniform(B * L, 0x7E4F0A45, 0.0, 1.0) > 0.1).astype(np.float32)
+    active[0] = 1.0
+    active[L] = 1.0
+    d = _lib.AttentionDesc()
+    _lib.lib.tfx_attention_desc_init(ctypes.byref(d), B, H, L, hd)
+    bd, ad = dev(bias), dev(active)
+    d.bias, d.active, d.causal = bd.data_ptr(), ad.data_ptr(), 1
+    out = empty(n)
+    ins = [dev(t) for t in (qh, kh, vh)]
+    call("tfx_attention_f32", *[P(t) for t in ins], P(out), ctypes.byref(d), S())
+    got = host(out).reshape(B, L, H, hd)  # (d, L, B) with d = H*hd fastest
+    want = attention_f64(qh, kh, vh, B, H, L, hd, 1.0 / np.sqrt(np.float32(hd)), bias, True, active)
+    want = want.transpose(0, 2, 1, 3).astype(np.float32)  # (B, L, H, hd)
+    assert_close(got.ravel(), want.ravel(), 2e-5, F32_ATOL_REL, f"attention core hd={hd}")
+
+
+def test_attention_rejects_bad_arguments():
+    d = _lib.AttentionDesc()
+    _lib.lib.tfx_attention_desc_init(ctypes.byref(d), 1, 1, 8, 8)
+    d.empty_rows = 7
+    rc = _lib.lib.tfx_attention_f32(None, None, None, None, ctypes.byref(d), None)
+    assert rc == -1 and b"empty_rows" in _lib.lib.tfx_last_error_string()

@@ -257,3 +257,66 @@ def test_rust_semantics_helpers(orc):
     assert orc.expm1_mlx_f32(-100.0) == -1.0
     assert abs(orc.expm1_mlx_f32(-1.0) - math.expm1(-1.0)) < 1e-6
     assert np.float32(0.70710678118654752440).view(np.uint32) == 0x3F3504F3
+
+
+def laya_known_answer_inputs(case, excluded):
+    """Inputs of crates/cpu-kernels/src/lib.rs:1212-1250: q = k = 0, v = feature + 1,
+    key 32 masked for every query (its v holds `excluded`), queries 0 and
+    length - 1 see no key."""
+    L, d = case["length"], case["hidden"]
+    qkv = np.zeros(3 * d * L, np.float32)
+    for key in range(L):
+        for f in range(d):
+            qkv[3 * d * key + 2 * d + f] = f + 1
+    keep = np.ones(L * L, np.uint8)  # keep[query + L * key]
+    for q in range(L):
+        keep[q + L * case["masked_key"]] = 0
+    for key in range(L):
+        keep[L * key] = 0
+        keep[L - 1 + L * key] = 0
+    for f in range(d):
+        qkv[3 * d * case["masked_key"] + 2 * d + f] = decode_value(excluded)
+    return qkv, keep
+
+
+def test_laya_attention_block_known_answer(orc):
+    """The reference's own test of laya_attention_block_into (lib.rs:1212-1250):
+    masked NaN / inf values never leak, rows without keys are NaN, every other
+    row averages v = feature + 1 exactly (within 1e-6)."""
+    case = golden_case("laya_attention_block_masked_nonfinite_and_empty_rows")
+    L, d = case["length"], case["hidden"]
+    for excluded in case["excluded_values"]:
+        qkv, keep = laya_known_answer_inputs(case, excluded)
+        out = orc.laya_attention_block_f32(qkv, keep, d, 1, L, 1).reshape(L, d)
+        for q in range(L):
+            if q in case["empty_queries"]:
+                assert np.all(np.isnan(out[q]))
+            else:
+                assert np.max(np.abs(out[q] - np.arange(1, d + 1))) <= case["tolerance"]["abs"]
+
+
+def test_attention_prep_restatements_agree(orc):
+    """The Laya block is split + RoPE + the shared head attention: its prep output
+    rotated by the cpu-kernels f32 tables equals a direct pair rotation, and the
+    Jeff prep normalises every head row to mean square 1 / (1 + w)^2 scaling."""
+    rng = np.random.default_rng(3)
+    L, B, H, hd = 9, 2, 3, 8
+    d = H * hd
+    qkv = rng.standard_normal(3 * d * L * B).astype(np.float32)
+    c, s = orc.rope_tables_powf_f32(10000.0, L, hd)
+    qh, kh, vh = orc.laya_qkv_prep_f32(qkv, d, H, L, B, c, s)
+    x = qkv.reshape(B, L, 3, H, hd)
+    q = x[:, :, 0].transpose(0, 2, 1, 3)  # (B, H, L, hd)
+    half = hd // 2
+    cc, ss = c.reshape(L, half), s.reshape(L, half)
+    a, b2 = q[..., :half], q[..., half:]
+    want = np.concatenate([a * cc - b2 * ss, a * ss + b2 * cc], axis=-1).astype(np.float32)
+    assert np.max(np.abs(qh.reshape(B, H, L, hd) - want)) < 1e-6
+    assert_bitwise(vh.reshape(B, H, L, hd), x[:, :, 2].transpose(0, 2, 1, 3).copy(), "v copy")
+    # Jeff: rotary 0 -> pure centred RMSNorm; with w = 0 the mean square is 1.
+    Lj, Hj, hdj = 7, 2, 16
+    qj = rng.standard_normal(Lj * Hj * hdj).astype(np.float32)
+    w0 = np.zeros(hdj, np.float32)
+    qhj, _, _ = orc.jeff_qkv_prep_f32(qj, qj, qj, w0, w0, None, None, Lj, Hj, hdj, 0, 1e-6)
+    ms = (qhj.reshape(Hj, Lj, hdj).astype(np.float64) ** 2).mean(-1)
+    assert np.max(np.abs(ms - 1.0)) < 1e-5
