@@ -401,6 +401,23 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
             lambda b: ops.rope_pairhalf(b[0], cos_t, sin_t, 2 * c["heads"], Lc, Bc, hd, hd,
                                         (hd, 3 * h, 3 * h * Lc, 1), out=b[1]),
             2 * (2 * h * Lc * Bc * 4), 2 * h * Lc * Bc)
+    # the chain's residual add fused into the LayerNorm after it (768 x 32768):
+    # a, b read once, the sum and y written once
+    dr, Tr = CHAIN["hidden"], CHAIN["batch"] * CHAIN["seq"]
+    wr2 = torch.rand(dr, generator=gen, device=device) + 0.5
+    measure("add_layernorm", lambda: (normal(dr * Tr), normal(dr * Tr), torch.empty(dr * Tr, device=device),
+                                      torch.empty(dr * Tr, device=device)),
+            lambda b: ops.add_layer_norm_feature_first(b[0], b[1], wr2, None, 1e-5, sum_out=b[2],
+                                                       out=b[3]),
+            4 * dr * Tr * 4 + dr * 4, dr * Tr)
+    # token embedding gather, columns layout (each token's vector contiguous):
+    # 32768 tokens of 768 from a 50368-entry table (ModernBERT's vocabulary)
+    Ve = 50368
+    table_e = normal(dr * Ve)
+    ids_e = torch.randint(0, Ve, (Tr,), generator=gen, device=device)
+    measure("embedding_columns", lambda: (torch.empty(dr * Tr, device=device),),
+            lambda b: ops.embedding_gather(table_e, ids_e, dr, Ve, Tr, 1, out=b[0]),
+            2 * dr * Tr * 4 + Tr * 8, dr * Tr)
     # the Laya attention block (split + RoPE + masked attention) on configs[3]'s
     # attention shape: batch 8, 12 heads, 512 tokens, head_dim 64; keep mask of
     # the sliding-window (128) layers and of the global layers, 37 padded keys
@@ -731,7 +748,8 @@ def main():
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
                          "masked_softmax_global, rope_qk, laya_attention_window, "
-                         "laya_attention_global, bias_add) and "
+                         "laya_attention_global, add_layernorm, embedding_columns, "
+                         "bias_add) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
     args = ap.parse_args()

@@ -223,6 +223,44 @@ TFX_API int tfx_rope_pairhalf_f32(const float* x, float* y, const float* cos_tab
 TFX_API int tfx_rope_tables_f32(double base, int64_t seq, int64_t rotary_dim, float* cos_host,
                         float* sin_host);
 
+/* ---- residual add fused into LayerNorm ------------------------------------------
+ * The chain's residual add followed by a feature-first LayerNorm as one pass
+ * (the "residual-add + LayerNorm" epilogue fusion; the reference runs the two
+ * ops separately, laya-infer's residual add then LayerNormFeatureFirstOp,
+ * crates/tenferro-ext/src/layernorm.rs:33-231). s = a + b (each sum rounded),
+ * y = LayerNorm(s) with tfx_layernorm_ff_f32's arithmetic: bit-identical to
+ * tfx_add_f32 then tfx_layernorm_ff_f32. s is written to sum_out when it is
+ * non-NULL (the residual stream the next layer needs). sum_out and y may each
+ * equal a or b exactly but not overlap them partially or each other. */
+TFX_API int tfx_add_layernorm_ff_f32(const float* a, const float* b, const float* weight,
+                                     const float* bias, float* sum_out, float* y, int64_t d,
+                                     int64_t cols, float eps, tfx_stream_t stream);
+
+/* ---- token embedding gather ------------------------------------------------------
+ * FusedScope::embedding_rows / embedding_columns (crates/tenferro-ext/src/
+ * cuda_fused.rs:817-898; kernel fused.cu:304-318): out(token t, feature f) =
+ * table(feature f, ids[t]).
+ *   TFX_EMBED_ROWS:    table row-major (hidden, vocab), element (f, id) at
+ *                      f*vocab + id; out time-first (length, hidden), (t, f) at
+ *                      t + length*f.
+ *   TFX_EMBED_COLUMNS: table column-major (hidden, vocab), element (f, id) at
+ *                      f + hidden*id; out feature-first (hidden, length), (f, t)
+ *                      at f + hidden*t.
+ * tfx_embedding_f32 takes the ids on the host, as the reference does, rejects
+ * any id outside [0, vocab) before launching (TFX_ERR_INVALID_ARGUMENT naming
+ * the first), and copies them into a stream-ordered scratch buffer.
+ * tfx_embedding_gather_f32 takes device ids and cannot validate them before
+ * launching: an out-of-range id yields a NaN vector (no memory is read out of
+ * bounds). */
+#define TFX_EMBED_ROWS 0
+#define TFX_EMBED_COLUMNS 1
+TFX_API int tfx_embedding_f32(const float* table, const int64_t* ids_host, float* out,
+                              int64_t hidden, int64_t vocab, int64_t length, int32_t layout,
+                              tfx_stream_t stream);
+TFX_API int tfx_embedding_gather_f32(const float* table, const int64_t* ids_device, float* out,
+                                     int64_t hidden, int64_t vocab, int64_t length,
+                                     int32_t layout, tfx_stream_t stream);
+
 /* ---- attention blocks -------------------------------------------------------
  * The attention cores of the two forwards, mirroring the reference's CUDA
  * path (FusedScope::laya_attention / jeff_attention, crates/tenferro-ext/src/

@@ -734,6 +734,18 @@ void orc_jeff_full_attention_f32(const float* q, const float* k, const float* v,
 }
 
 // ---------------------------------------------------------------------------
+// Token embedding gather, crates/tenferro-ext/src/cuda/fused.cu:304-318 with
+// the strides FusedScope passes (cuda_fused.rs:821-863).
+// ---------------------------------------------------------------------------
+void orc_embedding_f32(const float* table, const int64_t* ids, float* out, int64_t hidden,
+                       int64_t length, int64_t o_tok, int64_t o_feat, int64_t t_feat,
+                       int64_t t_tok) {
+  for (int64_t f = 0; f < hidden; ++f)
+    for (int64_t t = 0; t < length; ++t)
+      out[t * o_tok + f * o_feat] = table[f * t_feat + ids[t] * t_tok];
+}
+
+// ---------------------------------------------------------------------------
 // crates/tenferro-ext/src/lib.rs:273-285 -- erf_f64, Abramowitz-Stegun 7.1.26.
 // ---------------------------------------------------------------------------
 double orc_erf_f64(double x) {

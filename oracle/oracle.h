@@ -125,6 +125,13 @@ void orc_jeff_full_attention_f32(const float* q, const float* k, const float* v,
                                  int64_t head_dim, int64_t rotary_dim, float theta, float eps,
                                  float* out);
 
+/* Token embedding gather (fused.cu:304-318): out(t, f) = table(f, ids[t]) with
+ * table element (f, id) at f*t_feat + id*t_tok and out element (t, f) at
+ * t*o_tok + f*o_feat (ids already validated). */
+void orc_embedding_f32(const float* table, const int64_t* ids, float* out, int64_t hidden,
+                       int64_t length, int64_t o_tok, int64_t o_feat, int64_t t_feat,
+                       int64_t t_tok);
+
 /* ---- f64 composites (tenferro-infer, tenferro-ext lib.rs) ---------- */
 double orc_erf_f64(double x);                                   /* tenferro-ext lib.rs:273-285 */
 void orc_erf_f64_n(const double* x, double* y, int64_t n);

@@ -89,6 +89,8 @@ def _declare(L: ctypes.CDLL) -> None:
         "orc_jeff_full_attention_f32": (None, [
             _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64,
             ctypes.c_float, ctypes.c_float, _f32p]),
+        "orc_embedding_f32": (None, [_f32p, ctypes.POINTER(ctypes.c_int64), _f32p, _i64, _i64,
+                                     _i64, _i64, _i64, _i64]),
         "orc_erf_f64": (ctypes.c_double, [ctypes.c_double]),
         "orc_erf_f64_n": (None, [_f64p, _f64p, _i64]),
         "orc_gelu_erf_f64_n": (None, [_f64p, _f64p, _i64]),
@@ -293,6 +295,18 @@ def jeff_full_attention_f32(q, k, v, gate, q_norm, k_norm, mask, length, heads, 
     lib().orc_jeff_full_attention_f32(
         _p32(q), _p32(k), _p32(v), _p32(gate), _p32(q_norm), _p32(k_norm), _p32(mask), length,
         heads, head_dim, rotary_dim, ctypes.c_float(theta), ctypes.c_float(eps), _p32(out))
+    return out
+
+
+def embedding_f32(table, ids, hidden, vocab, layout):
+    """layout 0 (rows): table (hidden, vocab) row-major -> out (length, hidden)
+    time-first; layout 1 (columns): table column-major -> out (hidden, length)."""
+    length = ids.size
+    ids = np.ascontiguousarray(ids, dtype=np.int64)
+    out = np.empty(hidden * length, np.float32)
+    strides = (1, length, vocab, 1) if layout == 0 else (hidden, 1, 1, hidden)
+    lib().orc_embedding_f32(_p32(table), ids.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                            _p32(out), hidden, length, *strides)
     return out
 
 

@@ -272,6 +272,95 @@ __global__ void __launch_bounds__(256, 8) ln_smem_kernel(const float* __restrict
   }
 }
 
+// ---- residual add fused into the LayerNorm that follows it ----------------------------
+//
+// s = a + b per element, then ln_smem_kernel's arithmetic on s (same order of
+// every rounding), so y is bit-identical to tfx_add_f32 followed by
+// tfx_layernorm_ff_f32; s is also written when SUM. Both inputs are staged
+// with cp.async (two column slices per warp), so the sum never round-trips
+// through HBM before the normalisation reads it.
+template <int NV, bool BIAS, bool SUM>
+__global__ void __launch_bounds__(256, 4) add_ln_smem_kernel(
+    const float* __restrict__ a, const float* __restrict__ bsrc, const float* __restrict__ w,
+    const float* __restrict__ b, float* sum_out, float* y, uint32_t d, uint64_t cols, float eps) {
+  pdl_enter();
+  extern __shared__ float4 stage[];  // 8 warps x 2 x d floats
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t col = uint64_t(blockIdx.x) * 8 + warp;
+  if (col >= cols) return;  // the whole warp leaves together
+  const uint32_t dv = d / 4;
+  float4* sx = stage + warp * 2 * dv;
+  float4* sb = sx + dv;
+  const float4* ac = reinterpret_cast<const float4*>(a + col * d);
+  const float4* bc = reinterpret_cast<const float4*>(bsrc + col * d);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      cp_async16(sx + q, ac + q);
+      cp_async16(sb + q, bc + q);
+    }
+  }
+  cp_async_wait_all();
+  __syncwarp();
+  float4* sc = reinterpret_cast<float4*>(sum_out + col * d);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 u = sx[q], t = sb[q];
+      const float4 v = make_float4(__fadd_rn(u.x, t.x), __fadd_rn(u.y, t.y), __fadd_rn(u.z, t.z),
+                                   __fadd_rn(u.w, t.w));
+      sx[q] = v;
+      if constexpr (SUM) sc[q] = v;
+      s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v.x), v.y), v.z), v.w);
+    }
+  }
+  s = warp_sum(s);
+  const float dd = float(d);
+  const float mean = __fdiv_rn(s, dd);
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 v = sx[q];
+      const float cx = __fsub_rn(v.x, mean), cy = __fsub_rn(v.y, mean);
+      const float cz = __fsub_rn(v.z, mean), cw = __fsub_rn(v.w, mean);
+      ss = __fadd_rn(ss, __fmul_rn(cx, cx));
+      ss = __fadd_rn(ss, __fmul_rn(cy, cy));
+      ss = __fadd_rn(ss, __fmul_rn(cz, cz));
+      ss = __fadd_rn(ss, __fmul_rn(cw, cw));
+    }
+  }
+  ss = warp_sum(ss);
+  const float var = __fdiv_rn(ss, dd);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  float4* yc = reinterpret_cast<float4*>(y + col * d);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      const float4 v = sx[q];
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w) + q);
+      float4 o;
+      o.x = __fmul_rn(__fmul_rn(__fsub_rn(v.x, mean), inv), wv.x);
+      o.y = __fmul_rn(__fmul_rn(__fsub_rn(v.y, mean), inv), wv.y);
+      o.z = __fmul_rn(__fmul_rn(__fsub_rn(v.z, mean), inv), wv.z);
+      o.w = __fmul_rn(__fmul_rn(__fsub_rn(v.w, mean), inv), wv.w);
+      if constexpr (BIAS) {
+        const float4 bv = __ldg(reinterpret_cast<const float4*>(b) + q);
+        o.x = __fadd_rn(o.x, bv.x);
+        o.y = __fadd_rn(o.y, bv.y);
+        o.z = __fadd_rn(o.z, bv.z);
+        o.w = __fadd_rn(o.w, bv.w);
+      }
+      yc[q] = o;
+    }
+  }
+}
+
 // ---- LayerNorm: one CTA (256 threads) per column, column in registers --------------
 
 template <typename T>
@@ -932,6 +1021,83 @@ int tfx_layernorm_ff_f32(const float* x, const float* weight, const float* bias,
                          int64_t d, int64_t cols, float eps, tfx_stream_t stream) {
   return tfx::layernorm_ff<float>("tenferro-ext::layernorm_ff", x, weight, bias, y, d, cols, eps,
                                   stream);
+}
+
+int tfx_add_layernorm_ff_f32(const float* a, const float* b, const float* weight,
+                             const float* bias, float* sum_out, float* y, int64_t d, int64_t cols,
+                             float eps, tfx_stream_t stream) {
+  using namespace tfx;
+  clear_error();
+  const char* op = "tenferro-ext::add_layernorm_ff";
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TFX_REQUIRE(d >= 0 && cols >= 0, op, "shape", "extents must be non-negative");
+  if (d == 0 || cols == 0) return TFX_OK;
+  TFX_REQUIRE(a && b && weight && y, op, a ? (b ? (weight ? "y" : "weight") : "b") : "a",
+              "null pointer");
+  const size_t bytes = size_t(d) * size_t(cols) * 4;
+  auto ok_alias = [&](const void* p, const void* q) { return p == q || !overlaps(p, bytes, q, bytes); };
+  TFX_REQUIRE(ok_alias(a, y) && ok_alias(b, y), op, "y", "partially overlaps an input");
+  TFX_REQUIRE(!sum_out || (ok_alias(a, sum_out) && ok_alias(b, sum_out) &&
+                           !overlaps(sum_out, bytes, y, bytes)),
+              op, "sum_out", "overlaps y or partially overlaps an input");
+  TFX_REQUIRE(!overlaps(weight, size_t(d) * 4, y, bytes) &&
+                  (!sum_out || !overlaps(weight, size_t(d) * 4, sum_out, bytes)),
+              op, "weight", "overlaps an output");
+  int st = TFX_OK;
+  device_info(&st);
+  if (st != TFX_OK) return st;
+  const bool vec = d % 4 == 0 && aligned(a, 16) && aligned(b, 16) && aligned(y, 16) &&
+                   aligned(weight, 16) && (!bias || aligned(bias, 16)) &&
+                   (!sum_out || aligned(sum_out, 16));
+  const int64_t dv = d / 4;
+  static const bool use_regs = [] {
+    const char* e = getenv("TFX_LN_KERNEL");
+    return e && std::string(e) == "regs";
+  }();
+  if (vec && dv <= 32 * 6 && !use_regs && cols / 8 < (int64_t(1) << 31)) {
+    const unsigned grid = unsigned((cols + 7) / 8);
+    const uint32_t du = uint32_t(d);
+    const size_t smem = size_t(8) * 2 * size_t(d) * 4;
+    float* so = sum_out ? sum_out : y;  // unused when SUM is false
+#define TFX_ADD_LN(NVV, B, S)                                                                  \
+  {                                                                                            \
+    auto k = add_ln_smem_kernel<NVV, B, S>;                                                    \
+    if (smem > 48 * 1024) {                                                                    \
+      const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                                 int(smem));                                   \
+      if (e != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e));    \
+    }                                                                                          \
+    return launch_kernel(op, k, dim3(grid), dim3(256), smem, s, 1, a, b, weight, bias, so, y, \
+                         du, uint64_t(cols), eps);                                             \
+  }
+#define TFX_ADD_LN_NV(NVV)                                                \
+  if (dv <= 32 * NVV) {                                                   \
+    if (bias) {                                                           \
+      if (sum_out) TFX_ADD_LN(NVV, true, true) else TFX_ADD_LN(NVV, true, false)   \
+    } else {                                                              \
+      if (sum_out) TFX_ADD_LN(NVV, false, true) else TFX_ADD_LN(NVV, false, false) \
+    }                                                                     \
+  }
+    TFX_ADD_LN_NV(1)
+    TFX_ADD_LN_NV(2)
+    TFX_ADD_LN_NV(3)
+    TFX_ADD_LN_NV(4)
+    TFX_ADD_LN_NV(6)
+#undef TFX_ADD_LN_NV
+#undef TFX_ADD_LN
+  }
+  // Other shapes: the two ops back to back (identical results by construction).
+  float* tmp = sum_out;
+  if (!tmp) {
+    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), bytes, s) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(TFX_ERR_CUDA, op, "scratch", "cannot allocate the sum");
+    }
+  }
+  int rc = tfx_add_f32(a, b, tmp, d * cols, stream);
+  if (rc == TFX_OK) rc = tfx_layernorm_ff_f32(tmp, weight, bias, y, d, cols, eps, stream);
+  if (!sum_out) cudaFreeAsync(tmp, s);
+  return rc;
 }
 
 int tfx_layernorm_ff_f64(const double* x, const double* weight, const double* bias, double* y,

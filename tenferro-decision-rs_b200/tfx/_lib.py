@@ -97,6 +97,9 @@ SIGNATURES = {
     "tfx_rope_pairhalf_f32": (_int, [_p, _p, _p, _p, ctypes.POINTER(RopeDesc), _p]),
     "tfx_rope_tables_f32": (_int, [ctypes.c_double, _i64, _i64, _p, _p]),
     "tfx_rope_tables_powf_f32": (_int, [_f32, _i64, _i64, _p, _p]),
+    "tfx_add_layernorm_ff_f32": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _f32, _p]),
+    "tfx_embedding_f32": (_int, [_p, _p, _p, _i64, _i64, _i64, ctypes.c_int32, _p]),
+    "tfx_embedding_gather_f32": (_int, [_p, _p, _p, _i64, _i64, _i64, ctypes.c_int32, _p]),
     "tfx_laya_qkv_prep_f32": (_int, [_p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "tfx_jeff_qkv_prep_f32": (_int, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64,
                                      _i64, _f32, _p]),

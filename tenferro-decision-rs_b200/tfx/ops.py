@@ -223,3 +223,26 @@ def jeff_attention(q, k, v, gate, q_norm, k_norm, mask, cos_t, sin_t, length, he
                                      length, heads, head_dim, rotary_dim, ctypes.c_float(eps),
                                      _stream(q)))
     return y
+
+
+def add_layer_norm_feature_first(a, b, weight, bias=None, eps=1e-5, sum_out=None, out=None):
+    """s = a + b and LayerNorm(s) in one pass (feature-first (d, cols)); returns
+    (s or None, y). Bit-identical to add() then layer_norm_feature_first()."""
+    _cuda(a, torch.float32, "a")
+    _cuda(b, torch.float32, "b")
+    d = weight.numel()
+    y = torch.empty_like(a) if out is None else out
+    check(lib.tfx_add_layernorm_ff_f32(_ptr(a), _ptr(b), _ptr(weight), _ptr(bias), _ptr(sum_out),
+                                       _ptr(y), d, a.numel() // d, ctypes.c_float(eps),
+                                       _stream(a)))
+    return sum_out, y
+
+
+def embedding_gather(table, ids, hidden, vocab, length, layout, out=None):
+    """Gather with device int64 ids; layout 0 rows (time-first out), 1 columns
+    (feature-first out)."""
+    _cuda(table, torch.float32, "table")
+    y = torch.empty(hidden * length, device=table.device) if out is None else out
+    check(lib.tfx_embedding_gather_f32(_ptr(table), _ptr(ids), _ptr(y), hidden, vocab, length,
+                                       layout, _stream(table)))
+    return y
