@@ -66,7 +66,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }  // namespace
 
 bool encode_map_2d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
-                       uint64_t stride1, uint32_t box0, uint32_t box1, std::string* why) {
+                       uint64_t stride1, uint32_t box0, uint32_t box1, std::string* why,
+                       bool swizzle128) {
   const auto fn = encode_fn();
   if (!fn) {
     *why = "cuTensorMapEncodeTiled is not available from the driver";
@@ -78,7 +79,8 @@ bool encode_map_2d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     *why = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(r));
@@ -170,7 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   for (uint32_t k = 0; k < n_my; ++k) {
     const uint32_t s = k % a.stages, par = k & 1;
-    const bool ok = mbar_wait_bounded(&full[s], (k / a.stages) & 1, kWaitCycles);
+    // one thread polls (bounded), the rest wait in the CTA barrier
+    const bool ok = tid != 0 || mbar_wait_bounded(&full[s], (k / a.stages) & 1, kWaitCycles);
     const bool failed = __syncthreads_or(!ok);
     if (failed && tid == 0) atomicAdd(&g_wait_timeouts, 1u);
     const float* t = tiles_s + size_t(s) * stage_floats + 4 * q;
