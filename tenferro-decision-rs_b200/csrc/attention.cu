@@ -720,25 +720,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
   tc_fence_after();
   const uint32_t tm = tmem_base;
   const uint32_t lane_off = (warp & 3) * 32 << 16;
-  const uint32_t tS = tm, tO = tm + 128, tPh = tm + 256, tPl = tm + 384;
+  // TMEM: two S buffers (the P hi of a block is written over its own S), O,
+  // P lo. The S MMA of block j+1 runs while the softmax of block j does, and
+  // the PV MMA of block j while the first pass of block j+1 does.
+  const uint32_t tS0 = tm, tO = tm + 256, tPl = tm + 384;
   const int64_t kb_first = lo / kTK * kTK;
+  const uint32_t nblk = kb_first < hi ? uint32_t((hi - kb_first + kTK - 1) / kTK) : 0;
+
+  // issued / waited phases of bar_k, bar_s, bar_o (at most one outstanding
+  // each); after a give-up the outstanding ones are waited for again
+  uint32_t k_iss = 0, k_wt = 0, s_iss = 0, s_wt = 0, o_iss = 0, o_wt = 0;
+  auto issue_k = [&](int64_t kb) {
+    if (tid == 0) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(&bar_k, 2 * kRegion);
+      tma_load_2d(khi, &kmap, &bar_k, 0, int(row0 + kb));
+      tma_load_2d(khi + kRegion, &kmap, &bar_k, 32, int(row0 + kb));
+    }
+    ++k_iss;
+  };
+  const uint32_t id_s = idesc_tf32(128, 128), id_o = idesc_tf32(128, 64);
+  // wait for K(j), split it, issue S(j) into buffer j & 1
+  auto issue_s = [&](uint32_t j) -> bool {
+    if (cta_wait(&bar_k, k_wt & 1)) return false;
+    ++k_wt;
+    split_tile(khi, klo, tid);
+    fence_proxy_async_smem();  // generic writes read by the MMA (async proxy)
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t dst = tS0 + (j & 1) * 128;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (ks >> 2) * kRegion + (ks & 3) * 32;
+        const uint64_t ah = smem_desc_sw128(smem_addr(qhi + off));
+        const uint64_t al = smem_desc_sw128(smem_addr(qlo + off));
+        const uint64_t bhd = smem_desc_sw128(smem_addr(khi + off));
+        const uint64_t bl = smem_desc_sw128(smem_addr(klo + off));
+        mma_tf32_ss(dst, ah, bhd, id_s, ks > 0);
+        mma_tf32_ss(dst, ah, bl, id_s, 1);
+        mma_tf32_ss(dst, al, bhd, id_s, 1);
+      }
+      mma_commit(&bar_s);
+    }
+    ++s_iss;
+    return true;
+  };
 
   if (tid == 0) {
     mbar_arrive_expect_tx(&bar_q, 2 * kRegion);
     tma_load_2d(qhi, &qmap, &bar_q, 0, int(row0 + q0));
     tma_load_2d(qhi + kRegion, &qmap, &bar_q, 32, int(row0 + q0));
-    if (kb_first < hi) {
-      mbar_arrive_expect_tx(&bar_k, 2 * kRegion);
-      tma_load_2d(khi, &kmap, &bar_k, 0, int(row0 + kb_first));
-      tma_load_2d(khi + kRegion, &kmap, &bar_k, 32, int(row0 + kb_first));
-    }
   }
-  // pending: barriers whose phase an issued copy / MMA will still complete
-  // (bit 0 q, 1 k, 2 s, 3 o); after a give-up they are waited for again.
-  uint32_t pending = kb_first < hi ? 3u : 1u;
+  if (nblk > 0) issue_k(kb_first);
+  bool q_pending = true;
   bool failed = cta_wait(&bar_q, 0);
   if (!failed) {
-    pending &= ~1u;
+    q_pending = false;
     split_tile(qhi, qlo, tid);
   }
 
@@ -755,12 +794,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
   if (r_hi < r_lo) r_hi = r_lo;
   constexpr float kLog2e = 1.44269504088896341f;
   float m = -INFINITY, l = 0.0f;  // running max (natural units) and sum
-  bool inf_row = false, have_o = false;
-  uint32_t it = 0;
-  const uint32_t id_s = idesc_tf32(128, 128), id_o = idesc_tf32(128, 64);
+  bool inf_row = false;
   const uint32_t vk = tid & 127, vc0 = (tid >> 7) * 16;  // V staging: key, first channel
   float vreg[16];
-  auto load_v = [&](int64_t kb) {  // next V block into registers
+  auto load_v = [&](int64_t kb) {  // a V block into registers
     const int64_t key = kb + vk;
     if (key < hi && key >= lo) {
       const float4* src = reinterpret_cast<const float4*>(a.v + (row0 + key) * 64 + vc0);
@@ -774,42 +811,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
       for (int j = 0; j < 16; ++j) vreg[j] = 0.0f;
     }
   };
-  if (kb_first < hi) load_v(kb_first);
-  for (int64_t kb0 = kb_first; kb0 < hi && !failed; kb0 += kTK, ++it) {
-    {  // V block (in registers) -> transposed (row = channel, K = key), split
-      const uint32_t reg = (vk >> 5) * kVtRegion;
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const uint32_t off = reg + sw128_offset(vc0 + n, vk & 31);
-        const float h = tf32_round_finite(vreg[n]);
-        *reinterpret_cast<float*>(vthi + off) = h;
-        *reinterpret_cast<float*>(vtlo + off) = __fsub_rn(vreg[n], h);
-      }
-    }
-    failed = cta_wait(&bar_k, it & 1);
-    if (failed) break;
-    pending &= ~2u;
-    split_tile(khi, klo, tid);
-    fence_proxy_async_smem();  // these generic writes are read by the MMA (async proxy)
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * kRegion + (ks & 3) * 32;
-        const uint64_t ah = smem_desc_sw128(smem_addr(qhi + off));
-        const uint64_t al = smem_desc_sw128(smem_addr(qlo + off));
-        const uint64_t bhd = smem_desc_sw128(smem_addr(khi + off));
-        const uint64_t bl = smem_desc_sw128(smem_addr(klo + off));
-        mma_tf32_ss(tS, ah, bhd, id_s, ks > 0);
-        mma_tf32_ss(tS, ah, bl, id_s, 1);
-        mma_tf32_ss(tS, al, bhd, id_s, 1);
-      }
-      mma_commit(&bar_s);
-    }
-    pending |= 4u;
-    // the block's keep words travel while the MMA runs
+  if (!failed && nblk > 0) {
+    load_v(kb_first);
+    failed = !issue_s(0);
+  }
+
+  for (uint32_t j = 0; j < nblk && !failed; ++j) {
+    const int64_t kb0 = kb_first + int64_t(j) * kTK;
+    const uint32_t tSj = tS0 + (j & 1) * 128;
+    // keep words of a partial block travel while S(j) finishes
     const bool keep_full = !KEEP || (kb0 / 128 < 64 && ((full_bits >> (kb0 / 128)) & 1));
     uint4 kw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
     const bool keep_vec = uint64_t(L) % 16 == 0 &&
@@ -832,18 +842,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
         }
       }
     }
-    failed = cta_wait(&bar_s, it & 1);
-    if (failed) break;
-    pending &= ~4u;
-    tc_fence_after();
-    // K is consumed: the next block's K load overlaps this block's softmax
-    if (tid == 0 && kb0 + kTK < hi) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar_k, 2 * kRegion);
-      tma_load_2d(khi, &kmap, &bar_k, 0, int(row0 + kb0 + kTK));
-      tma_load_2d(khi + kRegion, &kmap, &bar_k, 32, int(row0 + kb0 + kTK));
+    if (cta_wait(&bar_s, s_wt & 1)) {
+      failed = true;
+      break;
     }
-    if (kb0 + kTK < hi) pending |= 2u;
+    ++s_wt;
+    tc_fence_after();
+    if (j + 1 < nblk) issue_k(kb0 + kTK);  // K(j) consumed by S(j)
     if (!keep_full) {
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
@@ -855,13 +860,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
 
     // pass 1: masked, scaled scores of this thread's 32 columns back into S;
     // the row max over the block from the four column groups. Keys of the
-    // row's interval [r_lo, r_hi) as block columns [c_lo, c_hi).
-    const int64_t c_lo64 = max(int64_t(0), min(int64_t(kTK), r_lo - kb0));
-    const int64_t c_hi64 = max(c_lo64, min(int64_t(kTK), r_hi - kb0));
-    const uint32_t c_lo = uint32_t(c_lo64), c_span = uint32_t(c_hi64 - c_lo64);
+    // row's interval [r_lo, r_hi) as block columns [c_lo, c_lo + c_span).
     // q, k and v are finite here (checked before launch), so a score is
     // finite unless q.k * scale (+ bias) overflows: +inf marks the row as
     // the reference's NaN / empty row, -inf contributes nothing either way.
+    const int64_t c_lo64 = max(int64_t(0), min(int64_t(kTK), r_lo - kb0));
+    const int64_t c_hi64 = max(c_lo64, min(int64_t(kTK), r_hi - kb0));
+    const uint32_t c_lo = uint32_t(c_lo64), c_span = uint32_t(c_hi64 - c_lo64);
     float mb = -INFINITY;
     bool inf_here = false;
     const bool row_full = c_lo == 0 && c_span == kTK && keep_full;
@@ -869,12 +874,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
     for (int c = 0; c < 32; c += 16) {
       const uint32_t col0 = g * 32 + c;
       float sv[16];
-      tmem_ld16(tS + lane_off + col0, sv);
+      tmem_ld16(tSj + lane_off + col0, sv);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const uint32_t col = col0 + j;
-        float sc = __fmul_rn(sv[j], a.scale);
+      for (int jj = 0; jj < 16; ++jj) {
+        const uint32_t col = col0 + jj;
+        float sc = __fmul_rn(sv[jj], a.scale);
         if constexpr (BIAS)
           sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kb0 + col) + uint64_t(L) * b)]);
         if (!row_full) {
@@ -885,10 +890,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
         if constexpr (ACTIVE) sc = a.active[uint64_t(b) * L + kb0 + col] != 0.0f ? sc : -INFINITY;
         if constexpr (BIAS) sc = sc == sc ? sc : -INFINITY;  // a NaN bias: nothing
         inf_here |= sc == INFINITY;
-        sv[j] = sc;
+        sv[jj] = sc;
         mb = fmaxf(mb, sc);
       }
-      tmem_st16(tS + lane_off + col0, sv);
+      tmem_st16(tSj + lane_off + col0, sv);
     }
     inf_row |= inf_here;
     red_max[g][row] = mb;
@@ -896,47 +901,74 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
     tmem_wait_st();
     __syncthreads();
     mb = fmaxf(fmaxf(red_max[0][row], red_max[1][row]), fmaxf(red_max[2][row], red_max[3][row]));
+
+    // PV(j-1) must be done: it read the other S buffer (S(j+1) goes there),
+    // P lo and V, and O is rescaled below
+    if (j > 0) {
+      if (cta_wait(&bar_o, o_wt & 1)) {
+        failed = true;
+        break;
+      }
+      ++o_wt;
+      tc_fence_after();
+    }
+    if (j + 1 < nblk && !issue_s(j + 1)) {
+      failed = true;
+      break;
+    }
+
     const float mn = fmaxf(m, mb);
     // exp(x - mn) = 2^(x log2e - mn log2e): one FMA and the hardware 2^x
-    // (relative error ~2^-22, inside the f32 bar)
+    // (relative error ~2^-22, inside the f32 bar). A +inf row max: the row
+    // is empty (NaN / 0); its p come from a finite stand-in so that nothing
+    // non-finite reaches the MMA.
     const float mnl = (mn == -INFINITY || mn == INFINITY) ? 0.0f : __fmul_rn(mn, kLog2e);
     auto exp_rel = [&](float x) {
       float y;
       asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, kLog2e, -mnl)));
       return y;
     };
-    // a +inf row max: the row is empty (NaN / 0); its p are computed from a
-    // finite stand-in so that nothing non-finite reaches the MMA
-    const float mn_safe = mn == INFINITY ? 0.0f : mn;
-    const float corr = mn_safe == -INFINITY ? 1.0f : exp_rel(m);
-    // pass 2: p = exp(s - max), split into the A operand of the PV product
+    const float corr = (mn == -INFINITY || mn == INFINITY) ? 1.0f : exp_rel(m);
+    // pass 2: p = exp(s - max) split into hi (over this block's S) and lo,
+    // the A operands of the PV product
     float ps = 0.0f;
 #pragma unroll 1
     for (int c = 0; c < 32; c += 16) {
       const uint32_t col0 = g * 32 + c;
       float sv[16], pl[16];
-      tmem_ld16(tS + lane_off + col0, sv);
+      tmem_ld16(tSj + lane_off + col0, sv);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float x = sv[j] == INFINITY ? -INFINITY : sv[j];
+      for (int jj = 0; jj < 16; ++jj) {
+        const float x = sv[jj] == INFINITY ? -INFINITY : sv[jj];
         const float p = exp_rel(x);  // -inf -> 0
         ps = __fadd_rn(ps, p);
-        sv[j] = tf32_round_finite(p);
-        pl[j] = __fsub_rn(p, sv[j]);
+        sv[jj] = tf32_round_finite(p);
+        pl[jj] = __fsub_rn(p, sv[jj]);
       }
-      tmem_st16(tPh + lane_off + col0, sv);
+      tmem_st16(tSj + lane_off + col0, sv);
       tmem_st16(tPl + lane_off + col0, pl);
     }
     red_sum[g][row] = ps;
-    if (have_o && __any_sync(0xffffffffu, corr != 1.0f)) {  // warp-uniform: ld/st are .aligned
+    if (j > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {  // warp-uniform: ld/st are .aligned
       float ov[16];
       tmem_ld16(tO + lane_off + g * 16, ov);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 16; ++j) ov[j] = __fmul_rn(ov[j], corr);
+      for (int jj = 0; jj < 16; ++jj) ov[jj] = __fmul_rn(ov[jj], corr);
       tmem_st16(tO + lane_off + g * 16, ov);
     }
+    {  // V(j) (in registers) -> transposed (row = channel, K = key), split
+      const uint32_t reg = (vk >> 5) * kVtRegion;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        const uint32_t off = reg + sw128_offset(vc0 + n, vk & 31);
+        const float h = tf32_round_finite(vreg[n]);
+        *reinterpret_cast<float*>(vthi + off) = h;
+        *reinterpret_cast<float*>(vtlo + off) = __fsub_rn(vreg[n], h);
+      }
+    }
+    fence_proxy_async_smem();
     tmem_wait_st();
     tc_fence_before();
     __syncthreads();
@@ -951,32 +983,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
         const uint32_t off = (ks >> 2) * kVtRegion + (ks & 3) * 32;
         const uint64_t bhd = smem_desc_sw128(smem_addr(vthi + off));
         const uint64_t bl = smem_desc_sw128(smem_addr(vtlo + off));
-        mma_tf32_ts(tO, tPh + ks * 8, bhd, id_o, (have_o || ks > 0) ? 1u : 0u);
-        mma_tf32_ts(tO, tPh + ks * 8, bl, id_o, 1);
+        mma_tf32_ts(tO, tSj + ks * 8, bhd, id_o, (j > 0 || ks > 0) ? 1u : 0u);
+        mma_tf32_ts(tO, tSj + ks * 8, bl, id_o, 1);
         mma_tf32_ts(tO, tPl + ks * 8, bhd, id_o, 1);
       }
       mma_commit(&bar_o);
     }
-    have_o = true;
-    pending |= 8u;
-    // the next V block travels while the PV product runs
-    if (kb0 + kTK < hi) load_v(kb0 + kTK);
-    failed = cta_wait(&bar_o, it & 1);
-    if (!failed) pending &= ~8u;
+    ++o_iss;
+    if (j + 1 < nblk) load_v(kb0 + kTK);  // the next V block travels meanwhile
+  }
+  if (!failed && o_iss > o_wt) {
+    failed = cta_wait(&bar_o, o_wt & 1);
+    if (!failed) ++o_wt;
     tc_fence_after();
   }
+  (void)inf_row;
 
   if (failed) {
     // give up: count it and let what is still in flight land before the
     // tensor memory and shared memory go away
     if (tid == 0) {
       atomicAdd(&g_tc_wait_timeouts, 1u);
-      if (pending & 1) mbar_wait_bounded(&bar_q, 0, kTcWait);
-      if (pending & 2) mbar_wait_bounded(&bar_k, it & 1, kTcWait);
-      if (pending & 4) mbar_wait_bounded(&bar_s, it & 1, kTcWait);
-      if (pending & 8) mbar_wait_bounded(&bar_o, it & 1, kTcWait);
+      if (q_pending) mbar_wait_bounded(&bar_q, 0, kTcWait);
+      if (k_iss > k_wt) mbar_wait_bounded(&bar_k, k_wt & 1, kTcWait);
+      if (s_iss > s_wt) mbar_wait_bounded(&bar_s, s_wt & 1, kTcWait);
+      if (o_iss > o_wt) mbar_wait_bounded(&bar_o, o_wt & 1, kTcWait);
     }
   } else {
+    const bool have_o = nblk > 0;
     const bool empty = !have_o || l == 0.0f || inf_s[row] != 0;
     const float ev = a.empty_nan ? NAN : 0.0f;
     float ov[16];
@@ -986,9 +1020,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
     }
     if (qi < L) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float val = empty ? ev : __fdiv_rn(ov[j], l);
-        store_out(a, b, uint32_t(qi), uint64_t(head) * 64 + g * 16 + j, val);
+      for (int jj = 0; jj < 16; ++jj) {
+        const float val = empty ? ev : __fdiv_rn(ov[jj], l);
+        store_out(a, b, uint32_t(qi), uint64_t(head) * 64 + g * 16 + jj, val);
       }
     }
   }

@@ -3,8 +3,9 @@
 //
 // A load is one cp.async.bulk.tensor of a box described by a CUtensorMap that
 // the host encodes (cuTensorMapEncodeTiled, reached through the runtime's
-// driver entry point so the library does not link libcuda). No load here
-// uses cluster multicast, and every tensor map covers this GPU's own memory.
+// driver entry point so the library does not link libcuda). Every load here
+// goes to the issuing CTA only, and every tensor map covers this GPU's own
+// memory.
 #pragma once
 
 #include <cuda.h>
