@@ -39,7 +39,7 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
     const float* __restrict__ qkv, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, float* __restrict__ qh, float* __restrict__ kh,
     float* __restrict__ vh, uint32_t hidden, uint32_t heads, uint32_t length, uint32_t hd,
-    uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len) {
+    uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len, uint8_t* flags) {
   pdl_enter();
   const uint32_t half = hd / 2;
   for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
@@ -86,6 +86,15 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
         ka[j] = __fsub_rn(__fmul_rn(a1, c[j]), __fmul_rn(b1, s[j]));
         kb[j] = __fadd_rn(__fmul_rn(a1, s[j]), __fmul_rn(b1, c[j]));
       }
+    }
+    if (flags) {  // heads holding a value the tensor-core attention cannot take
+      constexpr float kMax = 3.4e38f;
+      bool bad = false;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        bad |= !(fabsf(qa[j]) < kMax && fabsf(qb[j]) < kMax && fabsf(ka[j]) < kMax &&
+                 fabsf(kb[j]) < kMax && fabsf(va[j]) < kMax && fabsf(vb[j]) < kMax);
+      if (bad) flags[b * heads + head] = 1;
     }
     if constexpr (VEC == 4) {
       auto st4 = [](float* p, const float* v) {
@@ -455,6 +464,12 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
     }
   }
 
+  // a +inf score seen by any of the 16 lanes of a row empties the whole row
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int d = 1; d < 16; d <<= 1)
+      inf_row[i] = (__shfl_xor_sync(0xffffffffu, int(inf_row[i]), d) != 0) || inf_row[i];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const uint32_t qi = q0 + 4 * ty + i;
@@ -1035,6 +1050,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
 // value beyond the largest tf32, which the split cannot represent): the
 // tensor-core kernel leaves such heads to the f32 kernel, whose arithmetic
 // follows the reference's handling of non-finite values exactly.
+// CTA (slice, head): gridDim.x slices of each head's q, k and v; flags are
+// zeroed before the launch and only ever set to 1.
 __global__ void __launch_bounds__(256) attn_vcheck_kernel(const float* __restrict__ q,
                                                           const float* __restrict__ k,
                                                           const float* __restrict__ v,
@@ -1042,21 +1059,25 @@ __global__ void __launch_bounds__(256) attn_vcheck_kernel(const float* __restric
                                                           uint64_t per_head) {
   pdl_enter();
   constexpr float kMax = 3.4e38f;  // below the largest tf32 (rounding up stays finite)
+  const uint64_t n4 = per_head / 4, per_slice = (n4 + gridDim.x - 1) / gridDim.x;
+  const uint64_t i0 = uint64_t(blockIdx.x) * per_slice, i1 = min(n4, i0 + per_slice);
   bool bad = false;
   for (int t = 0; t < 3; ++t) {
     const float* base = t == 0 ? q : t == 1 ? k : v;
-    const float4* p = reinterpret_cast<const float4*>(base + uint64_t(blockIdx.x) * per_head);
-    for (uint64_t i = threadIdx.x; i < per_head / 4; i += 256) {
+    const float4* p = reinterpret_cast<const float4*>(base + uint64_t(blockIdx.y) * per_head);
+    for (uint64_t i = i0 + threadIdx.x; i < i1; i += 256) {
       const float4 w = ld_stream(p + i);
       bad |= !(fabsf(w.x) < kMax && fabsf(w.y) < kMax && fabsf(w.z) < kMax && fabsf(w.w) < kMax);
     }
   }
   bad = __syncthreads_or(bad);
-  if (threadIdx.x == 0) flags[blockIdx.x] = bad ? 1 : 0;
+  if (threadIdx.x == 0 && bad) flags[blockIdx.y] = 1;
 }
 
+// pre_flags: per-head flags already computed on the stream (the prep kernel
+// sets them), or null to run the check here.
 int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo& dev,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const uint8_t* pre_flags) {
   // 1 when not covered (nothing launched)
   const uint64_t rows = uint64_t(batch) * a.heads * a.length;
   if (a.hd != 64 || rows >= (uint64_t(1) << 31) || !aligned(a.q, 16) || !aligned(a.k, 16) ||
@@ -1076,15 +1097,21 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
     return fail(TFX_ERR_CUDA, op, "tensor map", why);
   const uint32_t nbh = batch * a.heads;
   uint8_t* flags = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&flags), nbh, stream);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  int rc = TFX_OK;
+  if (!pre_flags) {
+    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&flags), nbh, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, stream);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+    }
+    const unsigned slices = unsigned(std::max<uint64_t>(1, std::min<uint64_t>(
+        32, (uint64_t(dev.sms) * 8 + nbh - 1) / nbh)));
+    rc = launch_kernel(op, attn_vcheck_kernel, dim3(slices, nbh), dim3(256), 0, stream, 1, a.q,
+                       a.k, a.v, flags, uint64_t(a.length) * 64);
   }
-  int rc = launch_kernel(op, attn_vcheck_kernel, dim3(nbh), dim3(256), 0, stream, 1, a.q, a.k,
-                         a.v, flags, uint64_t(a.length) * 64);
   if (rc == TFX_OK) {
-    a.vflags = flags;
+    a.vflags = pre_flags ? pre_flags : flags;
     a.vflag_mode = 1;
     const dim3 grid((a.length + kTQ - 1) / kTQ, a.heads, batch);
     auto run = [&](auto kernel) -> int {
@@ -1117,16 +1144,17 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
                                            dim3((a.length + kQT - 1) / kQT, a.heads, batch),
                                            dim3(256), fsmem, stream, 1, a);
   }
-  cudaFreeAsync(flags, stream);
+  if (flags) cudaFreeAsync(flags, stream);
   return rc;
 }
 
-int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t stream) {
+int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t stream,
+                const uint8_t* pre_flags) {
   int st = TFX_OK;
   const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
   {
-    const int rc = attn_launch_tc(op, a, batch, dev, stream);
+    const int rc = attn_launch_tc(op, a, batch, dev, stream, pre_flags);
     if (rc != 1) return rc;
   }
   const bool vec = aligned(a.q, 16) && aligned(a.k, 16) && aligned(a.v, 16);
@@ -1163,7 +1191,7 @@ int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t 
 
 int laya_prep(const char* op, const float* qkv, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t hidden, int64_t heads, int64_t length,
-              int64_t batch, cudaStream_t stream) {
+              int64_t batch, cudaStream_t stream, uint8_t* flags = nullptr) {
   TFX_REQUIRE(hidden >= 0 && heads > 0 && length >= 0 && batch >= 0, op, "shape",
               "extents must be non-negative (heads positive)");
   TFX_REQUIRE(hidden % heads == 0, op, "hidden", "hidden must be a multiple of heads");
@@ -1190,10 +1218,10 @@ int laya_prep(const char* op, const float* qkv, const float* cos_t, const float*
   if (v4)
     return launch_kernel(op, laya_prep_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
                          sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
-                         uint32_t(hd), uint64_t(total), dc, dh, dl);
+                         uint32_t(hd), uint64_t(total), dc, dh, dl, flags);
   return launch_kernel(op, laya_prep_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
                        sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
-                       uint32_t(hd), uint64_t(total), dc, dh, dl);
+                       uint32_t(hd), uint64_t(total), dc, dh, dl, flags);
 }
 
 int jeff_prep(const char* op, const float* q, const float* k, const float* v,
@@ -1224,7 +1252,8 @@ int jeff_prep(const char* op, const float* q, const float* k, const float* v,
 }
 
 int attention(const char* op, const float* qh, const float* kh, const float* vh, float* out,
-              const tfx_attention_desc* d, cudaStream_t stream) {
+              const tfx_attention_desc* d, cudaStream_t stream,
+              const uint8_t* pre_flags = nullptr) {
   TFX_REQUIRE(d, op, "desc", "null pointer");
   TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->length >= 0 && d->head_dim >= 0, op, "shape",
               "extents must be non-negative");
@@ -1258,7 +1287,7 @@ int attention(const char* op, const float* qh, const float* kh, const float* vh,
   a.valid_len = d->valid_len;
   a.vflags = nullptr;
   a.vflag_mode = 0;
-  return attn_launch(op, a, uint32_t(d->batch), stream);
+  return attn_launch(op, a, uint32_t(d->batch), stream, pre_flags);
 }
 
 }  // namespace tfx
@@ -1346,19 +1375,24 @@ int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const fl
   int st = TFX_OK;
   device_info(&st);
   if (st != TFX_OK) return st;
+  // scratch: head-major q, k, v, then one flag byte per head (the prep
+  // kernel marks heads the tensor-core attention must leave to the f32 one)
   float* scratch = nullptr;
-  const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
+  const size_t nbh = size_t(batch * heads);
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4 + nbh, s);
+  uint8_t* flags = reinterpret_cast<uint8_t*>(scratch + 3 * n);
+  if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
   int rc = laya_prep(op, qkv, cos_table, sin_table, scratch, scratch + n, scratch + 2 * n, hidden,
-                     heads, length, batch, s);
+                     heads, length, batch, s, flags);
   if (rc == TFX_OK) {
     tfx_attention_desc d;
     tfx_attention_desc_init(&d, batch, heads, length, hidden / heads);
     d.keep = keep;
-    rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s);
+    rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s, flags);
   }
   cudaFreeAsync(scratch, s);
   return rc;

@@ -56,6 +56,22 @@ def test_laya_attention_block(orc, hd, heads, L, B, window, rope):
     assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"laya attention hd={hd} L={L}")
 
 
+def test_laya_attention_block_nonfinite_qk_routed(orc):
+    """Heads whose q or k hold NaN / inf leave the tensor-core kernel for the
+    f32 one (flags set by the prep kernel); results follow the reference:
+    non-finite scores contribute nothing, rows without a finite score are NaN."""
+    hd, heads, L, B = 64, 2, 96, 2
+    d = hd * heads
+    qkv = splitmix_normal(3 * d * L * B, 0x7E4F0A90)
+    x = qkv.reshape(B, L, 3, heads, hd)
+    x[1, 5, 0, 0, 3] = np.nan          # q of batch 1, head 0, token 5
+    x[0, 7, 1, 1, 10] = np.inf         # k of batch 0, head 1, token 7
+    keep = keep_window(L, B, 20, [L, L - 9])
+    got = gpu_laya_block(qkv, keep, d, heads, L, B)
+    want = orc.laya_attention_block_f32(qkv, keep, d, heads, L, B)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, "non-finite q / k")
+
+
 @pytest.mark.parametrize("hd", [4, 64])
 def test_laya_attention_block_known_answer(orc, hd):
     """crates/cpu-kernels/src/lib.rs:1212-1250 through the GPU (hd 4: the row
