@@ -57,9 +57,10 @@ TFX_API int tfx_version(void);
 /* Diagnostic, no counterpart in the reference: the number of bounded waits
  * inside libtfx kernels on the current device that gave up since the library
  * was loaded (a kernel that gives up leaves its output incomplete). Every wait
- * of a kernel on an asynchronous copy is bounded (about one second), so a lost
- * copy ends the kernel instead of hanging the GPU. Synchronous (reads device
- * memory). */
+ * of a kernel on an asynchronous copy or tensor-core operation (the TMA-
+ * pipelined RMSNorm, the tensor-core attention) is bounded (about one second),
+ * so a lost copy ends the kernel instead of hanging the GPU. Synchronous
+ * (reads device memory). */
 TFX_API int tfx_wait_timeouts(uint32_t* count);
 
 /* ---- erf / exact GELU ------------------------------------------------------

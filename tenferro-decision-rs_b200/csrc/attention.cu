@@ -220,16 +220,6 @@ __device__ __forceinline__ void analytic_range(const AttnArgs& a, int64_t q0, in
   *hi = max(l, h);
 }
 
-// key_kept without the keep tensor (causal, window, valid length, active).
-__device__ __forceinline__ bool key_kept_nokeep(const AttnArgs& a, uint32_t b, int64_t qi,
-                                                int64_t kj) {
-  if (a.causal && kj > qi) return false;
-  if (a.window >= 0 && (kj < qi - a.window || kj > qi + a.window)) return false;
-  if (a.valid_len >= 0 && kj >= a.valid_len) return false;
-  if (a.active && a.active[uint64_t(b) * a.length + kj] == 0.0f) return false;
-  return true;
-}
-
 __device__ __forceinline__ bool key_kept(const AttnArgs& a, uint32_t b, int64_t qi, int64_t kj) {
   if (a.causal && kj > qi) return false;
   if (a.window >= 0 && (kj < qi - a.window || kj > qi + a.window)) return false;
@@ -1188,6 +1178,12 @@ int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t 
 }  // namespace
 
 // ---- host entry points ---------------------------------------------------------------
+
+// Bounded waits of the tensor-core attention that gave up on the current device.
+int attention_wait_timeouts(uint32_t* count) {
+  const cudaError_t err = cudaMemcpyFromSymbol(count, g_tc_wait_timeouts, sizeof(uint32_t));
+  return err == cudaSuccess ? TFX_OK : fail(TFX_ERR_CUDA, "tfx", "wait timeouts", cudaGetErrorString(err));
+}
 
 int laya_prep(const char* op, const float* qkv, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t hidden, int64_t heads, int64_t length,

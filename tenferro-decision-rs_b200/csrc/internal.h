@@ -19,4 +19,8 @@ int masked_softmax_rows(const float* scores, float* probs, const tfx_softmax_des
 int rms_stream(const char* op, const float* x, const float* w, float* y, uint32_t rows,
                uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
 
+// attention.cu: the tensor-core attention's count of bounded waits that gave
+// up on the current device (cudaMemcpyFromSymbol; synchronous).
+int attention_wait_timeouts(uint32_t* count);
+
 }  // namespace tfx

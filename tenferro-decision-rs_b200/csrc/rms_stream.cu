@@ -352,8 +352,12 @@ extern "C" int tfx_wait_timeouts(uint32_t* count) {
   int st = TFX_OK;
   tfx::device_info(&st);
   if (st != TFX_OK) return st;
-  const cudaError_t err = cudaMemcpyFromSymbol(count, g_wait_timeouts, sizeof(uint32_t));
+  uint32_t rms = 0, attn = 0;
+  const cudaError_t err = cudaMemcpyFromSymbol(&rms, g_wait_timeouts, sizeof(uint32_t));
   if (err != cudaSuccess)
     return tfx::fail(TFX_ERR_CUDA, "tfx", "wait timeouts", cudaGetErrorString(err));
+  st = tfx::attention_wait_timeouts(&attn);
+  if (st != TFX_OK) return st;
+  *count = rms + attn;
   return TFX_OK;
 }

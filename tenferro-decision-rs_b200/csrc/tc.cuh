@@ -25,18 +25,12 @@
 
 namespace tfx {
 
-// Round to the nearest tf32 (10-bit mantissa, ties away from zero); the
-// result is an f32 whose 13 low mantissa bits are zero.
-__device__ __forceinline__ float tf32_round(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
-}
-
-// tf32_round for finite x on the integer pipe instead of the conversion unit:
-// adding half a tf32 ulp (bit 12) to the magnitude bits and clearing the 13
-// low bits rounds to nearest, ties away from zero -- the same result as
-// cvt.rna.tf32.f32 for every finite x below the largest tf32.
+// Round a finite x to the nearest tf32 (10-bit mantissa, ties away from
+// zero) on the integer pipe: adding half a tf32 ulp (bit 12) to the magnitude
+// bits and clearing the 13 low bits -- the result cvt.rna.tf32.f32 gives for
+// every finite x below the largest tf32, without the conversion unit (which
+// the softmax's exponentials already load). The result is an f32 whose 13
+// low mantissa bits are zero.
 __device__ __forceinline__ float tf32_round_finite(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }

@@ -209,3 +209,10 @@ def test_attention_rejects_bad_arguments():
     d.empty_rows = 7
     rc = _lib.lib.tfx_attention_f32(None, None, None, None, ctypes.byref(d), None)
     assert rc == -1 and b"empty_rows" in _lib.lib.tfx_last_error_string()
+
+
+def test_attention_no_wait_gave_up():
+    """Every bounded wait of the tensor-core kernels completed in the runs above."""
+    n = ctypes.c_uint32(99)
+    call("tfx_wait_timeouts", ctypes.byref(n))
+    assert n.value == 0
