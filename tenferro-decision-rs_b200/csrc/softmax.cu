@@ -134,11 +134,14 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
   return r;
 }
 
-template <int NV, int STRIDE, int SEM, bool TENSORS, class RMax, class RSum, class RAny>
+// BAND: the row's kept chunks number at most NV * STRIDE (guaranteed by the
+// caller from the analytic mask) while kv may be larger; the masked rest is
+// written by a loop over the whole row. Otherwise kv <= NV * STRIDE.
+template <int NV, int STRIDE, int SEM, bool TENSORS, bool BAND, class RMax, class RSum,
+          class RAny>
 __device__ __forceinline__ void softmax_row(const float4* __restrict__ src, float4* dst,
                                             const MaskArgs& m, const RowCtx& c, uint32_t kv,
                                             uint32_t tid, RMax rmax, RSum rsum, RAny rany) {
-  // Precondition: kv <= NV * STRIDE.
   constexpr float kMasked = SEM == kExclude ? -INFINITY : -1.0e30f;
   const uint32_t c0 = c.lo >> 2;
   const uint32_t hi = c.lo + c.span;
@@ -249,10 +252,15 @@ __device__ __forceinline__ void softmax_row(const float4* __restrict__ src, floa
   if (nch < kv) {  // uniform over the row's threads
     const float p_out = __fdiv_rn(e_out, sum);
     const float4 fill = make_float4(p_out, p_out, p_out, p_out);
+    if constexpr (BAND) {
+      for (uint32_t q4 = tid; q4 < kv; q4 += STRIDE)
+        if (q4 - c0 >= nch) dst[q4] = fill;
+    } else {
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const uint32_t q4 = j * STRIDE + tid;
-      if (q4 < kv && q4 - c0 >= nch) dst[q4] = fill;
+      for (int j = 0; j < NV; ++j) {
+        const uint32_t q4 = j * STRIDE + tid;
+        if (q4 < kv && q4 - c0 >= nch) dst[q4] = fill;
+      }
     }
   }
 }
@@ -277,7 +285,7 @@ __device__ __forceinline__ float group_sum(float v, unsigned mask) {
   return v;
 }
 
-template <int NV, int LANES, int SEM, bool TENSORS>
+template <int NV, int LANES, int SEM, bool TENSORS, bool BAND = false>
 __global__ void __launch_bounds__(256) softmax_lanes_kernel(const float* __restrict__ s,
                                                             float* __restrict__ p, uint64_t rows,
                                                             MaskArgs m) {
@@ -290,7 +298,7 @@ __global__ void __launch_bounds__(256) softmax_lanes_kernel(const float* __restr
       LANES == 32 ? 0xffffffffu : ((1u << LANES) - 1u) << (threadIdx.x & 31 & ~(LANES - 1));
   const RowCtx c = row_ctx(m, row);
   const uint32_t kv = uint32_t(m.k_len / 4);
-  softmax_row<NV, LANES, SEM, TENSORS>(
+  softmax_row<NV, LANES, SEM, TENSORS, BAND>(
       reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
       reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, lane,
       [mask](float x) { return group_max<LANES>(x, mask); },
@@ -308,7 +316,7 @@ __global__ void __launch_bounds__(256) softmax_cta_kernel(const float* __restric
   const uint64_t row = blockIdx.x;
   const RowCtx c = row_ctx(m, row);
   const uint32_t kv = uint32_t(m.k_len / 4);
-  softmax_row<NV, 256, SEM, TENSORS>(
+  softmax_row<NV, 256, SEM, TENSORS, false>(
       reinterpret_cast<const float4*>(s + row * uint64_t(m.k_len)),
       reinterpret_cast<float4*>(p + row * uint64_t(m.k_len)), m, c, kv, threadIdx.x,
       [&](float x) { return block_reduce(x, red, true); },
@@ -351,6 +359,21 @@ int launch_softmax(const char* op, const float* scores, float* probs, int64_t ro
                    const MaskArgs& m, cudaStream_t stream) {
   const bool vec = kl % 4 == 0 && aligned(scores, 16) && aligned(probs, 16);
   const int64_t kv = kl / 4;
+  // A sliding window bounds every row's kept interval to 2 * window + 1
+  // keys: eight lanes per row hold the band (at most 40 chunks, five per
+  // lane) and write the masked rest of the row in a loop, so the per-row work
+  // is spread over 8 lanes whatever k_len is.
+  // (Not when padded queries drop the window: their interval is the whole
+  // valid prefix.)
+  const int64_t band_chunks = m.window >= 0 ? (2 * m.window + 1 + 3) / 4 + 1 : kv;
+  if (!TENSORS && vec && m.window >= 0 && !m.skip_invalid_q && band_chunks <= 8 * 5 &&
+      kv > 8 * 5) {
+    const int64_t per = 32;
+    TFX_REQUIRE(rows / per < (int64_t(1) << 31), op, "shape", "too many rows for one call");
+    return launch_kernel(op, softmax_lanes_kernel<5, 8, SEM, TENSORS, true>,
+                         dim3(unsigned((rows + per - 1) / per)), dim3(256), 0, stream, 1, scores,
+                         probs, uint64_t(rows), m);
+  }
   if (vec && kv <= 32 * 8) {
     // Up to 32 keys per thread: 8 lanes per row up to 256 keys, 16 up to
     // 512, a warp up to 1024.

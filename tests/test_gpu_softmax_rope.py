@@ -159,6 +159,38 @@ def test_softmax_row_lengths_valid_len(orc, Lk, semantics):
     assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"softmax Lk={Lk}")
 
 
+@pytest.mark.parametrize("window,Lq,Lk,semantics,extra", [
+    (0, 40, 164, 0, {}), (1, 33, 256, 1, {"valid_len": 250}), (7, 64, 512, 0, {"causal": 1}),
+    (33, 100, 2052, 1, {"scale": 0.125}), (64, 512, 512, 0, {"valid_len": 475}),
+    (64, 512, 512, 1, {"valid_len": 475}), (77, 300, 4096, 0, {"valid_len": 200}),
+    (78, 160, 640, 0, {}), (50, 9, 9000, 1, {"causal": 1, "valid_len": 7})])
+def test_softmax_sliding_window_band(orc, window, Lq, Lk, semantics, extra):
+    """Sliding windows short enough for the banded row kernel (|q-k| <= window,
+    at most 40 kept float4 chunks, rows longer than that), rows at both sequence
+    edges, padded keys, causal, queries past the keys; window 78 just past the
+    band limit."""
+    B, H = 2, 3
+    s = splitmix_normal(B * H * Lq * Lk, 0x7E4F06A0 + window + Lk, std=3.0)
+    kw = dict(window=window, semantics=semantics, **extra)
+    got = gpu_softmax(s, B, H, Lq, Lk, **kw)
+    want = orc.masked_softmax_f32(s, B, H, Lq, Lk, **kw)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"softmax band w={window} Lk={Lk}")
+    if semantics == 0:  # keys outside the window: exactly 0 in every non-empty row
+        q = np.arange(Lq)[:, None]
+        k = np.arange(Lk)[None, :]
+        rows_ok = np.isfinite(want.reshape(B * H, Lq, Lk)).all(axis=2)
+        sel = rows_ok[:, :, None] & (np.abs(q - k) > window)[None]
+        assert np.all(got.reshape(B * H, Lq, Lk)[sel] == 0.0)
+
+
+def test_softmax_sliding_window_band_in_place(orc):
+    B, H, L = 2, 4, 384
+    s = splitmix_normal(B * H * L * L, 0x7E4F06B0, std=2.0)
+    got = gpu_softmax(s, B, H, L, L, in_place=True, window=16, scale=0.125, valid_len=L - 9)
+    want = orc.masked_softmax_f32(s, B, H, L, L, window=16, scale=0.125, valid_len=L - 9)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, "softmax band in place")
+
+
 @pytest.mark.parametrize("semantics", [0, 1])
 def test_softmax_wide_dynamic_range(orc, semantics):
     """Scores ~ N(0, 20): probabilities down to ~1e-40 (subnormal quotients,
