@@ -18,6 +18,10 @@ int masked_softmax_rows(const float* scores, float* probs, const tfx_softmax_des
 // alignment is not covered (nothing launched), else a status.
 int rms_stream(const char* op, const float* x, const float* w, float* y, uint32_t rows,
                uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
+// rms_stream.cu: the same op with a TMA box ring feeding registers (widths
+// 513 .. 2048); 1 when not covered, else a status.
+int rms_ring(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+             uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
 
 // attention.cu: the tensor-core attention's count of bounded waits that gave
 // up on the current device (cudaMemcpyFromSymbol; synchronous).

@@ -842,8 +842,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const float* x,
 }
 
 // Kernel choice for the f32 feature-last RMSNorm: 0 = automatic, 1 = cluster,
-// 2 = tile, 3 = split, 4 = 16-CTA cluster, 5 = TMA-pipelined stream;
-// TFX_RMS_KERNEL overrides it for tuning runs.
+// 2 = tile, 3 = split, 4 = 16-CTA cluster, 5 = TMA-pipelined stream, 6 = TMA
+// box ring into registers; TFX_RMS_KERNEL overrides it for tuning runs.
 int rms_kernel_choice() {
   static const int choice = [] {
     const char* e = getenv("TFX_RMS_KERNEL");
@@ -854,6 +854,7 @@ int rms_kernel_choice() {
            : s == "split"   ? 3
            : s == "cluster16" ? 4
            : s == "stream"  ? 5
+           : s == "ring"    ? 6
                             : 0;
   }();
   return choice;
@@ -957,8 +958,15 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
                            stream, 1, x, w, y, uint32_t(rows), uint32_t(width), eps, inv_width,
                            centered);
     }
-    // The streaming kernel reads x once with its loads always in flight; it
-    // covers aligned shapes with rows % 4 == 0 and width up to ~1700.
+    // The ring kernel (TMA boxes into registers) and the streaming kernel
+    // (whole tiles staged in shared memory) read x once with their loads
+    // always in flight; they cover aligned shapes with rows % 4 == 0, widths
+    // 513 .. 2048 and up to ~3300 respectively.
+    if (small && (choice == 0 || choice == 6)) {
+      const int rc = rms_ring(op, x, w, y, uint32_t(rows), uint32_t(width), centered, eps,
+                              inv_width, stream);
+      if (rc != 1) return rc;
+    }
     if (small && (choice == 0 || choice == 5)) {
       const int rc = rms_stream(op, x, w, y, uint32_t(rows), uint32_t(width), centered, eps,
                                 inv_width, stream);

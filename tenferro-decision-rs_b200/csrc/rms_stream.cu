@@ -307,7 +307,267 @@ int launch_stream(const char* op, const CUtensorMap& map, const StreamArgs& a, s
                        stream, CL, map, a);
 }
 
+// ---- ring variant: boxes through a shared-memory ring into registers -------------
+//
+// The stream kernel above holds each whole tile in shared memory until its
+// output is written, so a stage is busy for the tile's load, reduction and
+// store, and the next tile's load waits for all of it. Here one producer warp
+// keeps a ring of boxes (16 tokens x 256 features, 16 KB) in flight through
+// TMA, and 512 consumer threads copy each landed box into registers and hand
+// its slot straight back (one mbarrier arrival per warp), so HBM reads go on
+// while the consumers reduce and write. The tile being reduced lives in
+// registers: 16 tokens x width, width <= 2048 (up to 16 float4 per thread).
+// Tiles are dealt round-robin (tile c, c + grid, ...) so that at any moment
+// the SMs read neighbouring 64-byte runs of the same features: giving each
+// CTA a contiguous block of tiles measured 10 % slower at width 1024.
+// Measured against the stream kernel at 16384 x 1024 (one B200, CUDA graph
+// over rotating buffers): 25.7 us against 27.5 us; 32-token tiles (128-byte
+// runs, 6 slots) 26.5 us; 8 or 12 slots within 1 %.
+
+constexpr int kRingTok = 16;
+constexpr int kRingConsumers = 512;
+constexpr int kRingWarps = kRingConsumers / 32;
+constexpr int kRingThreads = kRingConsumers + 32;  // + the producer warp
+constexpr uint32_t kRingMaxSlots = 10;
+
+struct RingArgs {
+  const float* w;
+  float* y;
+  uint32_t rows, width;
+  uint32_t box1, nbox;  // features per box (256), boxes per tile
+  uint32_t tiles, slots;
+  float eps, inv_width;
+  int centered;
+};
+
+// Shared memory: slots x [box1][16] | w' [nbox * box1] | red [kRingWarps][16] |
+// scale [16] | full, empty mbarriers [slots each].
+inline size_t ring_smem_bytes(uint32_t box1, uint32_t nbox, uint32_t slots) {
+  return size_t(slots) * box1 * kRingTok * 4 + size_t(nbox) * box1 * 4 +
+         size_t(kRingWarps) * kRingTok * 4 + kRingTok * 4 + 2 * size_t(slots) * 8 + 8;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Barrier over the consumer threads only (named barrier `id`).
+__device__ __forceinline__ void consumers_sync(uint32_t id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kRingConsumers) : "memory");
+}
+// The same, returning whether any consumer passed p = true.
+__device__ __forceinline__ bool consumers_sync_or(uint32_t id, bool p) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred q, o;\n\tsetp.ne.u32 q, %1, 0;\n\t"
+      "barrier.cta.red.or.pred o, %2, %3, q;\n\tselp.u32 %0, 1, 0, o;\n\t}"
+      : "=r"(r)
+      : "r"(uint32_t(p)), "r"(id), "r"(kRingConsumers)
+      : "memory");
+  return r != 0;
+}
+
+// NBMAX: boxes per tile the registers are sized for (4: width <= 1024, 8:
+// width <= 2048). Consumer thread (q, fg): tokens 4q .. 4q+3 of the tile,
+// local features fg and fg + 128 of every box.
+template <int NBMAX>
+__global__ void __launch_bounds__(kRingThreads, 1)
+    rms_ring_kernel(const __grid_constant__ CUtensorMap xmap, RingArgs a) {
+  constexpr int NV = 2 * NBMAX;
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const uint32_t slot_floats = a.box1 * kRingTok;
+  float* ring = reinterpret_cast<float*>(smem);
+  float* w_s = ring + size_t(a.slots) * slot_floats;
+  float* red = w_s + a.nbox * a.box1;
+  float* scale_s = red + kRingWarps * kRingTok;
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(scale_s + kRingTok) + 7) & ~uintptr_t(7));
+  uint64_t* empty = full + a.slots;
+
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t units = gridDim.x;
+  const uint32_t n_my = a.tiles > blockIdx.x ? (a.tiles - blockIdx.x + units - 1) / units : 0;
+  if (tid == 0) {
+    for (uint32_t s = 0; s < a.slots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRingWarps);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_enter();  // x and w may come from the previous kernel on the stream
+
+  if (warp == kRingWarps) {  // producer: one elected lane issues every box
+    if (lane == 0) {
+      const uint32_t box_bytes = slot_floats * 4;
+      // s, ph: slot and phase parity of the next box. A reused slot waits for
+      // the release of the box issued into it one lap earlier (parity ph ^ 1).
+      uint32_t issued = 0, s = 0, ph = 0;
+      bool ok = true;
+      for (uint32_t k = 0; k < n_my && ok; ++k) {
+        const int tok0 = int((blockIdx.x + k * units) * kRingTok);
+        for (uint32_t b = 0; b < a.nbox; ++b) {
+          if (issued >= a.slots && !mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitCycles)) {
+            atomicAdd(&g_wait_timeouts, 1u);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], box_bytes);
+          tma_load_2d(ring + size_t(s) * slot_floats, &xmap, &full[s], tok0, int(b * a.box1));
+          ++issued;
+          if (++s == a.slots) s = 0, ph ^= 1u;
+        }
+      }
+      // Let every copy this CTA issued land before the CTA can exit (bounded):
+      // the last min(issued, slots) boxes, oldest first.
+      const uint32_t back = issued < a.slots ? issued : a.slots;
+      uint32_t ds = s, dph = ph;
+      for (uint32_t j = 0; j < back; ++j)
+        if (ds-- == 0) ds = a.slots - 1, dph ^= 1u;
+      for (uint32_t j = 0; j < back; ++j) {
+        mbar_wait_bounded(&full[ds], dph, kWaitCycles);
+        if (++ds == a.slots) ds = 0, dph ^= 1u;
+      }
+    }
+    return;
+  }
+
+  const uint32_t q = tid & 3, fg = tid >> 2;
+  for (uint32_t f = tid; f < a.nbox * a.box1; f += kRingConsumers) {
+    const float wf = f < a.width ? a.w[f] : 0.0f;
+    w_s[f] = a.centered ? __fadd_rn(1.0f, wf) : wf;
+  }
+  consumers_sync(2);
+  // Up to 1024 features the thread's weights stay in registers for all tiles.
+  constexpr bool kWReg = NBMAX <= 4;
+  float wr[kWReg ? NV : 1];
+  if constexpr (kWReg) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t b = uint32_t(i) >> 1, lf = fg + 128 * (uint32_t(i) & 1);
+      wr[i] = b < a.nbox && lf < a.box1 ? w_s[b * a.box1 + lf] : 0.0f;
+    }
+  }
+  uint32_t s = 0, ph = 0;  // slot and phase parity of the next box
+  for (uint32_t k = 0; k < n_my; ++k) {
+    float4 v[NV];
+    bool bad = false;
+#pragma unroll
+    for (int b = 0; b < NBMAX; ++b) {
+      v[2 * b] = v[2 * b + 1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (uint32_t(b) < a.nbox) {
+        if (!mbar_wait_bounded(&full[s], ph, kWaitCycles)) bad = true;
+        const float* t = ring + size_t(s) * slot_floats + 4 * q;
+        if (fg < a.box1) v[2 * b] = *reinterpret_cast<const float4*>(t + fg * kRingTok);
+        if (fg + 128 < a.box1)
+          v[2 * b + 1] = *reinterpret_cast<const float4*>(t + (fg + 128) * kRingTok);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (++s == a.slots) s = 0, ph ^= 1u;
+      }
+    }
+    // Sums of squares of the quad's 4 tokens over this thread's features
+    // (zero-filled past the width and the last token).
+    float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float2 a01 = make_float2(v[i].x, v[i].y), a23 = make_float2(v[i].z, v[i].w);
+      s01 = __fadd2_rn(s01, __fmul2_rn(a01, a01));
+      s23 = __fadd2_rn(s23, __fmul2_rn(a23, a23));
+    }
+#pragma unroll
+    for (int m = 4; m < 32; m <<= 1) {
+      s01.x = __fadd_rn(s01.x, __shfl_xor_sync(0xffffffffu, s01.x, m));
+      s01.y = __fadd_rn(s01.y, __shfl_xor_sync(0xffffffffu, s01.y, m));
+      s23.x = __fadd_rn(s23.x, __shfl_xor_sync(0xffffffffu, s23.x, m));
+      s23.y = __fadd_rn(s23.y, __shfl_xor_sync(0xffffffffu, s23.y, m));
+    }
+    if (lane < 4)
+      *reinterpret_cast<float4*>(red + warp * kRingTok + 4 * lane) =
+          make_float4(s01.x, s01.y, s23.x, s23.y);
+    if (consumers_sync_or(1, bad)) {  // a copy never landed: leave (counted once)
+      if (tid == 0) atomicAdd(&g_wait_timeouts, 1u);
+      return;
+    }
+    if (tid < kRingTok) {
+      float tot = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kRingWarps; ++w) tot = __fadd_rn(tot, red[w * kRingTok + tid]);
+      scale_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, a.inv_width), a.eps)));
+    }
+    consumers_sync(2);
+    const uint32_t tok = (blockIdx.x + k * units) * kRingTok + 4 * q;
+    if (tok < a.rows) {  // rows % 4 == 0: the whole quad is in range
+      const float4 sc = *reinterpret_cast<const float4*>(scale_s + 4 * q);
+      float* yq = a.y + tok;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const uint32_t b = uint32_t(i) >> 1, lf = fg + 128 * (uint32_t(i) & 1);
+        const uint32_t f = b * a.box1 + lf;
+        if (b < a.nbox && lf < a.box1 && f < a.width) {
+          const float wt = kWReg ? wr[kWReg ? i : 0] : w_s[f];
+          float4 o;
+          o.x = __fmul_rn(__fmul_rn(v[i].x, sc.x), wt);
+          o.y = __fmul_rn(__fmul_rn(v[i].y, sc.y), wt);
+          o.z = __fmul_rn(__fmul_rn(v[i].z, sc.z), wt);
+          o.w = __fmul_rn(__fmul_rn(v[i].w, sc.w), wt);
+          *reinterpret_cast<float4*>(yq + size_t(f) * a.rows) = o;
+        }
+      }
+    }
+  }
+}
+
+template <int NBMAX>
+int launch_ring(const char* op, const CUtensorMap& map, const RingArgs& a, size_t smem,
+                const DeviceInfo& dev, cudaStream_t stream) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  const int di = dev.device & 63;
+  std::call_once(once[di], [&] {
+    err[di] = cudaFuncSetAttribute(rms_ring_kernel<NBMAX>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, dev.smem_optin);
+  });
+  if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
+  const uint32_t units = std::min<uint32_t>(a.tiles, uint32_t(dev.sms));
+  return launch_kernel(op, rms_ring_kernel<NBMAX>, dim3(units), dim3(kRingThreads), smem, stream,
+                       1, map, a);
+}
+
 }  // namespace
+
+// Ring RMSNorm; 1 when the shape or alignment is not covered (nothing
+// launched), else a status. Covers rows % 4 == 0, 16-byte aligned x and y,
+// rows < 2^31 and 512 < width <= 2048.
+int rms_ring(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+             uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream) {
+  if (rows % 4 != 0 || rows >= (1u << 31) || !aligned(x, 16) || !aligned(y, 16)) return 1;
+  if (width <= 512 || width > 2048) return 1;
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  RingArgs a;
+  a.box1 = 256;
+  a.nbox = (width + a.box1 - 1) / a.box1;
+  a.slots = kRingMaxSlots;
+  while (a.slots > 2 && ring_smem_bytes(a.box1, a.nbox, a.slots) > size_t(dev.smem_optin))
+    --a.slots;
+  if (ring_smem_bytes(a.box1, a.nbox, a.slots) > size_t(dev.smem_optin)) return 1;
+  CUtensorMap map;
+  std::string why;
+  if (!encode_map_2d_f32(&map, x, rows, width, rows, kRingTok, a.box1, &why))
+    return fail(TFX_ERR_CUDA, op, "tensor map", why);
+  a.w = w;
+  a.y = y;
+  a.rows = rows;
+  a.width = width;
+  a.tiles = (rows + kRingTok - 1) / kRingTok;
+  a.eps = eps;
+  a.inv_width = inv_width;
+  a.centered = centered;
+  const size_t smem = ring_smem_bytes(a.box1, a.nbox, a.slots);
+  if (a.nbox <= 4) return launch_ring<4>(op, map, a, smem, dev, stream);
+  return launch_ring<8>(op, map, a, smem, dev, stream);
+}
 
 // Streaming RMSNorm; 1 when the shape or alignment is not covered (nothing
 // launched), else a status. Needs rows % 4 == 0, 16-byte aligned x and y,

@@ -20,7 +20,7 @@ from oracle import oracle as orc
 from tfx import ops
 from helpers import assert_close, splitmix_normal, F32_RTOL, F32_ATOL_REL
 for rows, width in [(16384, 1024), (4096, 2048), (258, 1025), (63, 31), (1000, 4096), (7, 9),
-                   (1000, 1000), (20000, 64)]:
+                   (1000, 1000), (20000, 64), (1004, 1500), (20, 600), (16388, 768)]:
     x = splitmix_normal(rows * width, 0x7E4F0900 + rows)
     w = splitmix_normal(width, 0x7E4F0901 + width, mean=1.0, std=0.1)
     for centered in (True, False):
@@ -32,7 +32,7 @@ print("variant ok")
 """
 
 
-@pytest.mark.parametrize("variant", ["cluster", "cluster16", "tile", "split", "stream"])
+@pytest.mark.parametrize("variant", ["cluster", "cluster16", "tile", "split", "stream", "ring"])
 def test_rms_variant(variant):
     code = SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
                          tests=os.path.join(ROOT, "tests"))
