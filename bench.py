@@ -224,6 +224,49 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------
 # our arm
 
+def pcie_rates(torch, device, nbytes=256 << 20):
+    """Pinned host <-> device copy rates in GB/s: each direction alone and
+    both at once (per direction); best of 3, host clock around synchronised
+    copies of 256 MiB."""
+    n = nbytes // 4
+    h_in = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    h_out = torch.empty(n, dtype=torch.float32, pin_memory=True)
+    d_in = torch.empty(n, dtype=torch.float32, device=device)
+    d_out = torch.empty(n, dtype=torch.float32, device=device)
+    s1, s2 = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def best(fn):
+        out = 1e30
+        for _ in range(3):
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(device)
+            out = min(out, time.perf_counter() - t0)
+        return out
+
+    def both():
+        with torch.cuda.stream(s1):
+            d_in.copy_(h_in, non_blocking=True)
+        with torch.cuda.stream(s2):
+            h_out.copy_(d_out, non_blocking=True)
+
+    up = best(lambda: d_in.copy_(h_in, non_blocking=True))
+    down = best(lambda: h_out.copy_(d_out, non_blocking=True))
+    bi = best(both)
+    return {"h2d": round(nbytes / up / 1e9, 1), "d2h": round(nbytes / down / 1e9, 1),
+            "both_each": round(nbytes / bi / 1e9, 1)}
+
+
+def pcie_call_seconds(bytes_in, bytes_out, pcie):
+    """Copy time of one host-buffer call: both directions at the concurrent
+    rate until the smaller is done, the rest at that direction's own rate."""
+    both = min(bytes_in, bytes_out)
+    rest_in, rest_out = bytes_in - both, bytes_out - both
+    return (both / (pcie["both_each"] * 1e9) + rest_in / (pcie["h2d"] * 1e9) +
+            rest_out / (pcie["d2h"] * 1e9))
+
+
 class Chain:
     """Device buffers and launch sequence of one chain step on this GPU."""
 
@@ -572,8 +615,10 @@ def run_ours(args):
         sess.geglu(hu, chain.I, out=hg)
 
     nb = lambda *ts: sum(t.numel() * t.element_size() for t in ts)  # noqa: E731
-    h2d = nb(hx0, hg1, hqkv, hsc, hx0, hattn, hh2, hg2, hu)
-    d2h = nb(hh1, hqk, hpr, hh2, hh3, hg)
+    # the RoPE call moves only the q and k rows of qkv (2-D copies), not v
+    qk_bytes = 2 * chain.h * chain.L * chain.B * 4
+    h2d = nb(hx0, hg1, hsc, hx0, hattn, hh2, hg2, hu) + qk_bytes
+    d2h = nb(hh1, hpr, hh2, hh3, hg) + qk_bytes
     e2e_step(0)
     barrier()
     w0 = time.perf_counter()
@@ -584,6 +629,15 @@ def run_ours(args):
     sess.close()
     e2e_ms = max_over_ranks(e2e_ms)
     e2e_value = world * e2e_steps * bytes_per_step / (e2e_ms * 1e-3) / 1e9
+    # PCIe roofline of that leg: copy rates measured on every rank at once,
+    # and per call the time its copies need with both directions busy.
+    barrier()
+    pcie = pcie_rates(torch, device)
+    T, h = chain.L * chain.B, chain.h
+    per_call = [(h * T * 4, h * T * 4), (qk_bytes, qk_bytes),
+                (hsc.numel() * 4, hpr.numel() * 4), (2 * h * T * 4, h * T * 4),
+                (h * T * 4, h * T * 4), (hu.numel() * 4, hg.numel() * 4)]
+    bound_ms = max_over_ranks(1e3 * sum(pcie_call_seconds(i, o, pcie) for i, o in per_call))
 
     ops_results = None
     if not args.no_ops:
@@ -652,6 +706,10 @@ def run_ours(args):
                      "us_per_launch": round(sm_ms * 1e3, 2)},
         "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "ms_per_step": round(e2e_ms / e2e_steps, 3),
+                "pcie_bound_ms_per_step": round(bound_ms, 3),
+                "frac_of_pcie_bound": round(bound_ms / (e2e_ms / e2e_steps), 3),
+                "pcie_gbs": pcie,
                 "path": "tfx_session_* host-buffer calls (pinned host memory, chunked "
                         "copy-in / kernel / copy-out pipelined over 3 streams), host clock"},
         "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,

@@ -395,11 +395,14 @@ TFX_API int tfx_session_add_f32(tfx_session* session, const float* a, const floa
 /* desc->valid_lens / add_mask / keep are host pointers here. */
 TFX_API int tfx_session_masked_softmax_f32(tfx_session* session, const float* scores,
                                            float* probs, const tfx_softmax_desc* desc);
-/* Tables are built from base as tfx_rope_tables_f32 does (and cached). y is x
- * with the described vectors rotated: within the extent the descriptor spans
- * (from element 0 to the last element of the last vector), elements that are
- * not rotated are copied from x; elements of y beyond that extent (e.g. the v
- * block after the last token of a qkv tensor) are not written. */
+/* Tables are built from base as tfx_rope_tables_f32 does (and cached). The
+ * described vectors of y are those of x rotated (channels past rotary_dim
+ * copied), as tfx_rope_pairhalf_f32 writes them. Elements of y that belong to
+ * no described vector (e.g. the v block of a qkv tensor) are left unchanged
+ * when y == x and are otherwise unspecified: when the vectors of a position
+ * are contiguous channels at the start of evenly pitched rows (stride_feat 1;
+ * q and k of a feature-first qkv tensor, or q alone) only they are copied, as
+ * 2-D copies; other layouts copy each batch item's whole extent. */
 TFX_API int tfx_session_rope_pairhalf_f32(tfx_session* session, const float* x, float* y,
                                           double base, const tfx_rope_desc* desc);
 

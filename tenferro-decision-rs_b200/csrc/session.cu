@@ -149,16 +149,45 @@ int d2h(const char* op, void* dst, const void* src, size_t bytes, cudaStream_t s
   return err == cudaSuccess ? TFX_OK : cuda_fail(op, "copy to host", err);
 }
 
-// Runs `chunks` chunks of `unit_count` units (the last one shorter); stage()
-// gets (first unit, units, stream, slot) and enqueues copies and the kernel.
+// Chunk sizes for `units` units with at most `per` per chunk. A call costs
+// its copies plus the first chunk's copy-in (nothing else can run yet) and
+// the last chunk's kernel and copy-out (nothing else is left to overlap), so
+// the sizes ramp up (per/8, per/4, per/2) at the start and down again at the
+// end; every chunk but the last is a multiple of `align` units.
+std::vector<int64_t> plan_chunks(int64_t units, int64_t per, int64_t align) {
+  align = std::max<int64_t>(1, align);
+  auto al = [&](int64_t v) { return std::max(std::min(align, per), v / align * align); };
+  const int64_t ramp[3] = {al(per / 8), al(per / 4), al(per / 2)};
+  const int64_t back = ramp[0] + ramp[1] + ramp[2];
+  std::vector<int64_t> sizes;
+  int64_t left = units;
+  auto take = [&](int64_t n) {
+    n = std::min(std::max<int64_t>(n, 1), left);
+    sizes.push_back(n);
+    left -= n;
+  };
+  for (int i = 0; i < 3 && left > 0; ++i) take(ramp[i]);
+  while (left > back + per) take(per);
+  if (left > back) take(std::min(per, (left - back + align - 1) / align * align));
+  for (int i = 2; i >= 0 && left > 0; --i) take(i == 0 ? left : ramp[i]);
+  return sizes;
+}
+
+// Runs the call's chunks (plan_chunks; at most per_chunk units each, so each
+// fits a slot sized for per_chunk) round-robin over the session's streams;
+// stage() gets (first unit, units, stream, slot) and enqueues copies and the
+// kernel.
 template <class Stage>
-int pipeline(tfx_session* s, const char* op, int64_t units, int64_t per_chunk, Stage stage) {
+int pipeline(tfx_session* s, const char* op, int64_t units, int64_t per_chunk, Stage stage,
+             int64_t align = 1) {
   int rc = TFX_OK;
-  int64_t k = 0;
-  for (int64_t u0 = 0; u0 < units && rc == TFX_OK; u0 += per_chunk, ++k) {
-    const int64_t n = std::min(per_chunk, units - u0);
+  int64_t k = 0, u0 = 0;
+  for (const int64_t n : plan_chunks(units, per_chunk, align)) {
+    if (rc != TFX_OK) break;
     const int idx = int(k % tfx_session::kStreams);
     rc = stage(u0, n, s->streams[idx], s->slot[idx]);
+    u0 += n;
+    ++k;
   }
   const int rc2 = sync_all(s, op);
   return rc != TFX_OK ? rc : rc2;
@@ -325,7 +354,7 @@ int tfx_session_rmsnorm_last_f32(tfx_session* s, const float* x, const float* we
     err = cudaMemcpy2DAsync(y + r0, size_t(rows) * 4, out, size_t(n) * 4, size_t(n) * 4,
                             size_t(width), cudaMemcpyDeviceToHost, st);
     return err == cudaSuccess ? TFX_OK : cuda_fail(op, "copy to host", err);
-  });
+  }, 4);
 }
 
 // ---- elementwise -----------------------------------------------------------------
@@ -348,7 +377,7 @@ static int session_unary(tfx_session* s, const char* op, const float* x, float* 
     if (r == TFX_OK) r = kernel(in, out, m, st);
     if (r == TFX_OK) r = d2h(op, y + i0, out, size_t(m) * 4, st);
     return r;
-  });
+  }, 64);
 }
 
 extern "C" {
@@ -389,7 +418,7 @@ static int session_binary(tfx_session* s, const char* op, const float* a, const 
     if (r == TFX_OK) r = kernel(ia, ib, out, m, st);
     if (r == TFX_OK) r = d2h(op, y + i0, out, size_t(m) * 4, st);
     return r;
-  });
+  }, 64);
 }
 
 extern "C" {
@@ -533,6 +562,39 @@ int tfx_session_rope_pairhalf_f32(tfx_session* s, const float* x, float* y, doub
                                  {it->second.second.data(), it->second.second.size() * 4}},
                          &dev);
   if (rc != TFX_OK) return rc;
+  const float* cd = static_cast<const float*>(dev[0]);
+  const float* sd = static_cast<const float*>(dev[1]);
+  // Common layout (a qkv tensor, or q / k alone): the vectors of one position
+  // span W contiguous-channel floats at the start of a row, and rows (batch
+  // item, position) are evenly pitched. Then only those W floats of each row
+  // cross PCIe, as 2-D copies into a compact staging layout -- for the
+  // feature-first qkv of the chain, q and k but not v.
+  const int64_t W = (d.n_vec - 1) * d.stride_vec + (d.head_dim - 1) * d.stride_feat + 1;
+  const int64_t pitch = d.seq > 1 ? d.stride_pos : (d.batch > 1 ? d.stride_batch : W);
+  const bool rows2d = d.stride_feat == 1 && pitch >= W &&
+                      (d.seq == 1 || d.batch == 1 || d.stride_batch == d.seq * d.stride_pos);
+  if (rows2d) {
+    const int64_t per2 = units_per_chunk(s, 2 * d.seq * W * 4);
+    rc = ensure_slots(s, size_t(per2 * d.seq * W) * 4, op);
+    if (rc != TFX_OK) return rc;
+    return pipeline(s, op, d.batch, per2, [&](int64_t b0, int64_t n, cudaStream_t st, char* slot) {
+      float* buf = reinterpret_cast<float*>(slot);
+      const int64_t row0 = b0 * d.seq;
+      cudaError_t err = cudaMemcpy2DAsync(buf, size_t(W) * 4, x + row0 * pitch, size_t(pitch) * 4,
+                                          size_t(W) * 4, size_t(n * d.seq),
+                                          cudaMemcpyHostToDevice, st);
+      if (err != cudaSuccess) return cuda_fail(op, "copy to device", err);
+      tfx_rope_desc cd_desc = d;
+      cd_desc.batch = n;
+      cd_desc.stride_pos = W;
+      cd_desc.stride_batch = d.seq * W;
+      const int r = tfx_rope_pairhalf_f32(buf, buf, cd, sd, &cd_desc, st);
+      if (r != TFX_OK) return r;
+      err = cudaMemcpy2DAsync(y + row0 * pitch, size_t(pitch) * 4, buf, size_t(W) * 4,
+                              size_t(W) * 4, size_t(n * d.seq), cudaMemcpyDeviceToHost, st);
+      return err == cudaSuccess ? TFX_OK : cuda_fail(op, "copy to host", err);
+    });
+  }
   // Extent of one batch item; batch items are chunked when they are laid out
   // one after another (batch is the outermost axis).
   const int64_t item = 1 + (d.n_vec - 1) * d.stride_vec + (d.seq - 1) * d.stride_pos +
@@ -545,8 +607,6 @@ int tfx_session_rope_pairhalf_f32(tfx_session* s, const float* x, float* y, doub
   const int64_t span = batch_outer ? (per - 1) * unit + item : total;
   rc = ensure_slots(s, size_t(span) * 4, op);
   if (rc != TFX_OK) return rc;
-  const float* cd = static_cast<const float*>(dev[0]);
-  const float* sd = static_cast<const float*>(dev[1]);
   return pipeline(s, op, d.batch, per, [&](int64_t b0, int64_t n, cudaStream_t st, char* slot) {
     float* buf = reinterpret_cast<float*>(slot);
     const int64_t first = batch_outer ? b0 * unit : 0;

@@ -95,3 +95,53 @@ def test_session_pinned_torch_tensors(orc, sess):
     y = torch.empty(n, dtype=torch.float32).pin_memory()
     sess.gelu_erf(x, out=y)
     assert_bitwise(y.numpy(), orc.gelu_erf_f32(x.numpy()), "session pinned gelu")
+
+
+def _vector_mask(size, n_vec, L, B, hd, strides):
+    sv, sp, sb, sf = strides
+    idx = (np.arange(n_vec)[:, None, None, None] * sv + np.arange(L)[None, :, None, None] * sp +
+           np.arange(B)[None, None, :, None] * sb + np.arange(hd)[None, None, None, :] * sf)
+    mask = np.zeros(size, dtype=bool)
+    mask[idx.ravel()] = True
+    return mask
+
+
+def test_session_rope_rows_copy_only_the_vectors(orc, sess):
+    # q and k of a feature-first qkv (3h, L, B): only their rows cross PCIe;
+    # v is not part of the call and y's v block keeps what it held.
+    hidden, hd, L, B = 768, 64, 512, 3
+    x = splitmix_normal(3 * hidden * L * B, 0x7E4F0860)
+    strides = (hd, 3 * hidden, 3 * hidden * L, 1)
+    y0 = np.full_like(x, 7.0)
+    y = sess.rope_pairhalf(x, 10000.0, 24, L, B, hd, hd, strides, out=y0.copy())
+    c, s = orc.rope_tables_f32(10000.0, L, hd)
+    want = orc.rope_pairhalf_f32(x, c, s, 24, L, B, hd, hd, strides)
+    m = _vector_mask(x.size, 24, L, B, hd, strides)
+    assert_bitwise(y[m], want[m], "session rope vectors")
+    assert np.all(y[~m] == 7.0), "session rope wrote outside the vectors"
+
+
+def test_session_rope_padded_batch_items_take_the_extent_copy(orc, sess):
+    # batch items padded apart (stride_batch != seq * stride_pos): whole extents
+    hidden, hd, L, B, pad = 256, 32, 100, 4, 96
+    strides = (hd, 3 * hidden, 3 * hidden * L + pad, 1)
+    x = splitmix_normal(strides[2] * B, 0x7E4F0861)
+    y = sess.rope_pairhalf(x, 160000.0, 16, L, B, hd, hd, strides, out=x.copy())
+    c, s = orc.rope_tables_f32(160000.0, L, hd)
+    assert_bitwise(y, orc.rope_pairhalf_f32(x, c, s, 16, L, B, hd, hd, strides),
+                   "session rope padded items")
+
+
+@pytest.mark.parametrize("cols", [1, 5, 63, 64, 65, 200, 1000])
+def test_session_chunk_plan_covers_every_column(orc, cols):
+    # 16 KiB chunks of 768-float columns: 2 units per chunk at most, so the
+    # ramped plan runs through its small-call and tail branches.
+    d = 768
+    x = splitmix_normal(d * cols, 0x7E4F0870 + cols)
+    w = splitmix_uniform(d, 0x7E4F0871, 0.5, 1.5)
+    with Session(0, chunk_bytes=16 * 1024 * 4) as s:
+        y = s.layer_norm_feature_first(x, w, None, 1e-5)
+        g = s.gelu_erf(x)
+    assert_close(y, orc.layer_norm_feature_first_f32(x, d, cols, w, None, 1e-5), F32_RTOL,
+                 F32_ATOL_REL, f"chunked layernorm {cols}")
+    assert_bitwise(g, orc.gelu_erf_f32(x), f"chunked gelu {cols}")
