@@ -224,6 +224,28 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------
 # our arm
 
+def bind_numa_local_cpus(torch, device):
+    """Restricts this process to the CPUs NVML reports as closest to `device`
+    (read-only query; nothing on the GPU is set), so that the pinned host
+    buffers it allocates afterwards are first touched on the GPU's own NUMA
+    node. Returns the number of CPUs kept, or None when NVML is unavailable."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cpus = {64 * i + b for i, w in enumerate(words) for b in range(64) if (int(w) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return len(cpus)
+    except Exception:
+        pass
+    return None
+
+
 def pcie_rates(torch, device, nbytes=256 << 20):
     """Pinned host <-> device copy rates in GB/s: each direction alone and
     both at once (per direction); best of 3, host clock around synchronised
@@ -539,6 +561,10 @@ def run_ours(args):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    # keep the process on its GPU's NUMA node while the e2e leg's pinned
+    # buffers are allocated and used (all host CPUs again for the CPU baseline)
+    all_cpus = os.sched_getaffinity(0)
+    numa_cpus = bind_numa_local_cpus(torch, device)
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
@@ -638,6 +664,7 @@ def run_ours(args):
                 (hsc.numel() * 4, hpr.numel() * 4), (2 * h * T * 4, h * T * 4),
                 (h * T * 4, h * T * 4), (hu.numel() * 4, hg.numel() * 4)]
     bound_ms = max_over_ranks(1e3 * sum(pcie_call_seconds(i, o, pcie) for i, o in per_call))
+    os.sched_setaffinity(0, all_cpus)
 
     ops_results = None
     if not args.no_ops:
@@ -709,7 +736,7 @@ def run_ours(args):
                 "ms_per_step": round(e2e_ms / e2e_steps, 3),
                 "pcie_bound_ms_per_step": round(bound_ms, 3),
                 "frac_of_pcie_bound": round(bound_ms / (e2e_ms / e2e_steps), 3),
-                "pcie_gbs": pcie,
+                "pcie_gbs": pcie, "numa_local_cpus": numa_cpus,
                 "path": "tfx_session_* host-buffer calls (pinned host memory, chunked "
                         "copy-in / kernel / copy-out pipelined over 3 streams), host clock"},
         "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,
