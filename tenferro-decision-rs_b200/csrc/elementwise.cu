@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tfx_math.h"
@@ -89,29 +90,96 @@ __global__ void __launch_bounds__(kThreads) map_kernel(uint32_t n, F f) {
   }
 }
 
+// Software-pipelined driver: the loads of a thread's next iteration are issued
+// before the current one is computed and stored, so every thread keeps U
+// vectors in flight through its arithmetic and stores instead of only between
+// iterations. Functors opt in with kPipelined. Measured on one B200 (CUDA
+// graph, rotating buffers): gated SiLU 116.2 -> 110.7 us, bias 9.9 -> 9.1 us,
+// GeGLU with one vector per thread 20.2 -> 19.4 us; erf / GELU stay on the
+// plain driver with two vectors per thread (29.0 -> 28.4 us), where the
+// pipelined one measured 30.4 us (more registers, fewer resident CTAs).
+template <class F, int U>
+__global__ void __launch_bounds__(kThreads) map_pipelined_kernel(uint32_t n, F f) {
+  pdl_enter();
+  const uint32_t step = gridDim.x * (kThreads * U);
+  uint32_t base = blockIdx.x * (kThreads * U) + threadIdx.x;
+  typename F::In cur[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint32_t i = base + u * kThreads;
+    if (i < n) cur[u] = f.load(i);
+  }
+  while (base < n) {
+    const bool more = base <= 0xFFFFFFFFu - step && base + step < n;  // next base in range
+    const uint32_t next = base + step;
+    typename F::In nxt[U];
+    if (more) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const uint32_t i = next + u * kThreads;
+        if (i < n) nxt[u] = f.load(i);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t i = base + u * kThreads;
+      if (i < n) f.store(i, cur[u]);
+    }
+    if (!more) break;
+#pragma unroll
+    for (int u = 0; u < U; ++u) cur[u] = nxt[u];
+    base = next;
+  }
+}
+
+// 1 = software-pipelined driver for functors that declare kPipelined (the
+// default), 0 = the plain driver everywhere; TFX_MAP_KERNEL=plain selects 0
+// for tuning runs.
+bool map_pipelining() {
+  static const bool on = [] {
+    const char* e = getenv("TFX_MAP_KERNEL");
+    return !(e && std::string(e) == "plain");
+  }();
+  return on;
+}
+
+template <class F, class = void>
+struct Pipelined : std::false_type {};
+template <class F>
+struct Pipelined<F, std::void_t<decltype(F::kPipelined)>>
+    : std::integral_constant<bool, F::kPipelined> {};
+template <class F>
+constexpr bool pipelined_functor() {
+  return Pipelined<F>::value;
+}
+
 template <class F, int U>
 int launch_map(const char* op, uint32_t n, const F& f, cudaStream_t stream) {
   if (n == 0) return TFX_OK;
   int st = TFX_OK;
   const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
-  static int occupancy = 0;  // per instantiation; identical on every B200
-  if (occupancy == 0) {
+  const bool piped = pipelined_functor<F>() && map_pipelining();
+  auto kernel = piped ? map_pipelined_kernel<F, U> : map_kernel<F, U>;
+  static int occupancy[2] = {0, 0};  // per instantiation; identical on every B200
+  int& occ = occupancy[piped ? 1 : 0];
+  if (occ == 0) {
     int blocks = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, map_kernel<F, U>, kThreads, 0) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, 0) !=
             cudaSuccess || blocks <= 0)
       blocks = 1;
-    occupancy = blocks;
+    occ = blocks;
   }
   const uint64_t need = (uint64_t(n) + kThreads * U - 1) / (kThreads * U);
-  const uint32_t grid = uint32_t(std::min<uint64_t>(need, uint64_t(dev.sms) * occupancy));
-  return launch_kernel(op, map_kernel<F, U>, dim3(grid), dim3(kThreads), 0, stream, 1, n, f);
+  const uint32_t grid = uint32_t(std::min<uint64_t>(need, uint64_t(dev.sms) * occ));
+  return launch_kernel(op, kernel, dim3(grid), dim3(kThreads), 0, stream, 1, n, f);
 }
 
 // ---- functors ------------------------------------------------------------------
 
 template <int N>
 struct ErfF {
+  static constexpr int kUnroll = 2;
   using In = Vec<N>;
   const float* x;
   float* y;
@@ -124,6 +192,7 @@ struct ErfF {
 
 template <int N>
 struct GeluF {
+  static constexpr int kUnroll = 2;
   using In = Vec<N>;
   const float* x;
   float* y;
@@ -138,6 +207,7 @@ struct GeluF {
 // [N*o, N*o + N) of the flattened (I, cols) result.
 template <int N>
 struct GegluF {
+  static constexpr bool kPipelined = true;
   struct In {
     Vec<N> v, g;
   };
@@ -175,6 +245,7 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 
 template <int N>
 struct SiluF {
+  static constexpr bool kPipelined = true;
   struct In {
     Vec<N> g, u;
   };
@@ -192,6 +263,7 @@ struct SiluF {
 
 template <int N>
 struct AddF {
+  static constexpr bool kPipelined = true;
   struct In {
     Vec<N> a, b;
   };
@@ -217,6 +289,7 @@ struct AddF {
 // (N*i) mod F. ACT: 0 identity, 1 GELU (reference erf), 2 ReLU.
 template <int N, int ACT, bool BIAS>
 struct BiasActF {
+  static constexpr bool kPipelined = ACT != 1;  // the GELU epilogue is arithmetic-bound like GeluF
   using In = Vec<N>;
   const float* x;
   const float* bias;
@@ -295,11 +368,18 @@ int vec_width(int64_t n, std::initializer_list<const void*> ptrs) {
 
 constexpr int64_t kMaxVectors = int64_t(1) << 31;
 
+// Vectors per thread and iteration for a functor: F::kUnroll, else 4.
+template <class F, class = void>
+struct Unroll : std::integral_constant<int, 4> {};
+template <class F>
+struct Unroll<F, std::void_t<decltype(F::kUnroll)>> : std::integral_constant<int, F::kUnroll> {};
+
 template <template <int> class F, class Make>
 int run_flat(const char* op, int64_t n, int width, Make make, cudaStream_t stream) {
   if (n / width >= kMaxVectors)
     return fail(TFX_ERR_UNSUPPORTED, op, "n", "more than 2^31 vectors in one call");
-  if (width == 4) return launch_map<F<4>, 4>(op, uint32_t(n / 4), make(F<4>{}), stream);
+  if (width == 4)
+    return launch_map<F<4>, Unroll<F<4>>::value>(op, uint32_t(n / 4), make(F<4>{}), stream);
   if (width == 2) return launch_map<F<2>, 4>(op, uint32_t(n / 2), make(F<2>{}), stream);
   return launch_map<F<1>, 8>(op, uint32_t(n), make(F<1>{}), stream);
 }
@@ -384,7 +464,7 @@ int tfx_geglu_ff_f32(const float* u, float* y, int64_t inter, int64_t cols, tfx_
     f.per_col = FastDiv(uint32_t(inter / w));
     return f;
   };
-  if (w == 4) return launch_map<GegluF<4>, 2>(op, uint32_t(n_out / 4), make(GegluF<4>{}), stream);
+  if (w == 4) return launch_map<GegluF<4>, 1>(op, uint32_t(n_out / 4), make(GegluF<4>{}), stream);
   if (w == 2) return launch_map<GegluF<2>, 4>(op, uint32_t(n_out / 2), make(GegluF<2>{}), stream);
   return launch_map<GegluF<1>, 8>(op, uint32_t(n_out), make(GegluF<1>{}), stream);
 }
