@@ -366,7 +366,10 @@ int vec_width(int64_t n, std::initializer_list<const void*> ptrs) {
   return a16 ? 4 : (a8 ? 2 : 1);
 }
 
-constexpr int64_t kMaxVectors = int64_t(1) << 31;
+// Vectors per launch: the kernels index vectors with 32 bits, so larger
+// tensors run as several launches over consecutive ranges (each a multiple of
+// 2^30 vectors, which keeps every range's base as aligned as the tensor's).
+constexpr int64_t kLaunchVectors = int64_t(1) << 30;
 
 // Vectors per thread and iteration for a functor: F::kUnroll, else 4.
 template <class F, class = void>
@@ -374,14 +377,22 @@ struct Unroll : std::integral_constant<int, 4> {};
 template <class F>
 struct Unroll<F, std::void_t<decltype(F::kUnroll)>> : std::integral_constant<int, F::kUnroll> {};
 
+// make(functor, element offset) points the functor at the range starting there.
 template <template <int> class F, class Make>
 int run_flat(const char* op, int64_t n, int width, Make make, cudaStream_t stream) {
-  if (n / width >= kMaxVectors)
-    return fail(TFX_ERR_UNSUPPORTED, op, "n", "more than 2^31 vectors in one call");
-  if (width == 4)
-    return launch_map<F<4>, Unroll<F<4>>::value>(op, uint32_t(n / 4), make(F<4>{}), stream);
-  if (width == 2) return launch_map<F<2>, 4>(op, uint32_t(n / 2), make(F<2>{}), stream);
-  return launch_map<F<1>, 8>(op, uint32_t(n), make(F<1>{}), stream);
+  const int64_t step = kLaunchVectors * width;
+  for (int64_t off = 0; off < n; off += step) {
+    const uint32_t nv = uint32_t(std::min(step, n - off) / width);
+    int rc;
+    if (width == 4)
+      rc = launch_map<F<4>, Unroll<F<4>>::value>(op, nv, make(F<4>{}, off), stream);
+    else if (width == 2)
+      rc = launch_map<F<2>, 4>(op, nv, make(F<2>{}, off), stream);
+    else
+      rc = launch_map<F<1>, 8>(op, nv, make(F<1>{}, off), stream);
+    if (rc != TFX_OK) return rc;
+  }
+  return TFX_OK;
 }
 
 }  // namespace
@@ -399,7 +410,8 @@ int tfx_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream) {
   TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
   TFX_REQUIRE(x == y || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
   const int w = vec_width(n, {x, y});
-  return run_flat<ErfF>(op, n, w, [&](auto f) { f.x = x; f.y = y; return f; }, stream);
+  return run_flat<ErfF>(op, n, w, [&](auto f, int64_t o) { f.x = x + o; f.y = y + o; return f; },
+                        stream);
 }
 
 int tfx_gelu_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream) {
@@ -410,7 +422,8 @@ int tfx_gelu_erf_f32(const float* x, float* y, int64_t n, tfx_stream_t stream) {
   TFX_REQUIRE(x && y, op, x ? "y" : "x", "null pointer");
   TFX_REQUIRE(x == y || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
   const int w = vec_width(n, {x, y});
-  return run_flat<GeluF>(op, n, w, [&](auto f) { f.x = x; f.y = y; return f; }, stream);
+  return run_flat<GeluF>(op, n, w, [&](auto f, int64_t o) { f.x = x + o; f.y = y + o; return f; },
+                         stream);
 }
 
 int tfx_erf_f64(const double* x, double* y, int64_t n, tfx_stream_t stream) {
@@ -455,18 +468,27 @@ int tfx_geglu_ff_f32(const float* u, float* y, int64_t inter, int64_t cols, tfx_
   TFX_REQUIRE(!overlaps(u, size_t(2 * n_out) * 4, y, size_t(n_out) * 4), op, "y",
               "output overlaps the input");
   int w = vec_width(inter, {u, y});
-  if (n_out / w >= kMaxVectors || inter / w > 0xFFFFFFFFll)
-    return fail(TFX_ERR_UNSUPPORTED, op, "shape", "more than 2^31 output vectors in one call");
-  auto make = [&](auto f) {
-    f.u = u;
-    f.y = y;
-    f.inter_vec = uint32_t(inter / w);
-    f.per_col = FastDiv(uint32_t(inter / w));
-    return f;
-  };
-  if (w == 4) return launch_map<GegluF<4>, 1>(op, uint32_t(n_out / 4), make(GegluF<4>{}), stream);
-  if (w == 2) return launch_map<GegluF<2>, 4>(op, uint32_t(n_out / 2), make(GegluF<2>{}), stream);
-  return launch_map<GegluF<1>, 8>(op, uint32_t(n_out), make(GegluF<1>{}), stream);
+  if (inter / w > kLaunchVectors)
+    return fail(TFX_ERR_UNSUPPORTED, op, "intermediate", "more than 2^30 vectors per column");
+  // whole columns per launch, at most 2^30 output vectors
+  const int64_t step = std::max<int64_t>(1, kLaunchVectors / (inter / w));
+  for (int64_t c0 = 0; c0 < cols; c0 += step) {
+    const int64_t nc = std::min(step, cols - c0);
+    const uint32_t nv = uint32_t(nc * (inter / w));
+    auto make = [&](auto f) {
+      f.u = u + c0 * 2 * inter;
+      f.y = y + c0 * inter;
+      f.inter_vec = uint32_t(inter / w);
+      f.per_col = FastDiv(uint32_t(inter / w));
+      return f;
+    };
+    int rc;
+    if (w == 4) rc = launch_map<GegluF<4>, 1>(op, nv, make(GegluF<4>{}), stream);
+    else if (w == 2) rc = launch_map<GegluF<2>, 4>(op, nv, make(GegluF<2>{}), stream);
+    else rc = launch_map<GegluF<1>, 8>(op, nv, make(GegluF<1>{}), stream);
+    if (rc != TFX_OK) return rc;
+  }
+  return TFX_OK;
 }
 
 int tfx_gated_silu_f32(const float* gate, const float* up, float* y, int64_t n,
@@ -479,8 +501,9 @@ int tfx_gated_silu_f32(const float* gate, const float* up, float* y, int64_t n,
   TFX_REQUIRE(y == gate || !overlaps(gate, n * 4, y, n * 4), op, "y", "partially overlaps gate");
   TFX_REQUIRE(y == up || !overlaps(up, n * 4, y, n * 4), op, "y", "partially overlaps up");
   const int w = vec_width(n, {gate, up, y});
-  return run_flat<SiluF>(op, n, w, [&](auto f) { f.gate = gate; f.up = up; f.y = y; return f; },
-                         stream);
+  return run_flat<SiluF>(
+      op, n, w,
+      [&](auto f, int64_t o) { f.gate = gate + o; f.up = up + o; f.y = y + o; return f; }, stream);
 }
 
 int tfx_gated_silu_stacked_f32(const float* gu, float* y, int64_t rows, int64_t inter,
@@ -496,8 +519,9 @@ int tfx_gated_silu_stacked_f32(const float* gu, float* y, int64_t rows, int64_t 
   const float* g = gu;
   const float* u = gu + n;  // column blocks gate | up of the column-major (rows, 2I)
   const int w = vec_width(n, {g, u, y});
-  return run_flat<SiluF>(op, n, w, [&](auto f) { f.gate = g; f.up = u; f.y = y; return f; },
-                         stream);
+  return run_flat<SiluF>(
+      op, n, w, [&](auto f, int64_t o) { f.gate = g + o; f.up = u + o; f.y = y + o; return f; },
+      stream);
 }
 
 int tfx_add_f32(const float* a, const float* b, float* y, int64_t n, tfx_stream_t stream) {
@@ -509,7 +533,9 @@ int tfx_add_f32(const float* a, const float* b, float* y, int64_t n, tfx_stream_
   TFX_REQUIRE(y == a || !overlaps(a, n * 4, y, n * 4), op, "y", "partially overlaps a");
   TFX_REQUIRE(y == b || !overlaps(b, n * 4, y, n * 4), op, "y", "partially overlaps b");
   const int w = vec_width(n, {a, b, y});
-  return run_flat<AddF>(op, n, w, [&](auto f) { f.a = a; f.b = b; f.y = y; return f; }, stream);
+  return run_flat<AddF>(
+      op, n, w, [&](auto f, int64_t o) { f.a = a + o; f.b = b + o; f.y = y + o; return f; },
+      stream);
 }
 
 int tfx_bias_act_ff_f32(const float* x, const float* bias, float* y, int64_t features,
@@ -525,16 +551,22 @@ int tfx_bias_act_ff_f32(const float* x, const float* bias, float* y, int64_t fea
   TFX_REQUIRE(y == x || !overlaps(x, n * 4, y, n * 4), op, "y", "partially overlaps x");
   TFX_REQUIRE(!bias || !overlaps(bias, features * 4, y, n * 4), op, "bias", "overlaps y");
   const int w = bias ? vec_width(features, {x, y, bias}) : vec_width(n, {x, y});
-  if (n / w >= kMaxVectors || features / w > 0xFFFFFFFFll)
-    return fail(TFX_ERR_UNSUPPORTED, op, "shape", "more than 2^31 vectors in one call");
-  const uint32_t nv = uint32_t(n / w);
+  if (features / w > kLaunchVectors)
+    return fail(TFX_ERR_UNSUPPORTED, op, "features", "more than 2^30 vectors per token");
+  // Launch ranges: whole tokens when a bias is indexed by feature, else flat.
+  const int64_t step = bias ? (kLaunchVectors / (features / w)) * features : kLaunchVectors * w;
   auto go = [&](auto f, auto unroll) {
-    f.x = x;
-    f.bias = bias;
-    f.y = y;
-    f.feat_vec = uint32_t(features / w);
-    f.per_tok = FastDiv(uint32_t(features / w));
-    return launch_map<decltype(f), decltype(unroll)::value>(op, nv, f, stream);
+    for (int64_t off = 0; off < n; off += step) {
+      f.x = x + off;
+      f.bias = bias;
+      f.y = y + off;
+      f.feat_vec = uint32_t(features / w);
+      f.per_tok = FastDiv(uint32_t(features / w));
+      const uint32_t nv = uint32_t(std::min(step, n - off) / w);
+      const int rc = launch_map<decltype(f), decltype(unroll)::value>(op, nv, f, stream);
+      if (rc != TFX_OK) return rc;
+    }
+    return int(TFX_OK);
   };
   using U4 = std::integral_constant<int, 4>;
   using U8 = std::integral_constant<int, 8>;
