@@ -392,6 +392,11 @@ TFX_API int tfx_session_bias_act_ff_f32(tfx_session* session, const float* x,
                                         int64_t tokens, int act);
 TFX_API int tfx_session_add_f32(tfx_session* session, const float* a, const float* b, float* y,
                                 int64_t n);
+/* tfx_add_layernorm_ff_f32 on host buffers (sum_out may be NULL). */
+TFX_API int tfx_session_add_layernorm_ff_f32(tfx_session* session, const float* a,
+                                             const float* b, const float* weight,
+                                             const float* bias, float* sum_out, float* y,
+                                             int64_t d, int64_t cols, float eps);
 /* desc->valid_lens / add_mask / keep are host pointers here. */
 TFX_API int tfx_session_masked_softmax_f32(tfx_session* session, const float* scores,
                                            float* probs, const tfx_softmax_desc* desc);

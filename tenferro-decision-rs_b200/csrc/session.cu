@@ -327,6 +327,42 @@ int tfx_session_layernorm_ff_f64(tfx_session* s, const double* x, const double* 
           int64_t n, cudaStream_t st) { return tfx_layernorm_ff_f64(in, w, b, out, dd, n, eps, st); });
 }
 
+// The residual add fused into the LayerNorm that follows it: a and b in, the
+// sum (when sum_out is not NULL) and y out, per chunk of columns.
+int tfx_session_add_layernorm_ff_f32(tfx_session* s, const float* a, const float* b,
+                                     const float* weight, const float* bias, float* sum_out,
+                                     float* y, int64_t d, int64_t cols, float eps) {
+  const char* op = "tenferro-ext::add_layernorm_ff";
+  TFX_SESSION_ENTER(op);
+  TFX_REQUIRE(d >= 0 && cols >= 0, op, "shape", "extents must be non-negative");
+  if (d == 0 || cols == 0) return TFX_OK;
+  TFX_REQUIRE(a && b && weight && y, op, !a ? "a" : (!b ? "b" : (!weight ? "weight" : "y")),
+              "null pointer");
+  std::vector<const void*> dev;
+  int rc = upload_params(s, op, {{weight, size_t(d) * 4}, {bias, bias ? size_t(d) * 4 : 0}},
+                         &dev);
+  if (rc != TFX_OK) return rc;
+  const int64_t planes = sum_out ? 4 : 3;  // a, b, y (+ sum)
+  const int64_t per = units_per_chunk(s, planes * d * 4);
+  rc = ensure_slots(s, size_t(planes * per * d) * 4, op);
+  if (rc != TFX_OK) return rc;
+  const float* wd = static_cast<const float*>(dev[0]);
+  const float* bd = static_cast<const float*>(dev[1]);
+  return pipeline(s, op, cols, per, [&](int64_t c0, int64_t n, cudaStream_t st, char* slot) {
+    float* ia = reinterpret_cast<float*>(slot);
+    float* ib = ia + per * d;
+    float* oy = ib + per * d;
+    float* os = sum_out ? oy + per * d : nullptr;
+    const size_t bytes = size_t(n * d) * 4;
+    int r = h2d(op, ia, a + c0 * d, bytes, st);
+    if (r == TFX_OK) r = h2d(op, ib, b + c0 * d, bytes, st);
+    if (r == TFX_OK) r = tfx_add_layernorm_ff_f32(ia, ib, wd, bd, os, oy, d, n, eps, st);
+    if (r == TFX_OK && os) r = d2h(op, sum_out + c0 * d, os, bytes, st);
+    if (r == TFX_OK) r = d2h(op, y + c0 * d, oy, bytes, st);
+    return r;
+  });
+}
+
 // ---- RMSNorm (rows, width), feature-last: chunks of rows are strided blocks ------
 
 int tfx_session_rmsnorm_last_f32(tfx_session* s, const float* x, const float* weight, float* y,

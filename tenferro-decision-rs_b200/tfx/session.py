@@ -125,6 +125,16 @@ class Session:
         check(lib.tfx_session_add_f32(self._h, _hptr(a), _hptr(b), _hptr(y), _numel(a)))
         return y
 
+    def add_layer_norm_feature_first(self, a, b, weight, bias=None, eps=1e-5, sum_out=None,
+                                     out=None):
+        """s = a + b and LayerNorm(s) on host buffers; returns (s or None, y)."""
+        d = _numel(weight)
+        y = _empty_like(a) if out is None else out
+        check(lib.tfx_session_add_layernorm_ff_f32(self._h, _hptr(a), _hptr(b), _hptr(weight),
+                                                   _hptr(bias), _hptr(sum_out), _hptr(y), d,
+                                                   _numel(a) // d, ctypes.c_float(eps)))
+        return sum_out, y
+
     def masked_softmax(self, scores, batch, heads, q_len, k_len, *, scale=1.0,
                        semantics=TFX_SOFTMAX_EXCLUDE, causal=False, window=-1,
                        window_skips_invalid_query=False, valid_len=-1, valid_lens=None,

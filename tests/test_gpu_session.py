@@ -145,3 +145,18 @@ def test_session_chunk_plan_covers_every_column(orc, cols):
     assert_close(y, orc.layer_norm_feature_first_f32(x, d, cols, w, None, 1e-5), F32_RTOL,
                  F32_ATOL_REL, f"chunked layernorm {cols}")
     assert_bitwise(g, orc.gelu_erf_f32(x), f"chunked gelu {cols}")
+
+
+def test_session_add_layernorm_matches_the_two_ops(orc, sess):
+    d, cols = 768, 2999
+    a = splitmix_normal(d * cols, 0x7E4F0880)
+    b = splitmix_normal(d * cols, 0x7E4F0881)
+    w = splitmix_uniform(d, 0x7E4F0882, 0.5, 1.5)
+    s_want = orc.add_f32(a, b)
+    y_want = sess.layer_norm_feature_first(s_want, w, None, 1e-5)
+    s_got, y_got = sess.add_layer_norm_feature_first(a, b, w, None, 1e-5,
+                                                     sum_out=np.empty_like(a))
+    assert_bitwise(s_got, s_want, "session add+ln sum")
+    assert_bitwise(y_got, y_want, "session add+ln y")
+    _, y_only = sess.add_layer_norm_feature_first(a, b, w, None, 1e-5)
+    assert_bitwise(y_only, y_want, "session add+ln without sum")
