@@ -12,6 +12,7 @@
 // holds and is kept for later calls; tfx_session_destroy frees it.
 
 #include <algorithm>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <string>
@@ -22,11 +23,12 @@
 #include "internal.h"
 
 struct tfx_session {
-  static constexpr int kStreams = 3;
+  static constexpr int kMaxStreams = 8;
   int device = 0;
-  cudaStream_t streams[kStreams] = {};
+  int nstreams = 3;  // streams (and staging slots) a call's chunks rotate over
+  cudaStream_t streams[kMaxStreams] = {};
   cudaEvent_t params_ready = nullptr;
-  char* slot[kStreams] = {};
+  char* slot[kMaxStreams] = {};
   size_t slot_cap = 0;
   char* params = nullptr;
   size_t params_cap = 0;
@@ -61,8 +63,8 @@ class DeviceGuard {
 };
 
 int sync_all(tfx_session* s, const char* op) {
-  for (auto st : s->streams) {
-    const cudaError_t err = cudaStreamSynchronize(st);
+  for (int i = 0; i < s->nstreams; ++i) {
+    const cudaError_t err = cudaStreamSynchronize(s->streams[i]);
     if (err != cudaSuccess) return cuda_fail(op, "stream", err);
   }
   return TFX_OK;
@@ -77,8 +79,8 @@ int ensure_slots(tfx_session* s, size_t bytes, const char* op) {
     p = nullptr;
   }
   s->slot_cap = 0;
-  for (auto& p : s->slot) {
-    const cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&p), bytes);
+  for (int i = 0; i < s->nstreams; ++i) {
+    const cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&s->slot[i]), bytes);
     if (err != cudaSuccess) return cuda_fail(op, "staging", err);
   }
   s->slot_cap = bytes;
@@ -132,7 +134,7 @@ int upload_params(tfx_session* s, const char* op, std::initializer_list<Param> i
   }
   cudaError_t err = cudaEventRecord(s->params_ready, s->streams[0]);
   if (err != cudaSuccess) return cuda_fail(op, "params", err);
-  for (int k = 1; k < tfx_session::kStreams; ++k) {
+  for (int k = 1; k < s->nstreams; ++k) {
     err = cudaStreamWaitEvent(s->streams[k], s->params_ready, 0);
     if (err != cudaSuccess) return cuda_fail(op, "params", err);
   }
@@ -184,7 +186,7 @@ int pipeline(tfx_session* s, const char* op, int64_t units, int64_t per_chunk, S
   int64_t k = 0, u0 = 0;
   for (const int64_t n : plan_chunks(units, per_chunk, align)) {
     if (rc != TFX_OK) break;
-    const int idx = int(k % tfx_session::kStreams);
+    const int idx = int(k % s->nstreams);
     rc = stage(u0, n, s->streams[idx], s->slot[idx]);
     u0 += n;
     ++k;
@@ -231,8 +233,10 @@ int tfx_session_create(int device, tfx_session** out) {
   if (st != TFX_OK) return st;
   auto* s = new tfx_session();
   s->device = device;
-  for (auto& stream : s->streams) {
-    err = cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking);
+  if (const char* e = getenv("TFX_SESSION_STREAMS"))  // tuning runs only
+    s->nstreams = std::max(2, std::min(tfx_session::kMaxStreams, atoi(e)));
+  for (int i = 0; i < s->nstreams; ++i) {
+    err = cudaStreamCreateWithFlags(&s->streams[i], cudaStreamNonBlocking);
     if (err != cudaSuccess) {
       tfx_session_destroy(s);
       return cuda_fail(op, "stream", err);
