@@ -12,6 +12,7 @@
 // sm_100's paired f32 FMA.
 
 #include <algorithm>
+#include <atomic>
 #include <string>
 #include <type_traits>
 
@@ -161,14 +162,19 @@ int launch_map(const char* op, uint32_t n, const F& f, cudaStream_t stream) {
   if (st != TFX_OK) return st;
   const bool piped = pipelined_functor<F>() && map_pipelining();
   auto kernel = piped ? map_pipelined_kernel<F, U> : map_kernel<F, U>;
-  static int occupancy[2] = {0, 0};  // per instantiation; identical on every B200
-  int& occ = occupancy[piped ? 1 : 0];
+  // per instantiation and driver; identical on every B200 (a race between two
+  // first calls only computes the same value twice)
+  static std::atomic<int> occupancy[2] = {0, 0};
+  int occ = occupancy[piped ? 1 : 0].load(std::memory_order_relaxed);
   if (occ == 0) {
     int blocks = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, 0) !=
-            cudaSuccess || blocks <= 0)
+            cudaSuccess || blocks <= 0) {
+      cudaGetLastError();
       blocks = 1;
+    }
     occ = blocks;
+    occupancy[piped ? 1 : 0].store(occ, std::memory_order_relaxed);
   }
   const uint64_t need = (uint64_t(n) + kThreads * U - 1) / (kThreads * U);
   const uint32_t grid = uint32_t(std::min<uint64_t>(need, uint64_t(dev.sms) * occ));
