@@ -352,6 +352,12 @@ class Chain:
     KERNELS_PER_STEP = 5
 
 
+def pct(values, q):
+    """Nearest-rank percentile of a list of samples."""
+    v = sorted(values)
+    return v[min(len(v) - 1, max(0, int(round(q * (len(v) - 1)))))]
+
+
 def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     """configs[0..3] per op: rotating buffer sets whose footprint is >= 2x L2;
     kernel time from an event pair around every launch. `only` restricts the
@@ -380,7 +386,8 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
             launch(bufs[k % sets])
             evs[k][1].record()
         torch.cuda.synchronize()
-        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+        per_launch = sorted(a.elapsed_time(b) for a, b in evs)
+        ms = statistics.mean(per_launch)
         # back-to-back launches with events only around the batch: the rate a
         # stream of these launches sustains (launch overlap included)
         b0 = torch.cuda.Event(enable_timing=True)
@@ -404,7 +411,7 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
         graph.replay()
         torch.cuda.synchronize()
         g_ms = []
-        for _ in range(5):  # median of five replays of the whole batch
+        for _ in range(9):  # median of nine replays of the whole batch
             g0 = torch.cuda.Event(enable_timing=True)
             g1 = torch.cuda.Event(enable_timing=True)
             g0.record()
@@ -426,6 +433,10 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
                          "frac_graph_of_measured": round(gbs_g / hbm_peak, 3),
                          "frac_graph_of_8tbs": round(gbs_g / 8000.0, 3),
                          "gelem_s_graph": round(elems / (ms_g * 1e-3) / 1e9, 2),
+                         "us_graph_p10_p90": [round(pct(g_ms, 0.1) * 1e3, 3),
+                                              round(pct(g_ms, 0.9) * 1e3, 3)],
+                         "us_p10_p50_p90": [round(pct(per_launch, q) * 1e3, 3)
+                                            for q in (0.1, 0.5, 0.9)],
                          "buffer_sets": sets}
         if touched is not None:
             g = touched / (ms * 1e-3) / 1e9
@@ -522,6 +533,20 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     return results
 
 
+def cpu_model():
+    """The host CPU's model name (/proc/cpuinfo) and the CPUs this process may use."""
+    name = "unknown"
+    try:
+        with open("/proc/cpuinfo") as fh:
+            for line in fh:
+                if line.startswith("model name"):
+                    name = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return f"{name}; {len(os.sched_getaffinity(0))} CPUs available"
+
+
 def cpu_baseline_sample(seconds=10.0, batch=4):
     """The oracle chain (reference rayon splits, all host threads) on a bounded
     sample of the workload: `batch` sequences instead of 64."""
@@ -558,7 +583,7 @@ def cpu_baseline_sample(seconds=10.0, batch=4):
         times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": round(nbytes / med / 1e9, 3), "unit": "GB/s", "cores": orc.threads(),
-            "kind": "port",
+            "kind": "port", "cpu_model": cpu_model(),
             "sample": f"oracle chain at batch {B} x seq {L} ({nbytes} algorithmic bytes), "
                       f"median of {len(times)} runs over ~{seconds:.0f} s"}
 
@@ -613,12 +638,14 @@ def run_ours(args):
     t1 = torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
+    wall0 = time.perf_counter()
     t0.record()
     clocks.mark(0)
     for i in range(args.steps):
         chain.step(i, sm_pairs[i])
     t1.record()
     torch.cuda.synchronize()
+    wall_ms_local = (time.perf_counter() - wall0) * 1e3
     clocks.mark(1)
     barrier()
     ms_local = t0.elapsed_time(t1)
@@ -627,6 +654,34 @@ def run_ours(args):
     sm_ms = statistics.mean(a.elapsed_time(b) for a, b in sm_pairs)
     sm_ms = max_over_ranks(sm_ms)
     value = world * args.steps * bytes_per_step / (ms * 1e-3) / 1e9
+    # host wall time from the barrier to the last event, slowest rank
+    wall_ms = max_over_ranks(wall_ms_local)
+
+    # strong scaling beside the weak line: the same 64-sequence batch split over
+    # the ranks (64 / N sequences each), device time, slowest rank
+    strong = None
+    if world > 1:
+        sb = max(1, CHAIN["batch"] // world)
+        schain = Chain(torch, ops, device, rank, sb)
+        s_steps = max(10, min(args.steps, 50))
+        for i in range(args.warmup):
+            schain.step(i)
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        s0.record()
+        for i in range(s_steps):
+            schain.step(i)
+        s1.record()
+        torch.cuda.synchronize()
+        barrier()
+        s_ms = max_over_ranks(s0.elapsed_time(s1))
+        s_bytes = world * sum(chain_bytes(batch=sb).values())
+        strong = {"value": round(s_steps * s_bytes / (s_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                  "ms_per_step": round(s_ms / s_steps, 4), "steps": s_steps,
+                  "batch_per_gpu": sb, "global_batch": sb * world}
+        del schain
 
     # end to end through the public host-buffer API (tfx_session_*): every step
     # copies its inputs from pinned host memory and its results back, pipelined
@@ -755,6 +810,8 @@ def run_ours(args):
                 "pcie_gbs": pcie, "numa_local_cpus": numa_cpus,
                 "path": "tfx_session_* host-buffer calls (pinned host memory, chunked "
                         "copy-in / kernel / copy-out pipelined over 3 streams), host clock"},
+        "wall_ms_timed_region": round(wall_ms, 3),
+        "strong_scaling": strong,
         "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,
         "clocks": clock_info,
         "cpu_baseline": cpu,
@@ -816,6 +873,7 @@ def run_reference(args):
                                f"batch {B} x seq {L}", "global_batch": B, "seq_len": L,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": orc.threads(),
+                         "cpu_model": cpu_model(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
