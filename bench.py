@@ -66,6 +66,13 @@ def chain_bytes(c=CHAIN, batch=None) -> dict:
     }
 
 
+def chain_elements(c=CHAIN, batch=None) -> int:
+    """Output elements of one chain step (Gelem/s counts these)."""
+    B = c["batch"] if batch is None else batch
+    T, h, I, H, L = B * c["seq"], c["hidden"], c["inter"], c["heads"], c["seq"]
+    return h * T + 2 * h * T + B * H * L * L + h * T + h * T + I * T
+
+
 def softmax_touched_bytes(batch, heads, L, window, valid_len):
     """HBM bytes the masked softmax must move: the 16-byte score chunks that
     intersect each row's kept key interval (masked scores never reach the
@@ -774,6 +781,8 @@ def run_ours(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4),
+        "gelem_s": round(world * args.steps * chain_elements() / (ms * 1e-3) / 1e9, 2),
+        "frac_of_aggregate_hbm": round(value / (world * hbm_peak), 3),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
