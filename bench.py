@@ -336,13 +336,19 @@ class Chain:
     def outputs(self):
         return [self.h1, self.qk, self.probs, self.h2, self.h3, self.g]
 
-    def step(self, i, sm_events=None):
+    def step(self, i, sm_events=None, op_events=None):
+        """One chain step. sm_events: an event pair around the softmax;
+        op_events: KERNELS_PER_STEP + 1 events recorded between the kernels."""
         c, ops = CHAIN, self.ops
         local = i % 2 == 0  # alternate sliding-window (local) and global layers
         cos_t, sin_t = self.tables["theta_local" if local else "theta_global"]
+        mark = (lambda k: op_events[k].record()) if op_events is not None else (lambda k: None)
+        mark(0)
         ops.layer_norm_feature_first(self.x0, self.gamma1, None, 1e-5, out=self.h1)
+        mark(1)
         ops.rope_pairhalf(self.qkv, cos_t, sin_t, 2 * self.H, self.L, self.B, self.hd, self.hd,
                           (self.hd, 3 * self.h, 3 * self.h * self.L, 1), out=self.qk)
+        mark(2)
         if sm_events is not None:
             sm_events[0].record()
         ops.masked_softmax(self.scores, self.B, self.H, self.L, self.L,
@@ -350,13 +356,19 @@ class Chain:
                            out=self.probs)
         if sm_events is not None:
             sm_events[1].record()
+        mark(3)
         # residual add fused into the LayerNorm that follows it (one pass,
         # bit-identical to ops.add then ops.layer_norm_feature_first)
         ops.add_layer_norm_feature_first(self.x0, self.attn, self.gamma2, None, 1e-5,
                                          sum_out=self.h2, out=self.h3)
+        mark(4)
         ops.geglu(self.u, self.I, out=self.g)
+        mark(5)
 
     KERNELS_PER_STEP = 5
+    # bytes each kernel must move (inputs read once, outputs written once);
+    # the softmax's are the touched bytes of a window / global pair, averaged
+    KERNEL_NAMES = ("layernorm", "rope_qk", "masked_softmax", "add_layernorm", "geglu")
 
 
 def pct(values, q):
@@ -661,6 +673,31 @@ def run_ours(args):
     sm_ms = statistics.mean(a.elapsed_time(b) for a, b in sm_pairs)
     sm_ms = max_over_ranks(sm_ms)
     value = world * args.steps * bytes_per_step / (ms * 1e-3) / 1e9
+
+    # per-kernel times of the chain (a separate pass with events between the
+    # kernels, an even number of steps so window and global softmax alternate)
+    kb = chain_bytes()
+    T_, h_ = CHAIN["batch"] * CHAIN["seq"], CHAIN["hidden"]
+    moved = {"layernorm": kb["layernorm"], "rope_qk": kb["rope"],
+             "masked_softmax": None, "add_layernorm": 4 * h_ * T_ * 4 + h_ * 4,
+             "geglu": kb["geglu"]}
+    k_steps = 20
+    k_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(Chain.KERNELS_PER_STEP + 1)]
+             for _ in range(k_steps)]
+    for i in range(k_steps):
+        chain.step(i, op_events=k_evs[i])
+    torch.cuda.synchronize()
+    chain_kernels = {}
+    for k, name in enumerate(Chain.KERNEL_NAMES):
+        us = statistics.mean(e[k].elapsed_time(e[k + 1]) for e in k_evs) * 1e3
+        nb = moved[name] if moved[name] is not None else (
+            softmax_touched_bytes(CHAIN["batch"], CHAIN["heads"], CHAIN["seq"], CHAIN["window"],
+                                  CHAIN["seq"] - CHAIN["pad"]) +
+            softmax_touched_bytes(CHAIN["batch"], CHAIN["heads"], CHAIN["seq"], -1,
+                                  CHAIN["seq"] - CHAIN["pad"])) / 2
+        chain_kernels[name] = {"us": round(us, 2), "bytes": int(nb),
+                               "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                               "frac_of_measured": round(nb / (us * 1e-6) / 1e9 / hbm_peak, 3)}
     # host wall time from the barrier to the last event, slowest rank
     wall_ms = max_over_ranks(wall_ms_local)
 
@@ -820,6 +857,7 @@ def run_ours(args):
                 "path": "tfx_session_* host-buffer calls (pinned host memory, chunked "
                         "copy-in / kernel / copy-out pipelined over 3 streams), host clock"},
         "wall_ms_timed_region": round(wall_ms, 3),
+        "chain_kernels": chain_kernels,
         "strong_scaling": strong,
         "gpu_launches": Chain.KERNELS_PER_STEP * args.steps,
         "clocks": clock_info,
