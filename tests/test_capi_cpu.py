@@ -122,3 +122,26 @@ def test_session_create_without_gpu_fails_loudly():
     assert _lib.lib.tfx_session_destroy(None) == 0
     assert _lib.lib.tfx_session_gelu_erf_f32(None, None, None, 4) == _lib.TFX_ERR_INVALID_ARGUMENT
     assert tfx.last_error() == "tenferro-ext::gelu_erf: session: null session"
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """A C99 translation unit (what a cgo / bindgen / N-API binding compiles)
+    includes tfx.h, takes the address of every function and links against
+    libtfx.so; the program then calls the host-only entry points."""
+    names = _lib.header_symbols()
+    src = tmp_path / "use_tfx.c"
+    src.write_text(
+        "#include <stdio.h>\n#include \"tfx.h\"\n"
+        "typedef void (*fn_t)(void);\nstatic fn_t const table[] = {\n" +
+        "".join(f"  (fn_t)&{n},\n" for n in names) +
+        "};\nint main(void) {\n"
+        "  printf(\"%d %d\\n\", tfx_version(), (int)(sizeof(table) / sizeof(table[0])));\n"
+        "  return tfx_layernorm_ff_f32(0, 0, 0, 0, 8, 2, 1e-5f, 0) == TFX_ERR_INVALID_ARGUMENT ? 0 : 1;\n"
+        "}\n")
+    exe = tmp_path / "use_tfx"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-pedantic", "-I",
+                    os.path.join(ROOT, "include"), str(src), "-o", str(exe), "-L", libdir,
+                    "-ltfx", f"-Wl,-rpath,{libdir}"], check=True, capture_output=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["10000", str(len(names))]
