@@ -545,6 +545,22 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
                 lambda b, keep_a=keep_a: ops.laya_attention_block(b[0], keep_a, da, Ha, La, Ba,
                                                                   cos_a, sin_a, out=b[1]),
                 nbytes_a, da * La * Ba, flops=4 * Ba * Ha * kept * hda)
+    # the Jeff (Qwen3.5) full-attention block: per-head centred RMSNorm and
+    # partial RoPE on q and k, causal attention over the active keys, sigmoid
+    # gate. Shape of one layer of a Qwen3.5-0.8B-like model (8 heads of 256,
+    # rotary 64; the checkpoint's config is not in the reference) at 2048 tokens.
+    Lj, Hj, hdj, rotj = 2048, 8, 256, 64
+    wj = Hj * hdj
+    cos_j, sin_j = ops.rope_tables_powf(1e7, Lj, rotj, device=device)
+    qn_j, kn_j = normal(hdj, 0.1), normal(hdj, 0.1)
+    active_j = torch.ones(Lj, device=device)
+    nbytes_j = 5 * Lj * wj * 4 + Lj * 4
+    measure("jeff_attention",
+            lambda: tuple(normal(Lj * wj) for _ in range(4)) + (torch.empty(Lj * wj,
+                                                                            device=device),),
+            lambda b: ops.jeff_attention(b[0], b[1], b[2], b[3], qn_j, kn_j, active_j, cos_j,
+                                         sin_j, Lj, Hj, hdj, rotj, 1e-6, out=b[4]),
+            nbytes_j, Lj * wj, flops=4 * Hj * (Lj * (Lj + 1) // 2) * hdj)
     F, T = 768, 8192
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
@@ -954,7 +970,8 @@ def main():
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
                          "masked_softmax_global, rope_qk, laya_attention_window, "
-                         "laya_attention_global, add_layernorm, embedding_columns, "
+                         "laya_attention_global, jeff_attention, add_layernorm, "
+                         "embedding_columns, "
                          "bias_add) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
