@@ -145,3 +145,16 @@ def test_header_is_plain_c_and_links(tmp_path):
                     "-ltfx", f"-Wl,-rpath,{libdir}"], check=True, capture_output=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
     assert out == ["10000", str(len(names))]
+
+
+def test_session_chunk_plan_invariants(tmp_path):
+    """The host-buffer session's chunk plan (csrc/chunk_plan.h) covers every
+    unit once, never exceeds the staging slot, keeps every chunk but the last
+    aligned, and starts and ends large calls with short chunks."""
+    exe = tmp_path / "chunk_plan_test"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-Werror", "-I",
+                    os.path.join(ROOT, "tenferro-decision-rs_b200", "csrc"),
+                    os.path.join(ROOT, "tests", "native", "chunk_plan_test.cpp"), "-o", str(exe)],
+                   check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and "bad=0" in res.stdout, res.stdout
