@@ -122,6 +122,10 @@ def test_session_create_without_gpu_fails_loudly():
     assert _lib.lib.tfx_session_destroy(None) == 0
     assert _lib.lib.tfx_session_gelu_erf_f32(None, None, None, 4) == _lib.TFX_ERR_INVALID_ARGUMENT
     assert tfx.last_error() == "tenferro-ext::gelu_erf: session: null session"
+    rc = _lib.lib.tfx_session_add_layernorm_ff_f32(None, None, None, None, None, None, None, 8, 2,
+                                                   ctypes.c_float(1e-5))
+    assert rc == _lib.TFX_ERR_INVALID_ARGUMENT
+    assert tfx.last_error() == "tenferro-ext::add_layernorm_ff: session: null session"
 
 
 def test_header_is_plain_c_and_links(tmp_path):
