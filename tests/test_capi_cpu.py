@@ -162,3 +162,60 @@ def test_session_chunk_plan_invariants(tmp_path):
                    check=True)
     res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
     assert res.returncode == 0 and "bad=0" in res.stdout, res.stdout
+
+
+# Entry points whose arguments are all checked before any CUDA call: with every
+# pointer NULL (the required data pointers among them) and every extent 8 the
+# call must fail as invalid argument (a null pointer, or a shape the op cannot
+# take), naming "op: field: message".
+_NO_CUDA_BEFORE_VALIDATION = [
+    "tfx_erf_f32", "tfx_gelu_erf_f32", "tfx_erf_f64", "tfx_gelu_erf_f64", "tfx_geglu_ff_f32",
+    "tfx_gated_silu_f32", "tfx_gated_silu_stacked_f32", "tfx_bias_act_ff_f32", "tfx_add_f32",
+    "tfx_layernorm_ff_f32", "tfx_layernorm_ff_f64", "tfx_rmsnorm_last_f32",
+    "tfx_rmsnorm_last_f64", "tfx_rmsnorm_last_f32_noalloc", "tfx_masked_softmax_f32",
+    "tfx_rope_pairhalf_f32", "tfx_add_layernorm_ff_f32", "tfx_embedding_f32",
+    "tfx_embedding_gather_f32", "tfx_laya_qkv_prep_f32", "tfx_jeff_qkv_prep_f32",
+    "tfx_attention_f32", "tfx_laya_attention_block_f32", "tfx_jeff_attention_f32",
+    "tfx_wait_timeouts", "tfx_session_set_chunk_bytes", "tfx_session_layernorm_ff_f32",
+    "tfx_session_layernorm_ff_f64", "tfx_session_rmsnorm_last_f32", "tfx_session_erf_f32",
+    "tfx_session_gelu_erf_f32", "tfx_session_geglu_ff_f32", "tfx_session_gated_silu_f32",
+    "tfx_session_bias_act_ff_f32", "tfx_session_add_f32", "tfx_session_add_layernorm_ff_f32",
+    "tfx_session_masked_softmax_f32", "tfx_session_rope_pairhalf_f32",
+]
+
+
+def _args(name, extent):
+    out = []
+    for t in _lib.SIGNATURES[name][1]:
+        if t is _lib._i64:
+            out.append(extent)
+        elif t is ctypes.c_float or t is ctypes.c_double:
+            out.append(t(1e-5))
+        elif t is _lib._int or t is ctypes.c_int32:
+            out.append(0)
+        else:
+            out.append(None)  # every pointer, descriptor and stream
+    return out
+
+
+@pytest.mark.parametrize("name", _NO_CUDA_BEFORE_VALIDATION)
+def test_null_pointers_are_invalid_arguments(name):
+    rc = getattr(_lib.lib, name)(*_args(name, 8))
+    msg = tfx.last_error()
+    assert rc == _lib.TFX_ERR_INVALID_ARGUMENT, (rc, msg)
+    assert msg.count(": ") >= 2 and msg.split(": ")[0].startswith(("tenferro-", "tfx")), msg
+
+
+def test_every_validated_entry_point_is_listed():
+    exempt = {"tfx_last_error_string", "tfx_version", "tfx_softmax_desc_init",
+              "tfx_attention_desc_init", "tfx_rope_tables_f32", "tfx_rope_tables_powf_f32",
+              "tfx_session_create", "tfx_session_destroy"}
+    assert set(_lib.header_symbols()) - exempt == set(_NO_CUDA_BEFORE_VALIDATION)
+
+
+@pytest.mark.parametrize("name", [n for n in _NO_CUDA_BEFORE_VALIDATION
+                                  if _lib._i64 in _lib.SIGNATURES[n][1]
+                                  and not n.startswith("tfx_session_")])
+def test_negative_extents_are_invalid_arguments(name):
+    rc = getattr(_lib.lib, name)(*_args(name, -1))
+    assert rc == _lib.TFX_ERR_INVALID_ARGUMENT, (rc, tfx.last_error())
