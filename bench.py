@@ -6,22 +6,26 @@ Headline workload: the ModernBERT-base-shaped
 non-GEMM layer chain at batch 64 x seq 512 per GPU (32768 tokens, hidden 768,
 12 heads x 64, GeGLU intermediate 1152): LayerNorm -> RoPE on q,k -> masked
 row softmax -> residual add -> LayerNorm -> GeGLU, the residual add fused into
-the LayerNorm after it (one kernel, bit-identical to the two ops; its bytes are
-counted as the two ops move them). A step is one pass of the chain; the GEMM
-outputs it consumes (qkv, scores, attention output, MLP input) are seeded
-synthetic tensors. Under torchrun each rank runs its own 64-sequence
-shard (weak scaling, no collective on the data path); `value` is the bytes all
-ranks moved divided by the slowest rank's device time.
+the LayerNorm after it (one kernel, bit-identical to the two ops). A step is
+one pass of the chain; the GEMM outputs it consumes (qkv, scores, attention
+output, MLP input) are seeded synthetic tensors. Under torchrun each rank runs
+its own 64-sequence shard (weak scaling, no collective on the data path);
+`value` is the bytes all ranks moved divided by the slowest rank's device time.
 
-Metric: algorithmic HBM bytes per second (each input read once, each output
-written once) -- the per-op GB/s of BASELINE.json. The same line carries the
-per-op numbers of configs[0..3] (rotating buffer sets >= 2x L2 per op), the
-roofline of the dominant kernel, an end-to-end number through host buffers, the
-SM clocks seen during the run, and the CPU oracle timed on the host cores.
+Metric: HBM GB/s over the bytes the kernels must move -- each input read once,
+each output written once, the fused add + LayerNorm as one pass, and only the
+score chunks the softmax mask keeps (2.73 GB per step on average over a window
+and a global layer). `value_reference_counted` divides the same time by the
+bytes the reference's unfused ops move (3.17 GB: dense softmax, separate add).
+The same line carries the per-op numbers of configs[0..3] (rotating buffer
+sets >= 2x L2 per op), the roofline of the dominant kernel, an end-to-end
+number through host buffers, the SM clocks seen during the run, and the CPU
+chain timed on the host cores at the same configuration (`cpu_baseline`).
 
 `--impl reference` times the reference's CPU algorithm (the oracle restatement
-of crates/cpu-kernels, threaded like its rayon splits) on a bounded sample of
-the same workload and prints the same metric with "impl": "reference".
+of crates/cpu-kernels and tenferro-infer, threaded like its rayon splits) on
+the same configuration -- batch 64 x seq 512, the same stages and bytes per
+step -- and prints the same metric with "impl": "reference".
 """
 
 from __future__ import annotations
@@ -64,6 +68,31 @@ def chain_bytes(c=CHAIN, batch=None) -> dict:
         "layernorm2": ln,
         "geglu": (2 * I + I) * T * 4,
     }
+
+
+def chain_moved_bytes(step, c=CHAIN, batch=None) -> dict:
+    """HBM bytes the B200 kernels of chain step `step` must move: the
+    LayerNorm, RoPE and GeGLU as `chain_bytes` counts them, the residual add
+    fused into the second LayerNorm (a, b read once, the sum and y written
+    once: 4 passes instead of the two ops' 5), and the masked softmax's touched
+    bytes (the kept score chunks read, every probability written; even steps
+    are sliding-window layers, odd steps global ones)."""
+    B = c["batch"] if batch is None else batch
+    T, h, L = B * c["seq"], c["hidden"], c["seq"]
+    a = chain_bytes(c, B)
+    window = c["window"] if step % 2 == 0 else -1
+    return {
+        "layernorm": a["layernorm"],
+        "rope_qk": a["rope"],
+        "masked_softmax": softmax_touched_bytes(B, c["heads"], L, window, L - c["pad"]),
+        "add_layernorm": 4 * h * T * 4 + h * 4,
+        "geglu": a["geglu"],
+    }
+
+
+def chain_moved_bytes_total(steps, c=CHAIN, batch=None) -> int:
+    """Bytes moved by steps 0 .. steps-1 of the chain on one GPU."""
+    return sum(sum(chain_moved_bytes(i, c, batch).values()) for i in range(steps))
 
 
 def chain_elements(c=CHAIN, batch=None) -> int:
@@ -582,45 +611,84 @@ def cpu_model():
     return f"{name}; {len(os.sched_getaffinity(0))} CPUs available"
 
 
-def cpu_baseline_sample(seconds=10.0, batch=4):
-    """The oracle chain (reference rayon splits, all host threads) on a bounded
-    sample of the workload: `batch` sequences instead of 64."""
-    import numpy as np
-    from oracle import oracle as orc
-    orc.build()
-    c = CHAIN
-    B, L, h, I, H, hd = batch, c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
-    T = B * L
-    rng = np.random.default_rng(1)
-    x0 = rng.standard_normal(h * T).astype(np.float32)
-    g1 = rng.uniform(0.5, 1.5, h).astype(np.float32)
-    qkv = rng.standard_normal(3 * h * T).astype(np.float32)
-    scores = (2 * rng.standard_normal(B * H * L * L)).astype(np.float32)
-    attn = rng.standard_normal(h * T).astype(np.float32)
-    u = (1.5 * rng.standard_normal(2 * I * T)).astype(np.float32)
-    cos_t, sin_t = orc.rope_tables_f32(c["theta_local"], L, hd)
-    nbytes = sum(chain_bytes(batch=B).values())
+class CpuChain:
+    """The chain on the host cores: the oracle restatement of the reference's
+    rayon CPU path (crates/cpu-kernels LayerNorm and GeGLU, tenferro-infer RoPE
+    and masked softmax), all host threads, inputs seeded and outputs allocated
+    once (the reference's `*_into` functions write into caller-owned outputs).
+    A step is the same five stages as `Chain.step` on the same shapes; even
+    steps are sliding-window layers (theta 10000), odd steps global ones."""
 
-    def one():
-        orc.layer_norm_feature_first_f32(x0, h, T, g1, None, 1e-5)
-        orc.rope_pairhalf_f32(qkv, cos_t, sin_t, 2 * H, L, B, hd, hd, (hd, 3 * h, 3 * h * L, 1))
-        orc.masked_softmax_f32(scores, B, H, L, L, window=c["window"], valid_len=L - c["pad"])
-        h2 = orc.add_f32(x0, attn)
-        orc.layer_norm_feature_first_f32(h2, h, T, g1, None, 1e-5)
-        orc.geglu_f32(u, I, T)
+    def __init__(self, batch, seed=2):
+        import numpy as np
+        from oracle import oracle as orc
+        orc.build()
+        self.orc = orc
+        c = CHAIN
+        B, L, h, I, H, hd = batch, c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
+        self.B, self.L, self.h, self.I, self.H, self.hd, self.T = B, L, h, I, H, hd, B * L
+        T = self.T
+        rng = np.random.default_rng(seed)
+        f32 = np.float32
+        self.x0 = rng.standard_normal(h * T, dtype=f32)
+        self.g1 = rng.uniform(0.5, 1.5, h).astype(f32)
+        self.g2 = rng.uniform(0.5, 1.5, h).astype(f32)
+        self.qkv = rng.standard_normal(3 * h * T, dtype=f32)
+        self.scores = rng.standard_normal(B * H * L * L, dtype=f32) * f32(2.0)
+        self.attn = rng.standard_normal(h * T, dtype=f32)
+        self.u = rng.standard_normal(2 * I * T, dtype=f32) * f32(1.5)
+        self.h1 = np.empty_like(self.x0)
+        self.qk = np.empty_like(self.qkv)
+        self.probs = np.empty_like(self.scores)
+        self.h2 = np.empty_like(self.x0)
+        self.h3 = np.empty_like(self.x0)
+        self.g = np.empty(I * T, dtype=f32)
+        self.tables = {k: orc.rope_tables_f32(c[k], L, hd) for k in ("theta_local", "theta_global")}
 
-    one()
-    times = []
-    t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end or len(times) < 3:
-        t0 = time.perf_counter()
-        one()
-        times.append(time.perf_counter() - t0)
-    med = statistics.median(times)
-    return {"value": round(nbytes / med / 1e9, 3), "unit": "GB/s", "cores": orc.threads(),
+    def step(self, i):
+        orc, c = self.orc, CHAIN
+        B, L, h, I, H, hd, T = self.B, self.L, self.h, self.I, self.H, self.hd, self.T
+        local = i % 2 == 0
+        cos_t, sin_t = self.tables["theta_local" if local else "theta_global"]
+        orc.layer_norm_feature_first_f32(self.x0, h, T, self.g1, None, 1e-5, out=self.h1)
+        orc.rope_pairhalf_f32(self.qkv, cos_t, sin_t, 2 * H, L, B, hd, hd,
+                              (hd, 3 * h, 3 * h * L, 1), out=self.qk)
+        orc.masked_softmax_f32(self.scores, B, H, L, L, window=c["window"] if local else -1,
+                               valid_len=L - c["pad"], out=self.probs)
+        orc.add_f32(self.x0, self.attn, out=self.h2)
+        orc.layer_norm_feature_first_f32(self.h2, h, T, self.g2, None, 1e-5, out=self.h3)
+        orc.geglu_f32(self.u, I, T, out=self.g)
+
+    def measure(self, steps, warmup):
+        """Runs `warmup` untimed steps, then times exactly `steps` steps on the
+        host clock. Returns (seconds per step over the timed steps, list of
+        per-step seconds)."""
+        for i in range(warmup):
+            self.step(i)
+        times = []
+        for i in range(steps):
+            t0 = time.perf_counter()
+            self.step(i)
+            times.append(time.perf_counter() - t0)
+        return sum(times) / len(times), times
+
+
+def cpu_chain_line(batch, steps, warmup):
+    """Times the CPU chain and returns the `cpu_baseline` object: the chain's
+    GB/s over the same per-step bytes as the GPU line (`chain_moved_bytes`),
+    so that the two values compare the time of the same work."""
+    chain = CpuChain(batch)
+    sec, times = chain.measure(steps, warmup)
+    nbytes = chain_moved_bytes_total(steps, batch=batch)
+    value = nbytes / sum(times) / 1e9
+    return {"value": round(value, 3), "unit": "GB/s", "cores": chain.orc.threads(),
             "kind": "port", "cpu_model": cpu_model(),
-            "sample": f"oracle chain at batch {B} x seq {L} ({nbytes} algorithmic bytes), "
-                      f"median of {len(times)} runs over ~{seconds:.0f} s"}
+            "ms_per_step": round(sec * 1e3, 2),
+            "ms_per_step_median": round(statistics.median(times) * 1e3, 2),
+            "sample": f"oracle chain (the reference's rayon CPU path restated) at the timed "
+                      f"config, batch {batch} x seq {CHAIN['seq']}: {warmup} warm-up and "
+                      f"{steps} timed steps (alternating window / global layers), "
+                      f"{nbytes // steps} bytes per step as the GPU line counts them"}
 
 
 def run_ours(args):
@@ -628,7 +696,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import tfx  # noqa: F401  (raises when libtfx.so is missing)
-    from tfx import ops
+    from tfx import ops, shard
 
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -644,26 +712,24 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=device)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, device=device)
+
+    def host_timer():
+        box = {}
+        return (lambda: box.__setitem__("t", time.perf_counter()),
+                lambda: (time.perf_counter() - box["t"]) * 1e3)
 
     hbm_peak, peak_src = measured_hbm()
     props = torch.cuda.get_device_properties(device)
     l2 = props.L2_cache_size
     chain = Chain(torch, ops, device, rank, CHAIN["batch"])
-    bytes_per_step = sum(chain_bytes().values())
+    ref_bytes_per_step = sum(chain_bytes().values())
 
-    for i in range(args.warmup):
-        chain.step(i)
-    torch.cuda.synchronize()
+    # every step of every phase runs under shard.run_step (via timed_region):
+    # a rank that raises ends all ranks at the same point
+    noop = lambda: None  # noqa: E731
+    shard.timed_region(chain.step, args.warmup, start=noop, stop=noop, device=device)
 
     clocks = ClockSampler(torch, device)
     clocks.start()
@@ -671,46 +737,41 @@ def run_ours(args):
                 for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    wall0 = time.perf_counter()
-    t0.record()
-    clocks.mark(0)
-    for i in range(args.steps):
-        chain.step(i, sm_pairs[i])
-    t1.record()
-    torch.cuda.synchronize()
-    wall_ms_local = (time.perf_counter() - wall0) * 1e3
-    clocks.mark(1)
-    barrier()
+    wall = {}
+
+    def start():
+        wall["t"] = time.perf_counter()
+        t0.record()
+        clocks.mark(0)
+
+    def stop():
+        t1.record()
+        torch.cuda.synchronize(device)
+        wall["ms"] = (time.perf_counter() - wall["t"]) * 1e3
+        clocks.mark(1)
+
+    shard.timed_region(lambda i: chain.step(i, sm_pairs[i]), args.steps, start=start, stop=stop,
+                       device=device)
     ms_local = t0.elapsed_time(t1)
+    wall_ms_local = wall["ms"]
     clock_info = clocks.stop()
     ms = max_over_ranks(ms_local)
-    sm_ms = statistics.mean(a.elapsed_time(b) for a, b in sm_pairs)
-    sm_ms = max_over_ranks(sm_ms)
-    value = world * args.steps * bytes_per_step / (ms * 1e-3) / 1e9
+    sm_ms = max_over_ranks(statistics.mean(a.elapsed_time(b) for a, b in sm_pairs))
+    moved_per_rank = chain_moved_bytes_total(args.steps)
+    value = world * moved_per_rank / (ms * 1e-3) / 1e9
+    value_ref_counted = world * args.steps * ref_bytes_per_step / (ms * 1e-3) / 1e9
 
     # per-kernel times of the chain (a separate pass with events between the
     # kernels, an even number of steps so window and global softmax alternate)
-    kb = chain_bytes()
-    T_, h_ = CHAIN["batch"] * CHAIN["seq"], CHAIN["hidden"]
-    moved = {"layernorm": kb["layernorm"], "rope_qk": kb["rope"],
-             "masked_softmax": None, "add_layernorm": 4 * h_ * T_ * 4 + h_ * 4,
-             "geglu": kb["geglu"]}
     k_steps = 20
     k_evs = [[torch.cuda.Event(enable_timing=True) for _ in range(Chain.KERNELS_PER_STEP + 1)]
              for _ in range(k_steps)]
-    for i in range(k_steps):
-        chain.step(i, op_events=k_evs[i])
-    torch.cuda.synchronize()
+    shard.timed_region(lambda i: chain.step(i, op_events=k_evs[i]), k_steps, start=noop,
+                       stop=noop, device=device)
     chain_kernels = {}
     for k, name in enumerate(Chain.KERNEL_NAMES):
         us = statistics.mean(e[k].elapsed_time(e[k + 1]) for e in k_evs) * 1e3
-        nb = moved[name] if moved[name] is not None else (
-            softmax_touched_bytes(CHAIN["batch"], CHAIN["heads"], CHAIN["seq"], CHAIN["window"],
-                                  CHAIN["seq"] - CHAIN["pad"]) +
-            softmax_touched_bytes(CHAIN["batch"], CHAIN["heads"], CHAIN["seq"], -1,
-                                  CHAIN["seq"] - CHAIN["pad"])) / 2
+        nb = sum(chain_moved_bytes(i)[name] for i in range(k_steps)) / k_steps
         chain_kernels[name] = {"us": round(us, 2), "bytes": int(nb),
                                "gbs": round(nb / (us * 1e-6) / 1e9, 1),
                                "frac_of_measured": round(nb / (us * 1e-6) / 1e9 / hbm_peak, 3)}
@@ -724,21 +785,13 @@ def run_ours(args):
         sb = max(1, CHAIN["batch"] // world)
         schain = Chain(torch, ops, device, rank, sb)
         s_steps = max(10, min(args.steps, 50))
-        for i in range(args.warmup):
-            schain.step(i)
+        shard.timed_region(schain.step, args.warmup, start=noop, stop=noop, device=device)
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
-        barrier()
-        torch.cuda.synchronize()
-        s0.record()
-        for i in range(s_steps):
-            schain.step(i)
-        s1.record()
-        torch.cuda.synchronize()
-        barrier()
+        shard.timed_region(schain.step, s_steps, start=s0.record, stop=s1.record, device=device)
         s_ms = max_over_ranks(s0.elapsed_time(s1))
-        s_bytes = world * sum(chain_bytes(batch=sb).values())
-        strong = {"value": round(s_steps * s_bytes / (s_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+        s_bytes = world * chain_moved_bytes_total(s_steps, batch=sb)
+        strong = {"value": round(s_bytes / (s_ms * 1e-3) / 1e9, 1), "unit": "GB/s",
                   "ms_per_step": round(s_ms / s_steps, 4), "steps": s_steps,
                   "batch_per_gpu": sb, "global_batch": sb * world}
         del schain
@@ -773,20 +826,16 @@ def run_ours(args):
     qk_bytes = 2 * chain.h * chain.L * chain.B * 4
     h2d = nb(hx0, hg1, hsc, hx0, hattn, hg2, hu) + qk_bytes
     d2h = nb(hh1, hpr, hh2, hh3, hg) + qk_bytes
-    e2e_step(0)
-    barrier()
-    w0 = time.perf_counter()
-    for i in range(e2e_steps):
-        e2e_step(i)
-    e2e_ms = (time.perf_counter() - w0) * 1e3
-    barrier()
+    shard.timed_region(e2e_step, 1, start=noop, stop=noop, device=device)
+    e_start, e_stop = host_timer()
+    e2e_ms = shard.timed_region(e2e_step, e2e_steps, start=e_start, stop=e_stop, device=device)
     sess.close()
     e2e_ms = max_over_ranks(e2e_ms)
-    e2e_value = world * e2e_steps * bytes_per_step / (e2e_ms * 1e-3) / 1e9
+    e2e_value = world * chain_moved_bytes_total(e2e_steps) / (e2e_ms * 1e-3) / 1e9
     # PCIe roofline of that leg: copy rates measured on every rank at once,
     # and per call the time its copies need with both directions busy.
-    barrier()
-    pcie = pcie_rates(torch, device)
+    shard.barrier(device)
+    pcie = shard.run_step(pcie_rates, torch, device, device=device)
     T, h = chain.L * chain.B, chain.h
     per_call = [(h * T * 4, h * T * 4), (qk_bytes, qk_bytes),
                 (hsc.numel() * 4, hpr.numel() * 4), (2 * h * T * 4, 2 * h * T * 4),
@@ -796,11 +845,12 @@ def run_ours(args):
 
     ops_results = None
     if not args.no_ops:
-        ops_results = run_ops_configs(torch, ops, device, l2, hbm_peak)
+        ops_results = shard.run_step(run_ops_configs, torch, ops, device, l2, hbm_peak,
+                                     device=device)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_sample(args.cpu_seconds)
+        cpu = cpu_chain_line(CHAIN["batch"], args.cpu_steps, 2)
 
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
@@ -811,15 +861,10 @@ def run_ours(args):
         except Exception:
             traffic = None
 
-    # The softmax reads only the score chunks its mask keeps: its algorithmic
-    # bytes per launch are those plus every probability written, averaged over
-    # the timed steps (even steps sliding-window, odd steps global).
-    c = CHAIN
-    t_local = softmax_touched_bytes(c["batch"], c["heads"], c["seq"], c["window"],
-                                    c["seq"] - c["pad"])
-    t_global = softmax_touched_bytes(c["batch"], c["heads"], c["seq"], -1, c["seq"] - c["pad"])
-    n_local = (args.steps + 1) // 2
-    sm_bytes = (n_local * t_local + (args.steps - n_local) * t_global) / args.steps
+    # The softmax reads only the score chunks its mask keeps: its bytes per
+    # launch are those plus every probability written, averaged over the
+    # timed steps (even steps sliding-window, odd steps global).
+    sm_bytes = sum(chain_moved_bytes(i)["masked_softmax"] for i in range(args.steps)) / args.steps
     sm_dense = chain_bytes()["softmax"]
     sm_gbs = sm_bytes / (sm_ms * 1e-3) / 1e9
     if world > 1:
@@ -834,8 +879,16 @@ def run_ours(args):
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(ms / args.steps, 4),
-        "gelem_s": round(world * args.steps * chain_elements() / (ms * 1e-3) / 1e9, 2),
         "frac_of_aggregate_hbm": round(value / (world * hbm_peak), 3),
+        "bytes_moved_per_step_per_gpu": moved_per_rank // args.steps,
+        "value_reference_counted": {
+            "value": round(value_ref_counted, 1), "unit": "GB/s",
+            "bytes_per_step_per_gpu": ref_bytes_per_step,
+            "frac_of_aggregate_hbm": round(value_ref_counted / (world * hbm_peak), 3),
+            "note": "the same time over the bytes the reference's unfused ops move (the dense "
+                    "softmax, the residual add and the LayerNorm as two passes); not a "
+                    "roofline figure: the kernels skip masked score chunks and fuse the add"},
+        "gelem_s": round(world * args.steps * chain_elements() / (ms * 1e-3) / 1e9, 2),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -850,17 +903,20 @@ def run_ours(args):
             "rope_theta": "10000 (even steps, sliding) / 160000 (odd steps, global)",
             "global_batch": CHAIN["batch"] * world, "seq_len": CHAIN["seq"],
             "parallelism": f"token-row shards x{world}, no collective",
-            "fusion": "residual add + second LayerNorm in one kernel (bit-identical to the two "
-                      "ops); bytes counted as the two ops move them: 503 MB algorithmic, "
-                      "403 MB moved",
-            "bytes_per_step_per_gpu": bytes_per_step,
-            "l2": "inputs larger than L2 (3.17 GB per step per GPU vs "
+            "bytes": "value counts the bytes the kernels must move: each input read once, each "
+                     "output written once, the residual add fused into the LayerNorm after it "
+                     "(403 MB instead of the two ops' 503 MB) and the softmax's kept score "
+                     "chunks (masked scores are never read); 2.73 GB per step on average",
+            "l2": "inputs larger than L2 (3.2 GB per step per GPU vs "
                   f"{l2 / 2**20:.0f} MiB L2); per-op configs rotate >= 2x L2 of buffers",
         },
         "roofline": {"kernel": "masked_softmax (chain)", "bound": "hbm",
                      "achieved": round(sm_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(sm_gbs / hbm_peak, 3), "peak_source": peak_src,
                      "bytes_per_launch": int(sm_bytes), "traffic": traffic,
+                     "traffic_source": "profiles/traffic.json: ncu dram__bytes_read.sum + "
+                                       "dram__bytes_write.sum of the chain's softmax launches "
+                                       "(not measured in this run)",
                      "bytes_per_launch_dense": sm_dense,
                      "dense_equivalent_gbs": round(sm_dense / (sm_ms * 1e-3) / 1e9, 1),
                      "us_per_launch": round(sm_ms * 1e3, 2)},
@@ -887,58 +943,28 @@ def run_ours(args):
 # reference arm
 
 def run_reference(args):
+    """The reference's CPU path (the oracle restatement of its rayon code, all
+    host threads) on the GPU arm's exact configuration: batch 64 x seq 512 per
+    step, the same five stages, the same bytes per step. Rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    from oracle import oracle as orc
-    orc.build()
-    import numpy as np
-    c = CHAIN
-    B = 8  # bounded sample: 8 of the 64 sequences per step
-    L, h, I, H, hd = c["seq"], c["hidden"], c["inter"], c["heads"], c["head_dim"]
-    T = B * L
-    rng = np.random.default_rng(2)
-    x0 = rng.standard_normal(h * T).astype(np.float32)
-    g1 = rng.uniform(0.5, 1.5, h).astype(np.float32)
-    qkv = rng.standard_normal(3 * h * T).astype(np.float32)
-    scores = (2 * rng.standard_normal(B * H * L * L)).astype(np.float32)
-    attn = rng.standard_normal(h * T).astype(np.float32)
-    u = (1.5 * rng.standard_normal(2 * I * T)).astype(np.float32)
-    tables = {k: orc.rope_tables_f32(c[k], L, hd) for k in ("theta_local", "theta_global")}
-    nbytes = sum(chain_bytes(batch=B).values())
-
-    def step(i):
-        local = i % 2 == 0
-        cos_t, sin_t = tables["theta_local" if local else "theta_global"]
-        orc.layer_norm_feature_first_f32(x0, h, T, g1, None, 1e-5)
-        orc.rope_pairhalf_f32(qkv, cos_t, sin_t, 2 * H, L, B, hd, hd, (hd, 3 * h, 3 * h * L, 1))
-        orc.masked_softmax_f32(scores, B, H, L, L, window=c["window"] if local else -1,
-                               valid_len=L - c["pad"])
-        h2 = orc.add_f32(x0, attn)
-        orc.layer_norm_feature_first_f32(h2, h, T, g1, None, 1e-5)
-        orc.geglu_f32(u, I, T)
-
-    for i in range(args.warmup):
-        step(i)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        step(i)
-    dt = time.perf_counter() - t0
-    value = args.steps * nbytes / dt / 1e9
-    sample = (f"oracle restatement of the reference's rayon CPU path, chain at batch {B} x seq "
-              f"{L} per step ({nbytes} algorithmic bytes)")
+    B, L = CHAIN["batch"], CHAIN["seq"]
+    cpu = cpu_chain_line(B, args.steps, args.warmup)
+    value = cpu["value"]
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded normals on the host)", "impl": "reference",
-        "config": {"workload": "configs[4]: ModernBERT-base non-GEMM chain, bounded sample "
-                               f"batch {B} x seq {L}", "global_batch": B, "seq_len": L,
+        "bytes_moved_per_step": chain_moved_bytes_total(args.steps) // args.steps,
+        "config": {"workload": "configs[4]: ModernBERT-base non-GEMM chain LN -> RoPE(q,k) -> "
+                               "masked softmax -> residual add -> LN -> GeGLU, batch 64 x seq "
+                               "512 per GPU",
+                   "tokens_per_gpu": B * L, "global_batch": B, "seq_len": L,
                    "parallelism": "host threads"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": orc.threads(),
-                         "cpu_model": cpu_model(),
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+        "cpu_baseline": cpu,
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -965,7 +991,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-ops", action="store_true", help="skip the per-op configs[0..3]")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-steps", type=int, default=6,
+                    help="timed steps of the CPU chain behind cpu_baseline (batch 64 each)")
     ap.add_argument("--only-op", default=None,
                     help="run only this per-op config (layernorm_f32, layernorm_f64, geglu, "
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "

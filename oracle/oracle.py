@@ -148,15 +148,17 @@ def expm1_mlx_f32(a: float) -> float:
     return float(lib().orc_expm1_mlx_f32(ctypes.c_float(a)))
 
 
-def layer_norm_feature_first_f32(x, d, cols, weight, bias, eps):
-    y = np.empty(d * cols, dtype=np.float32)
+def layer_norm_feature_first_f32(x, d, cols, weight, bias, eps, out=None):
+    y = np.empty(d * cols, dtype=np.float32) if out is None else out
+    assert y.size == d * cols
     lib().orc_layer_norm_feature_first_f32(_p32(x), d, cols, _p32(weight), _p32(bias),
                                            ctypes.c_float(eps), _p32(y))
     return y
 
 
-def geglu_f32(u, inter, cols):
-    y = np.empty(inter * cols, dtype=np.float32)
+def geglu_f32(u, inter, cols, out=None):
+    y = np.empty(inter * cols, dtype=np.float32) if out is None else out
+    assert y.size == inter * cols
     lib().orc_geglu_f32(_p32(u), inter, cols, _p32(y))
     return y
 
@@ -192,8 +194,9 @@ def gemm_bias_f32(x, weight, bias, in_dim, out_dim, length):
     return y
 
 
-def add_f32(a, b):
-    y = np.empty(a.size, dtype=np.float32)
+def add_f32(a, b, out=None):
+    y = np.empty(a.size, dtype=np.float32) if out is None else out
+    assert y.size == a.size == b.size
     lib().orc_add_f32(_p32(a), _p32(b), _p32(y), a.size)
     return y
 
@@ -201,8 +204,9 @@ def add_f32(a, b):
 def masked_softmax_f32(scores, batch, heads, q_len, k_len, *, scale=1.0, semantics=0,
                        causal=False, window=-1, window_skips_invalid_query=False,
                        valid_len=-1, valid_lens=None, add_mask=None, add_strides=(0, 0, 0),
-                       keep=None, keep_strides=(0, 0, 0)):
-    p = np.empty(batch * heads * q_len * k_len, dtype=np.float32)
+                       keep=None, keep_strides=(0, 0, 0), out=None):
+    p = np.empty(batch * heads * q_len * k_len, dtype=np.float32) if out is None else out
+    assert p.size == batch * heads * q_len * k_len
     vl = None
     if valid_lens is not None:
         valid_lens = np.ascontiguousarray(valid_lens, dtype=np.int32)
@@ -236,8 +240,14 @@ def rope_tables_f64(base, seq, rotary_dim):
 
 
 def rope_pairhalf_f32(x, cos_t, sin_t, n_vec, seq, batch, head_dim, rotary_dim, strides,
-                      out_size=None):
-    y = np.array(x, copy=True) if out_size is None else np.zeros(out_size, np.float32)
+                      out_size=None, out=None):
+    """Rotated copy of x. With `out`, only the described vectors are written
+    into it (the rest of `out` is left as it was)."""
+    if out is not None:
+        assert out.size == x.size
+        y = out
+    else:
+        y = np.array(x, copy=True) if out_size is None else np.zeros(out_size, np.float32)
     lib().orc_rope_pairhalf_f32(_p32(x), _p32(y), _p32(cos_t), _p32(sin_t), n_vec, seq, batch,
                                 head_dim, rotary_dim, *[int(s) for s in strides])
     return y

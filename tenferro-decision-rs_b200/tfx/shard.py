@@ -77,3 +77,39 @@ def run_step(fn, *args, device=None, **kwargs):
         raise ShardFailure(f"a rank failed its step: {err!r}" if err else
                            "another rank failed its step") from err
     return result
+
+
+def barrier(device=None) -> None:
+    """Process-group barrier (no-op for a single process)."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        if device is not None and getattr(device, "type", None) == "cuda":
+            dist.barrier(device_ids=[device.index])
+        else:
+            dist.barrier()
+
+
+def timed_region(step, steps: int, *, start, stop, device=None):
+    """The timed loop of a multi-rank benchmark: a barrier, then
+    start(); step(0) .. step(steps-1); stop() on every rank, inside one
+    run_step -- so the loop itself carries no collective, and a rank whose step
+    raises makes every rank raise ShardFailure right after the loop instead of
+    leaving the others blocked in the next collective. start/stop record the
+    clock (CUDA events on the launching stream, or the host clock); run_step
+    synchronises `device` before the ranks compare notes. Returns stop()'s
+    result."""
+    out = []
+
+    def loop():
+        start()
+        for i in range(steps):
+            step(i)
+        out.append(stop())
+
+    barrier(device)
+    if device is not None:
+        import torch
+        torch.cuda.synchronize(device)
+    run_step(loop, device=device)
+    barrier(device)
+    return out[0]

@@ -37,6 +37,24 @@ def test_softmax_touched_bytes_of_the_chain():
     assert written < local < glob <= 2 * written  # every probability written, kept scores read
 
 
+def test_moved_bytes_are_what_the_kernels_move():
+    """value's bytes: the fused add + LayerNorm as one pass and the softmax's
+    touched bytes, 2,731,751,424 per step averaged over a window and a global
+    step; below the reference-counted 3,170,899,968 by exactly the skipped
+    score chunks and the one pass the fusion removes."""
+    w, g = bench.chain_moved_bytes(0), bench.chain_moved_bytes(1)
+    assert bench.chain_moved_bytes_total(2) == 2 * 2_731_751_424
+    assert w["add_layernorm"] == g["add_layernorm"] == 4 * 768 * 32768 * 4 + 768 * 4
+    assert w["masked_softmax"] < g["masked_softmax"]  # the window keeps fewer chunks
+    ref = bench.chain_bytes()
+    fusion_saving = ref["residual_add"] + ref["layernorm2"] - w["add_layernorm"]
+    skipped = ref["softmax"] - (w["masked_softmax"] + g["masked_softmax"]) // 2
+    assert sum(ref.values()) - 2_731_751_424 == fusion_saving + skipped
+    weights = 2 * 768 * 4  # the two LayerNorm gains per step do not scale with batch
+    assert (bench.chain_moved_bytes_total(2, batch=8) - 2 * weights) * 8 == \
+        bench.chain_moved_bytes_total(2) - 2 * weights
+
+
 def test_chain_elements():
     T = 64 * 512
     assert bench.chain_elements() == 768 * T * 5 + 64 * 12 * 512 * 512 + 1152 * T
@@ -66,6 +84,11 @@ def test_reference_arm_prints_the_contract_line():
     assert line["metric"] == bench.METRIC and line["unit"] == "GB/s"
     assert line["value"] > 0 and line["higher_is_better"] is True
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["value"] == line["value"]
+    # the same configuration as the GPU arm: batch 64 x seq 512, the same bytes
+    assert line["config"]["global_batch"] == 64 and line["config"]["seq_len"] == 512
+    assert line["config"]["tokens_per_gpu"] == 32768
+    assert line["bytes_moved_per_step"] == bench.chain_moved_bytes_total(3) // 3
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     assert line["e2e"]["value"] == line["value"]
 

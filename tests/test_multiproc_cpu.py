@@ -67,7 +67,26 @@ def _worker(rank, world, port, fail_rank, out):
             except ShardFailure:
                 failed_at = i
                 break
-        out.put((rank, float(total.item()), t, results, failed_at))
+        # the bench's timed loop: one region of several steps, no collective
+        # inside it; a failing step fails every rank right after the region
+        from tfx.shard import timed_region
+        import time
+        seen = []
+
+        def region_step(i):
+            seen.append(i)
+            if rank == fail_rank and i == 2:
+                raise RuntimeError("injected host failure in the timed region")
+
+        box = {}
+        try:
+            ms = timed_region(region_step, 4,
+                              start=lambda: box.__setitem__("t", time.perf_counter()),
+                              stop=lambda: (time.perf_counter() - box["t"]) * 1e3)
+            region = ("ok", ms >= 0.0, len(seen))
+        except ShardFailure:
+            region = ("failed", True, len(seen))
+        out.put((rank, float(total.item()), t, results, failed_at, region))
     finally:
         dist.destroy_process_group()
 
@@ -84,10 +103,14 @@ def test_gloo_world2_max_and_failure_propagation(fail_rank):
         p.join(timeout=120)
         assert p.exitcode == 0
     got = sorted(out.get(timeout=10) for _ in procs)
-    for rank, total, t, results, failed_at in got:
+    for rank, total, t, results, failed_at, region in got:
         assert total == sum(range(64))
         assert t == 3.0  # max of 1.5, 3.0
         if fail_rank < 0:
             assert results == [0, 1, 2] and failed_at is None
+            assert region == ("ok", True, 4)
         else:
             assert results == [0] and failed_at == 1  # every rank stops at the failing step
+            # every rank raises after the region; the failing rank stopped at its step
+            assert region[0] == "failed"
+            assert region[2] == (3 if rank == fail_rank else 4)
