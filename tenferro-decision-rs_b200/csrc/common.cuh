@@ -91,16 +91,31 @@ __device__ __forceinline__ double ld_stream(const double* p) {
 // while the previous kernel on the stream is still finishing. It must call
 // pdl_wait() before touching global memory: that returns once the previous
 // grid has completed and its writes are visible (and guards against
-// overwriting what the previous grid still reads). pdl_launch_dependents()
-// lets the next kernel's CTAs be scheduled as soon as this grid's last CTA has
-// started; they in turn wait in their own pdl_wait().
+// overwriting what the previous grid still reads).
+//
+// Kernels do not trigger their dependents early (pdl_launch_dependents at the
+// start): the next grid's CTAs would then take the SM slots that free up first
+// and pile onto those SMs while the current grid still runs, and a grid whose
+// CTAs each own a fixed share of the work (one wave, or a persistent grid) is
+// then only as fast as its most loaded SM. Measured on configs[0] LayerNorm
+// (one wave of 1024 CTAs): 10.46 us with the early trigger, 9.88 us without;
+// the whole configs[4] chain 0.4502 -> 0.4437 ms per step, and 0.4516 with no
+// programmatic launch at all. Without the early trigger the next grid is
+// launched as the last CTAs of this one exit, before its completion is
+// signalled, which still hides most of the launch latency.
+// TFX_PDL_EARLY_TRIGGER=1 at build time restores the early trigger.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+#ifndef TFX_PDL_EARLY_TRIGGER
+#define TFX_PDL_EARLY_TRIGGER 0
+#endif
 __device__ __forceinline__ void pdl_enter() {
   pdl_wait();
+#if TFX_PDL_EARLY_TRIGGER
   pdl_launch_dependents();
+#endif
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -155,8 +170,11 @@ int launch_kernel(const char* op, void (*kernel)(KArgs...), dim3 grid, dim3 bloc
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
+#ifndef TFX_PDL_ATTR
+#define TFX_PDL_ATTR 1
+#endif
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = TFX_PDL_ATTR;
   unsigned n = 1;
   if (cluster > 1) {
     attr[1].id = cudaLaunchAttributeClusterDimension;

@@ -272,6 +272,128 @@ __global__ void __launch_bounds__(256, 8) ln_smem_kernel(const float* __restrict
   }
 }
 
+// ---- LayerNorm f32: persistent warps, each with a ring of column slots -------------
+//
+// One CTA of 16 warps per SM; warp g of G handles columns g, g + G, g + 2G, ...
+// Each warp owns LN_RING_SLOTS shared-memory slots of one column: while it
+// reduces and writes column k from its slot, cp.async copies columns k+1 and
+// k+2 into the other two, so every SM keeps 32 columns (96 KB at d = 768) in
+// flight and each column's arithmetic and store overlap later columns' loads.
+// The weights (and bias) are read once per warp into registers instead of once
+// per column. The lane -> element mapping and every rounding are those of
+// ln_smem_kernel, so the two kernels give identical bits.
+//
+// Why not one column per warp in a single wave (ln_smem_kernel): all 8192
+// columns of configs[0] request their reads at once, the memory system serves
+// them interleaved, most columns complete only near the end of the read
+// phase, and the arithmetic, the weight loads and the writes of nearly every
+// column then fall into the last microseconds. Measured on configs[0] (CUDA
+// graph of 40 launches over rotating buffers, no programmatic launch): 9.56 us
+// for this kernel, 9.96 us for ln_smem_kernel, 9.14 us for a copy of the same
+// bytes with the same warp-per-column tiling; 8 warps x 2 CTAs, 12 or 20
+// warps, 2 or 4 slots, and register double buffering instead of shared memory
+// all measured 9.5 - 10.3 us. With many columns per warp the ring loses (the
+// dispatcher below picks by column count).
+constexpr int LN_RING_WARPS = 16;
+constexpr int LN_RING_SLOTS = 3;
+
+template <int NV, bool BIAS>
+__global__ void __launch_bounds__(LN_RING_WARPS * 32, 1) ln_ring_kernel(
+    const float* x, const float* __restrict__ w, const float* __restrict__ b, float* y,
+    uint32_t d, uint64_t cols, float eps) {
+  pdl_enter();
+  extern __shared__ float4 stage[];  // LN_RING_WARPS x LN_RING_SLOTS x d floats
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint64_t gw = uint64_t(blockIdx.x) * LN_RING_WARPS + warp;
+  const uint64_t G = uint64_t(gridDim.x) * LN_RING_WARPS;
+  const uint32_t dv = d / 4;
+  if (gw >= cols) return;  // the whole warp leaves together
+  float4 wr[NV], br[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const uint32_t q = j * 32 + lane;
+    if (q < dv) {
+      wr[j] = __ldg(reinterpret_cast<const float4*>(w) + q);
+      if constexpr (BIAS) br[j] = __ldg(reinterpret_cast<const float4*>(b) + q);
+    }
+  }
+  float4* ring = stage + size_t(warp) * LN_RING_SLOTS * dv;
+  const uint64_t n = (cols - gw + G - 1) / G;  // columns of this warp
+  // Copies column k of this warp into slot k % LN_RING_SLOTS as one cp.async
+  // group (an empty group past the last column keeps the group count uniform).
+  auto issue = [&](uint64_t k) {
+    if (k < n) {
+      const float4* xc = reinterpret_cast<const float4*>(x + (gw + k * G) * d);
+      float4* sl = ring + (k % LN_RING_SLOTS) * dv;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const uint32_t q = j * 32 + lane;
+        if (q < dv) cp_async16(sl + q, xc + q);
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+#pragma unroll
+  for (int k = 0; k < LN_RING_SLOTS - 1; ++k) issue(k);
+  const float dd = float(d);
+  for (uint64_t k = 0; k < n; ++k) {
+    issue(k + LN_RING_SLOTS - 1);
+    // groups complete in order: all but the newest LN_RING_SLOTS - 1 are done
+    asm volatile("cp.async.wait_group %0;" ::"n"(LN_RING_SLOTS - 1) : "memory");
+    __syncwarp();
+    const float4* sl = ring + (k % LN_RING_SLOTS) * dv;
+    float4 v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const uint32_t q = j * 32 + lane;
+      if (q < dv) v[j] = sl[q];
+    }
+    // every lane has read the slot before any lane's next issue overwrites it
+    __syncwarp();
+    float s = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < dv)
+        s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, v[j].x), v[j].y), v[j].z), v[j].w);
+    s = warp_sum(s);
+    const float mean = __fdiv_rn(s, dd);
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j)
+      if (j * 32 + lane < dv) {
+        const float cx = __fsub_rn(v[j].x, mean), cy = __fsub_rn(v[j].y, mean);
+        const float cz = __fsub_rn(v[j].z, mean), cw = __fsub_rn(v[j].w, mean);
+        ss = __fadd_rn(ss, __fmul_rn(cx, cx));
+        ss = __fadd_rn(ss, __fmul_rn(cy, cy));
+        ss = __fadd_rn(ss, __fmul_rn(cz, cz));
+        ss = __fadd_rn(ss, __fmul_rn(cw, cw));
+      }
+    ss = warp_sum(ss);
+    const float var = __fdiv_rn(ss, dd);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    float4* yc = reinterpret_cast<float4*>(y + (gw + k * G) * d);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const uint32_t q = j * 32 + lane;
+      if (q < dv) {
+        float4 o;
+        o.x = __fmul_rn(__fmul_rn(__fsub_rn(v[j].x, mean), inv), wr[j].x);
+        o.y = __fmul_rn(__fmul_rn(__fsub_rn(v[j].y, mean), inv), wr[j].y);
+        o.z = __fmul_rn(__fmul_rn(__fsub_rn(v[j].z, mean), inv), wr[j].z);
+        o.w = __fmul_rn(__fmul_rn(__fsub_rn(v[j].w, mean), inv), wr[j].w);
+        if constexpr (BIAS) {
+          o.x = __fadd_rn(o.x, br[j].x);
+          o.y = __fadd_rn(o.y, br[j].y);
+          o.z = __fadd_rn(o.z, br[j].z);
+          o.w = __fadd_rn(o.w, br[j].w);
+        }
+        yc[q] = o;
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // ---- residual add fused into the LayerNorm that follows it ----------------------------
 //
 // s = a + b per element, then ln_smem_kernel's arithmetic on s (same order of
@@ -463,6 +585,25 @@ __global__ void __launch_bounds__(256) ln_generic_kernel(const T* x, const T* __
   }
 }
 
+// Launches ln_ring_kernel<NV, BIAS> on `grid` CTAs (at most one per SM),
+// opting the instance in to the device's largest dynamic shared memory once
+// per device.
+template <int NV, bool BIAS>
+int launch_ln_ring(const char* op, const DeviceInfo& dev, unsigned grid, size_t smem,
+                   cudaStream_t stream, const float* x, const float* w, const float* b, float* y,
+                   uint32_t d, uint64_t cols, float eps) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  const int di = dev.device & 63;
+  std::call_once(once[di], [&] {
+    err[di] = cudaFuncSetAttribute(ln_ring_kernel<NV, BIAS>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, dev.smem_optin);
+  });
+  if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
+  return launch_kernel(op, ln_ring_kernel<NV, BIAS>, dim3(grid), dim3(LN_RING_WARPS * 32), smem,
+                       stream, 1, x, w, b, y, d, cols, eps);
+}
+
 template <typename T>
 int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64_t d,
                  int64_t cols, T eps, cudaStream_t stream) {
@@ -485,13 +626,42 @@ int layernorm_ff(const char* op, const T* x, const T* w, const T* b, T* y, int64
   const int64_t dv = d / VN;
   const bool bias = b != nullptr;
   if constexpr (std::is_same_v<T, float>) {
-    // Shared-memory staged warp-per-column kernel (f32, d <= 1024); the
-    // register-resident one stays selectable for tuning (TFX_LN_KERNEL=regs).
-    static const bool use_regs = [] {
+    // Persistent ring kernel (f32, d <= 1024, up to ~5 columns per ring warp),
+    // else the one-wave shared-memory kernel; TFX_LN_KERNEL=ring / smem / regs
+    // forces one for tuning runs.
+    static const int choice = [] {
       const char* e = getenv("TFX_LN_KERNEL");
-      return e && std::string(e) == "regs";
+      const std::string v = e ? e : "";
+      return v == "regs" ? 2 : v == "smem" ? 1 : v == "ring" ? 3 : 0;
     }();
-    if (vec && dv <= 32 * 8 && !use_regs) {
+    const DeviceInfo& dev = device_info(&st);
+    const size_t ring_smem = size_t(LN_RING_WARPS) * LN_RING_SLOTS * size_t(d) * 4;
+    // The ring wins while each of its warps has few columns (configs[0]: 8192
+    // columns, 3.5 per warp: 9.56 us against 9.96); with many columns per warp
+    // its 16 warps per SM cannot hide each column's serial reductions and the
+    // one-wave-per-64-warps kernel is faster (32768 columns: 32.2 us against
+    // 35.7; equal at 16384).
+    const bool ring_shape = cols <= int64_t(5) * dev.sms * LN_RING_WARPS;
+    if (vec && dv <= 32 * 8 && ((choice == 0 && ring_shape) || choice == 3) &&
+        ring_smem <= size_t(dev.smem_optin)) {
+      const uint32_t du = uint32_t(d);
+      const unsigned grid = unsigned(std::min<int64_t>(
+          dev.sms, (cols + LN_RING_WARPS - 1) / LN_RING_WARPS));
+#define TFX_LN_RING(NVV)                                                                     \
+  if (dv <= 32 * NVV)                                                                        \
+    return bias ? launch_ln_ring<NVV, true>(op, dev, grid, ring_smem, stream, x, w, b, y, du, \
+                                            uint64_t(cols), eps)                             \
+                : launch_ln_ring<NVV, false>(op, dev, grid, ring_smem, stream, x, w, b, y, du, \
+                                             uint64_t(cols), eps);
+      TFX_LN_RING(1)
+      TFX_LN_RING(2)
+      TFX_LN_RING(3)
+      TFX_LN_RING(4)
+      TFX_LN_RING(6)
+      TFX_LN_RING(8)
+#undef TFX_LN_RING
+    }
+    if (vec && dv <= 32 * 8 && choice != 2) {
       TFX_REQUIRE(cols / 8 < (int64_t(1) << 31), op, "cols", "too many columns for one call");
       const unsigned grid = unsigned((cols + 7) / 8);
       const uint32_t du = uint32_t(d);

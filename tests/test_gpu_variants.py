@@ -62,7 +62,7 @@ print("variant ok")
 """
 
 
-@pytest.mark.parametrize("variant", ["regs", "smem"])
+@pytest.mark.parametrize("variant", ["regs", "smem", "ring"])
 def test_layernorm_variant(variant):
     code = LN_SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
                             tests=os.path.join(ROOT, "tests"))
@@ -70,3 +70,38 @@ def test_layernorm_variant(variant):
     res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
                          timeout=600)
     assert res.returncode == 0 and "variant ok" in res.stdout, res.stdout + res.stderr
+
+
+DIGEST_SCRIPT = r"""
+import sys, hashlib
+sys.path.insert(0, {root!r}); sys.path.insert(0, {pkg!r}); sys.path.insert(0, {tests!r})
+import torch
+from tfx import ops
+from helpers import splitmix_normal, splitmix_uniform
+h = hashlib.sha256()
+for d, cols in [(768, 8192), (768, 32768), (1024, 2500), (64, 7), (516, 4737)]:
+    x = torch.from_numpy(splitmix_normal(d * cols, 0x7E4F0A10 + d)).cuda()
+    w = torch.from_numpy(splitmix_uniform(d, 0x7E4F0A11 + d, 0.5, 1.5)).cuda()
+    b = torch.from_numpy(splitmix_normal(d, 0x7E4F0A12 + d, std=0.1)).cuda()
+    for bias in (None, b):
+        h.update(ops.layer_norm_feature_first(x, w, bias, 1e-5).cpu().numpy().tobytes())
+    ops.layer_norm_feature_first(x, w, b, 1e-5, out=x)  # in place
+    h.update(x.cpu().numpy().tobytes())
+print("digest", h.hexdigest())
+"""
+
+
+def test_layernorm_ring_gives_the_one_wave_kernels_bits():
+    """The persistent ring kernel (default) and the one-wave shared-memory
+    kernel use the same lane mapping and roundings: identical outputs,
+    in place included, with several columns per warp (32768 columns)."""
+    code = DIGEST_SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
+                                tests=os.path.join(ROOT, "tests"))
+    digests = []
+    for variant in ("ring", "smem"):
+        env = dict(os.environ, TFX_LN_KERNEL=variant)
+        res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True,
+                             text=True, timeout=600)
+        assert res.returncode == 0, res.stdout + res.stderr
+        digests.append([ln for ln in res.stdout.splitlines() if ln.startswith("digest")][-1])
+    assert digests[0] == digests[1]
