@@ -594,6 +594,27 @@ def run_ops_configs(torch, ops, device, l2_bytes, hbm_peak, only=None, reps=40):
     bias = normal(F, 0.02)
     measure("bias_add", lambda: (normal(F * T), torch.empty(F * T, device=device)),
             lambda b: ops.bias_act(b[0], bias, out=b[1]), 2 * F * T * 4 + F * 4, F * T)
+    # the MLP input projection with its GeGLU epilogue fused (tcgen05, 3xTF32):
+    # hidden 768 -> 2 x 1152 over configs[1]'s 8192 tokens; the (2304, 8192)
+    # projection never reaches HBM. Beside it the same work unfused, as the
+    # reference's CUDA path runs it: a cuBLAS f32 GEMM (through torch, TF32
+    # off), then the GeGLU kernel.
+    Kg, Ig, Tg = CHAIN["hidden"], CHAIN["inter"], 8192
+    wg = normal(2 * Ig * Kg, Kg ** -0.5)  # (in, 2I) column-major = torch (2I, in)
+    bg = normal(2 * Ig, 0.02)
+    flops_g = 2 * Tg * 2 * Ig * Kg
+    bytes_g = (Kg * Tg + 2 * Ig * Kg + 2 * Ig + Ig * Tg) * 4
+    measure("gemm_geglu", lambda: (normal(Kg * Tg), torch.empty(Ig * Tg, device=device)),
+            lambda b: ops.gemm_geglu(b[0], wg, bg, Ig, out=b[1]), bytes_g, Ig * Tg,
+            flops=flops_g)
+
+    def unfused(b):
+        p = torch.addmm(bg, b[0].view(Tg, Kg), wg.view(2 * Ig, Kg).t())  # (2I, T) feature-first
+        ops.geglu(p, Ig, out=b[1])
+
+    measure("gemm_geglu_unfused_cublas_f32", lambda: (normal(Kg * Tg),
+                                                      torch.empty(Ig * Tg, device=device)),
+            unfused, bytes_g, Ig * Tg, flops=flops_g)
     return results
 
 
@@ -998,8 +1019,8 @@ def main():
                          "gelu_erf, rmsnorm_last, gated_silu, masked_softmax, "
                          "masked_softmax_global, rope_qk, laya_attention_window, "
                          "laya_attention_global, jeff_attention, add_layernorm, "
-                         "embedding_columns, "
-                         "bias_add) and "
+                         "embedding_columns, bias_add, gemm_geglu, "
+                         "gemm_geglu_unfused_cublas_f32) and "
                          "print its result; for profiler captures")
     ap.add_argument("--op-reps", type=int, default=40)
     args = ap.parse_args()

@@ -58,7 +58,8 @@ TFX_API int tfx_version(void);
  * inside libtfx kernels on the current device that gave up since the library
  * was loaded (a kernel that gives up leaves its output incomplete). Every wait
  * of a kernel on an asynchronous copy or tensor-core operation (the TMA-
- * pipelined RMSNorm, the tensor-core attention) is bounded (about one second),
+ * pipelined RMSNorm, the tensor-core attention and GEMM epilogue) is bounded
+ * (about one second),
  * so a lost copy ends the kernel instead of hanging the GPU. Synchronous
  * (reads device memory). */
 TFX_API int tfx_wait_timeouts(uint32_t* count);
@@ -108,6 +109,41 @@ TFX_API int tfx_gated_silu_stacked_f32(const float* gu, float* y, int64_t rows, 
 #define TFX_ACT_RELU 2
 TFX_API int tfx_bias_act_ff_f32(const float* x, const float* bias, float* y, int64_t features,
                         int64_t tokens, int act, tfx_stream_t stream);
+
+/* ---- GEMM with a fused epilogue ---------------------------------------------
+ * The MLP projection with its epilogue in the same kernel (tcgen05 tensor
+ * cores, 3xTF32 for f32 accuracy; the projection never reaches HBM).
+ * x is feature-first (in_dim, length), weight is column-major (in_dim, out)
+ * -- element (i, o) at i + in_dim*o, the reference's layout --, bias is
+ * (out) or NULL:
+ *   p[o, t] = bias[o] + sum_i x[i + in_dim*t] * weight[i + in_dim*o]
+ * (cpu-kernels lib.rs:274-288 input_mul_weight_transpose_bias_into; 0
+ * instead of bias[o] when bias is NULL, input_mul_weight_transpose_into,
+ * lib.rs:257-267).
+ * tfx_gemm_geglu_ff_f32 replaces GemmGegluOp / EagerSessionGemmGegluExt::
+ * gemm_geglu (crates/tenferro-ext/src/gemm_geglu.rs:25-31,114-240,
+ * 268-310): out = 2*intermediate, y is (intermediate, length) with
+ *   y[j + intermediate*t] = gelu_erf(p[j, t]) * p[intermediate + j, t]
+ * (geglu_into, lib.rs:516-538, the f32 GELU above).
+ * tfx_gemm_bias_act_ff_f32 replaces GemmBiasOp (gemm_bias.rs:27,76-142), and
+ * with an activation the reference's GEMM followed by
+ * FusedScope::bias_act_first (cuda_fused.rs:704, kernel fused_bias_act,
+ * fused.cu:137): y is (out_dim, length), y[o + out_dim*t] = act(p[o, t]),
+ * act as tfx_bias_act_ff_f32.
+ * Results are within the f32 tolerance of the reference's f32 GEMM (summation
+ * order differs); the epilogue arithmetic is the reference's. Tiles of 128
+ * tokens holding a non-finite value (or |v| >= 2^60), and every tile when
+ * the weight does, are computed with the reference's sequential arithmetic so
+ * that inf / NaN propagate as there. y must not overlap x, weight or bias.
+ * Scratch (hi / lo copies of x and weight, about 8 * (in_dim rounded up to
+ * 32) * (length + out) bytes) is allocated stream-ordered and released on the
+ * stream. */
+TFX_API int tfx_gemm_geglu_ff_f32(const float* x, const float* weight, const float* bias,
+                                  float* y, int64_t in_dim, int64_t intermediate,
+                                  int64_t length, tfx_stream_t stream);
+TFX_API int tfx_gemm_bias_act_ff_f32(const float* x, const float* weight, const float* bias,
+                                     float* y, int64_t in_dim, int64_t out_dim, int64_t length,
+                                     int act, tfx_stream_t stream);
 
 /* Residual add of the encoder layer (laya-infer/src/model.rs add_assign):
  * y = a + b elementwise. y may equal a or b. */

@@ -354,3 +354,21 @@ def softmax_rows_f64(x, rows, cols):
     y = np.empty(rows * cols, dtype=np.float64)
     lib().orc_softmax_rows_f64(_p64(x), _p64(y), rows, cols)
     return y
+
+
+# ---- GEMM with an epilogue (crates/tenferro-ext/src/gemm_geglu.rs:209-238,
+# gemm_bias.rs:76-142): the sequential projection, then the epilogue op ------
+
+def gemm_geglu_f32(x, weight, bias, in_dim, intermediate, length):
+    """p = bias (or 0) + x.W over (in_dim, length) x (in_dim, 2I), then
+    geglu_into over (2I, length) -> (I, length)."""
+    out = 2 * intermediate
+    b = np.zeros(out, np.float32) if bias is None else bias
+    p = gemm_bias_f32(x, weight, b, in_dim, out, length)
+    return geglu_f32(p, intermediate, length)
+
+
+def gemm_bias_act_f32(x, weight, bias, in_dim, out_dim, length, act):
+    b = np.zeros(out_dim, np.float32) if bias is None else bias
+    p = gemm_bias_f32(x, weight, b, in_dim, out_dim, length)
+    return bias_act_f32(p, None, out_dim, length, act)

@@ -26,7 +26,7 @@ LIB = os.path.join(LIB_DIR, "libtfx.so")
 INCLUDE = os.path.join(ROOT, "include")
 
 SOURCES = ["runtime.cu", "elementwise.cu", "norms.cu", "softmax.cu", "rope.cu", "session.cu",
-           "rms_stream.cu", "attention.cu", "embedding.cu"]
+           "rms_stream.cu", "attention.cu", "embedding.cu", "gemm_epilogue.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [

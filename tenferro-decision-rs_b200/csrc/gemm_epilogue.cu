@@ -1,0 +1,643 @@
+// gemm_epilogue.cu -- the GEMM-epilogue fusions of the MLP projection:
+// GemmGegluOp (crates/tenferro-ext/src/gemm_geglu.rs:114-240, the projection
+// then geglu_into) and GemmBiasOp with an activation (gemm_bias.rs:76-142; on
+// CUDA the reference runs a GEMM, then FusedScope::bias_act_first,
+// cuda_fused.rs:704, kernel fused_bias_act, fused.cu:137), as one tcgen05
+// kernel whose epilogue reads the accumulators from tensor memory.
+//
+// Layouts (the reference's column-major ones): x is feature-first
+// (in_dim, length), element (i, t) at i + in_dim*t; weight is (in_dim, out)
+// with element (i, o) at i + in_dim*o; the projection is
+//   p[o, t] = bias[o] + sum_i x[i, t] * weight[i, o]
+// (cpu-kernels lib.rs:274-288, input_mul_weight_transpose_bias_into), and
+//   GeGLU:    y[j + I*t] = gelu_erf(p[j, t]) * p[I + j, t]   (out = 2I, lib.rs:516-538)
+//   bias+act: y[o + out*t] = act(p[o, t])
+// Only y is written: the (out, length) projection never reaches HBM.
+//
+// Arithmetic. f32 accuracy on the tensor cores by the 3xTF32 split: every
+// operand value v = hi + lo with hi and lo tf32 roundings (cvt.rna), and
+// x.w ~ xh.wh + xh.wl + xl.wh (the dropped xl.wl is ~2^-22 relative), f32
+// accumulation in TMEM. A prep kernel writes hi and lo of x and of the weight
+// into a stream-ordered scratch, with K padded to a multiple of 32 with zeros,
+// so every tensor-map constraint holds whatever the caller's shapes and
+// alignment. The epilogue adds the bias (one rounding) and applies the
+// reference's exact-erf GELU (tfx_math.h, bit-identical to gelu_erf_f32) or
+// ReLU. The result differs from the reference's f32 GEMM by summation order
+// and the split (f32 tolerance), not by the epilogue arithmetic.
+//
+// Non-finite operands (and |v| >= 2^60, whose split could overflow) take an
+// exact path: the prep kernel flags every 128-token tile of x that holds one
+// (and the whole call when the weight does); the tensor-core kernel skips
+// those tiles and a SIMT kernel computes them with the reference's operation
+// order (sequential sum from the bias, each product rounded, no FMA), so
+// inf / NaN propagate as in the reference.
+//
+// Kernel (one persistent CTA per SM, 320 threads):
+//   warp 0  TMA producer: per K chunk of 32, the x tile (128 tokens) hi and lo
+//           and the weight tile (256 output rows) hi and lo, 96 KB, into one
+//           of two shared-memory stages (128-byte swizzled, K-major);
+//   warp 1  TMEM owner and MMA issuer: 12 tcgen05.mma.kind::tf32 (M 128,
+//           N 256, K 8) per chunk into one of two 256-column partials;
+//   warps 2-9 epilogue: two warps per TMEM lane quarter (one token per
+//           thread, 128 of the 256 columns per warp) add every chunk's
+//           partial into f32 registers and release it to the MMA warp, then
+//           at the tile's end apply bias, GeGLU / activation and store.
+// For GeGLU the 256 columns are projection rows [n0, n0 + 128) (the GELU'd
+// half) and [I + n0, I + n0 + 128) (the gate half), so a thread holding
+// column c also holds column 128 + c. Every mbarrier wait is
+// bounded (~1 s); a role that gives up counts it, sets a CTA-wide abort flag
+// that ends the other roles' waits, and the CTA drains its own copies and
+// MMAs (bounded) and frees its TMEM before it exits.
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "internal.h"
+#include "tc.cuh"
+#include "tfx_math.h"
+#include "tma.cuh"
+
+// Bounded waits of the GEMM-epilogue kernel that gave up, per device.
+static __device__ uint32_t g_gemm_wait_timeouts;
+
+namespace tfx {
+namespace {
+
+constexpr int kEpiGeglu = 0;
+constexpr int kEpiBiasAct = 1;
+
+constexpr int kGThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epilogue
+constexpr int kEpiWarps = 8;
+constexpr int kBM = 128;  // tokens per tile
+constexpr int kBN = 256;  // projection rows per tile
+constexpr int kBK = 32;   // K values per stage (one 128-byte swizzle row)
+constexpr int kStages = 2;
+constexpr uint32_t kABytes = kBM * kBK * 4;                  // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 4;                  // 32 KB
+constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;  // 96 KB
+constexpr size_t kGemmSmem = size_t(kStages) * kStageBytes + 1024;
+constexpr long long kGemmWait = 1LL << 31;  // ~1 s at B200 clocks
+constexpr float kSplitLimit = 1152921504606846976.0f;  // 2^60
+
+struct GemmArgs {
+  float* y;
+  const float* bias;
+  const uint32_t* flags;  // [mtiles] x tiles with a non-finite value, then [1] the weight
+  uint32_t length;        // tokens
+  uint32_t nk;            // K chunks of 32
+  uint32_t nout;          // outputs per token: I (GeGLU) or out_dim (bias + act)
+  uint32_t inter;         // GeGLU: I, the row offset of the gate half
+  uint32_t mtiles, ntiles;
+  int vec4;               // every output row 16-byte aligned and nout % 4 == 0
+};
+
+__device__ __forceinline__ float tf32_rna(float v) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+  return __uint_as_float(r);
+}
+
+// ---- prep: hi / lo split with K padding ---------------------------------------------
+//
+// src (in_dim, cols) -> hi, lo (kp, cols_pad), element (k, c) at k + kp*c,
+// zero for k >= in_dim or c >= cols (the padding keeps every TMA box of the
+// kernel inside its tensor). A column holding a value that cannot be split
+// safely (not finite, or |v| >= 2^60) sets flags[c >> shift].
+template <int VEC>
+__global__ void __launch_bounds__(256) split_pad_kernel(const float* __restrict__ src,
+                                                        uint32_t in_dim, uint32_t cols,
+                                                        uint32_t cols_pad, uint32_t kp,
+                                                        float* __restrict__ hi,
+                                                        float* __restrict__ lo,
+                                                        uint32_t* __restrict__ flags,
+                                                        uint32_t shift) {
+  pdl_enter();
+  const uint32_t kq = kp / 4;  // float4 groups per padded column
+  const uint64_t total = uint64_t(kq) * cols_pad;
+  for (uint64_t g = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t c = uint32_t(g / kq), k0 = uint32_t(g % kq) * 4;
+    const float* s = src + uint64_t(c) * in_dim;
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c >= cols) {
+      // padding column: zeros
+    } else if (VEC == 4 && k0 + 4 <= in_dim) {
+      const float4 q = ld_stream(reinterpret_cast<const float4*>(s + k0));
+      v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = k0 + j < in_dim ? ld_stream(s + k0 + j) : 0.0f;
+    }
+    float h[4], l[4];
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (!(fabsf(v[j]) < kSplitLimit)) {  // inf, NaN, huge: the SIMT path computes the tile
+        bad = true;
+        h[j] = 0.0f;
+        l[j] = 0.0f;
+      } else {
+        h[j] = tf32_rna(v[j]);
+        l[j] = tf32_rna(__fsub_rn(v[j], h[j]));  // v - h is exact
+      }
+    }
+    const uint64_t o = uint64_t(c) * kp + k0;
+    *reinterpret_cast<float4*>(hi + o) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lo + o) = make_float4(l[0], l[1], l[2], l[3]);
+    if (bad) flags[c >> shift] = 1u;
+  }
+}
+
+// ---- the tensor-core kernel ----------------------------------------------------------
+
+struct GemmShared {
+  // smem stages: TMA -> MMA (full) and MMA -> TMA (empty); TMEM partial
+  // buffers: MMA -> epilogue (part_full) and epilogue -> MMA (part_empty)
+  uint64_t full[kStages], empty[kStages], part_full[2], part_empty[2], drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// Bounded wait on `bar` for the phase of the given parity; also ends when
+// another role of the CTA has given up. Returns false when it did not
+// complete (the first role to give up counts it and raises the abort flag).
+__device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, GemmShared* sh) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*reinterpret_cast<volatile int*>(&sh->abort)) return false;
+    if (clock64() - t0 > kGemmWait) {
+      if (atomicExch(&sh->abort, 1) == 0) atomicAdd(&g_gemm_wait_timeouts, 1u);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ bool tile_skipped(const GemmArgs& a, uint32_t m) {
+  return __ldcg(a.flags + m) != 0u || __ldcg(a.flags + a.mtiles) != 0u;
+}
+
+template <int EPI, int ACT>
+__device__ __forceinline__ float epi_act(float v) {
+  if constexpr (EPI == kEpiBiasAct && ACT == TFX_ACT_GELU_ERF) return math::gelu_mlx(v);
+  else if constexpr (EPI == kEpiBiasAct && ACT == TFX_ACT_RELU) return v > 0.0f ? v : 0.0f;
+  else return v;
+}
+
+// Accumulation. The tensor cores' f32 accumulation is not IEEE: each MMA
+// aligns the accumulator and its products to the largest exponent and keeps
+// about 22 bits below it (measured: an accumulator fed all 288 MMAs of a
+// 768-long contraction was off by up to 1.9e-6 of sum|x w|, ten times a
+// sequential f32 sum). So every K chunk of 32 gets a fresh accumulator,
+// filled in the order hi*lo, lo*hi (the small terms, accurate while the
+// partial is small), then hi*hi -- 4 truncating steps at the large scale per
+// chunk -- and the epilogue warps add each chunk's partial into f32 registers
+// (IEEE adds), with the bias added at the end: max error 1.3e-7 of sum|x w|
+// in a model of the hardware calibrated on the measurement above, on a par
+// with the sequential f32 sum of the reference (1.6e-7).
+template <int EPI, int ACT, bool BIAS>
+__global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
+    const __grid_constant__ CUtensorMap xh_map, const __grid_constant__ CUtensorMap xl_map,
+    const __grid_constant__ CUtensorMap wh_map, const __grid_constant__ CUtensorMap wl_map,
+    GemmArgs a) {
+  extern __shared__ __align__(1024) uint8_t gemm_smem[];
+  __shared__ GemmShared sh;
+  pdl_enter();
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t ntiles_total = a.mtiles * a.ntiles;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&sh.part_full[b], 1);
+      mbar_init(&sh.part_empty[b], kEpiWarps);  // one arrival per epilogue warp
+    }
+    mbar_init(&sh.drain, 1);
+    sh.abort = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) tmem_alloc(&sh.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tm = sh.tmem_base;
+
+  if (warp == 0) {
+    // ---- TMA producer ----
+    uint32_t issued[kStages] = {0, 0};
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+        const uint32_t m = tile / a.ntiles, n = tile - m * a.ntiles;
+        if (tile_skipped(a, m)) continue;
+        const int row_x = int(m * kBM);
+        int row_w0, row_w1;
+        if constexpr (EPI == kEpiGeglu) {
+          row_w0 = int(n * (kBN / 2));
+          row_w1 = int(a.inter + n * (kBN / 2));
+        } else {
+          row_w0 = int(n * kBN);
+          row_w1 = row_w0 + kBN / 2;
+        }
+        for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+          const uint32_t s = g % kStages, use = g / kStages;
+          if (use > 0 && !gemm_wait(&sh.empty[s], (use - 1) & 1, &sh)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = base + size_t(s) * kStageBytes;
+          mbar_arrive_expect_tx(&sh.full[s], kStageBytes);
+          const int k = int(kc * kBK);
+          tma_load_2d(st, &xh_map, &sh.full[s], k, row_x);
+          tma_load_2d(st + kABytes, &xl_map, &sh.full[s], k, row_x);
+          tma_load_2d(st + 2 * kABytes, &wh_map, &sh.full[s], k, row_w0);
+          tma_load_2d(st + 2 * kABytes + kBBytes / 2, &wh_map, &sh.full[s], k, row_w1);
+          tma_load_2d(st + 2 * kABytes + kBBytes, &wl_map, &sh.full[s], k, row_w0);
+          tma_load_2d(st + 2 * kABytes + kBBytes + kBBytes / 2, &wl_map, &sh.full[s], k, row_w1);
+          ++issued[s];
+        }
+      }
+      // let this CTA's copies still in flight land before the CTA can exit
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s] > 0) mbar_wait_bounded(&sh.full[s], (issued[s] - 1) & 1, kGemmWait);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer: one fresh partial per K chunk ----
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
+      uint32_t g = 0;
+      bool ok = true;
+      for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+        const uint32_t m = tile / a.ntiles;
+        if (tile_skipped(a, m)) continue;
+        for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+          const uint32_t s = g % kStages, use = g / kStages;
+          const uint32_t pb = g & 1, puse = g >> 1;
+          if ((puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
+              !gemm_wait(&sh.full[s], use & 1, &sh)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tm + pb * kBN;
+          const uint32_t st = smem_addr(base + size_t(s) * kStageBytes);
+          const uint32_t ah = st, al = st + kABytes, bh = st + 2 * kABytes,
+                         bl = st + 2 * kABytes + kBBytes;
+#pragma unroll
+          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x hi * w lo (starts the partial)
+            mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bl + ks * 32), idesc,
+                        ks != 0);
+#pragma unroll
+          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x lo * w hi
+            mma_tf32_ss(d, smem_desc_sw128(al + ks * 32), smem_desc_sw128(bh + ks * 32), idesc,
+                        1);
+#pragma unroll
+          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x hi * w hi
+            mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bh + ks * 32), idesc,
+                        1);
+          mma_commit(&sh.empty[s]);      // the stage is free once these MMAs have read it
+          mma_commit(&sh.part_full[pb]);  // and the partial is complete
+        }
+      }
+      // every MMA this thread issued has completed before TMEM is freed
+      mma_commit(&sh.drain);
+      mbar_wait_bounded(&sh.drain, 0, kGemmWait);
+    }
+    __syncwarp();
+  } else if (warp >= 2) {
+    // ---- epilogue: warp pairs per TMEM lane quarter, 128 columns each ----
+    const uint32_t q = warp & 3;               // TMEM lane quarter
+    const uint32_t half = (warp - 2) >> 2;     // which 128 of the 256 columns
+    const uint32_t row = q * 32 + lane;        // token within the tile
+    const uint32_t lane_off = (q * 32) << 16;
+    // GeGLU: value columns [64 half, 64 half + 64) and their gate columns
+    // 128 + the same; bias + act: columns [128 half, 128 half + 128).
+    const uint32_t c_lo = EPI == kEpiGeglu ? 64 * half : 128 * half;
+    const uint32_t c_hi = EPI == kEpiGeglu ? 128 + 64 * half : 128 * half + 64;
+    float acc[128];
+    uint32_t g = 0;
+    bool ok = true;
+    for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
+      const uint32_t m = tile / a.ntiles, n = tile - m * a.ntiles;
+      if (tile_skipped(a, m)) continue;
+#pragma unroll
+      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
+      for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+        const uint32_t pb = g & 1, puse = g >> 1;
+        bool got = true;
+        if (lane == 0) got = gemm_wait(&sh.part_full[pb], puse & 1, &sh);
+        if (!__shfl_sync(0xffffffffu, int(got), 0)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t src = tm + pb * kBN + lane_off;
+#pragma unroll
+        for (int c = 0; c < 128; c += 16) {  // one 16-column load in flight (registers)
+          float v[16];
+          tmem_ld16(src + (c < 64 ? c_lo + c : c_hi + c - 64), v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[c + j] = __fadd_rn(acc[c + j], v[j]);
+        }
+        // this warp's reads of the partial are complete: release it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.part_empty[pb]);
+      }
+      if (!ok) break;
+      const uint32_t t = m * kBM + row;
+      if (t >= a.length) continue;
+      if constexpr (EPI == kEpiGeglu) {
+        const uint32_t j0 = n * (kBN / 2) + 64 * half;  // first output row of this thread
+        if (j0 >= a.nout) continue;
+        const uint32_t valid = min(64u, a.nout - j0);
+        if constexpr (BIAS) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j)
+            if (uint32_t(j) < valid) {
+              acc[j] = __fadd_rn(acc[j], __ldg(a.bias + j0 + j));
+              acc[64 + j] = __fadd_rn(acc[64 + j], __ldg(a.bias + a.inter + j0 + j));
+            }
+        }
+        float* yr = a.y + uint64_t(t) * a.nout + j0;
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+          const float2 g0 = math::gelu_mlx2(make_float2(acc[c], acc[c + 1]));
+          const float2 g1 = math::gelu_mlx2(make_float2(acc[c + 2], acc[c + 3]));
+          const float4 o = make_float4(__fmul_rn(g0.x, acc[64 + c]), __fmul_rn(g0.y, acc[65 + c]),
+                                       __fmul_rn(g1.x, acc[66 + c]), __fmul_rn(g1.y, acc[67 + c]));
+          if (a.vec4 && uint32_t(c) + 4 <= valid) {
+            *reinterpret_cast<float4*>(yr + c) = o;
+          } else {
+            if (uint32_t(c) < valid) yr[c] = o.x;
+            if (uint32_t(c) + 1 < valid) yr[c + 1] = o.y;
+            if (uint32_t(c) + 2 < valid) yr[c + 2] = o.z;
+            if (uint32_t(c) + 3 < valid) yr[c + 3] = o.w;
+          }
+        }
+      } else {
+        const uint32_t o0 = n * kBN + 128 * half;  // first output row of this thread
+        if (o0 >= a.nout) continue;
+        const uint32_t valid = min(128u, a.nout - o0);
+        float* yr = a.y + uint64_t(t) * a.nout + o0;
+#pragma unroll
+        for (int c = 0; c < 128; c += 4) {
+          float v[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            v[j] = acc[c + j];
+            if constexpr (BIAS)
+              if (uint32_t(c + j) < valid) v[j] = __fadd_rn(v[j], __ldg(a.bias + o0 + c + j));
+          }
+          if constexpr (ACT == TFX_ACT_GELU_ERF) {
+            const float2 g0 = math::gelu_mlx2(make_float2(v[0], v[1]));
+            const float2 g1 = math::gelu_mlx2(make_float2(v[2], v[3]));
+            v[0] = g0.x; v[1] = g0.y; v[2] = g1.x; v[3] = g1.y;
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v[j] = epi_act<EPI, ACT>(v[j]);
+          }
+          if (a.vec4 && uint32_t(c) + 4 <= valid) {
+            *reinterpret_cast<float4*>(yr + c) = make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (uint32_t(c + j) < valid) yr[c + j] = v[j];
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_free(tm, 512);
+}
+
+// ---- SIMT path for the tiles with non-finite (or huge) operands ----------------------
+//
+// The reference's arithmetic: p = bias (or 0), then p = p + x*w for i = 0,
+// 1, ... (each product rounded), then the epilogue. Block = 128 tokens of one
+// tile, blockIdx.y = a group of 16 outputs.
+template <int EPI, int ACT>
+__global__ void __launch_bounds__(128) gemm_epi_simt_kernel(const float* __restrict__ x,
+                                                            const float* __restrict__ w,
+                                                            GemmArgs a, uint32_t in_dim,
+                                                            int force) {
+  pdl_enter();
+  const uint32_t m = blockIdx.x;
+  if (!force && __ldcg(a.flags + m) == 0u && __ldcg(a.flags + a.mtiles) == 0u) return;
+  const uint32_t t = m * kBM + threadIdx.x;
+  if (t >= a.length) return;
+  const float* xt = x + uint64_t(t) * in_dim;
+  const uint32_t o0 = blockIdx.y * 16;
+  for (uint32_t j = o0; j < min(o0 + 16, a.nout); ++j) {
+    auto proj = [&](uint32_t o) {
+      float p = a.bias ? a.bias[o] : 0.0f;
+      const float* wo = w + uint64_t(o) * in_dim;
+      for (uint32_t i = 0; i < in_dim; ++i) p = __fadd_rn(p, __fmul_rn(xt[i], wo[i]));
+      return p;
+    };
+    float out;
+    if constexpr (EPI == kEpiGeglu) out = __fmul_rn(math::gelu_mlx(proj(j)), proj(a.inter + j));
+    else out = epi_act<EPI, ACT>(proj(j));
+    a.y[uint64_t(t) * a.nout + j] = out;
+  }
+}
+
+// ---- host ----------------------------------------------------------------------------
+
+template <int EPI, int ACT, bool BIAS>
+int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const DeviceInfo& dev,
+              cudaStream_t stream) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  const int di = dev.device & 63;
+  std::call_once(once[di], [&] {
+    err[di] = cudaFuncSetAttribute(gemm_epi_tc_kernel<EPI, ACT, BIAS>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem));
+  });
+  if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
+  const uint32_t tiles = a.mtiles * a.ntiles;
+  const unsigned grid = unsigned(std::min<uint32_t>(tiles, uint32_t(dev.sms)));
+  return launch_kernel(op, gemm_epi_tc_kernel<EPI, ACT, BIAS>, dim3(grid), dim3(kGThreads),
+                       kGemmSmem, stream, 1, maps[0], maps[1], maps[2], maps[3], a);
+}
+
+template <int EPI, int ACT>
+int launch_all(const char* op, const float* x, const float* w, const CUtensorMap* maps,
+               const GemmArgs& a, uint32_t in_dim, bool force_simt, const DeviceInfo& dev,
+               cudaStream_t stream) {
+  int rc = TFX_OK;
+  if (!force_simt) {
+    rc = a.bias ? launch_tc<EPI, ACT, true>(op, maps, a, dev, stream)
+                : launch_tc<EPI, ACT, false>(op, maps, a, dev, stream);
+    if (rc != TFX_OK) return rc;
+  }
+  return launch_kernel(op, gemm_epi_simt_kernel<EPI, ACT>,
+                       dim3(a.mtiles, (a.nout + 15) / 16), dim3(128), 0, stream, 1, x, w, a,
+                       in_dim, force_simt ? 1 : 0);
+}
+
+size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
+
+// The shared host path. nproj = rows of the weight (2I or out_dim), nout =
+// outputs per token (I or out_dim).
+int gemm_epilogue(const char* op, int epi, int act, const float* x, const float* w,
+                  const float* bias, float* y, int64_t in_dim, int64_t nproj, int64_t nout,
+                  int64_t length, cudaStream_t stream) {
+  if (nout == 0 || length == 0) return TFX_OK;  // an empty output: a no-op, as the reference
+  TFX_REQUIRE(x || in_dim == 0, op, "x", "null pointer");
+  TFX_REQUIRE(w || in_dim == 0, op, "weight", "null pointer");
+  TFX_REQUIRE(y, op, "y", "null pointer");
+  TFX_REQUIRE(in_dim < (int64_t(1) << 31) && nproj < (int64_t(1) << 30) &&
+                  length < (int64_t(1) << 31),
+              op, "shape", "extents too large for one call");
+  const size_t ybytes = size_t(nout) * size_t(length) * 4;
+  TFX_REQUIRE(!overlaps(x, size_t(in_dim) * size_t(length) * 4, y, ybytes), op, "y",
+              "overlaps x");
+  TFX_REQUIRE(!overlaps(w, size_t(in_dim) * size_t(nproj) * 4, y, ybytes), op, "y",
+              "overlaps weight");
+  TFX_REQUIRE(!bias || !overlaps(bias, size_t(nproj) * 4, y, ybytes), op, "y", "overlaps bias");
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+
+  GemmArgs a{};
+  a.y = y;
+  a.bias = bias;
+  a.length = uint32_t(length);
+  a.nout = uint32_t(nout);
+  a.inter = uint32_t(epi == kEpiGeglu ? nout : 0);
+  a.mtiles = uint32_t((length + kBM - 1) / kBM);
+  a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
+                                       : (nout + kBN - 1) / kBN);
+  a.vec4 = nout % 4 == 0 && aligned(y, 16);
+  TFX_REQUIRE(uint64_t(a.mtiles) * a.ntiles < (uint64_t(1) << 31) && (nout + 15) / 16 < 65536,
+              op, "shape", "too many tiles for one call");
+  const uint64_t kp = round_up(size_t(in_dim), kBK);
+  a.nk = uint32_t(kp / kBK);
+
+  // scratch: x hi | x lo | w hi | w lo | flags, each region 1 KB aligned. Rows
+  // are padded with zeros so that every 128-row box the kernel loads lies
+  // inside its tensor: x to whole tiles, the weight past the last row a box
+  // can start at (GeGLU: I + 128 (ntiles - 1); bias + act: 256 ntiles - 128).
+  const uint64_t xrows = uint64_t(a.mtiles) * kBM;
+  const uint64_t wrows = epi == kEpiGeglu ? uint64_t(nproj) + kBN / 2
+                                          : uint64_t(a.ntiles) * kBN;
+  const size_t xbytes = round_up(kp * size_t(xrows) * 4, 1024);
+  const size_t wbytes = round_up(kp * size_t(wrows) * 4, 1024);
+  const size_t fbytes = round_up((size_t(a.mtiles) + 1) * 4, 1024);
+  uint8_t* scratch = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch),
+                                  2 * xbytes + 2 * wbytes + fbytes, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  }
+  float* xh = reinterpret_cast<float*>(scratch);
+  float* xl = reinterpret_cast<float*>(scratch + xbytes);
+  float* wh = reinterpret_cast<float*>(scratch + 2 * xbytes);
+  float* wl = reinterpret_cast<float*>(scratch + 2 * xbytes + wbytes);
+  uint32_t* flags = reinterpret_cast<uint32_t*>(scratch + 2 * xbytes + 2 * wbytes);
+  a.flags = flags;
+  const bool force_simt = in_dim == 0;
+  int rc = TFX_OK;
+  e = cudaMemsetAsync(flags, 0, (size_t(a.mtiles) + 1) * 4, stream);
+  if (e != cudaSuccess) rc = fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+
+  auto prep = [&](const float* src, uint64_t cols, uint64_t cols_pad, float* hi, float* lo,
+                  uint32_t* fl, uint32_t shift) {
+    const uint64_t total = kp / 4 * cols_pad;
+    const unsigned grid = unsigned(std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 8));
+    const bool v4 = in_dim % 4 == 0 && aligned(src, 16);
+    return v4 ? launch_kernel(op, split_pad_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, src,
+                              uint32_t(in_dim), uint32_t(cols), uint32_t(cols_pad), uint32_t(kp),
+                              hi, lo, fl, shift)
+              : launch_kernel(op, split_pad_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, src,
+                              uint32_t(in_dim), uint32_t(cols), uint32_t(cols_pad), uint32_t(kp),
+                              hi, lo, fl, shift);
+  };
+  CUtensorMap maps[4];
+  if (rc == TFX_OK && !force_simt) {
+    rc = prep(x, uint64_t(length), xrows, xh, xl, flags, 7);  // one flag per 128-token tile
+    if (rc == TFX_OK) rc = prep(w, uint64_t(nproj), wrows, wh, wl, flags + a.mtiles, 31);
+    std::string why;
+    const float* bases[4] = {xh, xl, wh, wl};
+    for (int i = 0; rc == TFX_OK && i < 4; ++i) {
+      const uint64_t rows = i < 2 ? xrows : wrows;
+      if (!encode_map_2d_f32(&maps[i], bases[i], kp, rows, kp, kBK, 128, &why, true))
+        rc = fail(TFX_ERR_CUDA, op, "tensor map", why);
+    }
+  }
+  if (rc == TFX_OK) {
+    if (epi == kEpiGeglu)
+      rc = launch_all<kEpiGeglu, 0>(op, x, w, maps, a, uint32_t(in_dim), force_simt, dev, stream);
+    else if (act == TFX_ACT_GELU_ERF)
+      rc = launch_all<kEpiBiasAct, TFX_ACT_GELU_ERF>(op, x, w, maps, a, uint32_t(in_dim),
+                                                      force_simt, dev, stream);
+    else if (act == TFX_ACT_RELU)
+      rc = launch_all<kEpiBiasAct, TFX_ACT_RELU>(op, x, w, maps, a, uint32_t(in_dim), force_simt,
+                                                  dev, stream);
+    else
+      rc = launch_all<kEpiBiasAct, TFX_ACT_IDENTITY>(op, x, w, maps, a, uint32_t(in_dim),
+                                                      force_simt, dev, stream);
+  }
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+
+}  // namespace
+
+int gemm_wait_timeouts(uint32_t* count) {
+  const cudaError_t err = cudaMemcpyFromSymbol(count, g_gemm_wait_timeouts, sizeof(uint32_t));
+  return err == cudaSuccess ? TFX_OK
+                            : fail(TFX_ERR_CUDA, "tfx", "wait timeouts", cudaGetErrorString(err));
+}
+
+}  // namespace tfx
+
+using namespace tfx;
+
+extern "C" {
+
+int tfx_gemm_geglu_ff_f32(const float* x, const float* weight, const float* bias, float* y,
+                          int64_t in_dim, int64_t intermediate, int64_t length,
+                          tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gemm_geglu";
+  TFX_REQUIRE(in_dim >= 0 && intermediate >= 0 && length >= 0, op, "shape",
+              "extents must be non-negative");
+  TFX_REQUIRE(intermediate < (int64_t(1) << 29), op, "intermediate",
+              "projected feature extent overflow");
+  return gemm_epilogue(op, kEpiGeglu, TFX_ACT_IDENTITY, x, weight, bias, y, in_dim,
+                       2 * intermediate, intermediate, length, stream);
+}
+
+int tfx_gemm_bias_act_ff_f32(const float* x, const float* weight, const float* bias, float* y,
+                             int64_t in_dim, int64_t out_dim, int64_t length, int act,
+                             tfx_stream_t stream) {
+  clear_error();
+  const char* op = "tenferro-ext::gemm_bias";
+  TFX_REQUIRE(in_dim >= 0 && out_dim >= 0 && length >= 0, op, "shape",
+              "extents must be non-negative");
+  TFX_REQUIRE(act == TFX_ACT_IDENTITY || act == TFX_ACT_GELU_ERF || act == TFX_ACT_RELU, op,
+              "act", "unknown activation " + std::to_string(act));
+  return gemm_epilogue(op, kEpiBiasAct, act, x, weight, bias, y, in_dim, out_dim, out_dim,
+                       length, stream);
+}
+
+}  // extern "C"

@@ -27,4 +27,7 @@ int rms_ring(const char* op, const float* x, const float* w, float* y, uint32_t 
 // up on the current device (cudaMemcpyFromSymbol; synchronous).
 int attention_wait_timeouts(uint32_t* count);
 
+// gemm_epilogue.cu: the same count for the tensor-core GEMM-epilogue kernel.
+int gemm_wait_timeouts(uint32_t* count);
+
 }  // namespace tfx

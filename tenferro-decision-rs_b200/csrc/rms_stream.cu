@@ -618,6 +618,9 @@ extern "C" int tfx_wait_timeouts(uint32_t* count) {
     return tfx::fail(TFX_ERR_CUDA, "tfx", "wait timeouts", cudaGetErrorString(err));
   st = tfx::attention_wait_timeouts(&attn);
   if (st != TFX_OK) return st;
-  *count = rms + attn;
+  uint32_t gemm = 0;
+  st = tfx::gemm_wait_timeouts(&gemm);
+  if (st != TFX_OK) return st;
+  *count = rms + attn + gemm;
   return TFX_OK;
 }

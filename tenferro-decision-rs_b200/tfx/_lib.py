@@ -87,6 +87,8 @@ SIGNATURES = {
     "tfx_gated_silu_stacked_f32": (_int, [_p, _p, _i64, _i64, _p]),
     "tfx_bias_act_ff_f32": (_int, [_p, _p, _p, _i64, _i64, _int, _p]),
     "tfx_add_f32": (_int, [_p, _p, _p, _i64, _p]),
+    "tfx_gemm_geglu_ff_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _p]),
+    "tfx_gemm_bias_act_ff_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "tfx_layernorm_ff_f32": (_int, [_p, _p, _p, _p, _i64, _i64, ctypes.c_float, _p]),
     "tfx_layernorm_ff_f64": (_int, [_p, _p, _p, _p, _i64, _i64, ctypes.c_double, _p]),
     "tfx_rmsnorm_last_f32": (_int, [_p, _p, _p, _i64, _i64, _int, ctypes.c_float, _p]),

@@ -21,7 +21,7 @@ from ._lib import (RopeDesc, SoftmaxDesc, TFX_ACT_GELU_ERF, TFX_ACT_IDENTITY, TF
 __all__ = [
     "erf", "gelu_erf", "geglu", "gated_silu", "gated_silu_stacked", "bias_act", "add",
     "layer_norm_feature_first", "rms_norm_last", "masked_softmax", "rope_tables",
-    "rope_pairhalf", "TFX_ACT_IDENTITY", "TFX_ACT_GELU_ERF", "TFX_ACT_RELU",
+    "rope_pairhalf", "gemm_geglu", "gemm_bias_act", "TFX_ACT_IDENTITY", "TFX_ACT_GELU_ERF", "TFX_ACT_RELU",
     "TFX_SOFTMAX_EXCLUDE", "TFX_SOFTMAX_FILL",
 ]
 
@@ -245,4 +245,35 @@ def embedding_gather(table, ids, hidden, vocab, length, layout, out=None):
     y = torch.empty(hidden * length, device=table.device) if out is None else out
     check(lib.tfx_embedding_gather_f32(_ptr(table), _ptr(ids), _ptr(y), hidden, vocab, length,
                                        layout, _stream(table)))
+    return y
+
+
+def gemm_geglu(x, weight, bias, intermediate, out=None):
+    """GemmGegluOp: x feature-first (in_dim, length) = torch (length, in_dim),
+    weight (in_dim, 2*intermediate) column-major = torch (2*intermediate,
+    in_dim), bias (2*intermediate) or None -> (intermediate, length) = torch
+    (length, intermediate)."""
+    _cuda(x, torch.float32, "x")
+    _cuda(weight, torch.float32, "weight")
+    _cuda(bias, torch.float32, "bias")
+    in_dim = weight.numel() // (2 * intermediate) if intermediate else 0
+    length = x.numel() // in_dim if in_dim else 0
+    y = torch.empty((length, intermediate), dtype=x.dtype, device=x.device) if out is None \
+        else out
+    check(lib.tfx_gemm_geglu_ff_f32(_ptr(x), _ptr(weight), _ptr(bias), _ptr(y), in_dim,
+                                    intermediate, length, _stream(x)))
+    return y
+
+
+def gemm_bias_act(x, weight, bias, out_dim, act=TFX_ACT_IDENTITY, out=None):
+    """GemmBiasOp with an activation: x (in_dim, length), weight (in_dim,
+    out_dim) column-major = torch (out_dim, in_dim) -> (out_dim, length)."""
+    _cuda(x, torch.float32, "x")
+    _cuda(weight, torch.float32, "weight")
+    _cuda(bias, torch.float32, "bias")
+    in_dim = weight.numel() // out_dim if out_dim else 0
+    length = x.numel() // in_dim if in_dim else 0
+    y = torch.empty((length, out_dim), dtype=x.dtype, device=x.device) if out is None else out
+    check(lib.tfx_gemm_bias_act_ff_f32(_ptr(x), _ptr(weight), _ptr(bias), _ptr(y), in_dim,
+                                       out_dim, length, act, _stream(x)))
     return y

@@ -92,8 +92,8 @@ def splitmix_uniform(n: int, seed: int, lo: float, hi: float, dtype=np.float32) 
 def ulp_distance_f32(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """|ulp distance| between float32 arrays (NaN==NaN counts as 0, NaN vs
     number as a huge distance)."""
-    a = np.ascontiguousarray(a, dtype=np.float32).view(np.int32).astype(np.int64)
-    b = np.ascontiguousarray(b, dtype=np.float32).view(np.int32).astype(np.int64)
+    a = np.ascontiguousarray(a, dtype=np.float32).ravel().view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, dtype=np.float32).ravel().view(np.int32).astype(np.int64)
     # map sign-magnitude to a monotone integer line
     a = np.where(a < 0, -(a & 0x7FFFFFFF), a)
     b = np.where(b < 0, -(b & 0x7FFFFFFF), b)
@@ -147,6 +147,8 @@ def assert_bitwise(actual, expected, what: str = "") -> None:
     a = np.ascontiguousarray(actual)
     r = np.ascontiguousarray(expected)
     assert a.shape == r.shape and a.dtype == r.dtype, (what, a.shape, r.shape, a.dtype, r.dtype)
+    if a.size == 0:
+        return
     both_nan = np.isnan(a) & np.isnan(r)
     same = (a.view(np.uint8).reshape(a.size, -1) == r.view(np.uint8).reshape(r.size, -1)).all(1)
     bad = ~(same | both_nan.ravel())

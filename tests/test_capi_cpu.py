@@ -176,7 +176,7 @@ _NO_CUDA_BEFORE_VALIDATION = [
     "tfx_rope_pairhalf_f32", "tfx_add_layernorm_ff_f32", "tfx_embedding_f32",
     "tfx_embedding_gather_f32", "tfx_laya_qkv_prep_f32", "tfx_jeff_qkv_prep_f32",
     "tfx_attention_f32", "tfx_laya_attention_block_f32", "tfx_jeff_attention_f32",
-    "tfx_wait_timeouts", "tfx_session_set_chunk_bytes", "tfx_session_layernorm_ff_f32",
+    "tfx_gemm_geglu_ff_f32", "tfx_gemm_bias_act_ff_f32", "tfx_wait_timeouts", "tfx_session_set_chunk_bytes", "tfx_session_layernorm_ff_f32",
     "tfx_session_layernorm_ff_f64", "tfx_session_rmsnorm_last_f32", "tfx_session_erf_f32",
     "tfx_session_gelu_erf_f32", "tfx_session_geglu_ff_f32", "tfx_session_gated_silu_f32",
     "tfx_session_bias_act_ff_f32", "tfx_session_add_f32", "tfx_session_add_layernorm_ff_f32",
