@@ -1082,8 +1082,8 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   if (disabled) return 1;
   CUtensorMap qmap, kmap;
   std::string why;
-  if (!encode_map_2d_f32(&qmap, a.q, 64, rows, 64, 32, kTQ, &why, true) ||
-      !encode_map_2d_f32(&kmap, a.k, 64, rows, 64, 32, kTK, &why, true))
+  if (!encode_map_2d_f32(&qmap, a.q, 64, rows, 64, 32, kTQ, &why, 128) ||
+      !encode_map_2d_f32(&kmap, a.k, 64, rows, 64, 32, kTK, &why, 128))
     return fail(TFX_ERR_CUDA, op, "tensor map", why);
   const uint32_t nbh = batch * a.heads;
   uint8_t* flags = nullptr;

@@ -52,6 +52,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -74,12 +75,11 @@ constexpr int kGThreads = 320;  // warp 0 TMA, warp 1 MMA + TMEM, warps 2-9 epil
 constexpr int kEpiWarps = 8;
 constexpr int kBM = 128;  // tokens per tile
 constexpr int kBN = 256;  // projection rows per tile
-constexpr int kBK = 32;   // K values per stage (one 128-byte swizzle row)
-constexpr int kStages = 2;
-constexpr uint32_t kABytes = kBM * kBK * 4;                  // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 4;                  // 32 KB
-constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;  // 96 KB
-constexpr size_t kGemmSmem = size_t(kStages) * kStageBytes + 1024;
+constexpr int kBK = 32;   // K padding of the scratch operands, and the largest stage
+constexpr int kMaxStages = 4;
+// Shared memory: the stage ring holds 192 KB whatever the stage width (two
+// stages of K 32, or four of K 16), plus alignment slack.
+constexpr size_t kGemmSmem = size_t(2) * (2 * kBM + 2 * kBN) * kBK * 4 + 1024;
 constexpr long long kGemmWait = 1LL << 31;  // ~1 s at B200 clocks
 constexpr float kSplitLimit = 1152921504606846976.0f;  // 2^60
 
@@ -157,7 +157,7 @@ __global__ void __launch_bounds__(256) split_pad_kernel(const float* __restrict_
 struct GemmShared {
   // smem stages: TMA -> MMA (full) and MMA -> TMA (empty); TMEM partial
   // buffers: MMA -> epilogue (part_full) and epilogue -> MMA (part_empty)
-  uint64_t full[kStages], empty[kStages], part_full[2], part_empty[2], drain;
+  uint64_t full[kMaxStages], empty[kMaxStages], part_full[2], part_empty[2], drain;
   uint32_t tmem_base;
   int abort;
 };
@@ -200,11 +200,24 @@ __device__ __forceinline__ float epi_act(float v) {
 // (IEEE adds), with the bias added at the end: max error 1.3e-7 of sum|x w|
 // in a model of the hardware calibrated on the measurement above, on a par
 // with the sequential f32 sum of the reference (1.6e-7).
-template <int EPI, int ACT, bool BIAS>
+//
+// Stages: SK K values per stage (32: 128-byte swizzled rows, two 96 KB
+// stages; 16: 64-byte swizzled rows, four 48 KB stages, so a stage is freed
+// and refilled after half as much MMA work). FK: K values per partial (the
+// drain period). Each stage's MMAs run small products first.
+template <int EPI, int ACT, bool BIAS, int SK, int FK>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
     const __grid_constant__ CUtensorMap xh_map, const __grid_constant__ CUtensorMap xl_map,
     const __grid_constant__ CUtensorMap wh_map, const __grid_constant__ CUtensorMap wl_map,
     GemmArgs a) {
+  static_assert((SK == 16 || SK == 32) && FK % SK == 0, "stage shape");
+  constexpr int kStages = 2 * kBK / SK;
+  constexpr uint32_t kABytes = kBM * SK * 4;
+  constexpr uint32_t kBBytes = kBN * SK * 4;
+  constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;
+  constexpr uint32_t kSpf = FK / SK;  // stages per partial
+  const uint32_t nst = a.nk * (kBK / SK);     // stages per tile
+  const uint32_t npart = (nst + kSpf - 1) / kSpf;  // partials per tile (the last may be short)
   extern __shared__ __align__(1024) uint8_t gemm_smem[];
   __shared__ GemmShared sh;
   pdl_enter();
@@ -234,7 +247,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
 
   if (warp == 0) {
     // ---- TMA producer ----
-    uint32_t issued[kStages] = {0, 0};
+    uint32_t issued[kStages] = {};
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
@@ -250,7 +263,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           row_w0 = int(n * kBN);
           row_w1 = row_w0 + kBN / 2;
         }
-        for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           if (use > 0 && !gemm_wait(&sh.empty[s], (use - 1) & 1, &sh)) {
             ok = false;
@@ -258,7 +271,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           }
           uint8_t* st = base + size_t(s) * kStageBytes;
           mbar_arrive_expect_tx(&sh.full[s], kStageBytes);
-          const int k = int(kc * kBK);
+          const int k = int(kc * SK);
           tma_load_2d(st, &xh_map, &sh.full[s], k, row_x);
           tma_load_2d(st + kABytes, &xl_map, &sh.full[s], k, row_x);
           tma_load_2d(st + 2 * kABytes, &wh_map, &sh.full[s], k, row_w0);
@@ -274,18 +287,23 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer: one fresh partial per K chunk ----
+    // ---- MMA issuer: one fresh partial per FK values of K ----
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_tf32(kBM, kBN);
-      uint32_t g = 0;
+      auto desc = [](uint32_t addr) {
+        if constexpr (SK == 32) return smem_desc_sw128(addr);
+        else return smem_desc_sw64(addr);
+      };
+      uint32_t g = 0, pg = 0;  // stages and partials issued
       bool ok = true;
       for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
         const uint32_t m = tile / a.ntiles;
         if (tile_skipped(a, m)) continue;
-        for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
-          const uint32_t pb = g & 1, puse = g >> 1;
-          if ((puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
+          const uint32_t pb = pg & 1, puse = pg >> 1;
+          const bool first = kc % kSpf == 0;
+          if ((first && puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
               !gemm_wait(&sh.full[s], use & 1, &sh)) {
             ok = false;
             break;
@@ -296,19 +314,19 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           const uint32_t ah = st, al = st + kABytes, bh = st + 2 * kABytes,
                          bl = st + 2 * kABytes + kBBytes;
 #pragma unroll
-          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x hi * w lo (starts the partial)
-            mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bl + ks * 32), idesc,
-                        ks != 0);
+          for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x hi * w lo (starts a partial)
+            mma_tf32_ss(d, desc(ah + ks * 32), desc(bl + ks * 32), idesc, !first || ks != 0);
 #pragma unroll
-          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x lo * w hi
-            mma_tf32_ss(d, smem_desc_sw128(al + ks * 32), smem_desc_sw128(bh + ks * 32), idesc,
-                        1);
+          for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x lo * w hi
+            mma_tf32_ss(d, desc(al + ks * 32), desc(bh + ks * 32), idesc, 1);
 #pragma unroll
-          for (uint32_t ks = 0; ks < kBK / 8; ++ks)  // x hi * w hi
-            mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bh + ks * 32), idesc,
-                        1);
-          mma_commit(&sh.empty[s]);      // the stage is free once these MMAs have read it
-          mma_commit(&sh.part_full[pb]);  // and the partial is complete
+          for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x hi * w hi
+            mma_tf32_ss(d, desc(ah + ks * 32), desc(bh + ks * 32), idesc, 1);
+          mma_commit(&sh.empty[s]);  // the stage is free once these MMAs have read it
+          if (kc % kSpf == kSpf - 1 || kc + 1 == nst) {
+            mma_commit(&sh.part_full[pb]);  // and the partial is complete
+            ++pg;
+          }
         }
       }
       // every MMA this thread issued has completed before TMEM is freed
@@ -326,15 +344,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
     // 128 + the same; bias + act: columns [128 half, 128 half + 128).
     const uint32_t c_lo = EPI == kEpiGeglu ? 64 * half : 128 * half;
     const uint32_t c_hi = EPI == kEpiGeglu ? 128 + 64 * half : 128 * half + 64;
-    float acc[128];
+    float2 acc2[64];  // 128 f32 sums, added two per instruction (FADD2)
     uint32_t g = 0;
     bool ok = true;
     for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
       const uint32_t m = tile / a.ntiles, n = tile - m * a.ntiles;
       if (tile_skipped(a, m)) continue;
 #pragma unroll
-      for (int j = 0; j < 128; ++j) acc[j] = 0.0f;
-      for (uint32_t kc = 0; kc < a.nk; ++kc, ++g) {
+      for (int j = 0; j < 64; ++j) acc2[j] = make_float2(0.0f, 0.0f);
+      for (uint32_t kc = 0; kc < npart; ++kc, ++g) {
         const uint32_t pb = g & 1, puse = g >> 1;
         bool got = true;
         if (lane == 0) got = gemm_wait(&sh.part_full[pb], puse & 1, &sh);
@@ -350,13 +368,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           tmem_ld16(src + (c < 64 ? c_lo + c : c_hi + c - 64), v);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 16; ++j) acc[c + j] = __fadd_rn(acc[c + j], v[j]);
+          for (int j = 0; j < 16; j += 2)
+            acc2[(c + j) / 2] = __fadd2_rn(acc2[(c + j) / 2], make_float2(v[j], v[j + 1]));
         }
         // this warp's reads of the partial are complete: release it
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.part_empty[pb]);
       }
+      float* acc = reinterpret_cast<float*>(acc2);
       if (!ok) break;
       const uint32_t t = m * kBM + row;
       if (t >= a.length) continue;
@@ -430,8 +450,9 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
 // ---- SIMT path for the tiles with non-finite (or huge) operands ----------------------
 //
 // The reference's arithmetic: p = bias (or 0), then p = p + x*w for i = 0,
-// 1, ... (each product rounded), then the epilogue. Block = 128 tokens of one
-// tile, blockIdx.y = a group of 16 outputs.
+// 1, ... (each product rounded), then the epilogue. One CTA per 128-token
+// tile (most exit at once: their tile was computed on the tensor cores), one
+// token per thread, blockIdx.y strides over groups of 16 outputs.
 template <int EPI, int ACT>
 __global__ void __launch_bounds__(128) gemm_epi_simt_kernel(const float* __restrict__ x,
                                                             const float* __restrict__ w,
@@ -443,38 +464,61 @@ __global__ void __launch_bounds__(128) gemm_epi_simt_kernel(const float* __restr
   const uint32_t t = m * kBM + threadIdx.x;
   if (t >= a.length) return;
   const float* xt = x + uint64_t(t) * in_dim;
-  const uint32_t o0 = blockIdx.y * 16;
-  for (uint32_t j = o0; j < min(o0 + 16, a.nout); ++j) {
-    auto proj = [&](uint32_t o) {
-      float p = a.bias ? a.bias[o] : 0.0f;
-      const float* wo = w + uint64_t(o) * in_dim;
-      for (uint32_t i = 0; i < in_dim; ++i) p = __fadd_rn(p, __fmul_rn(xt[i], wo[i]));
-      return p;
-    };
-    float out;
-    if constexpr (EPI == kEpiGeglu) out = __fmul_rn(math::gelu_mlx(proj(j)), proj(a.inter + j));
-    else out = epi_act<EPI, ACT>(proj(j));
-    a.y[uint64_t(t) * a.nout + j] = out;
+  for (uint32_t o0 = blockIdx.y * 16; o0 < a.nout; o0 += gridDim.y * 16) {
+    for (uint32_t j = o0; j < min(o0 + 16, a.nout); ++j) {
+      auto proj = [&](uint32_t o) {
+        float p = a.bias ? a.bias[o] : 0.0f;
+        const float* wo = w + uint64_t(o) * in_dim;
+        for (uint32_t i = 0; i < in_dim; ++i) p = __fadd_rn(p, __fmul_rn(xt[i], wo[i]));
+        return p;
+      };
+      float out;
+      if constexpr (EPI == kEpiGeglu) out = __fmul_rn(math::gelu_mlx(proj(j)), proj(a.inter + j));
+      else out = epi_act<EPI, ACT>(proj(j));
+      a.y[uint64_t(t) * a.nout + j] = out;
+    }
   }
 }
 
 // ---- host ----------------------------------------------------------------------------
 
-template <int EPI, int ACT, bool BIAS>
+template <int EPI, int ACT, bool BIAS, int SK, int FK>
 int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const DeviceInfo& dev,
               cudaStream_t stream) {
+  auto kernel = gemm_epi_tc_kernel<EPI, ACT, BIAS, SK, FK>;
   static std::once_flag once[64];
   static cudaError_t err[64];
   const int di = dev.device & 63;
   std::call_once(once[di], [&] {
-    err[di] = cudaFuncSetAttribute(gemm_epi_tc_kernel<EPI, ACT, BIAS>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, int(kGemmSmem));
+    err[di] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(kGemmSmem));
   });
   if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
   const uint32_t tiles = a.mtiles * a.ntiles;
   const unsigned grid = unsigned(std::min<uint32_t>(tiles, uint32_t(dev.sms)));
-  return launch_kernel(op, gemm_epi_tc_kernel<EPI, ACT, BIAS>, dim3(grid), dim3(kGThreads),
-                       kGemmSmem, stream, 1, maps[0], maps[1], maps[2], maps[3], a);
+  return launch_kernel(op, kernel, dim3(grid), dim3(kGThreads), kGemmSmem, stream, 1, maps[0],
+                       maps[1], maps[2], maps[3], a);
+}
+
+// Partial length of the tensor-core kernel: 0 = one partial per 32 values of K
+// (default), 1 = per 64 (2 % faster on the configs[1] projection, error still
+// below the reference's sequential sum: max 1.3e-7 of sum|x w| against 0.75e-7
+// and the reference's 3.6e-7). TFX_GEMM_STAGES = k32 / k32f64 selects one for
+// tuning runs. (Four stages of K 16 with 64-byte swizzle were measured 5 %
+// slower: the MMA pipe, not the copy latency, bounds the kernel.)
+int gemm_stage_layout() {
+  static const int v = [] {
+    const char* e = getenv("TFX_GEMM_STAGES");
+    return e && std::string(e) == "k32f64" ? 1 : 0;
+  }();
+  return v;
+}
+
+template <int EPI, int ACT, bool BIAS>
+int launch_tc_layout(const char* op, const CUtensorMap* maps, const GemmArgs& a,
+                     const DeviceInfo& dev, cudaStream_t stream) {
+  return gemm_stage_layout() == 1 ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
+                                  : launch_tc<EPI, ACT, BIAS, 32, 32>(op, maps, a, dev, stream);
 }
 
 template <int EPI, int ACT>
@@ -483,13 +527,13 @@ int launch_all(const char* op, const float* x, const float* w, const CUtensorMap
                cudaStream_t stream) {
   int rc = TFX_OK;
   if (!force_simt) {
-    rc = a.bias ? launch_tc<EPI, ACT, true>(op, maps, a, dev, stream)
-                : launch_tc<EPI, ACT, false>(op, maps, a, dev, stream);
+    rc = a.bias ? launch_tc_layout<EPI, ACT, true>(op, maps, a, dev, stream)
+                : launch_tc_layout<EPI, ACT, false>(op, maps, a, dev, stream);
     if (rc != TFX_OK) return rc;
   }
-  return launch_kernel(op, gemm_epi_simt_kernel<EPI, ACT>,
-                       dim3(a.mtiles, (a.nout + 15) / 16), dim3(128), 0, stream, 1, x, w, a,
-                       in_dim, force_simt ? 1 : 0);
+  const unsigned gy = std::min<unsigned>((a.nout + 15) / 16, 8);
+  return launch_kernel(op, gemm_epi_simt_kernel<EPI, ACT>, dim3(a.mtiles, gy), dim3(128), 0,
+                       stream, 1, x, w, a, in_dim, force_simt ? 1 : 0);
 }
 
 size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
@@ -526,8 +570,8 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
                                        : (nout + kBN - 1) / kBN);
   a.vec4 = nout % 4 == 0 && aligned(y, 16);
-  TFX_REQUIRE(uint64_t(a.mtiles) * a.ntiles < (uint64_t(1) << 31) && (nout + 15) / 16 < 65536,
-              op, "shape", "too many tiles for one call");
+  TFX_REQUIRE(uint64_t(a.mtiles) * a.ntiles < (uint64_t(1) << 31), op, "shape",
+              "too many tiles for one call");
   const uint64_t kp = round_up(size_t(in_dim), kBK);
   a.nk = uint32_t(kp / kBK);
 
@@ -579,7 +623,7 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
     const float* bases[4] = {xh, xl, wh, wl};
     for (int i = 0; rc == TFX_OK && i < 4; ++i) {
       const uint64_t rows = i < 2 ? xrows : wrows;
-      if (!encode_map_2d_f32(&maps[i], bases[i], kp, rows, kp, kBK, 128, &why, true))
+      if (!encode_map_2d_f32(&maps[i], bases[i], kp, rows, kp, kBK, 128, &why, kBK * 4))
         rc = fail(TFX_ERR_CUDA, op, "tensor map", why);
     }
   }

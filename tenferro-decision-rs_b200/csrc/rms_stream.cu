@@ -67,7 +67,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 bool encode_map_2d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                        uint64_t stride1, uint32_t box0, uint32_t box1, std::string* why,
-                       bool swizzle128) {
+                       int swizzle_bytes) {
   const auto fn = encode_fn();
   if (!fn) {
     *why = "cuTensorMapEncodeTiled is not available from the driver";
@@ -79,7 +79,9 @@ bool encode_map_2d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {

@@ -50,6 +50,17 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
+// The same for a K-major SW64 operand: rows of 64 bytes (16 f32 / tf32
+// values of K), the 16-byte chunks of row r permuted by the 64-byte swizzle,
+// 8-row atoms of 512 bytes (stride byte offset 512 >> 4), layout type
+// SWIZZLE_64B = 4 [61,64). A K step of 8 tf32 values moves the start by 32
+// bytes inside a row. This is the layout a TMA load with
+// CU_TENSOR_MAP_SWIZZLE_64B and a 16-value inner box writes.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
+  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t(1) << 16) | (uint64_t(512 >> 4) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(4) << 61);
+}
+
 // Instruction descriptor of tcgen05.mma.kind::tf32, f32 accumulate, both
 // operands K-major: c_format F32 [4,6), a/b_format TF32 [7,10) [10,13),
 // N >> 3 [17,23), M >> 4 [24,29).

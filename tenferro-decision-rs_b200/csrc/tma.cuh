@@ -18,12 +18,12 @@ namespace tfx {
 
 // Host: encodes a 2-D f32 tensor map over base[i0 + stride1 * i1] (i0 < dim0,
 // i1 < dim1, stride1 in elements) with box (box0, box1), zero fill out of
-// bounds, and no swizzle or (swizzle128, box0 * 4 == 128) the 128-byte
-// swizzle of tc.cuh's operand layout. Returns false and sets *why when the
-// driver refuses.
+// bounds, and no swizzle (swizzle_bytes 0) or the 64- / 128-byte swizzle of
+// tc.cuh's operand layouts (swizzle_bytes == box0 * 4). Returns false and sets
+// *why when the driver refuses.
 bool encode_map_2d_f32(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1,
                        uint64_t stride1, uint32_t box0, uint32_t box1, std::string* why,
-                       bool swizzle128 = false);
+                       int swizzle_bytes = 0);
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
