@@ -11,7 +11,9 @@
  * (crates/tenferro-ext/src, crates/tenferro-infer/src):
  *   - Layouts are the reference's column-major ones (first axis fastest).
  *     A feature-first activation (d, cols) stores column c at [c*d, (c+1)*d).
- *   - Inputs are borrowed, outputs are caller-owned; nothing is allocated.
+ *   - Inputs are borrowed, outputs are caller-owned. Calls that need scratch
+ *     (named at each) allocate it stream-ordered on the call's stream and
+ *     release it there; every other call allocates nothing.
  *   - Every call is asynchronous on the given stream (NULL = legacy default
  *     stream) and takes device pointers, except the tfx_session_* calls,
  *     which take host pointers and return when the host outputs are written.

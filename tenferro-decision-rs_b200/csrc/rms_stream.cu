@@ -349,9 +349,6 @@ inline size_t ring_smem_bytes(uint32_t box1, uint32_t nbox, uint32_t slots) {
          size_t(kRingWarps) * kRingTok * 4 + kRingTok * 4 + 2 * size_t(slots) * 8 + 8;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
 // Barrier over the consumer threads only (named barrier `id`).
 __device__ __forceinline__ void consumers_sync(uint32_t id) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kRingConsumers) : "memory");
