@@ -435,6 +435,16 @@ TFX_API int tfx_session_add_layernorm_ff_f32(tfx_session* session, const float* 
                                              const float* b, const float* weight,
                                              const float* bias, float* sum_out, float* y,
                                              int64_t d, int64_t cols, float eps);
+/* tfx_gemm_geglu_ff_f32 / tfx_gemm_bias_act_ff_f32 on host buffers (the
+ * executor of GemmGegluOp / GemmBiasOp on a CPU session's tensors): the weight
+ * and bias are uploaded once per call, x and y move in chunks of tokens. */
+TFX_API int tfx_session_gemm_geglu_ff_f32(tfx_session* session, const float* x,
+                                          const float* weight, const float* bias, float* y,
+                                          int64_t in_dim, int64_t intermediate, int64_t length);
+TFX_API int tfx_session_gemm_bias_act_ff_f32(tfx_session* session, const float* x,
+                                             const float* weight, const float* bias, float* y,
+                                             int64_t in_dim, int64_t out_dim, int64_t length,
+                                             int act);
 /* desc->valid_lens / add_mask / keep are host pointers here. */
 TFX_API int tfx_session_masked_softmax_f32(tfx_session* session, const float* scores,
                                            float* probs, const tfx_softmax_desc* desc);

@@ -23,6 +23,11 @@ int rms_stream(const char* op, const float* x, const float* w, float* y, uint32_
 int rms_ring(const char* op, const float* x, const float* w, float* y, uint32_t rows,
              uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
 
+// rms_stream.cu: the same op on 32-token tiles shared by a CTA pair (widths
+// 513 .. 1024); 1 when not covered, else a status.
+int rms_pair(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+             uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream);
+
 // attention.cu: the tensor-core attention's count of bounded waits that gave
 // up on the current device (cudaMemcpyFromSymbol; synchronous).
 int attention_wait_timeouts(uint32_t* count);

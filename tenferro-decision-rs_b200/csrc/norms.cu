@@ -1013,7 +1013,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const float* x,
 
 // Kernel choice for the f32 feature-last RMSNorm: 0 = automatic, 1 = cluster,
 // 2 = tile, 3 = split, 4 = 16-CTA cluster, 5 = TMA-pipelined stream, 6 = TMA
-// box ring into registers; TFX_RMS_KERNEL overrides it for tuning runs.
+// box ring into registers, 7 = the ring on 32-token tiles shared by a CTA
+// pair; TFX_RMS_KERNEL overrides it for tuning runs.
 int rms_kernel_choice() {
   static const int choice = [] {
     const char* e = getenv("TFX_RMS_KERNEL");
@@ -1025,6 +1026,7 @@ int rms_kernel_choice() {
            : s == "cluster16" ? 4
            : s == "stream"  ? 5
            : s == "ring"    ? 6
+           : s == "pair"    ? 7
                             : 0;
   }();
   return choice;
@@ -1132,6 +1134,11 @@ int rmsnorm_last(const char* op, const T* x, const T* w, T* y, int64_t rows, int
     // (whole tiles staged in shared memory) read x once with their loads
     // always in flight; they cover aligned shapes with rows % 4 == 0, widths
     // 513 .. 2048 and up to ~3300 respectively.
+    if (small && choice == 7) {
+      const int rc = rms_pair(op, x, w, y, uint32_t(rows), uint32_t(width), centered, eps,
+                              inv_width, stream);
+      if (rc != 1) return rc;
+    }
     if (small && (choice == 0 || choice == 6)) {
       const int rc = rms_ring(op, x, w, y, uint32_t(rows), uint32_t(width), centered, eps,
                               inv_width, stream);

@@ -532,6 +532,221 @@ int launch_ring(const char* op, const CUtensorMap& map, const RingArgs& a, size_
                        1, map, a);
 }
 
+// ---- pair variant: 32-token tiles shared by a CTA pair ------------------------------
+//
+// The ring kernel's 16-token tiles read one 64-byte run per feature; a copy
+// with that pattern already takes 24.8 us at 16384 x 1024, against 23.8 us
+// for 32-token tiles (128-byte runs). One SM cannot hold a 32-token tile
+// (128 KB at width 1024) in registers, and 512 such tiles over 148 SMs would
+// leave a 13 % tail. So a cluster of two CTAs shares each 32-token tile: CTA
+// r streams features [r*wc, r*wc + wc) (wc = half the width) through the same
+// TMA box ring (boxes of 32 tokens x 128 features), reduces its per-token
+// partial sums of squares, and stores them into the other CTA's shared memory
+// with st.async, which completes on that CTA's mbarrier -- no cluster barrier
+// per tile. Both CTAs add the two partials in rank order, so they compute the
+// same scale. Two exchange slots suffice: a CTA sends tile k's partials only
+// after it received the peer's partials of tile k - 1, which the peer sent
+// only after it finished reading the slot of tile k - 2.
+
+constexpr int kPairTok = 32;
+constexpr uint32_t kPairBox = 128;  // features per box
+constexpr uint32_t kPairMaxBoxes = 4;
+
+struct PairArgs {
+  const float* w;
+  float* y;
+  uint32_t rows, width;
+  uint32_t wc, nbox;  // features per CTA, boxes per CTA and tile
+  uint32_t tiles, slots;
+  float eps, inv_width;
+  int centered;
+};
+
+// Shared memory: slots x [128][32] | w' [512] | red [kRingWarps][32] |
+// exchange [2][32] | scale [32] | full, empty [slots each], exchange [2] mbarriers.
+inline size_t pair_smem_bytes(uint32_t slots) {
+  return size_t(slots) * kPairBox * kPairTok * 4 + kPairMaxBoxes * kPairBox * 4 +
+         size_t(kRingWarps) * kPairTok * 4 + 3 * kPairTok * 4 + (2 * size_t(slots) + 2) * 8 + 8;
+}
+
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t smem_addr_local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr_local), "r"(rank));
+  return r;
+}
+// 4 bytes into another CTA's shared memory, completing 4 bytes of transactions
+// on its mbarrier at `remote_bar` (both shared::cluster addresses).
+__device__ __forceinline__ void st_async_b32(uint32_t remote_addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(
+                   remote_addr),
+               "r"(__float_as_uint(v)), "r"(remote_bar)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kRingThreads, 1)
+    rms_pair_kernel(const __grid_constant__ CUtensorMap xmap, PairArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  constexpr uint32_t slot_floats = kPairBox * kPairTok;
+  float* ring = reinterpret_cast<float*>(smem);
+  float* w_s = ring + size_t(a.slots) * slot_floats;
+  float* red = w_s + kPairMaxBoxes * kPairBox;
+  float* xch = red + kRingWarps * kPairTok;  // written by the other CTA
+  float* scale_s = xch + 2 * kPairTok;
+  uint64_t* full = reinterpret_cast<uint64_t*>(
+      (reinterpret_cast<uintptr_t>(scale_s + kPairTok) + 7) & ~uintptr_t(7));
+  uint64_t* empty = full + a.slots;
+  uint64_t* xbar = empty + a.slots;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster.block_rank(), peer = rank ^ 1u;
+  const uint32_t unit = blockIdx.x >> 1, units = gridDim.x >> 1;
+  const uint32_t n_my = a.tiles > unit ? (a.tiles - unit + units - 1) / units : 0;
+  const uint32_t f_begin = rank * a.wc;
+  const uint32_t nf = a.width > f_begin ? min(a.wc, a.width - f_begin) : 0;
+  if (tid == 0) {
+    for (uint32_t s = 0; s < a.slots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRingWarps);
+    }
+    mbar_init(&xbar[0], 1);
+    mbar_init(&xbar[1], 1);
+    mbar_init_fence();
+  }
+  cluster.sync();  // both CTAs' mbarriers exist before any remote arrival
+  pdl_wait();      // x and w may come from the previous kernel on the stream
+
+  if (warp == kRingWarps) {  // producer: one elected lane issues every box
+    if (lane == 0) {
+      const uint32_t box_bytes = slot_floats * 4;
+      uint32_t issued = 0, s = 0, ph = 0;
+      bool ok = true;
+      for (uint32_t k = 0; k < n_my && ok; ++k) {
+        const int tok0 = int((unit + k * units) * kPairTok);
+        for (uint32_t b = 0; b < a.nbox; ++b) {
+          if (issued >= a.slots && !mbar_wait_bounded(&empty[s], ph ^ 1u, kWaitCycles)) {
+            atomicAdd(&g_wait_timeouts, 1u);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], box_bytes);
+          tma_load_2d(ring + size_t(s) * slot_floats, &xmap, &full[s], tok0,
+                      int(f_begin + b * kPairBox));
+          ++issued;
+          if (++s == a.slots) s = 0, ph ^= 1u;
+        }
+      }
+      // every copy this CTA issued lands before the CTA can exit (bounded)
+      const uint32_t back = issued < a.slots ? issued : a.slots;
+      uint32_t ds = s, dph = ph;
+      for (uint32_t j = 0; j < back; ++j)
+        if (ds-- == 0) ds = a.slots - 1, dph ^= 1u;
+      for (uint32_t j = 0; j < back; ++j) {
+        mbar_wait_bounded(&full[ds], dph, kWaitCycles);
+        if (++ds == a.slots) ds = 0, dph ^= 1u;
+      }
+    }
+    __syncwarp();
+  } else {
+    // consumer thread (q, fg): tokens 4q .. 4q+3 of the tile, local features
+    // fg and fg + 64 of every box
+    const uint32_t q = tid & 7, fg = tid >> 3;
+    for (uint32_t f = tid; f < kPairMaxBoxes * kPairBox; f += kRingConsumers) {
+      const float wf = f < nf ? a.w[f_begin + f] : 0.0f;
+      w_s[f] = a.centered ? __fadd_rn(1.0f, wf) : wf;
+    }
+    consumers_sync(2);
+    constexpr int NV = 2 * kPairMaxBoxes;
+    float wr[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) wr[i] = w_s[(i >> 1) * kPairBox + fg + 64 * (i & 1)];
+    const uint32_t xch_peer = map_to_rank(smem_addr(xch), peer);
+    const uint32_t xbar_peer = map_to_rank(smem_addr(xbar), peer);
+    uint32_t s = 0, ph = 0;
+    for (uint32_t k = 0; k < n_my; ++k) {
+      float4 v[NV];
+      bool bad = false;
+#pragma unroll
+      for (int b = 0; b < int(kPairMaxBoxes); ++b) {
+        v[2 * b] = v[2 * b + 1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (uint32_t(b) < a.nbox) {
+          if (!mbar_wait_bounded(&full[s], ph, kWaitCycles)) bad = true;
+          const float* t = ring + size_t(s) * slot_floats + 4 * q;
+          const uint32_t lf = b * kPairBox + fg;
+          if (lf < nf) v[2 * b] = *reinterpret_cast<const float4*>(t + fg * kPairTok);
+          if (lf + 64 < nf) v[2 * b + 1] = *reinterpret_cast<const float4*>(t + (fg + 64) * kPairTok);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[s]);
+          if (++s == a.slots) s = 0, ph ^= 1u;
+        }
+      }
+      float2 s01 = make_float2(0.0f, 0.0f), s23 = make_float2(0.0f, 0.0f);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const float2 a01 = make_float2(v[i].x, v[i].y), a23 = make_float2(v[i].z, v[i].w);
+        s01 = __fadd2_rn(s01, __fmul2_rn(a01, a01));
+        s23 = __fadd2_rn(s23, __fmul2_rn(a23, a23));
+      }
+#pragma unroll
+      for (int m = 8; m < 32; m <<= 1) {
+        s01.x = __fadd_rn(s01.x, __shfl_xor_sync(0xffffffffu, s01.x, m));
+        s01.y = __fadd_rn(s01.y, __shfl_xor_sync(0xffffffffu, s01.y, m));
+        s23.x = __fadd_rn(s23.x, __shfl_xor_sync(0xffffffffu, s23.x, m));
+        s23.y = __fadd_rn(s23.y, __shfl_xor_sync(0xffffffffu, s23.y, m));
+      }
+      if (lane < 8)
+        *reinterpret_cast<float4*>(red + warp * kPairTok + 4 * lane) =
+            make_float4(s01.x, s01.y, s23.x, s23.y);
+      if (consumers_sync_or(1, bad)) {  // a copy never landed: leave (counted once)
+        if (tid == 0) atomicAdd(&g_wait_timeouts, 1u);
+        break;
+      }
+      // this CTA's partial for token tid, to the other CTA's slot k & 1
+      float own = 0.0f;
+      const uint32_t xs = k & 1u;
+      if (tid < kPairTok) {
+#pragma unroll
+        for (int w = 0; w < kRingWarps; ++w) own = __fadd_rn(own, red[w * kPairTok + tid]);
+        if (tid == 0) mbar_arrive_expect_tx(&xbar[xs], kPairTok * 4);
+        st_async_b32(xch_peer + (xs * kPairTok + tid) * 4, own, xbar_peer + xs * 8);
+      }
+      // each reader observes the exchange mbarrier itself (the peer's async
+      // stores are visible to the threads that see the phase complete)
+      bool late = false;
+      if (tid < kPairTok) late = !mbar_wait_bounded(&xbar[xs], (k >> 1) & 1u, kWaitCycles);
+      if (consumers_sync_or(3, late)) {  // the other CTA's partials never came
+        if (tid == 0) atomicAdd(&g_wait_timeouts, 1u);
+        break;
+      }
+      if (tid < kPairTok) {
+        const float other = xch[xs * kPairTok + tid];
+        const float tot = rank == 0 ? __fadd_rn(own, other) : __fadd_rn(other, own);
+        scale_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, a.inv_width), a.eps)));
+      }
+      consumers_sync(2);
+      const uint32_t tok = (unit + k * units) * kPairTok + 4 * q;
+      if (tok < a.rows) {  // rows % 4 == 0: the whole quad is in range
+        const float4 sc = *reinterpret_cast<const float4*>(scale_s + 4 * q);
+        float* yq = a.y + tok;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const uint32_t lf = (uint32_t(i) >> 1) * kPairBox + fg + 64 * (uint32_t(i) & 1);
+          if (uint32_t(i >> 1) < a.nbox && lf < nf) {
+            float4 o;
+            o.x = __fmul_rn(__fmul_rn(v[i].x, sc.x), wr[i]);
+            o.y = __fmul_rn(__fmul_rn(v[i].y, sc.y), wr[i]);
+            o.z = __fmul_rn(__fmul_rn(v[i].z, sc.z), wr[i]);
+            o.w = __fmul_rn(__fmul_rn(v[i].w, sc.w), wr[i]);
+            *reinterpret_cast<float4*>(yq + size_t(f_begin + lf) * a.rows) = o;
+          }
+        }
+      }
+    }
+  }
+  // neither CTA leaves while the other may still store into its shared memory
+  cluster.sync();
+}
+
 }  // namespace
 
 // Ring RMSNorm; 1 when the shape or alignment is not covered (nothing
@@ -566,6 +781,48 @@ int rms_ring(const char* op, const float* x, const float* w, float* y, uint32_t 
   const size_t smem = ring_smem_bytes(a.box1, a.nbox, a.slots);
   if (a.nbox <= 4) return launch_ring<4>(op, map, a, smem, dev, stream);
   return launch_ring<8>(op, map, a, smem, dev, stream);
+}
+
+// Pair RMSNorm (32-token tiles shared by a CTA pair); 1 when the shape or
+// alignment is not covered (nothing launched), else a status. Covers rows %
+// 4 == 0, 16-byte aligned x and y, rows < 2^31 and 512 < width <= 1024.
+int rms_pair(const char* op, const float* x, const float* w, float* y, uint32_t rows,
+             uint32_t width, int centered, float eps, float inv_width, cudaStream_t stream) {
+  if (rows % 4 != 0 || rows >= (1u << 31) || !aligned(x, 16) || !aligned(y, 16)) return 1;
+  if (width <= 512 || width > 2 * kPairMaxBoxes * kPairBox) return 1;
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  PairArgs a;
+  a.wc = (width + 1) / 2;
+  a.nbox = (a.wc + kPairBox - 1) / kPairBox;
+  a.slots = kRingMaxSlots;
+  while (a.slots > 2 && pair_smem_bytes(a.slots) > size_t(dev.smem_optin)) --a.slots;
+  if (pair_smem_bytes(a.slots) > size_t(dev.smem_optin) || dev.sms < 2) return 1;
+  CUtensorMap map;
+  std::string why;
+  if (!encode_map_2d_f32(&map, x, rows, width, rows, kPairTok, kPairBox, &why))
+    return fail(TFX_ERR_CUDA, op, "tensor map", why);
+  a.w = w;
+  a.y = y;
+  a.rows = rows;
+  a.width = width;
+  a.tiles = (rows + kPairTok - 1) / kPairTok;
+  a.eps = eps;
+  a.inv_width = inv_width;
+  a.centered = centered;
+  const size_t smem = pair_smem_bytes(a.slots);
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  const int di = dev.device & 63;
+  std::call_once(once[di], [&] {
+    err[di] = cudaFuncSetAttribute(rms_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   dev.smem_optin);
+  });
+  if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
+  const uint32_t units = std::min<uint32_t>(a.tiles, uint32_t(dev.sms) / 2);
+  return launch_kernel(op, rms_pair_kernel, dim3(2 * units), dim3(kRingThreads), smem, stream, 2,
+                       map, a);
 }
 
 // Streaming RMSNorm; 1 when the shape or alignment is not covered (nothing

@@ -503,6 +503,76 @@ int tfx_session_bias_act_ff_f32(tfx_session* s, const float* x, const float* bia
   });
 }
 
+}  // extern "C"
+
+// ---- GEMM with a fused epilogue: weight and bias uploaded once, token chunks ------
+//
+// x chunks (in_dim x n) in, y chunks (nout x n) out; chunks are whole
+// 128-token tiles of the tensor-core kernel where the call allows.
+template <class Launch>
+static int session_gemm(tfx_session* s, const char* op, const float* x, const float* weight,
+                        const float* bias, float* y, int64_t in_dim, int64_t nproj,
+                        int64_t nout, int64_t length, Launch launch) {
+  TFX_REQUIRE(in_dim >= 0 && nproj >= 0 && nout >= 0 && length >= 0, op, "shape",
+              "extents must be non-negative");
+  if (nout == 0 || length == 0) return TFX_OK;
+  TFX_REQUIRE(x || in_dim == 0, op, "x", "null pointer");
+  TFX_REQUIRE(weight || in_dim == 0, op, "weight", "null pointer");
+  TFX_REQUIRE(y, op, "y", "null pointer");
+  std::vector<const void*> dev;
+  int rc = upload_params(s, op, {{weight, size_t(in_dim) * size_t(nproj) * 4},
+                                 {bias, bias ? size_t(nproj) * 4 : 0}},
+                         &dev);
+  if (rc != TFX_OK) return rc;
+  const int64_t per = units_per_chunk(s, (in_dim + nout) * 4, 128);
+  rc = ensure_slots(s, size_t(per * (in_dim + nout)) * 4, op);
+  if (rc != TFX_OK) return rc;
+  const float* wd = static_cast<const float*>(dev[0]);
+  const float* bd = static_cast<const float*>(dev[1]);
+  return pipeline(
+      s, op, length, per,
+      [&](int64_t t0, int64_t n, cudaStream_t st, char* slot) {
+        float* in = reinterpret_cast<float*>(slot);
+        float* out = in + per * in_dim;
+        int r = in_dim ? h2d(op, in, x + t0 * in_dim, size_t(n * in_dim) * 4, st) : TFX_OK;
+        if (r == TFX_OK) r = launch(in, wd, bd, out, n, st);
+        if (r == TFX_OK) r = d2h(op, y + t0 * nout, out, size_t(n * nout) * 4, st);
+        return r;
+      },
+      128);
+}
+
+extern "C" {
+
+int tfx_session_gemm_geglu_ff_f32(tfx_session* s, const float* x, const float* weight,
+                                  const float* bias, float* y, int64_t in_dim,
+                                  int64_t intermediate, int64_t length) {
+  const char* op = "tenferro-ext::gemm_geglu";
+  TFX_SESSION_ENTER(op);
+  TFX_REQUIRE(intermediate < (int64_t(1) << 29), op, "intermediate",
+              "projected feature extent overflow");
+  return session_gemm(s, op, x, weight, bias, y, in_dim, 2 * intermediate, intermediate, length,
+                      [&](const float* xi, const float* w, const float* b, float* yo, int64_t n,
+                          cudaStream_t st) {
+                        return tfx_gemm_geglu_ff_f32(xi, w, b, yo, in_dim, intermediate, n, st);
+                      });
+}
+
+int tfx_session_gemm_bias_act_ff_f32(tfx_session* s, const float* x, const float* weight,
+                                     const float* bias, float* y, int64_t in_dim, int64_t out_dim,
+                                     int64_t length, int act) {
+  const char* op = "tenferro-ext::gemm_bias";
+  TFX_SESSION_ENTER(op);
+  TFX_REQUIRE(act == TFX_ACT_IDENTITY || act == TFX_ACT_GELU_ERF || act == TFX_ACT_RELU, op,
+              "act", "unknown activation " + std::to_string(act));
+  return session_gemm(s, op, x, weight, bias, y, in_dim, out_dim, out_dim, length,
+                      [&](const float* xi, const float* w, const float* b, float* yo, int64_t n,
+                          cudaStream_t st) {
+                        return tfx_gemm_bias_act_ff_f32(xi, w, b, yo, in_dim, out_dim, n, act,
+                                                        st);
+                      });
+}
+
 // ---- masked softmax: chunks of whole rows; mask tensors uploaded once ------------
 
 static int64_t extent(int64_t n0, int64_t s0, int64_t n1, int64_t s1, int64_t n2, int64_t s2) {

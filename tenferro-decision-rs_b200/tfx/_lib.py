@@ -122,6 +122,8 @@ SIGNATURES = {
     "tfx_session_gated_silu_f32": (_int, [_p, _p, _p, _p, _i64]),
     "tfx_session_bias_act_ff_f32": (_int, [_p, _p, _p, _p, _i64, _i64, _int]),
     "tfx_session_add_f32": (_int, [_p, _p, _p, _p, _i64]),
+    "tfx_session_gemm_geglu_ff_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64]),
+    "tfx_session_gemm_bias_act_ff_f32": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _int]),
     "tfx_session_add_layernorm_ff_f32": (_int, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64,
                                                 ctypes.c_float]),
     "tfx_session_masked_softmax_f32": (_int, [_p, _p, _p, ctypes.POINTER(SoftmaxDesc)]),

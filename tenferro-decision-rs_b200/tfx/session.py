@@ -120,6 +120,25 @@ class Session:
                                               _numel(x) // features, act))
         return y
 
+    def gemm_geglu(self, x, weight, bias, intermediate, out=None):
+        """GemmGegluOp on host buffers: x (in_dim, length), weight (in_dim,
+        2*intermediate) column-major, bias (2*intermediate) or None."""
+        in_dim = _numel(weight) // (2 * intermediate) if intermediate else 0
+        length = _numel(x) // in_dim if in_dim else 0
+        y = _empty_like(x, intermediate * length) if out is None else out
+        check(lib.tfx_session_gemm_geglu_ff_f32(self._h, _hptr(x), _hptr(weight), _hptr(bias),
+                                                _hptr(y), in_dim, intermediate, length))
+        return y
+
+    def gemm_bias_act(self, x, weight, bias, out_dim, act=TFX_ACT_IDENTITY, out=None):
+        """GemmBiasOp (+ activation) on host buffers: weight (in_dim, out_dim)."""
+        in_dim = _numel(weight) // out_dim if out_dim else 0
+        length = _numel(x) // in_dim if in_dim else 0
+        y = _empty_like(x, out_dim * length) if out is None else out
+        check(lib.tfx_session_gemm_bias_act_ff_f32(self._h, _hptr(x), _hptr(weight), _hptr(bias),
+                                                   _hptr(y), in_dim, out_dim, length, act))
+        return y
+
     def add(self, a, b, out=None):
         y = _empty_like(a) if out is None else out
         check(lib.tfx_session_add_f32(self._h, _hptr(a), _hptr(b), _hptr(y), _numel(a)))

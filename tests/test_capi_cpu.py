@@ -179,7 +179,8 @@ _NO_CUDA_BEFORE_VALIDATION = [
     "tfx_gemm_geglu_ff_f32", "tfx_gemm_bias_act_ff_f32", "tfx_wait_timeouts", "tfx_session_set_chunk_bytes", "tfx_session_layernorm_ff_f32",
     "tfx_session_layernorm_ff_f64", "tfx_session_rmsnorm_last_f32", "tfx_session_erf_f32",
     "tfx_session_gelu_erf_f32", "tfx_session_geglu_ff_f32", "tfx_session_gated_silu_f32",
-    "tfx_session_bias_act_ff_f32", "tfx_session_add_f32", "tfx_session_add_layernorm_ff_f32",
+    "tfx_session_bias_act_ff_f32", "tfx_session_add_f32", "tfx_session_gemm_geglu_ff_f32",
+    "tfx_session_gemm_bias_act_ff_f32", "tfx_session_add_layernorm_ff_f32",
     "tfx_session_masked_softmax_f32", "tfx_session_rope_pairhalf_f32",
 ]
 

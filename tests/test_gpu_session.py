@@ -160,3 +160,26 @@ def test_session_add_layernorm_matches_the_two_ops(orc, sess):
     assert_bitwise(y_got, y_want, "session add+ln y")
     _, y_only = sess.add_layer_norm_feature_first(a, b, w, None, 1e-5)
     assert_bitwise(y_only, y_want, "session add+ln without sum")
+
+
+def test_session_gemm_geglu_and_bias_act_chunked(orc, sess):
+    """The fused GEMM epilogues on host buffers: 1 MiB chunks cut the 3000
+    tokens into whole 128-token tiles, so the result is bitwise the device
+    call's (each token depends on its own column of x only) and within the f32
+    bar of the oracle's projection + epilogue."""
+    from tfx import ops
+    in_dim, inter, length = 768, 1152, 3000
+    x = splitmix_normal(in_dim * length, 0x7E4F0860)
+    w = splitmix_normal(in_dim * 2 * inter, 0x7E4F0861, std=in_dim ** -0.5)
+    b = splitmix_normal(2 * inter, 0x7E4F0862, std=0.02)
+    y = sess.gemm_geglu(x, w, b, inter)
+    dev = ops.gemm_geglu(torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda(),
+                         torch.from_numpy(b).cuda(), inter).cpu().numpy().reshape(-1)
+    assert_bitwise(y, dev, "session gemm_geglu vs device call")
+    assert_close(y, orc.gemm_geglu_f32(x, w, b, in_dim, inter, length), F32_RTOL, F32_ATOL_REL,
+                 "session gemm_geglu")
+    out_dim = 300
+    w2 = splitmix_normal(in_dim * out_dim, 0x7E4F0863, std=in_dim ** -0.5)
+    y2 = sess.gemm_bias_act(x, w2, None, out_dim, act=2)
+    assert_close(y2, orc.gemm_bias_act_f32(x, w2, None, in_dim, out_dim, length, 2), F32_RTOL,
+                 F32_ATOL_REL, "session gemm_bias_act relu")

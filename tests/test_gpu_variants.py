@@ -32,7 +32,8 @@ print("variant ok")
 """
 
 
-@pytest.mark.parametrize("variant", ["cluster", "cluster16", "tile", "split", "stream", "ring"])
+@pytest.mark.parametrize("variant", ["cluster", "cluster16", "tile", "split", "stream", "ring",
+                                     "pair"])
 def test_rms_variant(variant):
     code = SCRIPT.format(root=ROOT, pkg=os.path.join(ROOT, "tenferro-decision-rs_b200"),
                          tests=os.path.join(ROOT, "tests"))
