@@ -885,14 +885,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
       for (int jj = 0; jj < 16; ++jj) {
         const uint32_t col = col0 + jj;
         float sc = __fmul_rn(sv[jj], a.scale);
+        // bias and active are read only for keys of the row's interval, which
+        // lie inside the tensors (a block can reach past the sequence)
+        const bool in_range = col - c_lo < c_span;
         if constexpr (BIAS)
-          sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kb0 + col) + uint64_t(L) * b)]);
+          if (in_range)
+            sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kb0 + col) + uint64_t(L) * b)]);
         if (!row_full) {
-          bool kept = col - c_lo < c_span;
+          bool kept = in_range;
           if (KEEP && !keep_full) kept = kept && keep_s[col * kTQ + row] != 0;
           sc = kept ? sc : -INFINITY;
         }
-        if constexpr (ACTIVE) sc = a.active[uint64_t(b) * L + kb0 + col] != 0.0f ? sc : -INFINITY;
+        if constexpr (ACTIVE)
+          sc = in_range && a.active[uint64_t(b) * L + kb0 + col] != 0.0f ? sc : -INFINITY;
         if constexpr (BIAS) sc = sc == sc ? sc : -INFINITY;  // a NaN bias: nothing
         inf_here |= sc == INFINITY;
         sv[jj] = sc;
@@ -1036,6 +1041,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
   if (warp == 0) tmem_free(tm, 512);
 }
 
+#include "attn_ws.cuh"
+
 // flags[bh] = 1 when q, k or v of head bh holds a non-finite value (or a
 // value beyond the largest tf32, which the split cannot represent): the
 // tensor-core kernel leaves such heads to the f32 kernel, whose arithmetic
@@ -1075,15 +1082,21 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
     return 1;
   const size_t smem = 8 * kRegion + 8 * kVtRegion + kTK * kTQ + 1024;
   if (smem > size_t(dev.smem_optin)) return 1;
-  static const bool disabled = [] {
+  // TFX_ATTN_KERNEL: f32 = the f32-pipe kernel only, tc1 = the single-loop
+  // tensor-core kernel, anything else = the warp-specialised one
+  static const int choice = [] {
     const char* e = getenv("TFX_ATTN_KERNEL");
-    return e && std::string(e) == "f32";
+    if (e && std::string(e) == "f32") return 0;
+    if (e && std::string(e) == "tc1") return 1;
+    return 2;
   }();
-  if (disabled) return 1;
-  CUtensorMap qmap, kmap;
+  if (choice == 0) return 1;
+  const bool ws = choice == 2 && kWsSmem <= size_t(dev.smem_optin);
+  CUtensorMap qmap, kmap, vmap;
   std::string why;
   if (!encode_map_2d_f32(&qmap, a.q, 64, rows, 64, 32, kTQ, &why, 128) ||
-      !encode_map_2d_f32(&kmap, a.k, 64, rows, 64, 32, kTK, &why, 128))
+      !encode_map_2d_f32(&kmap, a.k, 64, rows, 64, 32, ws ? kWsKB : kTK, &why, 128) ||
+      (ws && !encode_map_2d_f32(&vmap, a.v, 64, rows, 64, 32, kWsKB, &why, 128)))
     return fail(TFX_ERR_CUDA, op, "tensor map", why);
   const uint32_t nbh = batch * a.heads;
   uint8_t* flags = nullptr;
@@ -1110,8 +1123,25 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
       if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
       return launch_kernel(op, kernel, grid, dim3(kTcThreads), smem, stream, 1, qmap, kmap, a);
     };
+    auto run_ws = [&](auto kernel) -> int {
+      const cudaError_t e2 = cudaFuncSetAttribute(
+          kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
+      if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
+      return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1, qmap, kmap,
+                           vmap, a);
+    };
     const int sel = (a.keep ? 4 : 0) | (a.bias ? 2 : 0) | (a.active ? 1 : 0);
-    switch (sel) {
+    if (ws) switch (sel) {
+      case 0: rc = run_ws(attn_ws_kernel<false, false, false>); break;
+      case 1: rc = run_ws(attn_ws_kernel<false, false, true>); break;
+      case 2: rc = run_ws(attn_ws_kernel<false, true, false>); break;
+      case 3: rc = run_ws(attn_ws_kernel<false, true, true>); break;
+      case 4: rc = run_ws(attn_ws_kernel<true, false, false>); break;
+      case 5: rc = run_ws(attn_ws_kernel<true, false, true>); break;
+      case 6: rc = run_ws(attn_ws_kernel<true, true, false>); break;
+      default: rc = run_ws(attn_ws_kernel<true, true, true>); break;
+    }
+    else switch (sel) {
       case 0: rc = run(attn_tc_kernel<false, false, false>); break;
       case 1: rc = run(attn_tc_kernel<false, false, true>); break;
       case 2: rc = run(attn_tc_kernel<false, true, false>); break;

@@ -61,11 +61,35 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
          (uint64_t(1) << 46) | (uint64_t(4) << 61);
 }
 
+// Descriptor of an MN-major tf32 operand in the "128-byte swizzle, 32-byte
+// atoms" layout, the only MN-major layout the tf32 MMA reads: 128-byte rows
+// hold 32 consecutive values of N (M) for one K index, rows follow each other
+// (128 bytes apart), and the four 32-byte granules of row r sit at granule
+// index g ^ (r % 4) (address bits [5,7) XOR bits [7,9)). Groups of 4 rows are
+// 512 bytes apart (stride byte offset); the next 32 values of N start
+// `mn_stride` bytes further on (leading byte offset); layout type
+// SWIZZLE_128B_BASE32B = 1 [61,64). A K step of 8 moves the start by 1024
+// bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128b32_mn(uint32_t addr, uint32_t mn_stride) {
+  return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t((mn_stride >> 4) & 0x3FFF) << 16) |
+         (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(1) << 61);
+}
+
+// Byte offset of 16-byte chunk c (< 8) of row r in that layout.
+__device__ __forceinline__ uint32_t sw128b32_chunk(uint32_t r, uint32_t c) {
+  return r * 128 + ((((c >> 1) ^ (r & 3)) << 5) | ((c & 1) << 4));
+}
+
 // Instruction descriptor of tcgen05.mma.kind::tf32, f32 accumulate, both
 // operands K-major: c_format F32 [4,6), a/b_format TF32 [7,10) [10,13),
 // N >> 3 [17,23), M >> 4 [24,29).
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4) | (2u << 7) | (2u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+// The same with B MN-major (transpose-B bit 16).
+__host__ __device__ constexpr uint32_t idesc_tf32_bmn(int m, int n) {
+  return idesc_tf32(m, n) | (1u << 16);
 }
 
 // D (+)= A * B^T with A and B in shared memory.

@@ -203,6 +203,53 @@ def test_attention_core_bias_active_causal(hd):
     assert_close(got.ravel(), want.ravel(), 2e-5, F32_ATOL_REL, f"attention core hd={hd}")
 
 
+@pytest.mark.parametrize("L,causal,B", [(512, 0, 2), (333, 1, 1), (4160, 0, 1)])
+def test_attention_core_growing_scores(L, causal, B):
+    """Scores that grow along the keys (an additive bias rising by 40 over
+    the sequence, added exactly after the product) move each row's running
+    max again and again: the tensor-core kernels' rescale path. 4160 keys
+    pass the 64 blocks that the per-block keep bits cover and accumulate 65
+    blocks of P V; an active mask with holes makes every block a masked one.
+    (A steeper rise would push the scores to where one f32 rounding of the
+    score alone exceeds the tolerance, in any f32 implementation.)"""
+    H, hd = 2, 64
+    n = B * H * L * hd
+    qh, kh, vh = (splitmix_normal(n, 0x7E4F0B40 + i + L) for i in range(3))
+    ramp = (np.arange(L, dtype=np.float32) * np.float32(40.0 / L))[None, :, None]
+    bias = (np.broadcast_to(ramp, (B, L, L))
+            + splitmix_normal(B * L * L, 0x7E4F0B47 + L, std=0.5).reshape(B, L, L))
+    bias = np.ascontiguousarray(bias, np.float32).ravel()  # [b][k][q]
+    active = (splitmix_uniform(B * L, 0x7E4F0B44 + L, 0.0, 1.0) > 0.05).astype(np.float32)
+    active[0] = 1.0
+    d = _lib.AttentionDesc()
+    _lib.lib.tfx_attention_desc_init(ctypes.byref(d), B, H, L, hd)
+    ad, bd = dev(active), dev(bias)
+    d.active, d.bias, d.causal = ad.data_ptr(), bd.data_ptr(), causal
+    out = empty(n)
+    ins = [dev(t) for t in (qh, kh, vh)]
+    call("tfx_attention_f32", *[P(t) for t in ins], P(out), ctypes.byref(d), S())
+    got = host(out).reshape(B, L, H, hd)
+    want = attention_f64(qh, kh, vh, B, H, L, hd, 1.0 / np.sqrt(np.float32(hd)), bias,
+                         bool(causal), active)
+    want = want.transpose(0, 2, 1, 3).astype(np.float32)
+    assert_close(got.ravel(), want.ravel(), 2e-5, F32_ATOL_REL, f"growing scores L={L}")
+
+
+@pytest.mark.parametrize("window", [128, -1])
+def test_laya_attention_block_bert_shape(orc, window):
+    """The ModernBERT layer shape (head_dim 64) at 512 tokens, sliding window
+    128 and global with padded keys, against the oracle."""
+    hd, heads, L, B = 64, 2, 512, 2
+    d = hd * heads
+    qkv = splitmix_normal(3 * d * L * B, 0x7E4F0B50 + L + window)
+    valid = [L - 37, L - 64]
+    keep = keep_window(L, B, window if window >= 0 else L, valid)
+    tables = orc.rope_tables_powf_f32(160000.0 if window < 0 else 10000.0, L, hd)
+    got = gpu_laya_block(qkv, keep, d, heads, L, B, tables)
+    want = orc.laya_attention_block_f32(qkv, keep, d, heads, L, B, *tables)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"laya bert shape window={window}")
+
+
 def test_attention_rejects_bad_arguments():
     d = _lib.AttentionDesc()
     _lib.lib.tfx_attention_desc_init(ctypes.byref(d), 1, 1, 8, 8)

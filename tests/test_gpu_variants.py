@@ -106,3 +106,14 @@ def test_layernorm_ring_gives_the_one_wave_kernels_bits():
         assert res.returncode == 0, res.stdout + res.stderr
         digests.append([ln for ln in res.stdout.splitlines() if ln.startswith("digest")][-1])
     assert digests[0] == digests[1]
+
+
+@pytest.mark.parametrize("variant", ["tc1", "f32"])
+def test_attention_variant(variant):
+    """The attention tests again with the single-loop tensor-core kernel and
+    with the f32-pipe kernel (TFX_ATTN_KERNEL is read once per process)."""
+    env = dict(os.environ, TFX_ATTN_KERNEL=variant)
+    res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p",
+                          "no:cacheprovider", os.path.join(ROOT, "tests", "test_gpu_attention.py")],
+                         env=env, capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
