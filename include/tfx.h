@@ -12,8 +12,10 @@
  *   - Layouts are the reference's column-major ones (first axis fastest).
  *     A feature-first activation (d, cols) stores column c at [c*d, (c+1)*d).
  *   - Inputs are borrowed, outputs are caller-owned. Calls that need scratch
- *     (named at each) allocate it stream-ordered on the call's stream and
- *     release it there; every other call allocates nothing.
+ *     (named at each) allocate it stream-ordered on the call's stream, from a
+ *     per-device memory pool that libtfx owns (it keeps up to 1 GiB of freed
+ *     scratch mapped between calls; the caller's default pool is not
+ *     touched), and release it there; every other call allocates nothing.
  *   - Every call is asynchronous on the given stream (NULL = legacy default
  *     stream) and takes device pointers, except the tfx_session_* calls,
  *     which take host pointers and return when the host outputs are written.

@@ -551,610 +551,83 @@ __global__ void __launch_bounds__(128) attn_row_kernel(AttnArgs a) {
 
 
 // ---- tensor-core attention (head_dim 64) ---------------------------------------------
-//
-// CTA = 128 queries of one head, 4 warps; thread t owns query q0 + t (TMEM
-// lane t). Per 128-key block:
-//   1. the TMA unit loads the K block (two 32-value boxes, 128-byte swizzle)
-//      while the threads stage V transposed (row = channel, K = key) -- both
-//      K-major operands -- and every operand is split x = hi + lo with hi the
-//      tf32 rounding of x (3xTF32: hi*hi + hi*lo + lo*hi keeps f32-level
-//      accuracy; the dropped lo*lo term is ~2^-22 relative);
-//   2. one thread issues S = Q K^T as 3 x 8 tcgen05.mma (M 128, N 128, K 8)
-//      into TMEM;
-//   3. each thread reads its score row from TMEM, masks and scales it, and
-//      runs the online softmax; P (split hi / lo) goes back to TMEM, where it
-//      is the A operand of
-//   4. O += P V^T^T: 3 x 16 tcgen05.mma (M 128, N 64, K 8), O in TMEM,
-//      rescaled in place when the running max of a row grows.
-// At the end O / l is written. TMEM: S 128 + O 64 + P hi 128 + P lo 128
-// columns (512 allocated: one CTA per SM, its shared memory is 193 KB).
-// Every wait is bounded; a CTA that gives up counts it and leaves after its
-// tensor-memory work has drained (bounded again).
 
-constexpr int kTQ = 128;              // queries per CTA
-constexpr int kTK = 128;              // keys per block
-constexpr uint32_t kRegion = 16384;   // 128 rows x 128 bytes
-constexpr uint32_t kVtRegion = 8192;  // 64 channel rows x 128 bytes (32 keys)
-constexpr long long kTcWait = 1LL << 31;
+constexpr int kTQ = 128;                  // queries per CTA of the tensor-core kernel
+constexpr long long kTcWait = 1LL << 31;  // bound of every wait (SM cycles)
 
 __device__ uint32_t g_tc_wait_timeouts;
 
-// Four 16-byte chunks of a 128 x 64 operand tile (thread t: row t % 128,
-// logical chunks 4 (t / 128) .. +3, i.e. values 16 (t / 128) .. +15) split
-// into hi (in place) and lo. Eight consecutive lanes read eight consecutive
-// rows of the same logical chunk, which the swizzle spreads over eight
-// different 16-byte bank groups: no bank conflicts.
-__device__ __forceinline__ void split_tile(uint8_t* hi, uint8_t* lo, uint32_t tid) {
-  const uint32_t row = tid & 127, k0 = (tid >> 7) * 16;
-  const uint32_t region = (k0 >> 5) * kRegion;
-#pragma unroll
-  for (uint32_t c = 0; c < 4; ++c) {
-    const uint32_t off = region + sw128_offset(row, (k0 & 31) + 4 * c);
-    float4 x = *reinterpret_cast<float4*>(hi + off);
-    float4 h = make_float4(tf32_round_finite(x.x), tf32_round_finite(x.y),
-                           tf32_round_finite(x.z), tf32_round_finite(x.w));
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y),
-                                                       __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
-  }
-}
-
-// Keep-mask scan of keep_narrow, plus one bit per 128-key block: set when
-// every (query, key) of the block is kept by the keep tensor. Eight threads
-// read one key's 128 query bytes as 16-byte words (keep[q + L*(k + L*b)]:
-// the queries of a key are contiguous), so a warp reads four rows whole.
-__device__ void keep_narrow_blocks(const AttnArgs& a, uint32_t b, uint32_t q0, uint32_t nq,
-                                   int64_t* lo, int64_t* hi, int* red, unsigned long long* full) {
-  if (threadIdx.x == 0) {
-    red[0] = int(*hi);
-    red[1] = int(*lo) - 1;
-    *full = ~0ull;
-  }
-  __syncthreads();
-  const uint64_t L = a.length;
-  const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0;
-  const uint32_t c = threadIdx.x & 7;        // 16-query chunk of the row
-  const uint32_t i0 = c * 16, i1 = min(nq, i0 + 16);
-  const uint32_t per = blockDim.x >> 3;      // keys per pass
-  for (int64_t kbase = *lo; kbase < *hi; kbase += per) {
-    const int64_t kj = kbase + (threadIdx.x >> 3);
-    bool any = false, all = true;
-    if (kj < *hi && i0 < i1) {
-      const uint8_t* row = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
-      if (vec && i1 - i0 == 16) {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(row + i0));
-        any = (w.x | w.y | w.z | w.w) != 0;
-        auto zero_byte = [](uint32_t v) { return ((v - 0x01010101u) & ~v & 0x80808080u) != 0; };
-        all = !(zero_byte(w.x) || zero_byte(w.y) || zero_byte(w.z) || zero_byte(w.w));
-      } else {
-        for (uint32_t i = i0; i < i1; ++i) {
-          const bool k = row[i] != 0;
-          any |= k;
-          all &= k;
-        }
-      }
-    }
-#pragma unroll
-    for (int d = 1; d < 8; d <<= 1) {
-      any = __shfl_xor_sync(0xffffffffu, int(any), d) != 0 || any;
-      all = __shfl_xor_sync(0xffffffffu, int(all), d) != 0 && all;
-    }
-    if (c == 0 && kj < *hi) {
-      if (any) {
-        atomicMin(&red[0], int(kj));
-        atomicMax(&red[1], int(kj));
-      }
-      if (!all && kj / 128 < 64) atomicAnd(full, ~(1ull << (kj / 128)));
-    }
-  }
-  __syncthreads();
-  const int first = red[0], last = red[1];
-  __syncthreads();
-  if (first > last) {
-    *hi = *lo;
-  } else {
-    *lo = first;
-    *hi = int64_t(last) + 1;
-  }
-}
-
-constexpr int kTcThreads = 512;  // 16 warps: 4 column groups x 4 lane quarters
-
-// One thread polls the mbarrier (bounded); the others wait in the CTA
-// barrier, which costs no issue slots. Returns true when the wait gave up.
-// The barrier orders the completed copy / MMA before every thread's later
-// accesses (a tcgen05.fence::after_thread_sync follows where TMEM is read).
-__device__ __forceinline__ bool cta_wait(uint64_t* bar, uint32_t parity) {
-  bool ok = true;
-  if (threadIdx.x == 0) ok = mbar_wait_bounded(bar, parity, kTcWait);
-  return __syncthreads_or(!ok);
-}
-
-// KEEP / BIAS / ACTIVE: the keep tensor, the additive bias and the active key
-// mask are given (one instance per combination keeps registers for the others).
-template <bool KEEP, bool BIAS, bool ACTIVE>
-__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    AttnArgs a) {
-  extern __shared__ __align__(1024) uint8_t tc_smem[];
-  __shared__ uint64_t bar_q, bar_k, bar_s, bar_o;
-  __shared__ uint32_t tmem_base;
-  __shared__ int red[2];
-  __shared__ unsigned long long keep_full;
-  __shared__ float red_max[4][kTQ], red_sum[4][kTQ];
-  __shared__ int inf_s[kTQ];  // a kept score of the row was +inf (any column group)
-  pdl_enter();
-  const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t g = warp >> 2;                 // column group
-  const uint32_t row = (warp & 3) * 32 + lane;  // TMEM lane = query row of the tile
-  const uint32_t q0 = blockIdx.x * kTQ, head = blockIdx.y, b = blockIdx.z;
-  const uint32_t bh = b * a.heads + head;
-  if (routed_away(a, bh)) return;
-  const uint32_t L = a.length;
-  const uint32_t nq = min(uint32_t(kTQ), L - q0);
-  const uint64_t row0 = uint64_t(bh) * L;
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem) + 1023) &
-                                             ~uintptr_t(1023));
-  uint8_t* qhi = base;
-  uint8_t* qlo = base + 2 * kRegion;
-  uint8_t* khi = base + 4 * kRegion;
-  uint8_t* klo = base + 6 * kRegion;
-  uint8_t* vthi = base + 8 * kRegion;
-  uint8_t* vtlo = vthi + 4 * kVtRegion;
-  uint8_t* keep_s = vtlo + 4 * kVtRegion;  // [128 keys][128 queries] of a partial block
-
-  int64_t lo, hi;
-  analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
-  unsigned long long full_bits = 0;
-  if (KEEP && lo < hi) {
-    keep_narrow_blocks(a, b, q0, nq, &lo, &hi, red, &keep_full);
-    full_bits = keep_full;
-  }
-
-  if (tid == 0) {
-    mbar_init(&bar_q, 1);
-    mbar_init(&bar_k, 1);
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_o, 1);
-    mbar_init_fence();
-  }
-  if (tid < kTQ) inf_s[tid] = 0;
-  if (warp == 0) tmem_alloc(&tmem_base, 512);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tm = tmem_base;
-  const uint32_t lane_off = (warp & 3) * 32 << 16;
-  // TMEM: two S buffers (the P hi of a block is written over its own S), O,
-  // P lo. The S MMA of block j+1 runs while the softmax of block j does, and
-  // the PV MMA of block j while the first pass of block j+1 does.
-  const uint32_t tS0 = tm, tO = tm + 256, tPl = tm + 384;
-  const int64_t kb_first = lo / kTK * kTK;
-  const uint32_t nblk = kb_first < hi ? uint32_t((hi - kb_first + kTK - 1) / kTK) : 0;
-
-  // issued / waited phases of bar_k, bar_s, bar_o (at most one outstanding
-  // each); after a give-up the outstanding ones are waited for again
-  uint32_t k_iss = 0, k_wt = 0, s_iss = 0, s_wt = 0, o_iss = 0, o_wt = 0;
-  auto issue_k = [&](int64_t kb) {
-    if (tid == 0) {
-      fence_proxy_async_smem();
-      mbar_arrive_expect_tx(&bar_k, 2 * kRegion);
-      tma_load_2d(khi, &kmap, &bar_k, 0, int(row0 + kb));
-      tma_load_2d(khi + kRegion, &kmap, &bar_k, 32, int(row0 + kb));
-    }
-    ++k_iss;
-  };
-  const uint32_t id_s = idesc_tf32(128, 128), id_o = idesc_tf32(128, 64);
-  // wait for K(j), split it, issue S(j) into buffer j & 1
-  auto issue_s = [&](uint32_t j) -> bool {
-    if (cta_wait(&bar_k, k_wt & 1)) return false;
-    ++k_wt;
-    split_tile(khi, klo, tid);
-    fence_proxy_async_smem();  // generic writes read by the MMA (async proxy)
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t dst = tS0 + (j & 1) * 128;
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t off = (ks >> 2) * kRegion + (ks & 3) * 32;
-        const uint64_t ah = smem_desc_sw128(smem_addr(qhi + off));
-        const uint64_t al = smem_desc_sw128(smem_addr(qlo + off));
-        const uint64_t bhd = smem_desc_sw128(smem_addr(khi + off));
-        const uint64_t bl = smem_desc_sw128(smem_addr(klo + off));
-        mma_tf32_ss(dst, ah, bhd, id_s, ks > 0);
-        mma_tf32_ss(dst, ah, bl, id_s, 1);
-        mma_tf32_ss(dst, al, bhd, id_s, 1);
-      }
-      mma_commit(&bar_s);
-    }
-    ++s_iss;
-    return true;
-  };
-
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bar_q, 2 * kRegion);
-    tma_load_2d(qhi, &qmap, &bar_q, 0, int(row0 + q0));
-    tma_load_2d(qhi + kRegion, &qmap, &bar_q, 32, int(row0 + q0));
-  }
-  if (nblk > 0) issue_k(kb_first);
-  bool q_pending = true;
-  bool failed = cta_wait(&bar_q, 0);
-  if (!failed) {
-    q_pending = false;
-    split_tile(qhi, qlo, tid);
-  }
-
-  const int64_t qi = int64_t(q0) + row;
-  // This row's keys by the analytic conditions and the CTA's range: one
-  // interval [r_lo, r_hi), empty for rows past the sequence.
-  int64_t r_lo = lo, r_hi = qi < L ? hi : lo;
-  if (a.causal) r_hi = min(r_hi, qi + 1);
-  if (a.window >= 0) {
-    r_lo = max(r_lo, qi - a.window);
-    r_hi = min(r_hi, qi + a.window + 1);
-  }
-  if (a.valid_len >= 0) r_hi = min(r_hi, a.valid_len);
-  if (r_hi < r_lo) r_hi = r_lo;
-  constexpr float kLog2e = 1.44269504088896341f;
-  float m = -INFINITY, l = 0.0f;  // running max (natural units) and sum
-  bool inf_row = false;
-  const uint32_t vk = tid & 127, vc0 = (tid >> 7) * 16;  // V staging: key, first channel
-  float vreg[16];
-  auto load_v = [&](int64_t kb) {  // a V block into registers
-    const int64_t key = kb + vk;
-    if (key < hi && key >= lo) {
-      const float4* src = reinterpret_cast<const float4*>(a.v + (row0 + key) * 64 + vc0);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float4 t4 = ld_stream(src + j);
-        vreg[4 * j] = t4.x; vreg[4 * j + 1] = t4.y; vreg[4 * j + 2] = t4.z; vreg[4 * j + 3] = t4.w;
-      }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j) vreg[j] = 0.0f;
-    }
-  };
-  if (!failed && nblk > 0) {
-    load_v(kb_first);
-    failed = !issue_s(0);
-  }
-
-  for (uint32_t j = 0; j < nblk && !failed; ++j) {
-    const int64_t kb0 = kb_first + int64_t(j) * kTK;
-    const uint32_t tSj = tS0 + (j & 1) * 128;
-    // keep words of a partial block travel while S(j) finishes
-    const bool keep_full = !KEEP || (kb0 / 128 < 64 && ((full_bits >> (kb0 / 128)) & 1));
-    uint4 kw[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    const bool keep_vec = uint64_t(L) % 16 == 0 &&
-                          (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && nq == kTQ;
-    if (!keep_full) {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t w = tid + r * kTcThreads, kk = w >> 3, c = (w & 7) * 16;
-        const int64_t kj = kb0 + kk;
-        if (kj < hi) {
-          const uint8_t* src = a.keep + uint64_t(q0) + c + uint64_t(L) * (uint64_t(kj) + uint64_t(L) * b);
-          if (keep_vec) {
-            kw[r] = __ldg(reinterpret_cast<const uint4*>(src));
-          } else {
-            uint8_t tmp[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) tmp[i] = c + i < nq ? src[i] : 0;
-            memcpy(&kw[r], tmp, 16);
-          }
-        }
-      }
-    }
-    if (cta_wait(&bar_s, s_wt & 1)) {
-      failed = true;
-      break;
-    }
-    ++s_wt;
-    tc_fence_after();
-    if (j + 1 < nblk) issue_k(kb0 + kTK);  // K(j) consumed by S(j)
-    if (!keep_full) {
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint32_t w = tid + r * kTcThreads;
-        *reinterpret_cast<uint4*>(keep_s + (w >> 3) * kTQ + (w & 7) * 16) = kw[r];
-      }
-      __syncthreads();
-    }
-
-    // pass 1: masked, scaled scores of this thread's 32 columns back into S;
-    // the row max over the block from the four column groups. Keys of the
-    // row's interval [r_lo, r_hi) as block columns [c_lo, c_lo + c_span).
-    // q, k and v are finite here (checked before launch), so a score is
-    // finite unless q.k * scale (+ bias) overflows: +inf marks the row as
-    // the reference's NaN / empty row, -inf contributes nothing either way.
-    const int64_t c_lo64 = max(int64_t(0), min(int64_t(kTK), r_lo - kb0));
-    const int64_t c_hi64 = max(c_lo64, min(int64_t(kTK), r_hi - kb0));
-    const uint32_t c_lo = uint32_t(c_lo64), c_span = uint32_t(c_hi64 - c_lo64);
-    float mb = -INFINITY;
-    bool inf_here = false;
-    const bool row_full = c_lo == 0 && c_span == kTK && keep_full;
-#pragma unroll 1
-    for (int c = 0; c < 32; c += 16) {
-      const uint32_t col0 = g * 32 + c;
-      float sv[16];
-      tmem_ld16(tSj + lane_off + col0, sv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const uint32_t col = col0 + jj;
-        float sc = __fmul_rn(sv[jj], a.scale);
-        // bias and active are read only for keys of the row's interval, which
-        // lie inside the tensors (a block can reach past the sequence)
-        const bool in_range = col - c_lo < c_span;
-        if constexpr (BIAS)
-          if (in_range)
-            sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kb0 + col) + uint64_t(L) * b)]);
-        if (!row_full) {
-          bool kept = in_range;
-          if (KEEP && !keep_full) kept = kept && keep_s[col * kTQ + row] != 0;
-          sc = kept ? sc : -INFINITY;
-        }
-        if constexpr (ACTIVE)
-          sc = in_range && a.active[uint64_t(b) * L + kb0 + col] != 0.0f ? sc : -INFINITY;
-        if constexpr (BIAS) sc = sc == sc ? sc : -INFINITY;  // a NaN bias: nothing
-        inf_here |= sc == INFINITY;
-        sv[jj] = sc;
-        mb = fmaxf(mb, sc);
-      }
-      tmem_st16(tSj + lane_off + col0, sv);
-    }
-    inf_row |= inf_here;
-    red_max[g][row] = mb;
-    if (inf_here) inf_s[row] = 1;
-    tmem_wait_st();
-    __syncthreads();
-    mb = fmaxf(fmaxf(red_max[0][row], red_max[1][row]), fmaxf(red_max[2][row], red_max[3][row]));
-
-    // PV(j-1) must be done: it read the other S buffer (S(j+1) goes there),
-    // P lo and V, and O is rescaled below
-    if (j > 0) {
-      if (cta_wait(&bar_o, o_wt & 1)) {
-        failed = true;
-        break;
-      }
-      ++o_wt;
-      tc_fence_after();
-    }
-    if (j + 1 < nblk && !issue_s(j + 1)) {
-      failed = true;
-      break;
-    }
-
-    const float mn = fmaxf(m, mb);
-    // exp(x - mn) = 2^(x log2e - mn log2e): one FMA and the hardware 2^x
-    // (relative error ~2^-22, inside the f32 bar). A +inf row max: the row
-    // is empty (NaN / 0); its p come from a finite stand-in so that nothing
-    // non-finite reaches the MMA.
-    const float mnl = (mn == -INFINITY || mn == INFINITY) ? 0.0f : __fmul_rn(mn, kLog2e);
-    auto exp_rel = [&](float x) {
-      float y;
-      asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmaf_rn(x, kLog2e, -mnl)));
-      return y;
-    };
-    const float corr = (mn == -INFINITY || mn == INFINITY) ? 1.0f : exp_rel(m);
-    // pass 2: p = exp(s - max) split into hi (over this block's S) and lo,
-    // the A operands of the PV product
-    float ps = 0.0f;
-#pragma unroll 1
-    for (int c = 0; c < 32; c += 16) {
-      const uint32_t col0 = g * 32 + c;
-      float sv[16], pl[16];
-      tmem_ld16(tSj + lane_off + col0, sv);
-      tmem_wait_ld();
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const float x = sv[jj] == INFINITY ? -INFINITY : sv[jj];
-        const float p = exp_rel(x);  // -inf -> 0
-        ps = __fadd_rn(ps, p);
-        sv[jj] = tf32_round_finite(p);
-        pl[jj] = __fsub_rn(p, sv[jj]);
-      }
-      tmem_st16(tSj + lane_off + col0, sv);
-      tmem_st16(tPl + lane_off + col0, pl);
-    }
-    red_sum[g][row] = ps;
-    if (j > 0 && __any_sync(0xffffffffu, corr != 1.0f)) {  // warp-uniform: ld/st are .aligned
-      float ov[16];
-      tmem_ld16(tO + lane_off + g * 16, ov);
-      tmem_wait_ld();
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) ov[jj] = __fmul_rn(ov[jj], corr);
-      tmem_st16(tO + lane_off + g * 16, ov);
-    }
-    {  // V(j) (in registers) -> transposed (row = channel, K = key), split
-      const uint32_t reg = (vk >> 5) * kVtRegion;
-#pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const uint32_t off = reg + sw128_offset(vc0 + n, vk & 31);
-        const float h = tf32_round_finite(vreg[n]);
-        *reinterpret_cast<float*>(vthi + off) = h;
-        *reinterpret_cast<float*>(vtlo + off) = __fsub_rn(vreg[n], h);
-      }
-    }
-    fence_proxy_async_smem();
-    tmem_wait_st();
-    tc_fence_before();
-    __syncthreads();
-    ps = __fadd_rn(__fadd_rn(red_sum[0][row], red_sum[1][row]),
-                   __fadd_rn(red_sum[2][row], red_sum[3][row]));
-    l = __fmaf_rn(l, corr, ps);
-    m = mn;
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 16; ++ks) {
-        const uint32_t off = (ks >> 2) * kVtRegion + (ks & 3) * 32;
-        const uint64_t bhd = smem_desc_sw128(smem_addr(vthi + off));
-        const uint64_t bl = smem_desc_sw128(smem_addr(vtlo + off));
-        mma_tf32_ts(tO, tSj + ks * 8, bhd, id_o, (j > 0 || ks > 0) ? 1u : 0u);
-        mma_tf32_ts(tO, tSj + ks * 8, bl, id_o, 1);
-        mma_tf32_ts(tO, tPl + ks * 8, bhd, id_o, 1);
-      }
-      mma_commit(&bar_o);
-    }
-    ++o_iss;
-    if (j + 1 < nblk) load_v(kb0 + kTK);  // the next V block travels meanwhile
-  }
-  if (!failed && o_iss > o_wt) {
-    failed = cta_wait(&bar_o, o_wt & 1);
-    if (!failed) ++o_wt;
-    tc_fence_after();
-  }
-  (void)inf_row;
-
-  if (failed) {
-    // give up: count it and let what is still in flight land before the
-    // tensor memory and shared memory go away
-    if (tid == 0) {
-      atomicAdd(&g_tc_wait_timeouts, 1u);
-      if (q_pending) mbar_wait_bounded(&bar_q, 0, kTcWait);
-      if (k_iss > k_wt) mbar_wait_bounded(&bar_k, k_wt & 1, kTcWait);
-      if (s_iss > s_wt) mbar_wait_bounded(&bar_s, s_wt & 1, kTcWait);
-      if (o_iss > o_wt) mbar_wait_bounded(&bar_o, o_wt & 1, kTcWait);
-    }
-  } else {
-    const bool have_o = nblk > 0;
-    const bool empty = !have_o || l == 0.0f || inf_s[row] != 0;
-    const float ev = a.empty_nan ? NAN : 0.0f;
-    float ov[16];
-    if (have_o) {  // uniform over the CTA: every lane joins the .aligned load
-      tmem_ld16(tO + lane_off + g * 16, ov);
-      tmem_wait_ld();
-    }
-    if (qi < L) {
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const float val = empty ? ev : __fdiv_rn(ov[jj], l);
-        store_out(a, b, uint32_t(qi), uint64_t(head) * 64 + g * 16 + jj, val);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_free(tm, 512);
-}
-
 #include "attn_ws.cuh"
+static_assert(kWsTQ == kTQ, "the grid tiles the queries by 128");
 
-// flags[bh] = 1 when q, k or v of head bh holds a non-finite value (or a
-// value beyond the largest tf32, which the split cannot represent): the
-// tensor-core kernel leaves such heads to the f32 kernel, whose arithmetic
-// follows the reference's handling of non-finite values exactly.
-// CTA (slice, head): gridDim.x slices of each head's q, k and v; flags are
-// zeroed before the launch and only ever set to 1.
-__global__ void __launch_bounds__(256) attn_vcheck_kernel(const float* __restrict__ q,
-                                                          const float* __restrict__ k,
-                                                          const float* __restrict__ v,
-                                                          uint8_t* __restrict__ flags,
-                                                          uint64_t per_head) {
-  pdl_enter();
-  constexpr float kMax = 3.4e38f;  // below the largest tf32 (rounding up stays finite)
-  const uint64_t n4 = per_head / 4, per_slice = (n4 + gridDim.x - 1) / gridDim.x;
-  const uint64_t i0 = uint64_t(blockIdx.x) * per_slice, i1 = min(n4, i0 + per_slice);
-  bool bad = false;
-  for (int t = 0; t < 3; ++t) {
-    const float* base = t == 0 ? q : t == 1 ? k : v;
-    const float4* p = reinterpret_cast<const float4*>(base + uint64_t(blockIdx.y) * per_head);
-    for (uint64_t i = i0 + threadIdx.x; i < i1; i += 256) {
-      const float4 w = ld_stream(p + i);
-      bad |= !(fabsf(w.x) < kMax && fabsf(w.y) < kMax && fabsf(w.z) < kMax && fabsf(w.w) < kMax);
-    }
-  }
-  bad = __syncthreads_or(bad);
-  if (threadIdx.x == 0 && bad) flags[blockIdx.y] = 1;
-}
-
-// pre_flags: per-head flags already computed on the stream (the prep kernel
-// sets them), or null to run the check here.
+// The tensor-core path for head_dim 64: attn_img_split_kernel writes the tile
+// images (and, when pre_flags is null, the per-head flags of values the
+// tensor cores cannot take), attn_ws_kernel computes every unflagged head,
+// attn_flash_kernel the flagged ones. pre_flags: flags already computed on the
+// stream (the Laya prep kernel sets them). Returns 1 when the shape is not
+// covered (nothing launched).
 int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo& dev,
                    cudaStream_t stream, const uint8_t* pre_flags) {
-  // 1 when not covered (nothing launched)
   const uint64_t rows = uint64_t(batch) * a.heads * a.length;
   if (a.hd != 64 || rows >= (uint64_t(1) << 31) || !aligned(a.q, 16) || !aligned(a.k, 16) ||
-      !aligned(a.v, 16))
+      !aligned(a.v, 16) || kWsSmem > size_t(dev.smem_optin))
     return 1;
-  const size_t smem = 8 * kRegion + 8 * kVtRegion + kTK * kTQ + 1024;
-  if (smem > size_t(dev.smem_optin)) return 1;
-  // TFX_ATTN_KERNEL: f32 = the f32-pipe kernel only, tc1 = the single-loop
-  // tensor-core kernel, anything else = the warp-specialised one
-  static const int choice = [] {
+  // TFX_ATTN_KERNEL=f32: the f32-pipe kernel for every head
+  static const bool f32_only = [] {
     const char* e = getenv("TFX_ATTN_KERNEL");
-    if (e && std::string(e) == "f32") return 0;
-    if (e && std::string(e) == "tc1") return 1;
-    return 2;
+    return e && std::string(e) == "f32";
   }();
-  if (choice == 0) return 1;
-  const bool ws = choice == 2 && kWsSmem <= size_t(dev.smem_optin);
-  CUtensorMap qmap, kmap, vmap;
-  std::string why;
-  if (!encode_map_2d_f32(&qmap, a.q, 64, rows, 64, 32, kTQ, &why, 128) ||
-      !encode_map_2d_f32(&kmap, a.k, 64, rows, 64, 32, ws ? kWsKB : kTK, &why, 128) ||
-      (ws && !encode_map_2d_f32(&vmap, a.v, 64, rows, 64, 32, kWsKB, &why, 128)))
-    return fail(TFX_ERR_CUDA, op, "tensor map", why);
+  if (f32_only) return 1;
   const uint32_t nbh = batch * a.heads;
-  uint8_t* flags = nullptr;
-  int rc = TFX_OK;
-  if (!pre_flags) {
-    cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&flags), nbh, stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, stream);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
-    }
-    const unsigned slices = unsigned(std::max<uint64_t>(1, std::min<uint64_t>(
-        32, (uint64_t(dev.sms) * 8 + nbh - 1) / nbh)));
-    rc = launch_kernel(op, attn_vcheck_kernel, dim3(slices, nbh), dim3(256), 0, stream, 1, a.q,
-                       a.k, a.v, flags, uint64_t(a.length) * 64);
+  // scratch: the flags (unless given), then the tile images of q, k, v (hi
+  // and lo, padded to whole tiles: 512 bytes per padded row and tensor)
+  const uint32_t lq = (a.length + kWsTQ - 1) / kWsTQ * kWsTQ;
+  const uint32_t lk = (a.length + kWsKB - 1) / kWsKB * kWsKB;
+  const size_t qimg_bytes = size_t(nbh) * lq * 512;
+  const size_t kimg_bytes = size_t(nbh) * lk * 512;
+  const size_t flag_bytes = pre_flags ? 0 : (size_t(nbh) + 255) / 256 * 256;
+  uint8_t* scratch = nullptr;
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch),
+                                 flag_bytes + qimg_bytes + 2 * kimg_bytes, stream);
+  if (e == cudaSuccess && flag_bytes) e = cudaMemsetAsync(scratch, 0, nbh, stream);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
+  uint8_t* flags = pre_flags ? nullptr : scratch;
+  uint8_t* qimg = scratch + flag_bytes;
+  uint8_t* kimg = qimg + qimg_bytes;
+  uint8_t* vimg = kimg + kimg_bytes;
+  const uint64_t total = uint64_t(nbh) * lq * 16;
+  const unsigned blocks = unsigned(std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 16));
+  int rc = launch_kernel(op, attn_img_split_kernel, dim3(blocks), dim3(256), 0, stream, 1, a.q,
+                         a.k, a.v, qimg, kimg, vimg, a.length, lq, lk, total, flags);
   if (rc == TFX_OK) {
     a.vflags = pre_flags ? pre_flags : flags;
     a.vflag_mode = 1;
-    const dim3 grid((a.length + kTQ - 1) / kTQ, a.heads, batch);
+    const dim3 grid(lq / kWsTQ, a.heads, batch);
     auto run = [&](auto kernel) -> int {
-      const cudaError_t e2 =
-          cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-      if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
-      return launch_kernel(op, kernel, grid, dim3(kTcThreads), smem, stream, 1, qmap, kmap, a);
-    };
-    auto run_ws = [&](auto kernel) -> int {
       const cudaError_t e2 = cudaFuncSetAttribute(
           kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
       if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
-      return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1, qmap, kmap,
-                           vmap, a);
+      return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1,
+                           static_cast<const uint8_t*>(qimg), static_cast<const uint8_t*>(kimg),
+                           static_cast<const uint8_t*>(vimg), lk / kWsKB, a);
     };
-    const int sel = (a.keep ? 4 : 0) | (a.bias ? 2 : 0) | (a.active ? 1 : 0);
-    if (ws) switch (sel) {
-      case 0: rc = run_ws(attn_ws_kernel<false, false, false>); break;
-      case 1: rc = run_ws(attn_ws_kernel<false, false, true>); break;
-      case 2: rc = run_ws(attn_ws_kernel<false, true, false>); break;
-      case 3: rc = run_ws(attn_ws_kernel<false, true, true>); break;
-      case 4: rc = run_ws(attn_ws_kernel<true, false, false>); break;
-      case 5: rc = run_ws(attn_ws_kernel<true, false, true>); break;
-      case 6: rc = run_ws(attn_ws_kernel<true, true, false>); break;
-      default: rc = run_ws(attn_ws_kernel<true, true, true>); break;
-    }
-    else switch (sel) {
-      case 0: rc = run(attn_tc_kernel<false, false, false>); break;
-      case 1: rc = run(attn_tc_kernel<false, false, true>); break;
-      case 2: rc = run(attn_tc_kernel<false, true, false>); break;
-      case 3: rc = run(attn_tc_kernel<false, true, true>); break;
-      case 4: rc = run(attn_tc_kernel<true, false, false>); break;
-      case 5: rc = run(attn_tc_kernel<true, false, true>); break;
-      case 6: rc = run(attn_tc_kernel<true, true, false>); break;
-      default: rc = run(attn_tc_kernel<true, true, true>); break;
+    switch ((a.keep ? 4 : 0) | (a.bias ? 2 : 0) | (a.active ? 1 : 0)) {
+      case 0: rc = run(attn_ws_kernel<false, false, false>); break;
+      case 1: rc = run(attn_ws_kernel<false, false, true>); break;
+      case 2: rc = run(attn_ws_kernel<false, true, false>); break;
+      case 3: rc = run(attn_ws_kernel<false, true, true>); break;
+      case 4: rc = run(attn_ws_kernel<true, false, false>); break;
+      case 5: rc = run(attn_ws_kernel<true, false, true>); break;
+      case 6: rc = run(attn_ws_kernel<true, true, false>); break;
+      default: rc = run(attn_ws_kernel<true, true, true>); break;
     }
   }
   if (rc == TFX_OK) {
-    // heads whose V holds a non-finite value: the f32 kernel, which skips the
-    // keys whose probability is 0 (the reference's rule)
+    // heads holding a value the tensor cores cannot take: the f32 kernel,
+    // which skips the keys whose probability is 0 (the reference's rule)
     a.vflag_mode = 2;
     const size_t fsmem = size_t(64 * 64 * 3 + 64 * 68) * 4;
     const cudaError_t fe = cudaFuncSetAttribute(
@@ -1164,7 +637,7 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
                                            dim3((a.length + kQT - 1) / kQT, a.heads, batch),
                                            dim3(256), fsmem, stream, 1, a);
   }
-  if (flags) cudaFreeAsync(flags, stream);
+  cudaFreeAsync(scratch, stream);
   return rc;
 }
 
@@ -1405,7 +878,7 @@ int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const fl
   // kernel marks heads the tensor-core attention must leave to the f32 one)
   float* scratch = nullptr;
   const size_t nbh = size_t(batch * heads);
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4 + nbh, s);
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4 + nbh, s);
   uint8_t* flags = reinterpret_cast<uint8_t*>(scratch + 3 * n);
   if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, s);
   if (e != cudaSuccess) {
@@ -1441,7 +914,7 @@ int tfx_jeff_attention_f32(const float* q, const float* k, const float* v, const
   device_info(&st);
   if (st != TFX_OK) return st;
   float* scratch = nullptr;
-  const cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
+  const cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));

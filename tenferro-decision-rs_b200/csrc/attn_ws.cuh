@@ -1,83 +1,109 @@
-// attn_ws.cuh -- warp-specialised tensor-core attention for head_dim 64
-// (included by attention.cu inside its anonymous namespace; uses AttnArgs,
-// routed_away, analytic_range and store_out from there).
+// attn_ws.cuh -- tensor-core attention for head_dim 64 over pre-split
+// operand tiles (included by attention.cu inside its anonymous namespace;
+// uses AttnArgs, routed_away, analytic_range and store_out from there).
 //
-// Same arithmetic class as attn_tc_kernel -- S = Q K^T and P V on tcgen05 as
-// 3xTF32 (hi*hi + hi*lo + lo*hi, each operand split x = tf32(x) + rest),
-// online softmax in f32 -- with the work spread over roles that run
-// concurrently:
+// S = Q K^T and P V run on tcgen05 as 3xTF32 (hi*hi + hi*lo + lo*hi, each
+// operand split x = tf32(x) + rest; the dropped lo*lo term is ~2^-22
+// relative), the online softmax in f32. The design follows two measured
+// facts of the tensor cores:
+//   * one thread issues at most about one tcgen05.mma every ~100 cycles,
+//     whatever N is; M128 N64 K8 products (the only N that P V of head_dim 64
+//     has) are therefore issue-bound, and two issuing threads nearly double
+//     the rate;
+//   * the f32 accumulation of an MMA keeps about 22 bits below the largest
+//     exponent involved, so a long sum in one TMEM accumulator drifts.
 //
-//   warp 0      TMA: Q once, then K and V of each 64-key block into two-slot
-//               rings (a K slot is freed once S of its block has been
-//               computed, a V slot after PV);
-//   warp 1      MMA issuer: S(j+1) is issued before PV(j);
-//   warps 2-5   split: each raw tile is rewritten in place as its tf32 part
-//               plus a second tile with the rest; keys outside the CTA's
-//               range are zeroed; V moves into the MN-major layout the PV
-//               product reads; the keep / active masks of a partial block are
-//               packed into one 32-bit word per (query row, column group);
-//   warps 6-13  softmax: thread = (query row, column group of 32 keys).
+// Operands. attn_img_split_kernel writes q, k and v once as tf32 hi / lo
+// "tile images": byte for byte the shared-memory layout the MMAs read, so the
+// attention kernel moves each tile with one bulk copy and does no conversion:
+//   Q: 128-query tiles, K-major 128-byte swizzle (16-byte chunk c of row r at
+//      c ^ (r % 8)), two 32-channel regions of 16 KB, hi then lo (64 KB);
+//   K: 64-key tiles, the same layout, regions of 8 KB, hi then lo (32 KB);
+//   V: 64-key tiles, rows = keys, MN-major in the 32-byte-atom swizzle that
+//      MN-major tf32 operands need (32-byte granule g of row r at g ^ (r % 4)),
+//      regions of 8 KB, hi then lo (32 KB).
+// Rows past the sequence are zero, so no tile holds another head's values.
 //
-// Tensor-pipe use. An MMA of M128 N64 K8 is short next to the pipe's latency
-// from one accumulation into the same TMEM columns to the next, so a block's
-// MMAs are spread over independent accumulators: S over two (k-steps 0-3 and
-// 4-7, summed by the softmax threads in f32), PV over the two column groups.
+// Roles (12 warps):
+//   warp 0      bulk copies: Q once, K and V of each 64-key block into
+//               two-slot rings;
+//   warps 1, 2  MMA issuers, one per block parity: issuer p computes S(j) and
+//               P V(j) of the blocks j = p mod 2 in program order, so the
+//               buffers that S(j + 2) overwrites are read by P V(j) of the
+//               same thread (tcgen05.mma of one thread run in order);
+//   warp 3      mask words: the keep / active masks of a partial block packed
+//               into one 32-bit word per (query row, column group), up to
+//               four blocks ahead of the softmax;
+//   warps 4-11  softmax: thread = (query row, column group g of 32 keys).
 //
-// Accumulation. The tensor cores do not accumulate in IEEE f32 (each MMA
-// keeps about 22 bits below the largest exponent of the accumulator and its
-// products), so PV of each block starts a fresh TMEM partial, and the softmax
-// threads add the partial of block j into an f32 sum (TMEM, through
-// registers) while block j + 1 is processed. A sequence of thousands of keys then stays within the f32
-// tolerance (one TMEM accumulator for the whole row drifts by ~1e-4).
+// TMEM (512 columns, one CTA per SM): block j (p = j & 1) has S, then P hi,
+// in columns 128 p + [0, 64), P lo in 128 p + [64, 128), and its P V partial
+// of group g in 256 + 128 p + 64 g (a fresh partial per block). The softmax
+// threads add the partial of block j into f32 registers while block j + 1 is
+// processed, so a sequence of any length stays within the f32 tolerance.
 //
 // Softmax. Each column group g keeps its own running max m_g, sum l_g and
-// output O_g, so the softmax threads never exchange values inside
-// the loop; the groups are merged once at the end: m = max(m_0, m_1),
+// output O_g, so the softmax threads never exchange values inside the loop;
+// the groups are merged once at the end: m = max(m_0, m_1),
 // O = sum O_g e^(m_g - m), l = sum l_g e^(m_g - m). A row's running max only
 // moves when a block's max exceeds it by more than 8 (natural log units);
 // until then p = e^(s - m) is at most e^8, which f32 holds as exactly as
-// p <= 1.
-//
-// TMEM (512 columns allocated, one CTA per SM): block j uses columns
-// 128 (j & 1) + [0, 64) for the first S accumulator (then P hi) and + [64,
-// 128) for the second (then P lo); the PV partial of group g is at 256 + 64 g
-// and its f32 sum at 384 + 64 g.
-// Shared memory: Q hi, Q lo (32 KB each), K slots (hi 16 KB + lo 16 KB) x 2,
-// V slots the same, mask words 2 KB, keep staging 8 KB + 256 B: 203 KB.
+// p <= 1, and nothing is rescaled.
 //
 // Every wait is bounded; a role that gives up raises the CTA's abort flag,
-// which ends the other roles' waits; the TMA warp then waits for the copies
-// it issued and the MMA warp for the MMAs it issued before TMEM is freed.
+// which ends the other roles' waits; the copy warp then waits for the copies
+// it issued and each issuer for its MMAs before TMEM is freed.
 
-constexpr int kWsThreads = 448;
+constexpr int kWsThreads = 384;
 constexpr int kWsTQ = 128;                  // queries per CTA
 constexpr int kWsKB = 64;                   // keys per block
 constexpr uint32_t kWsQRegion = 16384;      // 128 rows x 128 bytes
 constexpr uint32_t kWsKRegion = 8192;       // 64 rows x 128 bytes
-constexpr uint32_t kWsQBytes = 2 * kWsQRegion;   // one of Q hi / Q lo
-constexpr uint32_t kWsTile = 2 * kWsKRegion;     // one of K hi / K lo / V hi / V lo
+constexpr uint32_t kWsQPlane = 2 * kWsQRegion;   // Q hi or Q lo
+constexpr uint32_t kWsTile = 2 * kWsKRegion;     // K / V hi or lo
 constexpr uint32_t kWsSlot = 2 * kWsTile;        // hi + lo
-constexpr uint32_t kWsOffQlo = kWsQBytes;
-constexpr uint32_t kWsOffK = 2 * kWsQBytes;
+constexpr uint32_t kWsOffQlo = kWsQPlane;
+constexpr uint32_t kWsOffK = 2 * kWsQPlane;
 constexpr uint32_t kWsOffV = kWsOffK + 2 * kWsSlot;
+constexpr uint32_t kWsWordSlots = 4;       // mask-word slots (blocks in flight)
 constexpr uint32_t kWsOffWords = kWsOffV + 2 * kWsSlot;     // [slot][group][row] u32
-constexpr uint32_t kWsOffKeep = kWsOffWords + 2 * 2 * kWsTQ * 4;  // [key][query] bytes
-constexpr uint32_t kWsOffActive = kWsOffKeep + kWsKB * kWsTQ;     // [key] f32
-constexpr uint32_t kWsSmem = kWsOffActive + kWsKB * 4 + 1024;     // + alignment slack
+constexpr uint32_t kWsSmem = kWsOffWords + kWsWordSlots * 2 * kWsTQ * 4 + 1024;  // + slack
 constexpr float kWsRescale = 8.0f;          // natural-log headroom before m moves
 constexpr uint32_t kWsStage = 68;           // output staging row stride (floats)
 
 struct WsShared {
-  uint64_t q_full, q_split;
-  uint64_t k_full[2], k_split[2], k_empty[2];
-  uint64_t v_full[2], v_split[2], v_empty[2];
-  uint64_t s_full[2], p_ready[2];
-  uint64_t o_done, o_final, drain;
+  uint64_t q_full;
+  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+  uint64_t s_full[2], p_ready[2], o_done[2], drain[2];
+  uint64_t w_ready[kWsWordSlots], w_free[kWsWordSlots];
   uint32_t tmem_base;
   int abort;
   int kmin, kmax;
   unsigned long long notfull;
 };
+
+// Byte offsets inside the tile images (and inside the shared-memory copies
+// of the tiles), for 4 consecutive channels ch .. ch + 3 (ch % 4 == 0) of
+// row r of the tile.
+__host__ __device__ __forceinline__ uint32_t img_kmajor_off(uint32_t r, uint32_t ch,
+                                                            uint32_t region_bytes) {
+  return (ch >> 5) * region_bytes + r * 128 + ((((ch & 31) >> 2) ^ (r & 7)) << 4);
+}
+__host__ __device__ __forceinline__ uint32_t img_v_off(uint32_t r, uint32_t ch) {
+  return (ch >> 5) * kWsKRegion + r * 128 + ((((ch & 31) >> 3) ^ (r & 3)) << 5) +
+         (((ch & 7) >> 2) << 4);
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global memory into shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
 
 // Bounded wait; also ends when another role has given up. Returns false when
 // the phase did not complete (the first role to give up counts it).
@@ -100,14 +126,11 @@ __device__ __forceinline__ bool ws_wait_warp(uint64_t* bar, uint32_t parity, WsS
   return !__any_sync(0xffffffffu, !ws_wait(bar, parity, sh));
 }
 
-// Named barriers of the role groups (0 is __syncthreads).
-__device__ __forceinline__ void ws_split_sync() {  // the 128 split threads
-  asm volatile("bar.sync 2, 128;" ::: "memory");
-}
-__device__ __forceinline__ void ws_softmax_sync() {  // the 256 softmax threads
+// The 256 softmax threads: named barrier 1, and bar.red.or (every thread
+// gets the same answer).
+__device__ __forceinline__ void ws_softmax_sync() {
   asm volatile("bar.sync 1, 256;" ::: "memory");
 }
-// bar.red.or over the 256 softmax threads: every thread gets the same answer.
 __device__ __forceinline__ bool ws_softmax_any(bool v) {
   uint32_t r;
   asm volatile(
@@ -121,68 +144,56 @@ __device__ __forceinline__ bool ws_softmax_any(bool v) {
   return r != 0;
 }
 
-// Rewrites `bytes` of a K-major swizzled tile (128-byte rows; row r of a
-// region of `rows` rows is query / key first_row + r) in place as tf32(x) and
-// writes x - tf32(x) at the same offset of `lo`. Rows outside [keep_lo,
-// keep_hi) become 0 in both. The swizzle only permutes 16-byte chunks inside
-// a row, so the pass is elementwise. 128 threads; thread t takes chunks t,
-// t + 128, ...
-__device__ __forceinline__ void ws_split(uint8_t* hi, uint8_t* lo, uint32_t bytes, uint32_t rows,
-                                         int64_t first_row, int64_t keep_lo, int64_t keep_hi,
-                                         uint32_t t) {
-  const uint32_t lo_row = uint32_t(max(int64_t(0), min(int64_t(rows), keep_lo - first_row)));
-  const uint32_t hi_row = uint32_t(max(int64_t(lo_row), min(int64_t(rows), keep_hi - first_row)));
-#pragma unroll 4
-  for (uint32_t c = t; c < bytes / 16; c += 128) {
-    const uint32_t off = c * 16;
-    const uint32_t r = (off / 128) % rows;
-    float4 x = *reinterpret_cast<const float4*>(hi + off);
-    if (r - lo_row >= hi_row - lo_row) x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    const float4 h = make_float4(tf32_round_finite(x.x), tf32_round_finite(x.y),
-                                 tf32_round_finite(x.z), tf32_round_finite(x.w));
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) = make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y),
-                                                       __fsub_rn(x.z, h.z), __fsub_rn(x.w, h.w));
-  }
-}
-
-// The V tile of one slot: raw values as the TMA wrote them (two regions of
-// 64 key rows x 32 channels, standard 128-byte swizzle: 16-byte chunk c of
-// row r at chunk c ^ (r % 8)) become tf32 hi (in place) and lo, both in the
-// MN-major 32-byte-atom layout the PV product reads. Thread t owns row t % 64
-// of region t / 64 and reads the whole row before writing it, so the
-// permutation in place is safe. Keys outside [keep_lo, keep_hi) become 0.
-__device__ __forceinline__ void ws_split_v(uint8_t* hi, uint8_t* lo, int64_t first_key,
-                                           int64_t keep_lo, int64_t keep_hi, uint32_t t) {
-  const uint32_t r = t & 63, region = (t >> 6) * kWsKRegion;
-  const int64_t key = first_key + r;
-  const bool zero = key < keep_lo || key >= keep_hi;
-  float4 x[8];
-#pragma unroll
-  for (uint32_t c = 0; c < 8; ++c) {
-    x[c] = *reinterpret_cast<const float4*>(hi + region + r * 128 + ((c ^ (r & 7)) << 4));
-    if (zero) x[c] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-  }
-#pragma unroll
-  for (uint32_t c = 0; c < 8; ++c) {
-    const float4 h = make_float4(tf32_round_finite(x[c].x), tf32_round_finite(x[c].y),
-                                 tf32_round_finite(x[c].z), tf32_round_finite(x[c].w));
-    const uint32_t off = region + sw128b32_chunk(r, c);
-    *reinterpret_cast<float4*>(hi + off) = h;
-    *reinterpret_cast<float4*>(lo + off) =
-        make_float4(__fsub_rn(x[c].x, h.x), __fsub_rn(x[c].y, h.y), __fsub_rn(x[c].z, h.z),
-                    __fsub_rn(x[c].w, h.w));
+// One thread per (head, row of the padded query length lq, 4 channels): q, k
+// and v of that row (0 past the sequence; k and v only for rows below lk)
+// split into tf32 hi / lo and written into the tile images. flags[bh] = 1
+// (when flags is given) if a value of the head is non-finite or beyond the
+// largest tf32: the f32 kernel takes that head.
+__global__ void __launch_bounds__(256) attn_img_split_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    uint8_t* __restrict__ qimg, uint8_t* __restrict__ kimg, uint8_t* __restrict__ vimg,
+    uint32_t L, uint32_t lq, uint32_t lk, uint64_t total, uint8_t* flags) {
+  pdl_enter();
+  constexpr float kMax = 3.4e38f;  // below the largest tf32 (rounding up stays finite)
+  const uint32_t nqt = lq / kWsTQ, nkt = lk / kWsKB;
+  for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
+       n += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t ch = uint32_t(n & 15) * 4;
+    const uint64_t rest = n >> 4;
+    const uint64_t bh = rest / lq;
+    const uint32_t r = uint32_t(rest - bh * lq);
+    const uint64_t src = (bh * L + r) * 64 + ch;
+    bool bad = false;
+    auto put = [&](const float* x_src, uint8_t* img, uint64_t tile_bytes, uint32_t off) {
+      float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (r < L) x = ld_stream(reinterpret_cast<const float4*>(x_src + src));
+      bad |= !(fabsf(x.x) < kMax && fabsf(x.y) < kMax && fabsf(x.z) < kMax && fabsf(x.w) < kMax);
+      const float4 h = make_float4(tf32_round_finite(x.x), tf32_round_finite(x.y),
+                                   tf32_round_finite(x.z), tf32_round_finite(x.w));
+      *reinterpret_cast<float4*>(img + off) = h;
+      *reinterpret_cast<float4*>(img + tile_bytes / 2 + off) =
+          make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z),
+                      __fsub_rn(x.w, h.w));
+    };
+    put(q, qimg + (bh * nqt + r / kWsTQ) * (2 * kWsQPlane), 2 * kWsQPlane,
+        img_kmajor_off(r % kWsTQ, ch, kWsQRegion));
+    if (r < lk) {
+      const uint64_t kt = (bh * nkt + r / kWsKB) * kWsSlot;
+      put(k, kimg + kt, kWsSlot, img_kmajor_off(r % kWsKB, ch, kWsKRegion));
+      put(v, vimg + kt, kWsSlot, img_v_off(r % kWsKB, ch));
+    }
+    if (bad && flags) flags[bh] = 1;
   }
 }
 
 // Keep-mask scan over the keys [lo, hi) for the queries [q0, q0 + nq): narrows
 // [lo, hi) to the keys some query keeps and returns one bit per 64-key block
-// (block index kj / 64 < 64) that has a (query, key) the mask drops. Every
-// thread of the CTA gets the results. Eight threads read one key's 128 query
-// bytes as 16-byte words (keep[q + L*(k + L*b)]: the queries of a key are
-// contiguous); each thread issues its loads for ten keys before using any of
-// them, and the results are reduced per warp, then once per warp in shared
-// memory.
+// (block index kj / 64 < 64), set when the mask keeps every (query, key) of
+// the block. Every thread of the CTA gets the results. Eight threads read one
+// key's 128 query bytes as 16-byte words (keep[q + L*(k + L*b)]: the queries
+// of a key are contiguous); each thread issues its loads for twelve keys before
+// using any of them, and the results are reduced per warp, then once per warp
+// in shared memory.
 __device__ unsigned long long ws_keep_scan(const AttnArgs& a, uint32_t b, uint32_t q0,
                                            uint32_t nq, int64_t* lo, int64_t* hi,
                                            WsShared& sh) {
@@ -197,7 +208,7 @@ __device__ unsigned long long ws_keep_scan(const AttnArgs& a, uint32_t b, uint32
   const uint32_t i0 = c * 16, i1 = min(nq, i0 + 16);
   const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && i1 - i0 == 16;
   const uint32_t per = blockDim.x >> 3;  // keys per pass
-  constexpr int U = 10;
+  constexpr int U = 12;
   int kmin = 0x7fffffff, kmax = -1;
   unsigned long long nf = 0;
   if (i0 < i1) {
@@ -218,14 +229,14 @@ __device__ unsigned long long ws_keep_scan(const AttnArgs& a, uint32_t b, uint32
         bool any = false, all = true;
         if (vec) {
           any = (w[u].x | w[u].y | w[u].z | w[u].w) != 0;
-          auto zero_byte = [](uint32_t v) { return ((v - 0x01010101u) & ~v & 0x80808080u) != 0; };
+          auto zero_byte = [](uint32_t x) { return ((x - 0x01010101u) & ~x & 0x80808080u) != 0; };
           all = !(zero_byte(w[u].x) || zero_byte(w[u].y) || zero_byte(w[u].z) || zero_byte(w[u].w));
         } else {
           const uint8_t* row = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
           for (uint32_t i = i0; i < i1; ++i) {
-            const bool k = row[i] != 0;
-            any |= k;
-            all &= k;
+            const bool kk = row[i] != 0;
+            any |= kk;
+            all &= kk;
           }
         }
         if (any) {
@@ -260,87 +271,92 @@ __device__ unsigned long long ws_keep_scan(const AttnArgs& a, uint32_t b, uint32
   return ~notfull;
 }
 
-// Mask words of the 64-key block at kb for the split threads (t = query row
-// of the CTA): bit c of words[g * 128 + t] is set when key kb + 32 g + c is in
-// [lo, hi), the keep tensor keeps (query, key) and the key is active. The keep
-// tile is first staged in shared memory with 16-byte loads (all issued before
-// any is used), so that each row's 64 bits come from shared memory.
+// Bit i of the result: byte i of the 16 bytes w is non-zero.
+__device__ __forceinline__ uint32_t nonzero_bytes16(uint4 w) {
+  auto nib = [](uint32_t x) {
+    const uint32_t t = (((x & 0x7f7f7f7fu) + 0x7f7f7f7fu) | x) & 0x80808080u;  // byte MSB = non-zero
+    const uint32_t b = t >> 7;                                                   // bits 0, 8, 16, 24
+    return (b | (b >> 7) | (b >> 14) | (b >> 21)) & 0xFu;
+  };
+  return nib(w.x) | (nib(w.y) << 4) | (nib(w.z) << 8) | (nib(w.w) << 12);
+}
+
+// Transposes the 32 x 32 bit matrix whose row i is lane i's x: afterwards
+// bit j of lane i is bit i of lane j's input. Five exchange stages: lanes i
+// and i ^ s swap the off-diagonal s x s blocks of each 2s x 2s block.
+__device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, uint32_t lane) {
+  const uint32_t masks[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    const uint32_t sft = 16u >> k, m = masks[k];
+    const uint32_t y = __shfl_xor_sync(0xffffffffu, x, sft);
+    x = (lane & sft) ? ((x & ~m) | ((y & ~m) >> sft)) : ((x & m) | ((y & m) << sft));
+  }
+  return x;
+}
+
+// Mask words of the 64-key block at kb, built by one warp: bit c of
+// words[g * 128 + row] is set when key kb + 32 g + c is in [lo, hi), the keep
+// tensor keeps (query q0 + row, key) and the key is active. Lane c reads the
+// 128 query bytes of keys kb + c and kb + 32 + c (contiguous in
+// keep[q + L*(k + L*b)]) as sixteen 16-byte loads, all issued before any is
+// used, turns them into 32-row masks, and a bit transpose of each 32 x 32
+// block leaves row r's word in lane r.
 template <bool KEEP, bool ACTIVE>
 __device__ __forceinline__ void ws_build_words(const AttnArgs& a, uint32_t b, uint32_t q0,
                                                uint32_t nq, int64_t kb, int64_t lo, int64_t hi,
-                                               uint8_t* keep_s, float* act_s, uint32_t* words,
-                                               uint32_t t) {
+                                               uint32_t* words, uint32_t lane) {
   const uint64_t L = a.length;
-  if constexpr (KEEP) {
-    const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && nq == kWsTQ;
-    uint4 w[4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const uint32_t idx = t + 128 * r, key = idx >> 3, c = (idx & 7) * 16;
-      const int64_t kj = kb + key;
-      w[r] = make_uint4(0, 0, 0, 0);
-      if (kj >= lo && kj < hi) {
-        const uint8_t* src = a.keep + uint64_t(q0) + c + L * (uint64_t(kj) + L * b);
-        if (vec) {
-          w[r] = __ldg(reinterpret_cast<const uint4*>(src));
-        } else {
-          uint8_t tmp[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) tmp[i] = c + i < nq ? src[i] : 0;
-          memcpy(&w[r], tmp, 16);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const uint32_t idx = t + 128 * r;
-      *reinterpret_cast<uint4*>(keep_s + (idx >> 3) * kWsTQ + (idx & 7) * 16) = w[r];
-    }
-  }
-  if constexpr (ACTIVE) {
-    if (t < kWsKB) {
-      const int64_t kj = kb + t;
-      act_s[t] = kj >= lo && kj < hi ? a.active[uint64_t(b) * L + uint64_t(kj)] : 0.0f;
-    }
-  }
-  ws_split_sync();
+  const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && nq == kWsTQ;
+  bool kon[2];
+  uint4 w[2][8];
 #pragma unroll
   for (uint32_t g = 0; g < 2; ++g) {
-    uint32_t w = 0;
+    const int64_t kj = kb + 32 * g + lane;
+    kon[g] = kj >= lo && kj < hi;
+    if constexpr (ACTIVE)
+      if (kon[g]) kon[g] = a.active[uint64_t(b) * L + uint64_t(kj)] != 0.0f;
 #pragma unroll
-    for (uint32_t c = 0; c < 32; ++c) {
-      const uint32_t key = 32 * g + c;
-      const int64_t kj = kb + key;
-      bool kept = t < nq && kj >= lo && kj < hi;
-      if constexpr (KEEP) kept = kept && keep_s[key * kWsTQ + t] != 0;
-      if constexpr (ACTIVE) kept = kept && act_s[key] != 0.0f;
-      w |= uint32_t(kept) << c;
+    for (int i = 0; i < 8; ++i) w[g][i] = make_uint4(0, 0, 0, 0);
+    if (KEEP && vec && kon[g]) {
+      const uint4* src = reinterpret_cast<const uint4*>(a.keep + uint64_t(q0) +
+                                                        L * (uint64_t(kj) + L * b));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[g][i] = __ldg(src + i);
     }
-    words[g * kWsTQ + t] = w;
   }
-  ws_split_sync();  // the staging is rewritten by the next call
+#pragma unroll
+  for (uint32_t g = 0; g < 2; ++g) {
+    const int64_t kj = kb + 32 * g + lane;
+#pragma unroll
+    for (int rc = 0; rc < 4; ++rc) {
+      uint32_t rm = 0;  // bit r: query row 32 rc + r kept for this lane's key
+      if (kon[g]) {
+        if constexpr (KEEP) {
+          if (vec) {
+            rm = nonzero_bytes16(w[g][2 * rc]) | (nonzero_bytes16(w[g][2 * rc + 1]) << 16);
+          } else {
+            const uint8_t* src = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
+            for (uint32_t r = 0; r < 32 && 32 * rc + r < nq; ++r)
+              if (src[32 * rc + r] != 0) rm |= 1u << r;
+          }
+        } else {
+          const uint32_t n = nq > 32u * rc ? min(32u, nq - 32u * rc) : 0u;
+          rm = n == 32 ? ~0u : ((1u << n) - 1u);
+        }
+      }
+      words[g * kWsTQ + 32 * rc + lane] = warp_transpose32(rm, lane);
+    }
+  }
+  __syncwarp();
 }
 
-// bar.red.or over the 128 split threads (named barrier 2).
-__device__ __forceinline__ bool ws_split_any(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 2, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(uint32_t(v))
-      : "memory");
-  return r != 0;
-}
-
-// qmap: q rows with a {32, 128} box; kmap / vmap: k / v rows with a {32, 64}
-// box; all three 128-byte swizzled (attention.cu encodes them).
+// qimg / kimg / vimg: the tile images of attn_img_split_kernel, nkt key tiles
+// per head (gridDim.x query tiles).
 template <bool KEEP, bool BIAS, bool ACTIVE>
 __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
-    const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-    const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+    const uint8_t* __restrict__ qimg, const uint8_t* __restrict__ kimg,
+    const uint8_t* __restrict__ vimg, uint32_t nkt, AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t ws_smem[];
   __shared__ WsShared sh;
   pdl_enter();
@@ -350,12 +366,37 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   if (routed_away(a, bh)) return;
   const uint32_t L = a.length;
   const uint32_t nq = min(uint32_t(kWsTQ), L - q0);
-  const uint64_t row0 = uint64_t(bh) * L;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws_smem) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* qhi = base;
-  uint8_t* qlo = base + kWsOffQlo;
   uint32_t* words = reinterpret_cast<uint32_t*>(base + kWsOffWords);  // [slot][group][row]
+
+  if (tid == 0) {
+    mbar_init(&sh.q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sh.k_full[s], 1);
+      mbar_init(&sh.k_empty[s], 1);
+      mbar_init(&sh.v_full[s], 1);
+      mbar_init(&sh.v_empty[s], 1);
+      mbar_init(&sh.s_full[s], 1);
+      mbar_init(&sh.p_ready[s], 256);
+      mbar_init(&sh.o_done[s], 1);
+      mbar_init(&sh.drain[s], 1);
+    }
+    for (uint32_t s = 0; s < kWsWordSlots; ++s) {
+      mbar_init(&sh.w_ready[s], 32);
+      mbar_init(&sh.w_free[s], 256);
+    }
+    sh.abort = 0;
+    mbar_init_fence();
+  }
+  __syncthreads();
+  // Q travels while the keep mask is scanned
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&sh.q_full, 2 * kWsQPlane);
+    bulk_load(qhi, qimg + (uint64_t(bh) * gridDim.x + blockIdx.x) * (2 * kWsQPlane),
+              2 * kWsQPlane, &sh.q_full);
+  }
 
   int64_t lo, hi;
   analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
@@ -363,33 +404,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   if (KEEP && lo < hi) full_bits = ws_keep_scan(a, b, q0, nq, &lo, &hi, sh);
   const int64_t kb_first = lo / kWsKB * kWsKB;
   const uint32_t nblk = kb_first < hi ? uint32_t((hi - kb_first + kWsKB - 1) / kWsKB) : 0;
+  const uint32_t kt0 = uint32_t(kb_first / kWsKB);  // key tile of block 0
   // mask words are built (and read) for block j when this holds
   auto need_words = [&](uint32_t j) {
     if (ACTIVE) return true;
     if (!KEEP) return false;
-    const int64_t blk = (kb_first >> 6) + j;
+    const uint32_t blk = kt0 + j;
     return !(blk < 64 && ((full_bits >> blk) & 1));
   };
 
-  if (tid == 0) {
-    mbar_init(&sh.q_full, 1);
-    mbar_init(&sh.q_split, 128);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.k_full[s], 1);
-      mbar_init(&sh.k_split[s], 128);
-      mbar_init(&sh.k_empty[s], 1);
-      mbar_init(&sh.v_full[s], 1);
-      mbar_init(&sh.v_split[s], 128);
-      mbar_init(&sh.v_empty[s], 1);
-      mbar_init(&sh.s_full[s], 1);
-      mbar_init(&sh.p_ready[s], 256);
-    }
-    mbar_init(&sh.o_done, 1);
-    mbar_init(&sh.o_final, 1);
-    mbar_init(&sh.drain, 1);
-    sh.abort = 0;
-    mbar_init_fence();
-  }
   if (warp == 1) tmem_alloc(&sh.tmem_base, 512);
   tc_fence_before();
   __syncthreads();
@@ -397,26 +420,19 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   const uint32_t tm = sh.tmem_base;
 
   if (warp == 0) {
-    // ---- TMA producer ----
-    if (lane == 0 && nblk > 0) {
-      mbar_arrive_expect_tx(&sh.q_full, kWsQBytes);
-      tma_load_2d(qhi, &qmap, &sh.q_full, 0, int(row0 + q0));
-      tma_load_2d(qhi + kWsQRegion, &qmap, &sh.q_full, 32, int(row0 + q0));
+    // ---- bulk copies ----
+    if (lane == 0) {
       uint32_t kiss[2] = {0, 0}, viss[2] = {0, 0};
       for (uint32_t j = 0; j < nblk; ++j) {
         const uint32_t s = j & 1, use = j >> 1;
-        const int row = int(row0 + kb_first + int64_t(j) * kWsKB);
-        uint8_t* ks = base + kWsOffK + s * kWsSlot;
-        uint8_t* vs = base + kWsOffV + s * kWsSlot;
+        const uint64_t tile = (uint64_t(bh) * nkt + kt0 + j) * kWsSlot;
         if (use > 0 && !ws_wait(&sh.k_empty[s], (use - 1) & 1, &sh)) break;
-        mbar_arrive_expect_tx(&sh.k_full[s], kWsTile);
-        tma_load_2d(ks, &kmap, &sh.k_full[s], 0, row);
-        tma_load_2d(ks + kWsKRegion, &kmap, &sh.k_full[s], 32, row);
+        mbar_arrive_expect_tx(&sh.k_full[s], kWsSlot);
+        bulk_load(base + kWsOffK + s * kWsSlot, kimg + tile, kWsSlot, &sh.k_full[s]);
         ++kiss[s];
         if (use > 0 && !ws_wait(&sh.v_empty[s], (use - 1) & 1, &sh)) break;
-        mbar_arrive_expect_tx(&sh.v_full[s], kWsTile);
-        tma_load_2d(vs, &vmap, &sh.v_full[s], 0, row);
-        tma_load_2d(vs + kWsKRegion, &vmap, &sh.v_full[s], 32, row);
+        mbar_arrive_expect_tx(&sh.v_full[s], kWsSlot);
+        bulk_load(base + kWsOffV + s * kWsSlot, vimg + tile, kWsSlot, &sh.v_full[s]);
         ++viss[s];
       }
       // the copies this thread issued land before the CTA can exit
@@ -427,52 +443,42 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---- MMA issuer ----
-    if (lane == 0 && nblk > 0) {
+  } else if (warp <= 2) {
+    // ---- MMA issuer p: blocks j = p, p + 2, ... (slot and buffers p) ----
+    const uint32_t p = warp - 1;
+    if (lane == 0 && nblk > p) {
       constexpr uint32_t id_s = idesc_tf32(kWsTQ, kWsKB);
       constexpr uint32_t id_o = idesc_tf32_bmn(kWsTQ, 64);
-      // S(j): chain A (k-steps 0-3) and chain B (4-7) issued alternately
-      auto issue_s = [&](uint32_t j) -> bool {
-        const uint32_t s = j & 1;
-        if (!ws_wait(&sh.k_split[s], (j >> 1) & 1, &sh)) return false;
+      // descriptors built once; an offset moves the start address field
+      // (address >> 4, no carry out of its 14 bits inside shared memory)
+      const uint64_t dqh = smem_desc_sw128(smem_addr(qhi));
+      const uint64_t dql = dqh + (kWsQPlane >> 4);
+      const uint64_t dkh = smem_desc_sw128(smem_addr(base + kWsOffK + p * kWsSlot));
+      const uint64_t dkl = dkh + (kWsTile >> 4);
+      const uint64_t dvh =
+          smem_desc_sw128b32_mn(smem_addr(base + kWsOffV + p * kWsSlot), kWsKRegion);
+      const uint64_t dvl = dvh + (kWsTile >> 4);
+      const uint32_t ts = tm + 128 * p, tpl = ts + 64, to = tm + 256 + 128 * p;
+      bool ok = ws_wait(&sh.q_full, 0, &sh);
+      for (uint32_t j = p; ok && j < nblk; j += 2) {
+        const uint32_t use = j >> 1;
+        if (!ws_wait(&sh.k_full[p], use & 1, &sh)) break;
         tc_fence_after();
-        const uint32_t dst = tm + 128 * s;
-        // descriptors built once; an offset moves the start address field
-        // (address >> 4, no carry out of its 14 bits inside shared memory)
-        const uint64_t dqh = smem_desc_sw128(smem_addr(qhi));
-        const uint64_t dql = smem_desc_sw128(smem_addr(qlo));
-        const uint64_t dkh = smem_desc_sw128(smem_addr(base + kWsOffK + s * kWsSlot));
-        const uint64_t dkl = dkh + (kWsTile >> 4);
+        // S(j) = Q K^T: 8 k-steps x (hi hi, hi lo, lo hi)
 #pragma unroll
-        for (uint32_t kk = 0; kk < 4; ++kk) {
-#pragma unroll
-          for (uint32_t prod = 0; prod < 3; ++prod) {
-#pragma unroll
-            for (uint32_t ch = 0; ch < 2; ++ch) {
-              const uint64_t a_q = (prod == 2 ? dql : dqh) + ((ch * kWsQRegion + kk * 32) >> 4);
-              const uint64_t b_k = (prod == 1 ? dkl : dkh) + ((ch * kWsKRegion + kk * 32) >> 4);
-              mma_tf32_ss(dst + 64 * ch, a_q, b_k, id_s, (kk > 0 || prod > 0) ? 1u : 0u);
-            }
-          }
+        for (uint32_t ks = 0; ks < 8; ++ks) {
+          const uint32_t oq = ((ks >> 2) * kWsQRegion + (ks & 3) * 32) >> 4;
+          const uint32_t okk = ((ks >> 2) * kWsKRegion + (ks & 3) * 32) >> 4;
+          mma_tf32_ss(ts, dqh + oq, dkh + okk, id_s, ks > 0);
+          mma_tf32_ss(ts, dqh + oq, dkl + okk, id_s, 1);
+          mma_tf32_ss(ts, dql + oq, dkh + okk, id_s, 1);
         }
-        mma_commit(&sh.s_full[s]);
-        mma_commit(&sh.k_empty[s]);  // K slot free once these MMAs have read it
-        return true;
-      };
-      bool ok = ws_wait(&sh.q_split, 0, &sh) && issue_s(0);
-      for (uint32_t j = 0; ok && j < nblk; ++j) {
-        if (j + 1 < nblk && !issue_s(j + 1)) break;
-        const uint32_t s = j & 1;
-        if (!ws_wait(&sh.p_ready[s], (j >> 1) & 1, &sh) ||
-            !ws_wait(&sh.v_split[s], (j >> 1) & 1, &sh))
+        mma_commit(&sh.s_full[p]);
+        mma_commit(&sh.k_empty[p]);  // the K slot is free once these have read it
+        if (!ws_wait(&sh.p_ready[p], use & 1, &sh) || !ws_wait(&sh.v_full[p], use & 1, &sh))
           break;
         tc_fence_after();
-        // PV(j): a fresh partial per column group, the two groups alternating
-        const uint32_t ph = tm + 128 * s, pl = ph + 64;
-        const uint64_t dvh = smem_desc_sw128b32_mn(smem_addr(base + kWsOffV + s * kWsSlot),
-                                                   kWsKRegion);
-        const uint64_t dvl = dvh + (kWsTile >> 4);
+        // P V(j): a fresh partial per column group, the groups alternating
 #pragma unroll
         for (uint32_t kk = 0; kk < 4; ++kk) {
 #pragma unroll
@@ -480,63 +486,40 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
 #pragma unroll
             for (uint32_t g = 0; g < 2; ++g) {
               const uint32_t ks = 4 * g + kk;
-              const uint32_t a_t = (prod == 2 ? pl : ph) + ks * 8;
-              const uint64_t b_v = (prod == 1 ? dvl : dvh) + ((ks * 1024) >> 4);
-              mma_tf32_ts(tm + 256 + 64 * g, a_t, b_v, id_o, (kk > 0 || prod > 0) ? 1u : 0u);
+              mma_tf32_ts(to + 64 * g, (prod == 2 ? tpl : ts) + ks * 8,
+                          (prod == 1 ? dvl : dvh) + ks * (1024 >> 4), id_o,
+                          (kk > 0 || prod > 0) ? 1u : 0u);
             }
           }
         }
-        mma_commit(&sh.o_done);
-        mma_commit(&sh.v_empty[s]);
-        if (j + 1 == nblk) mma_commit(&sh.o_final);
+        mma_commit(&sh.o_done[p]);
+        mma_commit(&sh.v_empty[p]);
       }
-      // every MMA issued has completed before TMEM is freed
-      mma_commit(&sh.drain);
-      mbar_wait_bounded(&sh.drain, 0, kTcWait);
+      // every MMA this thread issued has completed before TMEM is freed
+      mma_commit(&sh.drain[p]);
+      mbar_wait_bounded(&sh.drain[p], 0, kTcWait);
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ---- split: tf32 hi in place, lo beside it; mask words of partial blocks ----
-    const uint32_t t = tid - 64;  // 0..127, also the query row of the mask words
-    if (nblk > 0) {
-      // every decision to go on is taken by all 128 split threads together
-      // (they meet at named barriers)
-      bool ok = !ws_split_any(!ws_wait(&sh.q_full, 0, &sh));
-      if (ok) {  // rows past the sequence (another head's queries) become 0
-        ws_split(qhi, qlo, kWsQBytes, kWsTQ, q0, q0, int64_t(q0) + nq, t);
-        fence_proxy_async_smem();
-        mbar_arrive(&sh.q_split);
-      }
-      for (uint32_t j = 0; ok && j < nblk; ++j) {
-        const uint32_t s = j & 1, ph = (j >> 1) & 1;
-        const int64_t kb = kb_first + int64_t(j) * kWsKB;
-        uint8_t* ks = base + kWsOffK + s * kWsSlot;
-        uint8_t* vs = base + kWsOffV + s * kWsSlot;
-        if (ws_split_any(!ws_wait(&sh.k_full[s], ph, &sh))) break;
-        ws_split(ks, ks + kWsTile, kWsTile, kWsKB, kb, lo, hi, t);
-        // k_split(j) follows the softmax of block j - 2: it has finished with
-        // this word slot, and no softmax thread still waits for k_split of
-        // block j - 2 (so k_split never runs two phases ahead of a waiter)
-        if (j >= 2 && ws_split_any(!ws_wait(&sh.p_ready[s], ((j - 2) >> 1) & 1, &sh))) break;
-        if (need_words(j))
-          ws_build_words<KEEP, ACTIVE>(a, b, q0, nq, kb, lo, hi, base + kWsOffKeep,
-                                       reinterpret_cast<float*>(base + kWsOffActive),
-                                       words + s * 2 * kWsTQ, t);
-        fence_proxy_async_smem();
-        mbar_arrive(&sh.k_split[s]);
-        if (ws_split_any(!ws_wait(&sh.v_full[s], ph, &sh))) break;
-        ws_split_v(vs, vs + kWsTile, kb, lo, hi, t);
-        fence_proxy_async_smem();
-        mbar_arrive(&sh.v_split[s]);
-      }
+  } else if (warp == 3) {
+    // ---- mask words, up to four blocks ahead of the softmax ----
+    for (uint32_t j = 0; j < nblk; ++j) {
+      const uint32_t s = j % kWsWordSlots;
+      // every softmax thread has read its word of block j - 4 from this slot
+      // (w_free of block j cannot complete before the words of block j exist,
+      // so the parity wait is exact)
+      if (j >= kWsWordSlots &&
+          !ws_wait_warp(&sh.w_free[s], ((j - kWsWordSlots) / kWsWordSlots) & 1, &sh))
+        break;
+      if (need_words(j))
+        ws_build_words<KEEP, ACTIVE>(a, b, q0, nq, kb_first + int64_t(j) * kWsKB, lo, hi,
+                                     words + s * 2 * kWsTQ, lane);
+      mbar_arrive(&sh.w_ready[s]);
     }
   } else {
     // ---- softmax: thread = (query row, column group g of 32 keys) ----
-    const uint32_t g = (warp - 6) >> 2, quarter = warp & 3;
+    const uint32_t g = (warp - 4) >> 2, quarter = warp & 3;
     const uint32_t row = quarter * 32 + lane;
     const uint32_t lane_off = (quarter * 32) << 16;
-    const uint32_t tO = tm + 256 + 64 * g + lane_off;    // this group's PV partial
-    const uint32_t tAcc = tm + 384 + 64 * g + lane_off;  // its f32 sum of the partials
     const int64_t qi = int64_t(q0) + row;
     // this row's keys by the analytic conditions and the CTA's range
     int64_t r_lo = lo, r_hi = qi < L ? hi : lo;
@@ -549,42 +532,58 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
     if (r_hi < r_lo) r_hi = r_lo;
     constexpr float kLog2e = 1.44269504088896341f;
     float m = -INFINITY, l = 0.0f;  // running max (natural units), sum
+    float o[64];                    // this group's output row (f32 sum of the partials)
+#pragma unroll
+    for (int c = 0; c < 64; ++c) o[c] = 0.0f;
     bool inf_row = false, failed = false;
+    // o = (o + partial of the block of parity q) * corr
+    auto drain = [&](uint32_t q, float corr) {
+      const uint32_t tO = tm + 256 + 128 * q + 64 * g + lane_off;
+#pragma unroll
+      for (uint32_t c = 0; c < 64; c += 32) {
+        float pv[32];
+        tmem_ld16(tO + c, pv);
+        tmem_ld16(tO + c + 16, pv + 16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[c + i] = __fmul_rn(__fadd_rn(o[c + i], pv[i]), corr);
+      }
+    };
     for (uint32_t j = 0; j < nblk; ++j) {
-      const uint32_t s = j & 1, ph = (j >> 1) & 1;
+      const uint32_t p = j & 1, ph = (j >> 1) & 1;
       const int64_t k0 = kb_first + int64_t(j) * kWsKB + 32 * g;  // key of column 0
-      const bool nw = need_words(j);
-      if (!ws_wait_warp(&sh.s_full[s], ph, &sh) ||
-          (nw && !ws_wait_warp(&sh.k_split[s], ph, &sh))) {
+      const uint32_t ws = j % kWsWordSlots;
+      if (!ws_wait_warp(&sh.s_full[p], ph, &sh) ||
+          !ws_wait_warp(&sh.w_ready[ws], (j / kWsWordSlots) & 1, &sh)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      const uint32_t word = nw ? words[(s * 2 + g) * kWsTQ + row] : ~0u;
-      const int64_t c_lo64 = max(int64_t(0), min(int64_t(32), r_lo - k0));
-      const int64_t c_hi64 = max(c_lo64, min(int64_t(32), r_hi - k0));
-      const uint32_t c_lo = uint32_t(c_lo64), c_span = uint32_t(c_hi64 - c_lo64);
-      const uint32_t tA = tm + 128 * s + 32 * g + lane_off, tB = tA + 64;
-      float sv[32];
-      {
-        float sa[32], sb[32];
-        tmem_ld16(tA, sa);
-        tmem_ld16(tA + 16, sa + 16);
-        tmem_ld16(tB, sb);
-        tmem_ld16(tB + 16, sb + 16);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[i] = __fmul_rn(__fadd_rn(sa[i], sb[i]), a.scale);
+      uint32_t word = need_words(j) ? words[(ws * 2 + g) * kWsTQ + row] : ~0u;
+      mbar_arrive(&sh.w_free[ws]);
+      {  // keys of the row's interval [r_lo, r_hi) as bits [c_lo, c_lo + c_span)
+        const int64_t c_lo64 = max(int64_t(0), min(int64_t(32), r_lo - k0));
+        const int64_t c_hi64 = max(c_lo64, min(int64_t(32), r_hi - k0));
+        const uint32_t c_lo = uint32_t(c_lo64), c_span = uint32_t(c_hi64 - c_lo64);
+        word &= c_span == 32 ? ~0u : c_span == 0 ? 0u : (((1u << c_span) - 1u) << c_lo);
       }
+      const uint32_t tS = tm + 128 * p + 32 * g + lane_off;
+      float sv[32];
+      tmem_ld16(tS, sv);
+      tmem_ld16(tS + 16, sv + 16);
+      tmem_wait_ld();
       float mb = -INFINITY;
-      if (!BIAS && c_span == 32 && word == ~0u) {  // every key of the span kept
+      if (!BIAS && word == ~0u) {  // every key of the block kept
 #pragma unroll
-        for (uint32_t c = 0; c < 32; ++c) mb = fmaxf(mb, sv[c]);
+        for (uint32_t c = 0; c < 32; ++c) {
+          sv[c] = __fmul_rn(sv[c], a.scale);
+          mb = fmaxf(mb, sv[c]);
+        }
       } else {
 #pragma unroll
         for (uint32_t c = 0; c < 32; ++c) {
-          float sc = sv[c];
-          const bool kept = c - c_lo < c_span && ((word >> c) & 1);
+          float sc = __fmul_rn(sv[c], a.scale);
+          const bool kept = (word >> c) & 1;
           if constexpr (BIAS)  // read only for kept keys: those lie inside the tensor
             if (kept) sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(k0 + c) + uint64_t(L) * b)]);
           sc = kept ? sc : -INFINITY;
@@ -609,8 +608,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
         }
       }
       // p = e^(s - mn) = 2^(s log2e - mn log2e): one FMA and the hardware 2^x
-      // (relative error ~2^-22), split into tf32 hi (over the first S
-      // accumulator) and lo (over the second)
+      // (relative error ~2^-22), split into tf32 hi (over S) and lo
       const float mnl = mn == -INFINITY ? 0.0f : __fmul_rn(mn, kLog2e);
       float ps = 0.0f;
 #pragma unroll
@@ -618,134 +616,87 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
         float phi[16], plo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float p;
-          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(p) : "f"(__fmaf_rn(sv[h + i], kLog2e, -mnl)));
-          ps = __fadd_rn(ps, p);
-          phi[i] = tf32_round_finite(p);
-          plo[i] = __fsub_rn(p, phi[i]);
+          float pr;
+          asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(pr) : "f"(__fmaf_rn(sv[h + i], kLog2e, -mnl)));
+          ps = __fadd_rn(ps, pr);
+          phi[i] = tf32_round_finite(pr);
+          plo[i] = __fsub_rn(pr, phi[i]);
         }
-        tmem_st16(tA + h, phi);
-        tmem_st16(tB + h, plo);
+        tmem_st16(tS + h, phi);
+        tmem_st16(tS + 64 + h, plo);
       }
       l = __fmaf_rn(l, corr, ps);
       m = mn;
-      // the partial of block j - 1 goes into the f32 sum before PV(j)
-      // overwrites it: acc = (acc + partial) * corr. The parity wait is
-      // exact: PV(j-2) has completed (S(j), whose completion this thread has
-      // seen, was issued after it) and PV(j) cannot start before this
-      // thread's P(j).
+      // the partial of block j - 1 goes into o before P V(j + 1) overwrites
+      // it. The parity wait is exact: this thread waited for the partial of
+      // block j - 3 (the previous phase) and P V(j + 1) cannot start before
+      // this thread's P(j + 1).
       if (j > 0) {
-        if (!ws_wait_warp(&sh.o_done, (j - 1) & 1, &sh)) {
+        if (!ws_wait_warp(&sh.o_done[p ^ 1], ((j - 1) >> 1) & 1, &sh)) {
           failed = true;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (uint32_t c = 0; c < 64; c += 32) {
-          float pv[32], av[32];
-          tmem_ld16(tO + c, pv);
-          tmem_ld16(tO + c + 16, pv + 16);
-          if (j > 1) {
-            tmem_ld16(tAcc + c, av);
-            tmem_ld16(tAcc + c + 16, av + 16);
-          }
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            av[i] = __fmul_rn(j > 1 ? __fadd_rn(av[i], pv[i]) : pv[i], corr);
-          tmem_st16(tAcc + c, av);
-          tmem_st16(tAcc + c + 16, av + 16);
-        }
+        drain(p ^ 1, corr);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&sh.p_ready[s]);
+      mbar_arrive(&sh.p_ready[p]);
     }
-    // o_final, not o_done: PV(nblk - 2) is issued after S(nblk - 1), so a
-    // parity wait on o_done could see the phase of PV(nblk - 2) still open
-    // and take it for the completed phase before
-    if (!failed && nblk > 0) {
-      failed = !ws_wait_warp(&sh.o_final, 0, &sh);
+    if (!failed && nblk > 0) {  // the partial of the last block
+      const uint32_t q = (nblk - 1) & 1;
+      failed = !ws_wait_warp(&sh.o_done[q], ((nblk - 1) >> 1) & 1, &sh);
       tc_fence_after();
+      if (!failed) drain(q, 1.0f);
     }
     if (!ws_softmax_any(failed)) {
-      // merge the two column groups through the (now idle) K ring: group g
-      // keeps its own half of the channels (acc + last partial) and hands
-      // the other half over
-      float* xo = reinterpret_cast<float*>(base + kWsOffK);  // [group][row][33]
-      float* xm = xo + 2 * kWsTQ * 33;
-      float* xl = xm + 2 * kWsTQ;
-      int* xi = reinterpret_cast<int*>(xl + 2 * kWsTQ);
-      const uint32_t other = 1 - g;
-      float own[32];
+      // merge the two column groups and write the output through shared
+      // memory (the idle K and V rings): every thread leaves its row of O_g
+      // and m_g, l_g there; then the 256 threads take 16-byte output chunks
+      // in a rolled loop (code that runs once per CTA stays small)
+      float* xo = reinterpret_cast<float*>(base + kWsOffK);  // [group][row][kWsStage]
+      float* xs = xo + 2 * kWsTQ * kWsStage;                 // m, l: [group][row]
+      int* xi = reinterpret_cast<int*>(xs + 4 * kWsTQ);      // +inf seen: [group][row]
 #pragma unroll
-      for (uint32_t h = 0; h < 2; ++h) {
-        float v[32];
-        if (nblk > 0) {  // uniform over the CTA: every lane joins the .aligned loads
-          float av[32];
-          tmem_ld16(tO + 32 * h, v);
-          tmem_ld16(tO + 32 * h + 16, v + 16);
-          if (nblk > 1) {
-            tmem_ld16(tAcc + 32 * h, av);
-            tmem_ld16(tAcc + 32 * h + 16, av + 16);
-          }
-          tmem_wait_ld();
-          if (nblk > 1) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(av[i], v[i]);
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-        }
-        if (h == g) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) own[i] = v[i];
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) xo[(g * kWsTQ + row) * 33 + i] = v[i];
-        }
-      }
-      xm[g * kWsTQ + row] = m;
-      xl[g * kWsTQ + row] = l;
+      for (uint32_t c = 0; c < 64; c += 4)
+        *reinterpret_cast<float4*>(xo + (g * kWsTQ + row) * kWsStage + c) =
+            make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+      xs[g * kWsTQ + row] = m;
+      xs[2 * kWsTQ + g * kWsTQ + row] = l;
       xi[g * kWsTQ + row] = inf_row;
       ws_softmax_sync();
-      const float mo = xm[other * kWsTQ + row], lo_o = xl[other * kWsTQ + row];
-      const bool inf_any = inf_row || xi[other * kWsTQ + row] != 0;
-      const float mx = fmaxf(m, mo);
-      const float fs = m == -INFINITY ? 0.0f : expf(m - mx);
-      const float fo = mo == -INFINITY ? 0.0f : expf(mo - mx);
-      const float lsum = __fadd_rn(__fmul_rn(l, fs), __fmul_rn(lo_o, fo));
-      const bool empty = nblk == 0 || lsum == 0.0f || inf_any;
-      const float ev = a.empty_nan ? NAN : 0.0f;
-      const float rl = __frcp_rn(lsum);
-#pragma unroll
-      for (uint32_t c = 0; c < 32; ++c) {
-        const float v = __fadd_rn(__fmul_rn(own[c], fs),
-                                  __fmul_rn(xo[(other * kWsTQ + row) * 33 + c], fo));
-        own[c] = empty ? ev : __fmul_rn(v, rl);
+      // per-row factors, once per row: O = (O_0 f0 + O_1 f1) / l
+      float* xf = xs + 4 * kWsTQ + 2 * kWsTQ;  // past xi: [row][4] = f0, f1, 1 / l, empty
+      if (g == 0) {
+        const float m1 = xs[kWsTQ + row], l1 = xs[3 * kWsTQ + row];
+        const float mx = fmaxf(m, m1);
+        const float f0 = m == -INFINITY ? 0.0f : expf(m - mx);
+        const float f1 = m1 == -INFINITY ? 0.0f : expf(m1 - mx);
+        const float lsum = __fadd_rn(__fmul_rn(l, f0), __fmul_rn(l1, f1));
+        const bool empty = nblk == 0 || lsum == 0.0f || inf_row || xi[kWsTQ + row] != 0;
+        *reinterpret_cast<float4*>(xf + 4 * row) =
+            make_float4(f0, f1, __frcp_rn(lsum), empty ? 1.0f : 0.0f);
       }
-      // feature-contiguous output rows (the Laya block's and the attention
-      // core's layouts): staged in the idle V ring, then written as whole
-      // 256-byte rows; any other layout element by element
+      ws_softmax_sync();
       const bool vec = a.out_feat == 1 && (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                        a.out_tok % 4 == 0 && a.out_batch % 4 == 0 &&
                        (!a.gate || ((reinterpret_cast<uintptr_t>(a.gate) & 15) == 0 &&
                                     a.gate_offset % 4 == 0));
-      if (vec) {
-        float* stage = reinterpret_cast<float*>(base + kWsOffV);  // [row][kWsStage]
-#pragma unroll
-        for (uint32_t c = 0; c < 32; c += 4)
-          *reinterpret_cast<float4*>(stage + row * kWsStage + 32 * g + c) =
-              make_float4(own[c], own[c + 1], own[c + 2], own[c + 3]);
-        ws_softmax_sync();
-        const uint32_t ts = tid - 192;  // 0..255
-#pragma unroll
-        for (uint32_t i = 0; i < 8; ++i) {
-          const uint32_t idx = ts + 256 * i, r = idx >> 4, c4 = (idx & 15) * 4;
-          const uint32_t qr = q0 + r;
-          if (qr >= L) continue;
-          float4 v4 = *reinterpret_cast<const float4*>(stage + r * kWsStage + c4);
+      const float ev = a.empty_nan ? NAN : 0.0f;
+#pragma unroll 1
+      for (uint32_t idx = tid - 128; idx < kWsTQ * 16; idx += 256) {
+        const uint32_t r = idx >> 4, c4 = (idx & 15) * 4, qr = q0 + r;
+        if (qr >= L) continue;
+        const float4 fr = *reinterpret_cast<const float4*>(xf + 4 * r);
+        const float f0 = fr.x, f1 = fr.y, rl = fr.z;
+        const bool empty = fr.w != 0.0f;
+        const float4 o0 = *reinterpret_cast<const float4*>(xo + r * kWsStage + c4);
+        const float4 o1 = *reinterpret_cast<const float4*>(xo + (kWsTQ + r) * kWsStage + c4);
+        auto mix = [&](float x0, float x1) {
+          return empty ? ev : __fmul_rn(__fadd_rn(__fmul_rn(x0, f0), __fmul_rn(x1, f1)), rl);
+        };
+        float4 v4 = make_float4(mix(o0.x, o1.x), mix(o0.y, o1.y), mix(o0.z, o1.z), mix(o0.w, o1.w));
+        if (vec) {
           const int64_t oi = int64_t(qr) * a.out_tok + int64_t(head) * 64 + c4 +
                              int64_t(b) * a.out_batch;
           if (a.gate) {
@@ -756,11 +707,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
             v4 = make_float4(sg(v4.x, g4.x), sg(v4.y, g4.y), sg(v4.z, g4.z), sg(v4.w, g4.w));
           }
           *reinterpret_cast<float4*>(a.out + oi) = v4;
+        } else {
+          const uint64_t f = uint64_t(head) * 64 + c4;
+          store_out(a, b, qr, f, v4.x);
+          store_out(a, b, qr, f + 1, v4.y);
+          store_out(a, b, qr, f + 2, v4.z);
+          store_out(a, b, qr, f + 3, v4.w);
         }
-      } else if (qi < L) {
-#pragma unroll
-        for (uint32_t c = 0; c < 32; ++c)
-          store_out(a, b, uint32_t(qi), uint64_t(head) * 64 + 32 * g + c, own[c]);
       }
     }
   }

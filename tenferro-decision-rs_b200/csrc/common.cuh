@@ -36,6 +36,12 @@ struct DeviceInfo {
 // The current device's attributes, read once per device.
 const DeviceInfo& device_info(int* status);
 
+// Stream-ordered scratch from a per-device memory pool owned by libtfx (the
+// caller's default pool is left alone). The pool keeps up to 1 GiB of freed
+// scratch mapped across synchronisations, so calls that need the same
+// scratch again do not map fresh memory; free with cudaFreeAsync.
+cudaError_t scratch_malloc(void** ptr, size_t bytes, cudaStream_t stream);
+
 // ---- argument checks -----------------------------------------------------------
 
 inline bool aligned(const void* p, uintptr_t bytes) {

@@ -125,7 +125,7 @@ int tfx_embedding_f32(const float* table, const int64_t* ids_host, float* out, i
   if (st != TFX_OK) return st;
   int64_t* ids = nullptr;
   const size_t bytes = size_t(length) * sizeof(int64_t);
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&ids), bytes, s);
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&ids), bytes, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));

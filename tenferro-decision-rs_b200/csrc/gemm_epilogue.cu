@@ -586,7 +586,7 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   const size_t wbytes = round_up(kp * size_t(wrows) * 4, 1024);
   const size_t fbytes = round_up((size_t(a.mtiles) + 1) * 4, 1024);
   uint8_t* scratch = nullptr;
-  cudaError_t e = cudaMallocAsync(reinterpret_cast<void**>(&scratch),
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch),
                                   2 * xbytes + 2 * wbytes + fbytes, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();

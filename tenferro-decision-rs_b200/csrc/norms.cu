@@ -1074,7 +1074,7 @@ int rms_split(const char* op, const float* x, const float* w, float* y, uint32_t
   const uint32_t tiles = (rows + tr - 1) / tr;
   if (chunks > 65535) return 1;
   float* partial = nullptr;
-  if (cudaMallocAsync(reinterpret_cast<void**>(&partial), size_t(chunks) * rows * 4, stream) !=
+  if (scratch_malloc(reinterpret_cast<void**>(&partial), size_t(chunks) * rows * 4, stream) !=
       cudaSuccess) {
     cudaGetLastError();  // clear the allocation failure; the caller falls back
     return 1;
@@ -1274,7 +1274,7 @@ int tfx_add_layernorm_ff_f32(const float* a, const float* b, const float* weight
   // Other shapes: the two ops back to back (identical results by construction).
   float* tmp = sum_out;
   if (!tmp) {
-    if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), bytes, s) != cudaSuccess) {
+    if (scratch_malloc(reinterpret_cast<void**>(&tmp), bytes, s) != cudaSuccess) {
       cudaGetLastError();
       return fail(TFX_ERR_CUDA, op, "scratch", "cannot allocate the sum");
     }

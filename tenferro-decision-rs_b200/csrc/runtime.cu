@@ -75,6 +75,34 @@ const DeviceInfo& device_info(int* status) {
   return g_info[dev];
 }
 
+namespace {
+cudaMemPool_t g_pool[kMaxDevices];
+std::once_flag g_pool_once[kMaxDevices];
+}  // namespace
+
+cudaError_t scratch_malloc(void** ptr, size_t bytes, cudaStream_t stream) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= kMaxDevices) return cudaMallocAsync(ptr, bytes, stream);
+  std::call_once(g_pool_once[dev], [dev] {
+    cudaMemPoolProps props = {};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      cudaGetLastError();
+      return;  // scratch then comes from the device's default pool
+    }
+    uint64_t keep = uint64_t(1) << 30;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    g_pool[dev] = pool;
+  });
+  if (g_pool[dev] == nullptr) return cudaMallocAsync(ptr, bytes, stream);
+  return cudaMallocFromPoolAsync(ptr, bytes, g_pool[dev], stream);
+}
+
 }  // namespace tfx
 
 extern "C" {

@@ -35,11 +35,6 @@ __device__ __forceinline__ float tf32_round_finite(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// Byte offset of (row r, value k < 32) in a K-major 128-byte-swizzled region.
-__device__ __forceinline__ uint32_t sw128_offset(uint32_t r, uint32_t k) {
-  return r * 128 + (((k >> 2) ^ (r & 7)) << 4) + ((k & 3) << 2);
-}
-
 // Shared-memory matrix descriptor for a K-major SW128 operand starting at
 // shared address `addr` (1024-byte atoms; +32 bytes per K step allowed).
 // Fields: start >> 4 [0,14), leading byte offset 1 (unused for swizzled
@@ -73,11 +68,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t addr) {
 __device__ __forceinline__ uint64_t smem_desc_sw128b32_mn(uint32_t addr, uint32_t mn_stride) {
   return uint64_t((addr >> 4) & 0x3FFF) | (uint64_t((mn_stride >> 4) & 0x3FFF) << 16) |
          (uint64_t(512 >> 4) << 32) | (uint64_t(1) << 46) | (uint64_t(1) << 61);
-}
-
-// Byte offset of 16-byte chunk c (< 8) of row r in that layout.
-__device__ __forceinline__ uint32_t sw128b32_chunk(uint32_t r, uint32_t c) {
-  return r * 128 + ((((c >> 1) ^ (r & 3)) << 5) | ((c & 1) << 4));
 }
 
 // Instruction descriptor of tcgen05.mma.kind::tf32, f32 accumulate, both
