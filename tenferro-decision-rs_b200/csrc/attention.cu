@@ -586,9 +586,18 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   const size_t qimg_bytes = size_t(nbh) * lq * 512;
   const size_t kimg_bytes = size_t(nbh) * lk * 512;
   const size_t flag_bytes = pre_flags ? 0 : (size_t(nbh) + 255) / 256 * 256;
+  // the mask digest (keep / active): 1 KB of words and one summary byte per
+  // (batch, query tile, key tile)
+  const bool mask = a.keep || a.active;
+  const uint32_t nqt = lq / kWsTQ, nkt = lk / kWsKB;
+  const size_t digest_tiles = mask ? size_t(batch) * nqt * nkt : 0;
+  const size_t words_bytes = digest_tiles * 1024;
+  const size_t summary_bytes = (digest_tiles + 255) / 256 * 256;
   uint8_t* scratch = nullptr;
   cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch),
-                                 flag_bytes + qimg_bytes + 2 * kimg_bytes, stream);
+                                 flag_bytes + qimg_bytes + 2 * kimg_bytes + words_bytes +
+                                     summary_bytes,
+                                 stream);
   if (e == cudaSuccess && flag_bytes) e = cudaMemsetAsync(scratch, 0, nbh, stream);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -598,31 +607,34 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   uint8_t* qimg = scratch + flag_bytes;
   uint8_t* kimg = qimg + qimg_bytes;
   uint8_t* vimg = kimg + kimg_bytes;
+  uint32_t* words = reinterpret_cast<uint32_t*>(vimg + kimg_bytes);
+  uint8_t* summary = reinterpret_cast<uint8_t*>(words) + words_bytes;
   const uint64_t total = uint64_t(nbh) * lq * 16;
   const unsigned blocks = unsigned(std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 16));
   int rc = launch_kernel(op, attn_img_split_kernel, dim3(blocks), dim3(256), 0, stream, 1, a.q,
                          a.k, a.v, qimg, kimg, vimg, a.length, lq, lk, total, flags);
+  if (rc == TFX_OK && mask)
+    rc = launch_kernel(op, attn_keep_digest_kernel, dim3(nkt, nqt, batch), dim3(32), 0, stream, 1,
+                       a, nqt, nkt, words, summary);
   if (rc == TFX_OK) {
     a.vflags = pre_flags ? pre_flags : flags;
     a.vflag_mode = 1;
-    const dim3 grid(lq / kWsTQ, a.heads, batch);
+    const dim3 grid(nqt, a.heads, batch);
     auto run = [&](auto kernel) -> int {
       const cudaError_t e2 = cudaFuncSetAttribute(
           kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
       if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
       return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1,
                            static_cast<const uint8_t*>(qimg), static_cast<const uint8_t*>(kimg),
-                           static_cast<const uint8_t*>(vimg), lk / kWsKB, a);
+                           static_cast<const uint8_t*>(vimg), nkt,
+                           static_cast<const uint32_t*>(words),
+                           static_cast<const uint8_t*>(summary), a);
     };
-    switch ((a.keep ? 4 : 0) | (a.bias ? 2 : 0) | (a.active ? 1 : 0)) {
-      case 0: rc = run(attn_ws_kernel<false, false, false>); break;
-      case 1: rc = run(attn_ws_kernel<false, false, true>); break;
-      case 2: rc = run(attn_ws_kernel<false, true, false>); break;
-      case 3: rc = run(attn_ws_kernel<false, true, true>); break;
-      case 4: rc = run(attn_ws_kernel<true, false, false>); break;
-      case 5: rc = run(attn_ws_kernel<true, false, true>); break;
-      case 6: rc = run(attn_ws_kernel<true, true, false>); break;
-      default: rc = run(attn_ws_kernel<true, true, true>); break;
+    switch ((mask ? 2 : 0) | (a.bias ? 1 : 0)) {
+      case 0: rc = run(attn_ws_kernel<false, false>); break;
+      case 1: rc = run(attn_ws_kernel<false, true>); break;
+      case 2: rc = run(attn_ws_kernel<true, false>); break;
+      default: rc = run(attn_ws_kernel<true, true>); break;
     }
   }
   if (rc == TFX_OK) {

@@ -24,17 +24,20 @@
 //      regions of 8 KB, hi then lo (32 KB).
 // Rows past the sequence are zero, so no tile holds another head's values.
 //
-// Roles (12 warps):
+// Masks. The keep and active masks do not depend on the head, so
+// attn_keep_digest_kernel condenses them once per call: per (batch, query
+// tile, 64-key block) one 32-bit word per (query row, column group) and a
+// summary byte (some / every (query, key) kept). A CTA narrows its key range
+// from the summary row and its softmax threads load their words directly.
+//
+// Roles (11 warps):
 //   warp 0      bulk copies: Q once, K and V of each 64-key block into
 //               two-slot rings;
 //   warps 1, 2  MMA issuers, one per block parity: issuer p computes S(j) and
 //               P V(j) of the blocks j = p mod 2 in program order, so the
 //               buffers that S(j + 2) overwrites are read by P V(j) of the
 //               same thread (tcgen05.mma of one thread run in order);
-//   warp 3      mask words: the keep / active masks of a partial block packed
-//               into one 32-bit word per (query row, column group), up to
-//               four blocks ahead of the softmax;
-//   warps 4-11  softmax: thread = (query row, column group g of 32 keys).
+//   warps 3-10  softmax: thread = (query row, column group g of 32 keys).
 //
 // TMEM (512 columns, one CTA per SM): block j (p = j & 1) has S, then P hi,
 // in columns 128 p + [0, 64), P lo in 128 p + [64, 128), and its P V partial
@@ -54,7 +57,7 @@
 // which ends the other roles' waits; the copy warp then waits for the copies
 // it issued and each issuer for its MMAs before TMEM is freed.
 
-constexpr int kWsThreads = 384;
+constexpr int kWsThreads = 352;
 constexpr int kWsTQ = 128;                  // queries per CTA
 constexpr int kWsKB = 64;                   // keys per block
 constexpr uint32_t kWsQRegion = 16384;      // 128 rows x 128 bytes
@@ -65,9 +68,7 @@ constexpr uint32_t kWsSlot = 2 * kWsTile;        // hi + lo
 constexpr uint32_t kWsOffQlo = kWsQPlane;
 constexpr uint32_t kWsOffK = 2 * kWsQPlane;
 constexpr uint32_t kWsOffV = kWsOffK + 2 * kWsSlot;
-constexpr uint32_t kWsWordSlots = 4;       // mask-word slots (blocks in flight)
-constexpr uint32_t kWsOffWords = kWsOffV + 2 * kWsSlot;     // [slot][group][row] u32
-constexpr uint32_t kWsSmem = kWsOffWords + kWsWordSlots * 2 * kWsTQ * 4 + 1024;  // + slack
+constexpr uint32_t kWsSmem = kWsOffV + 2 * kWsSlot + 1024;  // + alignment slack
 constexpr float kWsRescale = 8.0f;          // natural-log headroom before m moves
 constexpr uint32_t kWsStage = 68;           // output staging row stride (floats)
 
@@ -75,11 +76,9 @@ struct WsShared {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
   uint64_t s_full[2], p_ready[2], o_done[2], drain[2];
-  uint64_t w_ready[kWsWordSlots], w_free[kWsWordSlots];
   uint32_t tmem_base;
   int abort;
   int kmin, kmax;
-  unsigned long long notfull;
 };
 
 // Byte offsets inside the tile images (and inside the shared-memory copies
@@ -186,91 +185,6 @@ __global__ void __launch_bounds__(256) attn_img_split_kernel(
   }
 }
 
-// Keep-mask scan over the keys [lo, hi) for the queries [q0, q0 + nq): narrows
-// [lo, hi) to the keys some query keeps and returns one bit per 64-key block
-// (block index kj / 64 < 64), set when the mask keeps every (query, key) of
-// the block. Every thread of the CTA gets the results. Eight threads read one
-// key's 128 query bytes as 16-byte words (keep[q + L*(k + L*b)]: the queries
-// of a key are contiguous); each thread issues its loads for twelve keys before
-// using any of them, and the results are reduced per warp, then once per warp
-// in shared memory.
-__device__ unsigned long long ws_keep_scan(const AttnArgs& a, uint32_t b, uint32_t q0,
-                                           uint32_t nq, int64_t* lo, int64_t* hi,
-                                           WsShared& sh) {
-  if (threadIdx.x == 0) {
-    sh.kmin = 0x7fffffff;
-    sh.kmax = -1;
-    sh.notfull = 0;
-  }
-  __syncthreads();
-  const uint64_t L = a.length;
-  const uint32_t c = threadIdx.x & 7;  // 16-query chunk of the row
-  const uint32_t i0 = c * 16, i1 = min(nq, i0 + 16);
-  const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && i1 - i0 == 16;
-  const uint32_t per = blockDim.x >> 3;  // keys per pass
-  constexpr int U = 12;
-  int kmin = 0x7fffffff, kmax = -1;
-  unsigned long long nf = 0;
-  if (i0 < i1) {
-    for (int64_t base = *lo + (threadIdx.x >> 3); base < *hi; base += int64_t(per) * U) {
-      uint4 w[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t kj = base + int64_t(u) * per;
-        w[u] = make_uint4(0, 0, 0, 0);
-        if (vec && kj < *hi)
-          w[u] = __ldg(reinterpret_cast<const uint4*>(a.keep + uint64_t(q0) + i0 +
-                                                      L * (uint64_t(kj) + L * b)));
-      }
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t kj = base + int64_t(u) * per;
-        if (kj >= *hi) break;
-        bool any = false, all = true;
-        if (vec) {
-          any = (w[u].x | w[u].y | w[u].z | w[u].w) != 0;
-          auto zero_byte = [](uint32_t x) { return ((x - 0x01010101u) & ~x & 0x80808080u) != 0; };
-          all = !(zero_byte(w[u].x) || zero_byte(w[u].y) || zero_byte(w[u].z) || zero_byte(w[u].w));
-        } else {
-          const uint8_t* row = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
-          for (uint32_t i = i0; i < i1; ++i) {
-            const bool kk = row[i] != 0;
-            any |= kk;
-            all &= kk;
-          }
-        }
-        if (any) {
-          kmin = min(kmin, int(kj));
-          kmax = max(kmax, int(kj));
-        }
-        if (!all && (kj >> 6) < 64) nf |= 1ull << (kj >> 6);
-      }
-    }
-  }
-  kmin = __reduce_min_sync(0xffffffffu, kmin);
-  kmax = __reduce_max_sync(0xffffffffu, kmax);
-  const uint32_t nf_lo = __reduce_or_sync(0xffffffffu, uint32_t(nf));
-  const uint32_t nf_hi = __reduce_or_sync(0xffffffffu, uint32_t(nf >> 32));
-  if ((threadIdx.x & 31) == 0) {
-    if (kmax >= 0) {
-      atomicMin(&sh.kmin, kmin);
-      atomicMax(&sh.kmax, kmax);
-    }
-    const unsigned long long m = (uint64_t(nf_hi) << 32) | nf_lo;
-    if (m) atomicOr(&sh.notfull, m);
-  }
-  __syncthreads();
-  const int first = sh.kmin, last = sh.kmax;
-  const unsigned long long notfull = sh.notfull;
-  if (first > last) {
-    *hi = *lo;
-  } else {
-    *lo = first;
-    *hi = int64_t(last) + 1;
-  }
-  return ~notfull;
-}
-
 // Bit i of the result: byte i of the 16 bytes w is non-zero.
 __device__ __forceinline__ uint32_t nonzero_bytes16(uint4 w) {
   auto nib = [](uint32_t x) {
@@ -295,68 +209,89 @@ __device__ __forceinline__ uint32_t warp_transpose32(uint32_t x, uint32_t lane) 
   return x;
 }
 
-// Mask words of the 64-key block at kb, built by one warp: bit c of
-// words[g * 128 + row] is set when key kb + 32 g + c is in [lo, hi), the keep
-// tensor keeps (query q0 + row, key) and the key is active. Lane c reads the
-// 128 query bytes of keys kb + c and kb + 32 + c (contiguous in
-// keep[q + L*(k + L*b)]) as sixteen 16-byte loads, all issued before any is
-// used, turns them into 32-row masks, and a bit transpose of each 32 x 32
-// block leaves row r's word in lane r.
-template <bool KEEP, bool ACTIVE>
-__device__ __forceinline__ void ws_build_words(const AttnArgs& a, uint32_t b, uint32_t q0,
-                                               uint32_t nq, int64_t kb, int64_t lo, int64_t hi,
-                                               uint32_t* words, uint32_t lane) {
+// Digest of the keep / active masks, the same for every head: one warp per
+// (64-key block kt, 128-query tile qt, batch b) writes
+//   words[((b * nqt + qt) * nkt + kt) * 256 + 128 g + row]: bit c set when
+//     key 64 kt + 32 g + c lies in the tile's analytic range, the keep tensor
+//     keeps (query 128 qt + row, key) and the key is active;
+//   summary[(b * nqt + qt) * nkt + kt]: bit 0 = some (query, key) of the block
+//     is kept, bit 1 = every (query, key) of the block inside the analytic
+//     range is kept (the attention kernel then needs no words).
+// Lane c reads the 128 query bytes of keys 64 kt + c and 64 kt + 32 + c
+// (contiguous in keep[q + L*(k + L*b)]) as sixteen 16-byte loads, turns them
+// into 32-row masks, and a bit transpose of each 32 x 32 block leaves row r's
+// word in lane r.
+__global__ void __launch_bounds__(32) attn_keep_digest_kernel(AttnArgs a, uint32_t nqt,
+                                                              uint32_t nkt, uint32_t* words,
+                                                              uint8_t* summary) {
+  pdl_enter();
+  const uint32_t kt = blockIdx.x, qt = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
   const uint64_t L = a.length;
-  const bool vec = L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 && nq == kWsTQ;
-  bool kon[2];
+  const uint32_t q0 = qt * kWsTQ, nq = min(uint32_t(kWsTQ), uint32_t(L) - q0);
+  int64_t lo, hi;
+  analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
+  const int64_t kb = int64_t(kt) * kWsKB;
+  const bool vec = a.keep && L % 16 == 0 && (reinterpret_cast<uintptr_t>(a.keep) & 15) == 0 &&
+                   nq == kWsTQ;
+  bool kin[2], kon[2];
   uint4 w[2][8];
 #pragma unroll
   for (uint32_t g = 0; g < 2; ++g) {
     const int64_t kj = kb + 32 * g + lane;
-    kon[g] = kj >= lo && kj < hi;
-    if constexpr (ACTIVE)
-      if (kon[g]) kon[g] = a.active[uint64_t(b) * L + uint64_t(kj)] != 0.0f;
+    kin[g] = kj >= lo && kj < hi;
+    kon[g] = kin[g];
+    if (a.active && kon[g]) kon[g] = a.active[uint64_t(b) * L + uint64_t(kj)] != 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) w[g][i] = make_uint4(0, 0, 0, 0);
-    if (KEEP && vec && kon[g]) {
+    if (vec && kon[g]) {
       const uint4* src = reinterpret_cast<const uint4*>(a.keep + uint64_t(q0) +
                                                         L * (uint64_t(kj) + L * b));
 #pragma unroll
       for (int i = 0; i < 8; ++i) w[g][i] = __ldg(src + i);
     }
   }
+  uint32_t* out = words + ((uint64_t(b) * nqt + qt) * nkt + kt) * 256;
+  bool any = false, all = true;
 #pragma unroll
   for (uint32_t g = 0; g < 2; ++g) {
     const int64_t kj = kb + 32 * g + lane;
+    const uint32_t in_keys = __ballot_sync(0xffffffffu, kin[g]);  // keys of the analytic range
 #pragma unroll
     for (int rc = 0; rc < 4; ++rc) {
+      const uint32_t n = nq > 32u * rc ? min(32u, nq - 32u * rc) : 0u;
+      const uint32_t rows = n == 32 ? ~0u : ((1u << n) - 1u);
       uint32_t rm = 0;  // bit r: query row 32 rc + r kept for this lane's key
       if (kon[g]) {
-        if constexpr (KEEP) {
-          if (vec) {
-            rm = nonzero_bytes16(w[g][2 * rc]) | (nonzero_bytes16(w[g][2 * rc + 1]) << 16);
-          } else {
-            const uint8_t* src = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
-            for (uint32_t r = 0; r < 32 && 32 * rc + r < nq; ++r)
-              if (src[32 * rc + r] != 0) rm |= 1u << r;
-          }
+        if (!a.keep) {
+          rm = rows;
+        } else if (vec) {
+          rm = nonzero_bytes16(w[g][2 * rc]) | (nonzero_bytes16(w[g][2 * rc + 1]) << 16);
         } else {
-          const uint32_t n = nq > 32u * rc ? min(32u, nq - 32u * rc) : 0u;
-          rm = n == 32 ? ~0u : ((1u << n) - 1u);
+          const uint8_t* src = a.keep + uint64_t(q0) + L * (uint64_t(kj) + L * b);
+          for (uint32_t r = 0; r < n; ++r)
+            if (src[32 * rc + r] != 0) rm |= 1u << r;
         }
       }
-      words[g * kWsTQ + 32 * rc + lane] = warp_transpose32(rm, lane);
+      const uint32_t word = warp_transpose32(rm, lane);
+      out[g * kWsTQ + 32 * rc + lane] = word;
+      const bool row_valid = 32u * rc + lane < nq;
+      any |= word != 0;
+      all &= !row_valid || (word & in_keys) == in_keys;
     }
   }
-  __syncwarp();
+  any = __any_sync(0xffffffffu, any);
+  all = __all_sync(0xffffffffu, all);
+  if (lane == 0) summary[(uint64_t(b) * nqt + qt) * nkt + kt] = uint8_t(any) | uint8_t(all) << 1;
 }
 
 // qimg / kimg / vimg: the tile images of attn_img_split_kernel, nkt key tiles
-// per head (gridDim.x query tiles).
-template <bool KEEP, bool BIAS, bool ACTIVE>
+// per head (gridDim.x query tiles). MASK: a keep or active mask is given, and
+// words / summary are its digest (attn_keep_digest_kernel).
+template <bool MASK, bool BIAS>
 __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
     const uint8_t* __restrict__ qimg, const uint8_t* __restrict__ kimg,
-    const uint8_t* __restrict__ vimg, uint32_t nkt, AttnArgs a) {
+    const uint8_t* __restrict__ vimg, uint32_t nkt, const uint32_t* __restrict__ words,
+    const uint8_t* __restrict__ summary, AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t ws_smem[];
   __shared__ WsShared sh;
   pdl_enter();
@@ -369,7 +304,6 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws_smem) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* qhi = base;
-  uint32_t* words = reinterpret_cast<uint32_t*>(base + kWsOffWords);  // [slot][group][row]
 
   if (tid == 0) {
     mbar_init(&sh.q_full, 1);
@@ -383,11 +317,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       mbar_init(&sh.o_done[s], 1);
       mbar_init(&sh.drain[s], 1);
     }
-    for (uint32_t s = 0; s < kWsWordSlots; ++s) {
-      mbar_init(&sh.w_ready[s], 32);
-      mbar_init(&sh.w_free[s], 256);
-    }
     sh.abort = 0;
+    sh.kmin = 0x7fffffff;
+    sh.kmax = -1;
     mbar_init_fence();
   }
   __syncthreads();
@@ -400,18 +332,35 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
 
   int64_t lo, hi;
   analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
-  unsigned long long full_bits = ~0ull;
-  if (KEEP && lo < hi) full_bits = ws_keep_scan(a, b, q0, nq, &lo, &hi, sh);
+  // the digest of this (batch, query tile): its key blocks' summary bytes
+  // and mask words
+  const uint64_t drow = uint64_t(b) * gridDim.x + blockIdx.x;
+  const uint8_t* srow = MASK ? summary + drow * nkt : nullptr;
+  const uint32_t* wrow = MASK ? words + drow * nkt * 256 : nullptr;
+  if (MASK && lo < hi) {  // narrow [lo, hi) to the blocks that keep some (query, key)
+    int first = 0x7fffffff, last = -1;
+    for (int64_t kt = lo / kWsKB + tid; kt * kWsKB < hi; kt += kWsThreads)
+      if (__ldg(srow + kt) & 1) {
+        first = min(first, int(kt));
+        last = max(last, int(kt));
+      }
+    first = __reduce_min_sync(0xffffffffu, first);
+    last = __reduce_max_sync(0xffffffffu, last);
+    if (lane == 0 && last >= 0) {
+      atomicMin(&sh.kmin, first);
+      atomicMax(&sh.kmax, last);
+    }
+    __syncthreads();
+    if (sh.kmax < 0) {
+      hi = lo;
+    } else {
+      lo = max(lo, int64_t(sh.kmin) * kWsKB);
+      hi = min(hi, (int64_t(sh.kmax) + 1) * kWsKB);
+    }
+  }
   const int64_t kb_first = lo / kWsKB * kWsKB;
   const uint32_t nblk = kb_first < hi ? uint32_t((hi - kb_first + kWsKB - 1) / kWsKB) : 0;
   const uint32_t kt0 = uint32_t(kb_first / kWsKB);  // key tile of block 0
-  // mask words are built (and read) for block j when this holds
-  auto need_words = [&](uint32_t j) {
-    if (ACTIVE) return true;
-    if (!KEEP) return false;
-    const uint32_t blk = kt0 + j;
-    return !(blk < 64 && ((full_bits >> blk) & 1));
-  };
 
   if (warp == 1) tmem_alloc(&sh.tmem_base, 512);
   tc_fence_before();
@@ -500,24 +449,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       mbar_wait_bounded(&sh.drain[p], 0, kTcWait);
     }
     __syncwarp();
-  } else if (warp == 3) {
-    // ---- mask words, up to four blocks ahead of the softmax ----
-    for (uint32_t j = 0; j < nblk; ++j) {
-      const uint32_t s = j % kWsWordSlots;
-      // every softmax thread has read its word of block j - 4 from this slot
-      // (w_free of block j cannot complete before the words of block j exist,
-      // so the parity wait is exact)
-      if (j >= kWsWordSlots &&
-          !ws_wait_warp(&sh.w_free[s], ((j - kWsWordSlots) / kWsWordSlots) & 1, &sh))
-        break;
-      if (need_words(j))
-        ws_build_words<KEEP, ACTIVE>(a, b, q0, nq, kb_first + int64_t(j) * kWsKB, lo, hi,
-                                     words + s * 2 * kWsTQ, lane);
-      mbar_arrive(&sh.w_ready[s]);
-    }
   } else {
     // ---- softmax: thread = (query row, column group g of 32 keys) ----
-    const uint32_t g = (warp - 4) >> 2, quarter = warp & 3;
+    const uint32_t g = (warp - 3) >> 2, quarter = warp & 3;
     const uint32_t row = quarter * 32 + lane;
     const uint32_t lane_off = (quarter * 32) << 16;
     const int64_t qi = int64_t(q0) + row;
@@ -552,15 +486,19 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
     for (uint32_t j = 0; j < nblk; ++j) {
       const uint32_t p = j & 1, ph = (j >> 1) & 1;
       const int64_t k0 = kb_first + int64_t(j) * kWsKB + 32 * g;  // key of column 0
-      const uint32_t ws = j % kWsWordSlots;
-      if (!ws_wait_warp(&sh.s_full[p], ph, &sh) ||
-          !ws_wait_warp(&sh.w_ready[ws], (j / kWsWordSlots) & 1, &sh)) {
+      // this row's mask word of the block (its loads travel during the wait)
+      uint32_t word = ~0u;
+      uint8_t smy = 2;
+      if (MASK) {
+        word = __ldg(wrow + (kt0 + j) * 256 + g * kWsTQ + row);
+        smy = __ldg(srow + kt0 + j);
+      }
+      if (!ws_wait_warp(&sh.s_full[p], ph, &sh)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      uint32_t word = need_words(j) ? words[(ws * 2 + g) * kWsTQ + row] : ~0u;
-      mbar_arrive(&sh.w_free[ws]);
+      if (smy & 2) word = ~0u;  // every (query, key) of the block kept
       {  // keys of the row's interval [r_lo, r_hi) as bits [c_lo, c_lo + c_span)
         const int64_t c_lo64 = max(int64_t(0), min(int64_t(32), r_lo - k0));
         const int64_t c_hi64 = max(c_lo64, min(int64_t(32), r_hi - k0));
@@ -684,7 +622,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
                                     a.gate_offset % 4 == 0));
       const float ev = a.empty_nan ? NAN : 0.0f;
 #pragma unroll 1
-      for (uint32_t idx = tid - 128; idx < kWsTQ * 16; idx += 256) {
+      for (uint32_t idx = tid - 96; idx < kWsTQ * 16; idx += 256) {
         const uint32_t r = idx >> 4, c4 = (idx & 15) * 4, qr = q0 + r;
         if (qr >= L) continue;
         const float4 fr = *reinterpret_cast<const float4*>(xf + 4 * r);
