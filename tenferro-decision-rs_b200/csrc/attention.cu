@@ -29,17 +29,67 @@
 namespace tfx {
 namespace {
 
+// ---- tile images ------------------------------------------------------------------------
+//
+// The tensor-core attention (head_dim 64) reads q, k and v as tf32 hi / lo
+// "tile images": byte for byte the shared-memory layout its MMAs read (layout
+// described in attn_ws.cuh), written once by the Laya prep kernel or by
+// attn_img_split_kernel. Per head: Q in 128-query tiles (hi 32 KB then lo
+// 32 KB), K and V in 64-key tiles (hi 16 KB then lo 16 KB each).
+constexpr int kWsTQ = 128;                  // queries per tile
+constexpr int kWsKB = 64;                   // keys per tile
+constexpr uint32_t kWsQRegion = 16384;      // 128 rows x 128 bytes
+constexpr uint32_t kWsKRegion = 8192;       // 64 rows x 128 bytes
+constexpr uint32_t kWsQPlane = 2 * kWsQRegion;   // Q hi or Q lo
+constexpr uint32_t kWsTile = 2 * kWsKRegion;     // K / V hi or lo
+constexpr uint32_t kWsSlot = 2 * kWsTile;        // hi + lo
+
+// Byte offsets inside the tile images (and inside the shared-memory copies
+// of the tiles), for 4 consecutive channels ch .. ch + 3 (ch % 4 == 0) of
+// row r of the tile.
+__host__ __device__ __forceinline__ uint32_t img_kmajor_off(uint32_t r, uint32_t ch,
+                                                            uint32_t region_bytes) {
+  return (ch >> 5) * region_bytes + r * 128 + ((((ch & 31) >> 2) ^ (r & 7)) << 4);
+}
+__host__ __device__ __forceinline__ uint32_t img_v_off(uint32_t r, uint32_t ch) {
+  return (ch >> 5) * kWsKRegion + r * 128 + ((((ch & 31) >> 3) ^ (r & 3)) << 5) +
+         (((ch & 7) >> 2) << 4);
+}
+
+// hi / lo of 4 values for a tile image: hi = tf32(x), lo = x - hi (exact);
+// a value the tensor cores cannot take (non-finite, or beyond the largest
+// tf32) is kept whole in hi with lo = 0, so hi + lo gives back every value.
+__device__ __forceinline__ void img_split4(float4 x, float4* hi, float4* lo, bool* bad) {
+  constexpr float kMax = 3.4e38f;  // below the largest tf32 (rounding up stays finite)
+  float h[4], l[4];
+  const float v[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool ok = fabsf(v[i]) < kMax;
+    *bad |= !ok;
+    h[i] = ok ? tf32_round_finite(v[i]) : v[i];
+    l[i] = ok ? __fsub_rn(v[i], h[i]) : 0.0f;
+  }
+  *hi = make_float4(h[0], h[1], h[2], h[3]);
+  *lo = make_float4(l[0], l[1], l[2], l[3]);
+}
+
+
 // ---- Laya prep: split + full-width RoPE ------------------------------------------------
 
 // One thread per (token row, head, VEC pairs): q and k pairs (i, i + half)
 // rotated as a*c - b*s, a*s + b*c with every product rounded (lib.rs:
-// 996-1008); v copied.
-template <int VEC>
+// 996-1008); v copied. IMG (head_dim 64, VEC 4): q, k, v go straight into the
+// tensor-core attention's tile images (qimg / kimg / vimg, nqt / nkt tiles
+// per head) instead of the head-major qh / kh / vh.
+template <int VEC, bool IMG = false>
 __global__ void __launch_bounds__(256) laya_prep_kernel(
     const float* __restrict__ qkv, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, float* __restrict__ qh, float* __restrict__ kh,
     float* __restrict__ vh, uint32_t hidden, uint32_t heads, uint32_t length, uint32_t hd,
-    uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len, uint8_t* flags) {
+    uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len, uint8_t* flags,
+    uint8_t* __restrict__ qimg, uint8_t* __restrict__ kimg, uint8_t* __restrict__ vimg,
+    uint32_t nqt, uint32_t nkt) {
   pdl_enter();
   const uint32_t half = hd / 2;
   for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
@@ -86,6 +136,28 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
         ka[j] = __fsub_rn(__fmul_rn(a1, c[j]), __fmul_rn(b1, s[j]));
         kb[j] = __fadd_rn(__fmul_rn(a1, s[j]), __fmul_rn(b1, c[j]));
       }
+    }
+    if constexpr (IMG) {
+      static_assert(VEC == 4, "tile images take 4 channels at a time");
+      const uint64_t bh = uint64_t(b) * heads + head;
+      bool bad = false;
+      auto put = [&](uint8_t* tile, uint32_t plane, uint32_t off, const float* v) {
+        float4 h, lo;
+        img_split4(make_float4(v[0], v[1], v[2], v[3]), &h, &lo, &bad);
+        *reinterpret_cast<float4*>(tile + off) = h;
+        *reinterpret_cast<float4*>(tile + plane + off) = lo;
+      };
+      uint8_t* qt = qimg + (bh * nqt + l / kWsTQ) * (2 * kWsQPlane);
+      const uint32_t rq = l % kWsTQ, rk = l % kWsKB;
+      put(qt, kWsQPlane, img_kmajor_off(rq, i0, kWsQRegion), qa);
+      put(qt, kWsQPlane, img_kmajor_off(rq, half + i0, kWsQRegion), qb);
+      const uint64_t kv = (bh * nkt + l / kWsKB) * kWsSlot;
+      put(kimg + kv, kWsTile, img_kmajor_off(rk, i0, kWsKRegion), ka);
+      put(kimg + kv, kWsTile, img_kmajor_off(rk, half + i0, kWsKRegion), kb);
+      put(vimg + kv, kWsTile, img_v_off(rk, i0), va);
+      put(vimg + kv, kWsTile, img_v_off(rk, half + i0), vb);
+      if (bad && flags) flags[bh] = 1;
+      continue;
     }
     if (flags) {  // heads holding a value the tensor-core attention cannot take
       constexpr float kMax = 3.4e38f;
@@ -198,7 +270,39 @@ struct AttnArgs {
   // then runs on them only (vflag_mode 2); 0 = no routing.
   const uint8_t* vflags;
   int vflag_mode;
+  // head_dim 64 only: q, k, v as tile images (nqt / nkt tiles per head)
+  // instead of the head-major q / k / v, when qimg is set
+  const uint8_t* qimg = nullptr;
+  const uint8_t* kimg = nullptr;
+  const uint8_t* vimg = nullptr;
+  uint32_t nqt = 0, nkt = 0;
 };
+
+// Channels ch .. ch + 3 of row `row` of head bh of q (t = 0), k (1) or v (2):
+// from the head-major tensor, or hi + lo of its tile image (exact: the image
+// keeps hi + lo == x for every value).
+__device__ __forceinline__ float4 attn_ld4(const AttnArgs& a, int t, uint64_t bh, uint32_t row,
+                                           uint32_t ch) {
+  if (a.qimg) {
+    const uint8_t* tile;
+    uint32_t plane, off;
+    if (t == 0) {
+      tile = a.qimg + (bh * a.nqt + row / kWsTQ) * (2 * kWsQPlane);
+      plane = kWsQPlane;
+      off = img_kmajor_off(row % kWsTQ, ch, kWsQRegion);
+    } else {
+      tile = (t == 1 ? a.kimg : a.vimg) + (bh * a.nkt + row / kWsKB) * kWsSlot;
+      plane = kWsTile;
+      off = t == 1 ? img_kmajor_off(row % kWsKB, ch, kWsKRegion) : img_v_off(row % kWsKB, ch);
+    }
+    const float4 h = __ldg(reinterpret_cast<const float4*>(tile + off));
+    const float4 l = __ldg(reinterpret_cast<const float4*>(tile + plane + off));
+    return make_float4(__fadd_rn(h.x, l.x), __fadd_rn(h.y, l.y), __fadd_rn(h.z, l.z),
+                       __fadd_rn(h.w, l.w));
+  }
+  const float* src = t == 0 ? a.q : t == 1 ? a.k : a.v;
+  return ld_stream(reinterpret_cast<const float4*>(src + (bh * a.length + row) * a.hd + ch));
+}
 
 __device__ __forceinline__ bool routed_away(const AttnArgs& a, uint32_t bh) {
   if (a.vflag_mode == 1) return a.vflags[bh] != 0;
@@ -296,7 +400,7 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
   if (routed_away(a, b * a.heads + head)) return;
   const uint32_t L = a.length;
   const uint32_t nq = min(uint32_t(kQT), L - q0);
-  const uint64_t base = (uint64_t(b) * a.heads + head) * L * HD;
+  const uint64_t bh = uint64_t(b) * a.heads + head;
   int64_t lo, hi;
   analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
   if (a.keep && lo < hi) keep_narrow(a, b, q0, nq, &lo, &hi, red);
@@ -304,7 +408,7 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
   for (uint32_t idx = tid; idx < kQT * HD / 4; idx += 256) {
     const uint32_t qq = idx % kQT, h4 = idx / kQT;
     float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (qq < nq) val = ld_stream(reinterpret_cast<const float4*>(a.q + base + uint64_t(q0 + qq) * HD + 4 * h4));
+    if (qq < nq) val = attn_ld4(a, 0, bh, q0 + qq, 4 * h4);
     Qt[(4 * h4 + 0) * kQT + qq] = val.x;
     Qt[(4 * h4 + 1) * kQT + qq] = val.y;
     Qt[(4 * h4 + 2) * kQT + qq] = val.z;
@@ -333,7 +437,7 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
       const uint32_t kk = idx % KB, h4 = idx / KB;
       float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (kb0 + kk < L)
-        val = ld_stream(reinterpret_cast<const float4*>(a.k + base + uint64_t(kb0 + kk) * HD + 4 * h4));
+        val = attn_ld4(a, 1, bh, uint32_t(kb0 + kk), 4 * h4);
       Kt[(4 * h4 + 0) * KB + kk] = val.x;
       Kt[(4 * h4 + 1) * KB + kk] = val.y;
       Kt[(4 * h4 + 2) * KB + kk] = val.z;
@@ -344,7 +448,7 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
       const uint32_t kk = idx / (HD / 4), h4 = idx % (HD / 4);
       float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (kb0 + kk < L)
-        val = ld_stream(reinterpret_cast<const float4*>(a.v + base + uint64_t(kb0 + kk) * HD + 4 * h4));
+        val = attn_ld4(a, 2, bh, uint32_t(kb0 + kk), 4 * h4);
       bad |= !(fabsf(val.x) < INFINITY && fabsf(val.y) < INFINITY && fabsf(val.z) < INFINITY &&
                fabsf(val.w) < INFINITY);
       *reinterpret_cast<float4*>(Vs + kk * HD + 4 * h4) = val;
@@ -564,27 +668,32 @@ static_assert(kWsTQ == kTQ, "the grid tiles the queries by 128");
 // images (and, when pre_flags is null, the per-head flags of values the
 // tensor cores cannot take), attn_ws_kernel computes every unflagged head,
 // attn_flash_kernel the flagged ones. pre_flags: flags already computed on the
-// stream (the Laya prep kernel sets them). Returns 1 when the shape is not
-// covered (nothing launched).
-int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo& dev,
-                   cudaStream_t stream, const uint8_t* pre_flags) {
-  const uint64_t rows = uint64_t(batch) * a.heads * a.length;
-  if (a.hd != 64 || rows >= (uint64_t(1) << 31) || !aligned(a.q, 16) || !aligned(a.k, 16) ||
-      !aligned(a.v, 16) || kWsSmem > size_t(dev.smem_optin))
-    return 1;
+// stream (the Laya prep kernel sets them). When a.qimg is set, the images
+// exist already (the Laya prep kernel wrote them, with pre_flags) and q, k,
+// v are not read. Returns 1 when the shape is not covered (nothing launched).
+bool attn_tc_covers(uint32_t hd, uint64_t rows, const DeviceInfo& dev) {
   // TFX_ATTN_KERNEL=f32: the f32-pipe kernel for every head
   static const bool f32_only = [] {
     const char* e = getenv("TFX_ATTN_KERNEL");
     return e && std::string(e) == "f32";
   }();
-  if (f32_only) return 1;
+  return !f32_only && hd == 64 && rows < (uint64_t(1) << 31) && kWsSmem <= size_t(dev.smem_optin);
+}
+
+int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo& dev,
+                   cudaStream_t stream, const uint8_t* pre_flags) {
+  const uint64_t rows = uint64_t(batch) * a.heads * a.length;
+  const bool have_img = a.qimg != nullptr;
+  if (!attn_tc_covers(a.hd, rows, dev) ||
+      (!have_img && (!aligned(a.q, 16) || !aligned(a.k, 16) || !aligned(a.v, 16))))
+    return 1;
   const uint32_t nbh = batch * a.heads;
   // scratch: the flags (unless given), then the tile images of q, k, v (hi
   // and lo, padded to whole tiles: 512 bytes per padded row and tensor)
   const uint32_t lq = (a.length + kWsTQ - 1) / kWsTQ * kWsTQ;
   const uint32_t lk = (a.length + kWsKB - 1) / kWsKB * kWsKB;
-  const size_t qimg_bytes = size_t(nbh) * lq * 512;
-  const size_t kimg_bytes = size_t(nbh) * lk * 512;
+  const size_t qimg_bytes = have_img ? 0 : size_t(nbh) * lq * 512;
+  const size_t kimg_bytes = have_img ? 0 : size_t(nbh) * lk * 512;
   const size_t flag_bytes = pre_flags ? 0 : (size_t(nbh) + 255) / 256 * 256;
   // the mask digest (keep / active): 1 KB of words and one summary byte per
   // (batch, query tile, key tile)
@@ -604,15 +713,21 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
   uint8_t* flags = pre_flags ? nullptr : scratch;
-  uint8_t* qimg = scratch + flag_bytes;
-  uint8_t* kimg = qimg + qimg_bytes;
-  uint8_t* vimg = kimg + kimg_bytes;
-  uint32_t* words = reinterpret_cast<uint32_t*>(vimg + kimg_bytes);
+  uint8_t* own = scratch + flag_bytes;
+  const uint8_t* qimg = have_img ? a.qimg : own;
+  const uint8_t* kimg = have_img ? a.kimg : own + qimg_bytes;
+  const uint8_t* vimg = have_img ? a.vimg : own + qimg_bytes + kimg_bytes;
+  uint32_t* words = reinterpret_cast<uint32_t*>(own + qimg_bytes + 2 * kimg_bytes);
   uint8_t* summary = reinterpret_cast<uint8_t*>(words) + words_bytes;
-  const uint64_t total = uint64_t(nbh) * lq * 16;
-  const unsigned blocks = unsigned(std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 16));
-  int rc = launch_kernel(op, attn_img_split_kernel, dim3(blocks), dim3(256), 0, stream, 1, a.q,
-                         a.k, a.v, qimg, kimg, vimg, a.length, lq, lk, total, flags);
+  int rc = TFX_OK;
+  if (!have_img) {
+    const uint64_t total = uint64_t(nbh) * lq * 16;
+    const unsigned blocks =
+        unsigned(std::min<uint64_t>((total + 255) / 256, uint64_t(dev.sms) * 16));
+    rc = launch_kernel(op, attn_img_split_kernel, dim3(blocks), dim3(256), 0, stream, 1, a.q, a.k,
+                       a.v, own, own + qimg_bytes, own + qimg_bytes + kimg_bytes, a.length, lq,
+                       lk, total, flags);
+  }
   if (rc == TFX_OK && mask)
     rc = launch_kernel(op, attn_keep_digest_kernel, dim3(nkt, nqt, batch), dim3(32), 0, stream, 1,
                        a, nqt, nkt, words, summary);
@@ -624,9 +739,8 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
       const cudaError_t e2 = cudaFuncSetAttribute(
           kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
       if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
-      return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1,
-                           static_cast<const uint8_t*>(qimg), static_cast<const uint8_t*>(kimg),
-                           static_cast<const uint8_t*>(vimg), nkt,
+      return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1, qimg, kimg,
+                           vimg, nkt,
                            static_cast<const uint32_t*>(words),
                            static_cast<const uint8_t*>(summary), a);
     };
@@ -700,25 +814,31 @@ int attention_wait_timeouts(uint32_t* count) {
   return err == cudaSuccess ? TFX_OK : fail(TFX_ERR_CUDA, "tfx", "wait timeouts", cudaGetErrorString(err));
 }
 
+// img (optional): the tensor-core attention's tile images (q, k, v) to write
+// instead of qh / kh / vh (head_dim 64, vector path only; rows past the
+// sequence are left to attn_img_pad_kernel).
 int laya_prep(const char* op, const float* qkv, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t hidden, int64_t heads, int64_t length,
-              int64_t batch, cudaStream_t stream, uint8_t* flags = nullptr) {
+              int64_t batch, cudaStream_t stream, uint8_t* flags = nullptr,
+              uint8_t* const* img = nullptr) {
   TFX_REQUIRE(hidden >= 0 && heads > 0 && length >= 0 && batch >= 0, op, "shape",
               "extents must be non-negative (heads positive)");
   TFX_REQUIRE(hidden % heads == 0, op, "hidden", "hidden must be a multiple of heads");
   const int64_t hd = hidden / heads;
   TFX_REQUIRE(hd % 2 == 0, op, "head_dim", "head_dim must be even");
   if (hidden == 0 || length == 0 || batch == 0) return TFX_OK;
-  TFX_REQUIRE(qkv && qh && kh && vh, op, "tensors", "null pointer");
+  TFX_REQUIRE(qkv && (img || (qh && kh && vh)), op, "tensors", "null pointer");
   TFX_REQUIRE((cos_t == nullptr) == (sin_t == nullptr), op, "tables",
               "cos and sin tables must both be given or both be null");
   int st = TFX_OK;
   device_info(&st);
   if (st != TFX_OK) return st;
   const int64_t half = hd / 2;
-  const bool v4 = half % 4 == 0 && hidden % 4 == 0 && aligned(qkv, 16) && aligned(qh, 16) &&
-                  aligned(kh, 16) && aligned(vh, 16) &&
+  const bool v4 = half % 4 == 0 && hidden % 4 == 0 && aligned(qkv, 16) &&
+                  (img || (aligned(qh, 16) && aligned(kh, 16) && aligned(vh, 16))) &&
                   (!cos_t || (aligned(cos_t, 16) && aligned(sin_t, 16)));
+  if (img && !(v4 && hd == 64))
+    return fail(TFX_ERR_UNSUPPORTED, op, "layout", "tile images need head_dim 64 and 16-byte rows");
   const int64_t vec = v4 ? 4 : 1;
   const int64_t chunks = half / vec;
   const int64_t total = batch * length * heads * chunks;
@@ -726,13 +846,24 @@ int laya_prep(const char* op, const float* qkv, const float* cos_t, const float*
               "too many elements for one call");
   const unsigned grid = unsigned(std::min<int64_t>((total + 255) / 256, 148 * 16));
   const FastDiv dc{uint32_t(chunks)}, dh{uint32_t(heads)}, dl{uint32_t(length)};
+  uint8_t* const no_img = nullptr;
+  if (img) {
+    const uint32_t nqt = uint32_t((length + kWsTQ - 1) / kWsTQ);
+    const uint32_t nkt = uint32_t((length + kWsKB - 1) / kWsKB);
+    return launch_kernel(op, laya_prep_kernel<4, true>, dim3(grid), dim3(256), 0, stream, 1, qkv,
+                         cos_t, sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads),
+                         uint32_t(length), uint32_t(hd), uint64_t(total), dc, dh, dl, flags,
+                         img[0], img[1], img[2], nqt, nkt);
+  }
   if (v4)
     return launch_kernel(op, laya_prep_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
                          sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
-                         uint32_t(hd), uint64_t(total), dc, dh, dl, flags);
+                         uint32_t(hd), uint64_t(total), dc, dh, dl, flags, no_img, no_img, no_img,
+                         0u, 0u);
   return launch_kernel(op, laya_prep_kernel<1>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
                        sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
-                       uint32_t(hd), uint64_t(total), dc, dh, dl, flags);
+                       uint32_t(hd), uint64_t(total), dc, dh, dl, flags, no_img, no_img, no_img,
+                       0u, 0u);
 }
 
 int jeff_prep(const char* op, const float* q, const float* k, const float* v,
@@ -762,16 +893,18 @@ int jeff_prep(const char* op, const float* q, const float* k, const float* v,
                        vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps);
 }
 
+// img (optional, head_dim 64 with attn_tc_covers): q, k, v as tile images
+// instead of qh / kh / vh.
 int attention(const char* op, const float* qh, const float* kh, const float* vh, float* out,
               const tfx_attention_desc* d, cudaStream_t stream,
-              const uint8_t* pre_flags = nullptr) {
+              const uint8_t* pre_flags = nullptr, uint8_t* const* img = nullptr) {
   TFX_REQUIRE(d, op, "desc", "null pointer");
   TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->length >= 0 && d->head_dim >= 0, op, "shape",
               "extents must be non-negative");
   TFX_REQUIRE(d->empty_rows == TFX_ATTN_EMPTY_NAN || d->empty_rows == TFX_ATTN_EMPTY_ZERO, op,
               "empty_rows", "unknown value " + std::to_string(d->empty_rows));
   if (d->batch == 0 || d->heads == 0 || d->length == 0 || d->head_dim == 0) return TFX_OK;
-  TFX_REQUIRE(qh && kh && vh && out, op, "tensors", "null pointer");
+  TFX_REQUIRE((img || (qh && kh && vh)) && out, op, "tensors", "null pointer");
   TFX_REQUIRE(d->length < (int64_t(1) << 31) && d->heads < 65536 && d->batch < 65536, op,
               "shape", "too large");
   TFX_REQUIRE(d->head_dim <= 1024, op, "head_dim", "head_dim above 1024");
@@ -798,6 +931,13 @@ int attention(const char* op, const float* qh, const float* kh, const float* vh,
   a.valid_len = d->valid_len;
   a.vflags = nullptr;
   a.vflag_mode = 0;
+  if (img) {
+    a.qimg = img[0];
+    a.kimg = img[1];
+    a.vimg = img[2];
+    a.nqt = uint32_t((d->length + kWsTQ - 1) / kWsTQ);
+    a.nkt = uint32_t((d->length + kWsKB - 1) / kWsKB);
+  }
   return attn_launch(op, a, uint32_t(d->batch), stream, pre_flags);
 }
 
@@ -886,24 +1026,46 @@ int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const fl
   int st = TFX_OK;
   device_info(&st);
   if (st != TFX_OK) return st;
-  // scratch: head-major q, k, v, then one flag byte per head (the prep
-  // kernel marks heads the tensor-core attention must leave to the f32 one)
-  float* scratch = nullptr;
+  const int64_t hd = hidden / heads;
   const size_t nbh = size_t(batch * heads);
-  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4 + nbh, s);
-  uint8_t* flags = reinterpret_cast<uint8_t*>(scratch + 3 * n);
+  const DeviceInfo& dev = device_info(&st);
+  // head_dim 64 on the tensor cores: the prep kernel writes the attention's
+  // tile images directly (hi / lo, 512 bytes per padded row and tensor);
+  // otherwise head-major q, k, v. Then one flag byte per head (heads the
+  // tensor-core attention leaves to the f32 one).
+  const bool img = hd == 64 && aligned(qkv, 16) &&
+                   (!cos_table || (aligned(cos_table, 16) && aligned(sin_table, 16))) &&
+                   attn_tc_covers(64, uint64_t(n / hd), dev);
+  const uint64_t lq = uint64_t((length + kWsTQ - 1) / kWsTQ) * kWsTQ;
+  const uint64_t lk = uint64_t((length + kWsKB - 1) / kWsKB) * kWsKB;
+  const size_t data_bytes = img ? nbh * (lq + 2 * lk) * 512 : size_t(3 * n) * 4;
+  uint8_t* scratch = nullptr;
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), data_bytes + nbh, s);
+  uint8_t* flags = scratch + data_bytes;
   if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
-  int rc = laya_prep(op, qkv, cos_table, sin_table, scratch, scratch + n, scratch + 2 * n, hidden,
-                     heads, length, batch, s, flags);
+  float* raw = reinterpret_cast<float*>(scratch);
+  uint8_t* const images[3] = {scratch, scratch + nbh * lq * 512, scratch + nbh * (lq + lk) * 512};
+  int rc = img ? laya_prep(op, qkv, cos_table, sin_table, nullptr, nullptr, nullptr, hidden,
+                           heads, length, batch, s, flags, images)
+               : laya_prep(op, qkv, cos_table, sin_table, raw, raw + n, raw + 2 * n, hidden,
+                           heads, length, batch, s, flags);
+  if (rc == TFX_OK && img && lq != uint64_t(length)) {  // rows past the sequence: 0
+    const uint64_t total = nbh * (lq - uint64_t(length)) * 16;
+    rc = launch_kernel(op, attn_img_pad_kernel, dim3(unsigned(std::min<uint64_t>(
+                                                     (total + 255) / 256, uint64_t(dev.sms) * 8))),
+                       dim3(256), 0, s, 1, images[0], images[1], images[2], uint32_t(length),
+                       uint32_t(lq), uint32_t(lk), total);
+  }
   if (rc == TFX_OK) {
     tfx_attention_desc d;
-    tfx_attention_desc_init(&d, batch, heads, length, hidden / heads);
+    tfx_attention_desc_init(&d, batch, heads, length, hd);
     d.keep = keep;
-    rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s, flags);
+    rc = img ? attention(op, nullptr, nullptr, nullptr, out, &d, s, flags, images)
+             : attention(op, raw, raw + n, raw + 2 * n, out, &d, s, flags);
   }
   cudaFreeAsync(scratch, s);
   return rc;

@@ -58,13 +58,6 @@
 // it issued and each issuer for its MMAs before TMEM is freed.
 
 constexpr int kWsThreads = 352;
-constexpr int kWsTQ = 128;                  // queries per CTA
-constexpr int kWsKB = 64;                   // keys per block
-constexpr uint32_t kWsQRegion = 16384;      // 128 rows x 128 bytes
-constexpr uint32_t kWsKRegion = 8192;       // 64 rows x 128 bytes
-constexpr uint32_t kWsQPlane = 2 * kWsQRegion;   // Q hi or Q lo
-constexpr uint32_t kWsTile = 2 * kWsKRegion;     // K / V hi or lo
-constexpr uint32_t kWsSlot = 2 * kWsTile;        // hi + lo
 constexpr uint32_t kWsOffQlo = kWsQPlane;
 constexpr uint32_t kWsOffK = 2 * kWsQPlane;
 constexpr uint32_t kWsOffV = kWsOffK + 2 * kWsSlot;
@@ -80,18 +73,6 @@ struct WsShared {
   int abort;
   int kmin, kmax;
 };
-
-// Byte offsets inside the tile images (and inside the shared-memory copies
-// of the tiles), for 4 consecutive channels ch .. ch + 3 (ch % 4 == 0) of
-// row r of the tile.
-__host__ __device__ __forceinline__ uint32_t img_kmajor_off(uint32_t r, uint32_t ch,
-                                                            uint32_t region_bytes) {
-  return (ch >> 5) * region_bytes + r * 128 + ((((ch & 31) >> 2) ^ (r & 7)) << 4);
-}
-__host__ __device__ __forceinline__ uint32_t img_v_off(uint32_t r, uint32_t ch) {
-  return (ch >> 5) * kWsKRegion + r * 128 + ((((ch & 31) >> 3) ^ (r & 3)) << 5) +
-         (((ch & 7) >> 2) << 4);
-}
 
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
 // global memory into shared memory, completing on `bar`.
@@ -153,7 +134,6 @@ __global__ void __launch_bounds__(256) attn_img_split_kernel(
     uint8_t* __restrict__ qimg, uint8_t* __restrict__ kimg, uint8_t* __restrict__ vimg,
     uint32_t L, uint32_t lq, uint32_t lk, uint64_t total, uint8_t* flags) {
   pdl_enter();
-  constexpr float kMax = 3.4e38f;  // below the largest tf32 (rounding up stays finite)
   const uint32_t nqt = lq / kWsTQ, nkt = lk / kWsKB;
   for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
        n += uint64_t(gridDim.x) * blockDim.x) {
@@ -166,13 +146,10 @@ __global__ void __launch_bounds__(256) attn_img_split_kernel(
     auto put = [&](const float* x_src, uint8_t* img, uint64_t tile_bytes, uint32_t off) {
       float4 x = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       if (r < L) x = ld_stream(reinterpret_cast<const float4*>(x_src + src));
-      bad |= !(fabsf(x.x) < kMax && fabsf(x.y) < kMax && fabsf(x.z) < kMax && fabsf(x.w) < kMax);
-      const float4 h = make_float4(tf32_round_finite(x.x), tf32_round_finite(x.y),
-                                   tf32_round_finite(x.z), tf32_round_finite(x.w));
+      float4 h, lo;
+      img_split4(x, &h, &lo, &bad);
       *reinterpret_cast<float4*>(img + off) = h;
-      *reinterpret_cast<float4*>(img + tile_bytes / 2 + off) =
-          make_float4(__fsub_rn(x.x, h.x), __fsub_rn(x.y, h.y), __fsub_rn(x.z, h.z),
-                      __fsub_rn(x.w, h.w));
+      *reinterpret_cast<float4*>(img + tile_bytes / 2 + off) = lo;
     };
     put(q, qimg + (bh * nqt + r / kWsTQ) * (2 * kWsQPlane), 2 * kWsQPlane,
         img_kmajor_off(r % kWsTQ, ch, kWsQRegion));
@@ -182,6 +159,37 @@ __global__ void __launch_bounds__(256) attn_img_split_kernel(
       put(v, vimg + kt, kWsSlot, img_v_off(r % kWsKB, ch));
     }
     if (bad && flags) flags[bh] = 1;
+  }
+}
+
+// Zeroes the rows past the sequence (L .. lq - 1 of Q, L .. lk - 1 of K and
+// V; hi and lo) in the last tile of every head's images, for images that a
+// kernel writing only the rows below L (the Laya prep kernel) produced.
+__global__ void __launch_bounds__(256) attn_img_pad_kernel(uint8_t* __restrict__ qimg,
+                                                           uint8_t* __restrict__ kimg,
+                                                           uint8_t* __restrict__ vimg, uint32_t L,
+                                                           uint32_t lq, uint32_t lk,
+                                                           uint64_t total) {
+  pdl_enter();
+  const uint32_t pad = lq - L, nqt = lq / kWsTQ, nkt = lk / kWsKB;
+  const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
+       n += uint64_t(gridDim.x) * blockDim.x) {
+    const uint32_t ch = uint32_t(n & 15) * 4;
+    const uint64_t rest = n >> 4, bh = rest / pad;
+    const uint32_t r = L + uint32_t(rest - bh * pad);
+    uint8_t* qt = qimg + (bh * nqt + r / kWsTQ) * (2 * kWsQPlane);
+    const uint32_t oq = img_kmajor_off(r % kWsTQ, ch, kWsQRegion);
+    *reinterpret_cast<float4*>(qt + oq) = z;
+    *reinterpret_cast<float4*>(qt + kWsQPlane + oq) = z;
+    if (r < lk) {
+      const uint64_t kv = (bh * nkt + r / kWsKB) * kWsSlot;
+      const uint32_t ok = img_kmajor_off(r % kWsKB, ch, kWsKRegion), ov = img_v_off(r % kWsKB, ch);
+      *reinterpret_cast<float4*>(kimg + kv + ok) = z;
+      *reinterpret_cast<float4*>(kimg + kv + kWsTile + ok) = z;
+      *reinterpret_cast<float4*>(vimg + kv + ov) = z;
+      *reinterpret_cast<float4*>(vimg + kv + kWsTile + ov) = z;
+    }
   }
 }
 
