@@ -8,8 +8,8 @@
 // facts of the tensor cores:
 //   * one thread issues at most about one tcgen05.mma every ~100 cycles,
 //     whatever N is; M128 N64 K8 products (the only N that P V of head_dim 64
-//     has) are therefore issue-bound, and two issuing threads nearly double
-//     the rate;
+//     has) are therefore issue-bound, and several issuing threads multiply
+//     the rate (two measured at 1.8x);
 //   * the f32 accumulation of an MMA keeps about 22 bits below the largest
 //     exponent involved, so a long sum in one TMEM accumulator drifts.
 //
@@ -30,20 +30,21 @@
 // summary byte (some / every (query, key) kept). A CTA narrows its key range
 // from the summary row and its softmax threads load their words directly.
 //
-// Roles (11 warps):
-//   warp 0      bulk copies: Q once, K and V of each 64-key block into
-//               two-slot rings;
-//   warps 1, 2  MMA issuers, one per block parity: issuer p computes S(j) and
-//               P V(j) of the blocks j = p mod 2 in program order, so the
-//               buffers that S(j + 2) overwrites are read by P V(j) of the
-//               same thread (tcgen05.mma of one thread run in order);
-//   warps 3-10  softmax: thread = (query row, column group g of 32 keys).
+// Roles (12 warps):
+//   warp 0      bulk copies (Q once, K and V of each 64-key block into
+//               two-slot rings) and P V of column group 1 for every block;
+//   warps 1-3   MMA issuers: issuer p computes S(j) and P V of column group
+//               0 of the blocks j = p mod 3 (both halves of P V run at once:
+//               one thread issues at most one MMA per ~100 cycles); S(j + 3)
+//               waits until both halves of P V(j) have read buffer p;
+//   warps 4-11  softmax: thread = (query row, column group g of 32 keys).
 //
-// TMEM (512 columns, one CTA per SM): block j (p = j & 1) has S, then P hi,
-// in columns 128 p + [0, 64), P lo in 128 p + [64, 128), and its P V partial
-// of group g in 256 + 128 p + 64 g (a fresh partial per block). The softmax
-// threads add the partial of block j into f32 registers while block j + 1 is
-// processed, so a sequence of any length stays within the f32 tolerance.
+// TMEM (512 columns, one CTA per SM): block j (p = j % 3) has S, then P hi,
+// in columns 128 p + [0, 64), P lo in 128 p + [64, 128); the P V partial of
+// group g is at 384 + 64 g, fresh for every block. The softmax threads add
+// the partial of block j into f32 registers while block j + 1 is processed
+// (before P V(j + 1), which waits for them, overwrites it), so a sequence of
+// any length stays within the f32 tolerance.
 //
 // Softmax. Each column group g keeps its own running max m_g, sum l_g and
 // output O_g, so the softmax threads never exchange values inside the loop;
@@ -57,7 +58,8 @@
 // which ends the other roles' waits; the copy warp then waits for the copies
 // it issued and each issuer for its MMAs before TMEM is freed.
 
-constexpr int kWsThreads = 352;
+constexpr int kWsThreads = 384;
+constexpr uint32_t kWsIssuers = 3;          // MMA issuers (block j -> issuer j % 3)
 constexpr uint32_t kWsOffQlo = kWsQPlane;
 constexpr uint32_t kWsOffK = 2 * kWsQPlane;
 constexpr uint32_t kWsOffV = kWsOffK + 2 * kWsSlot;
@@ -67,8 +69,9 @@ constexpr uint32_t kWsStage = 68;           // output staging row stride (floats
 
 struct WsShared {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], p_ready[2], o_done[2], drain[2];
+  uint64_t k_empty[2], v_empty[2];  // per K / V slot (block j -> slot j % 2)
+  uint64_t k_full[kWsIssuers], v_full[kWsIssuers], s_full[kWsIssuers];  // per issuer
+  uint64_t p_ready[kWsIssuers], o_done[kWsIssuers], drain[kWsIssuers + 1];
   uint32_t tmem_base;
   int abort;
   int kmin, kmax;
@@ -316,15 +319,17 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   if (tid == 0) {
     mbar_init(&sh.q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.k_full[s], 1);
       mbar_init(&sh.k_empty[s], 1);
-      mbar_init(&sh.v_full[s], 1);
-      mbar_init(&sh.v_empty[s], 1);
-      mbar_init(&sh.s_full[s], 1);
-      mbar_init(&sh.p_ready[s], 256);
-      mbar_init(&sh.o_done[s], 1);
-      mbar_init(&sh.drain[s], 1);
+      mbar_init(&sh.v_empty[s], 2);  // both halves of P V
     }
+    for (uint32_t q = 0; q < kWsIssuers; ++q) {
+      mbar_init(&sh.k_full[q], 1);
+      mbar_init(&sh.v_full[q], 1);
+      mbar_init(&sh.s_full[q], 1);
+      mbar_init(&sh.p_ready[q], 256);
+      mbar_init(&sh.o_done[q], 2);  // both halves of P V
+    }
+    for (uint32_t q = 0; q <= kWsIssuers; ++q) mbar_init(&sh.drain[q], 1);
     sh.abort = 0;
     sh.kmin = 0x7fffffff;
     sh.kmax = -1;
@@ -376,49 +381,98 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   tc_fence_after();
   const uint32_t tm = sh.tmem_base;
 
+  constexpr uint32_t id_o = idesc_tf32_bmn(kWsTQ, 64);
+  // P V(j) of column group g: 4 k-steps x (P hi V hi, P hi V lo, P lo V hi)
+  // into a fresh partial (keys 32 g .. 32 g + 31 of the block)
+  auto issue_pv = [&](uint32_t j, uint32_t g) {
+    const uint32_t ph = tm + 128 * (j % kWsIssuers), pl = ph + 64;
+    const uint64_t dvh =
+        smem_desc_sw128b32_mn(smem_addr(base + kWsOffV + (j & 1) * kWsSlot), kWsKRegion);
+    const uint64_t dvl = dvh + (kWsTile >> 4);
+#pragma unroll
+    for (uint32_t kk = 0; kk < 4; ++kk) {
+      const uint32_t ks = 4 * g + kk;
+#pragma unroll
+      for (uint32_t prod = 0; prod < 3; ++prod)
+        mma_tf32_ts(tm + 384 + 64 * g, (prod == 2 ? pl : ph) + ks * 8,
+                    (prod == 1 ? dvl : dvh) + ks * (1024 >> 4), id_o,
+                    (kk > 0 || prod > 0) ? 1u : 0u);
+    }
+  };
+
   if (warp == 0) {
-    // ---- bulk copies ----
+    // ---- bulk copies, and P V of column group 1 ----
     if (lane == 0) {
-      uint32_t kiss[2] = {0, 0}, viss[2] = {0, 0};
-      for (uint32_t j = 0; j < nblk; ++j) {
-        const uint32_t s = j & 1, use = j >> 1;
-        const uint64_t tile = (uint64_t(bh) * nkt + kt0 + j) * kWsSlot;
-        if (use > 0 && !ws_wait(&sh.k_empty[s], (use - 1) & 1, &sh)) break;
-        mbar_arrive_expect_tx(&sh.k_full[s], kWsSlot);
-        bulk_load(base + kWsOffK + s * kWsSlot, kimg + tile, kWsSlot, &sh.k_full[s]);
-        ++kiss[s];
-        if (use > 0 && !ws_wait(&sh.v_empty[s], (use - 1) & 1, &sh)) break;
-        mbar_arrive_expect_tx(&sh.v_full[s], kWsSlot);
-        bulk_load(base + kWsOffV + s * kWsSlot, vimg + tile, kWsSlot, &sh.v_full[s]);
-        ++viss[s];
+      // block j goes to slot j % 2 and completes on the full barrier of its
+      // issuer j % 3 (each full barrier's waiters see its phases in order)
+      uint32_t kiss[kWsIssuers] = {0, 0, 0}, viss[kWsIssuers] = {0, 0, 0};
+      auto load_k = [&](uint32_t j) {
+        const uint32_t q = j % kWsIssuers;
+        mbar_arrive_expect_tx(&sh.k_full[q], kWsSlot);
+        bulk_load(base + kWsOffK + (j & 1) * kWsSlot,
+                  kimg + (uint64_t(bh) * nkt + kt0 + j) * kWsSlot, kWsSlot, &sh.k_full[q]);
+        ++kiss[q];
+      };
+      auto load_v = [&](uint32_t j) {
+        const uint32_t q = j % kWsIssuers;
+        mbar_arrive_expect_tx(&sh.v_full[q], kWsSlot);
+        bulk_load(base + kWsOffV + (j & 1) * kWsSlot,
+                  vimg + (uint64_t(bh) * nkt + kt0 + j) * kWsSlot, kWsSlot, &sh.v_full[q]);
+        ++viss[q];
+      };
+      for (uint32_t j = 0; j < 2 && j < nblk; ++j) {
+        load_k(j);
+        load_v(j);
       }
-      // the copies this thread issued land before the CTA can exit
+      for (uint32_t j = 0; j < nblk; ++j) {
+        const uint32_t s = j & 1, q = j % kWsIssuers, use = j / kWsIssuers;
+        // K(j + 2) once S(j) has read slot s
+        if (j + 2 < nblk) {
+          if (!ws_wait(&sh.k_empty[s], (j >> 1) & 1, &sh)) break;
+          load_k(j + 2);
+        }
+        // P V(j), group 1, beside the issuer's group 0
+        if (!ws_wait(&sh.p_ready[q], use & 1, &sh) || !ws_wait(&sh.v_full[q], use & 1, &sh))
+          break;
+        tc_fence_after();
+        issue_pv(j, 1);
+        mma_commit(&sh.o_done[q]);
+        mma_commit(&sh.v_empty[s]);
+        // V(j + 2) once both halves of P V(j) have read slot s
+        if (j + 2 < nblk) {
+          if (!ws_wait(&sh.v_empty[s], (j >> 1) & 1, &sh)) break;
+          load_v(j + 2);
+        }
+      }
+      // every MMA this thread issued has completed, and the copies it issued
+      // have landed, before the CTA can exit
+      mma_commit(&sh.drain[kWsIssuers]);
+      mbar_wait_bounded(&sh.drain[kWsIssuers], 0, kTcWait);
       mbar_wait_bounded(&sh.q_full, 0, kTcWait);
-      for (int s = 0; s < 2; ++s) {
-        if (kiss[s] > 0) mbar_wait_bounded(&sh.k_full[s], (kiss[s] - 1) & 1, kTcWait);
-        if (viss[s] > 0) mbar_wait_bounded(&sh.v_full[s], (viss[s] - 1) & 1, kTcWait);
+      for (uint32_t q = 0; q < kWsIssuers; ++q) {
+        if (kiss[q] > 0) mbar_wait_bounded(&sh.k_full[q], (kiss[q] - 1) & 1, kTcWait);
+        if (viss[q] > 0) mbar_wait_bounded(&sh.v_full[q], (viss[q] - 1) & 1, kTcWait);
       }
     }
     __syncwarp();
-  } else if (warp <= 2) {
-    // ---- MMA issuer p: blocks j = p, p + 2, ... (slot and buffers p) ----
+  } else if (warp <= kWsIssuers) {
+    // ---- MMA issuer p: blocks j = p, p + 3, ... (S / P buffer p, K / V slot j % 2) ----
     const uint32_t p = warp - 1;
     if (lane == 0 && nblk > p) {
       constexpr uint32_t id_s = idesc_tf32(kWsTQ, kWsKB);
-      constexpr uint32_t id_o = idesc_tf32_bmn(kWsTQ, 64);
       // descriptors built once; an offset moves the start address field
       // (address >> 4, no carry out of its 14 bits inside shared memory)
       const uint64_t dqh = smem_desc_sw128(smem_addr(qhi));
       const uint64_t dql = dqh + (kWsQPlane >> 4);
-      const uint64_t dkh = smem_desc_sw128(smem_addr(base + kWsOffK + p * kWsSlot));
-      const uint64_t dkl = dkh + (kWsTile >> 4);
-      const uint64_t dvh =
-          smem_desc_sw128b32_mn(smem_addr(base + kWsOffV + p * kWsSlot), kWsKRegion);
-      const uint64_t dvl = dvh + (kWsTile >> 4);
-      const uint32_t ts = tm + 128 * p, tpl = ts + 64, to = tm + 256 + 128 * p;
+      const uint32_t ts = tm + 128 * p;
       bool ok = ws_wait(&sh.q_full, 0, &sh);
-      for (uint32_t j = p; ok && j < nblk; j += 2) {
-        const uint32_t use = j >> 1;
+      for (uint32_t j = p; ok && j < nblk; j += kWsIssuers) {
+        const uint32_t use = j / kWsIssuers, s = j & 1;
+        const uint64_t dkh = smem_desc_sw128(smem_addr(base + kWsOffK + s * kWsSlot));
+        const uint64_t dkl = dkh + (kWsTile >> 4);
+        // buffer p is free once both halves of P V(j - 3) have read P(j - 3)
+        // (group 1 comes from the copy thread)
+        if (use > 0 && !ws_wait(&sh.o_done[p], (use - 1) & 1, &sh)) break;
         if (!ws_wait(&sh.k_full[p], use & 1, &sh)) break;
         tc_fence_after();
         // S(j) = Q K^T: 8 k-steps x (hi hi, hi lo, lo hi)
@@ -431,26 +485,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
           mma_tf32_ss(ts, dql + oq, dkh + okk, id_s, 1);
         }
         mma_commit(&sh.s_full[p]);
-        mma_commit(&sh.k_empty[p]);  // the K slot is free once these have read it
+        mma_commit(&sh.k_empty[s]);  // the K slot is free once these have read it
         if (!ws_wait(&sh.p_ready[p], use & 1, &sh) || !ws_wait(&sh.v_full[p], use & 1, &sh))
           break;
         tc_fence_after();
-        // P V(j): a fresh partial per column group, the groups alternating
-#pragma unroll
-        for (uint32_t kk = 0; kk < 4; ++kk) {
-#pragma unroll
-          for (uint32_t prod = 0; prod < 3; ++prod) {
-#pragma unroll
-            for (uint32_t g = 0; g < 2; ++g) {
-              const uint32_t ks = 4 * g + kk;
-              mma_tf32_ts(to + 64 * g, (prod == 2 ? tpl : ts) + ks * 8,
-                          (prod == 1 ? dvl : dvh) + ks * (1024 >> 4), id_o,
-                          (kk > 0 || prod > 0) ? 1u : 0u);
-            }
-          }
-        }
+        issue_pv(j, 0);  // group 1: the copy thread, at the same time
         mma_commit(&sh.o_done[p]);
-        mma_commit(&sh.v_empty[p]);
+        mma_commit(&sh.v_empty[s]);
       }
       // every MMA this thread issued has completed before TMEM is freed
       mma_commit(&sh.drain[p]);
@@ -459,7 +500,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
     __syncwarp();
   } else {
     // ---- softmax: thread = (query row, column group g of 32 keys) ----
-    const uint32_t g = (warp - 3) >> 2, quarter = warp & 3;
+    const uint32_t g = (warp - 1 - kWsIssuers) >> 2, quarter = warp & 3;
     const uint32_t row = quarter * 32 + lane;
     const uint32_t lane_off = (quarter * 32) << 16;
     const int64_t qi = int64_t(q0) + row;
@@ -478,9 +519,15 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
 #pragma unroll
     for (int c = 0; c < 64; ++c) o[c] = 0.0f;
     bool inf_row = false, failed = false;
-    // o = (o + partial of the block of parity q) * corr
-    auto drain = [&](uint32_t q, float corr) {
-      const uint32_t tO = tm + 256 + 128 * q + 64 * g + lane_off;
+    uint32_t word_next = ~0u;  // mask word and summary byte of the next block
+    uint8_t smy_next = 2;
+    if (MASK && nblk > 0) {
+      word_next = __ldg(wrow + kt0 * 256 + g * kWsTQ + row);
+      smy_next = __ldg(srow + kt0);
+    }
+    // o = (o + the P V partial) * corr
+    auto drain = [&](float corr) {
+      const uint32_t tO = tm + 384 + 64 * g + lane_off;
 #pragma unroll
       for (uint32_t c = 0; c < 64; c += 32) {
         float pv[32];
@@ -492,14 +539,14 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       }
     };
     for (uint32_t j = 0; j < nblk; ++j) {
-      const uint32_t p = j & 1, ph = (j >> 1) & 1;
+      const uint32_t p = j % kWsIssuers, ph = (j / kWsIssuers) & 1;
       const int64_t k0 = kb_first + int64_t(j) * kWsKB + 32 * g;  // key of column 0
-      // this row's mask word of the block (its loads travel during the wait)
-      uint32_t word = ~0u;
-      uint8_t smy = 2;
-      if (MASK) {
-        word = __ldg(wrow + (kt0 + j) * 256 + g * kWsTQ + row);
-        smy = __ldg(srow + kt0 + j);
+      // this row's mask word of the block, loaded one block ahead
+      uint32_t word = word_next;
+      const uint8_t smy = smy_next;
+      if (MASK && j + 1 < nblk) {
+        word_next = __ldg(wrow + (kt0 + j + 1) * 256 + g * kWsTQ + row);
+        smy_next = __ldg(srow + kt0 + j + 1);
       }
       if (!ws_wait_warp(&sh.s_full[p], ph, &sh)) {
         failed = true;
@@ -573,27 +620,29 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       }
       l = __fmaf_rn(l, corr, ps);
       m = mn;
-      // the partial of block j - 1 goes into o before P V(j + 1) overwrites
-      // it. The parity wait is exact: this thread waited for the partial of
-      // block j - 3 (the previous phase) and P V(j + 1) cannot start before
-      // this thread's P(j + 1).
+      // the partial of block j - 1 goes into o before P V(j) overwrites it
+      // (P V(j) waits for this thread's p_ready). The parity wait on the
+      // issuer of block j - 1 is exact: this thread waited for that issuer's
+      // previous phase (block j - 4), and its next one (block j + 2) cannot
+      // start before this thread's P(j + 2).
       if (j > 0) {
-        if (!ws_wait_warp(&sh.o_done[p ^ 1], ((j - 1) >> 1) & 1, &sh)) {
+        const uint32_t q = (j - 1) % kWsIssuers;
+        if (!ws_wait_warp(&sh.o_done[q], ((j - 1) / kWsIssuers) & 1, &sh)) {
           failed = true;
           break;
         }
         tc_fence_after();
-        drain(p ^ 1, corr);
+        drain(corr);
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&sh.p_ready[p]);
     }
     if (!failed && nblk > 0) {  // the partial of the last block
-      const uint32_t q = (nblk - 1) & 1;
-      failed = !ws_wait_warp(&sh.o_done[q], ((nblk - 1) >> 1) & 1, &sh);
+      const uint32_t q = (nblk - 1) % kWsIssuers;
+      failed = !ws_wait_warp(&sh.o_done[q], ((nblk - 1) / kWsIssuers) & 1, &sh);
       tc_fence_after();
-      if (!failed) drain(q, 1.0f);
+      if (!failed) drain(1.0f);
     }
     if (!ws_softmax_any(failed)) {
       // merge the two column groups and write the output through shared
@@ -630,7 +679,7 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
                                     a.gate_offset % 4 == 0));
       const float ev = a.empty_nan ? NAN : 0.0f;
 #pragma unroll 1
-      for (uint32_t idx = tid - 96; idx < kWsTQ * 16; idx += 256) {
+      for (uint32_t idx = tid - 32 * (1 + kWsIssuers); idx < kWsTQ * 16; idx += 256) {
         const uint32_t r = idx >> 4, c4 = (idx & 15) * 4, qr = q0 + r;
         if (qr >= L) continue;
         const float4 fr = *reinterpret_cast<const float4*>(xf + 4 * r);
