@@ -81,8 +81,12 @@ __device__ __forceinline__ void img_split4(float4 x, float4* hi, float4* lo, boo
 // rotated as a*c - b*s, a*s + b*c with every product rounded (lib.rs:
 // 996-1008); v copied. IMG (head_dim 64, VEC 4): q, k, v go straight into the
 // tensor-core attention's tile images (qimg / kimg / vimg, nqt / nkt tiles
-// per head) instead of the head-major qh / kh / vh.
-template <int VEC, bool IMG = false>
+// per head) instead of the head-major qh / kh / vh. LATE: the grid waits for
+// the previous one at its end instead of its start. The previous grid is then
+// the mask digest, which waited for everything before it and let this grid
+// start at once; this grid reads nothing the digest writes, and waiting at the
+// end makes its completion imply the digest's for the attention that follows.
+template <int VEC, bool IMG = false, bool LATE = false>
 __global__ void __launch_bounds__(256) laya_prep_kernel(
     const float* __restrict__ qkv, const float* __restrict__ cos_t,
     const float* __restrict__ sin_t, float* __restrict__ qh, float* __restrict__ kh,
@@ -90,7 +94,7 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
     uint64_t total, FastDiv div_chunks, FastDiv div_heads, FastDiv div_len, uint8_t* flags,
     uint8_t* __restrict__ qimg, uint8_t* __restrict__ kimg, uint8_t* __restrict__ vimg,
     uint32_t nqt, uint32_t nkt) {
-  pdl_enter();
+  if constexpr (!LATE) pdl_enter();
   const uint32_t half = hd / 2;
   for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
        n += uint64_t(gridDim.x) * blockDim.x) {
@@ -181,6 +185,7 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
       vh[dst + i0] = va[0]; vh[dst + half + i0] = vb[0];
     }
   }
+  if constexpr (LATE) pdl_wait();  // this grid completes after the previous one
 }
 
 // ---- Jeff prep: centred per-head RMSNorm + partial RoPE --------------------------------
@@ -276,6 +281,9 @@ struct AttnArgs {
   const uint8_t* kimg = nullptr;
   const uint8_t* vimg = nullptr;
   uint32_t nqt = 0, nkt = 0;
+  // the mask digest, when computed before the call (attn_keep_digest_kernel)
+  const uint32_t* digest_words = nullptr;
+  const uint8_t* digest_summary = nullptr;
 };
 
 // Channels ch .. ch + 3 of row `row` of head bh of q (t = 0), k (1) or v (2):
@@ -698,8 +706,9 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   // the mask digest (keep / active): 1 KB of words and one summary byte per
   // (batch, query tile, key tile)
   const bool mask = a.keep || a.active;
+  const bool have_digest = a.digest_words != nullptr;
   const uint32_t nqt = lq / kWsTQ, nkt = lk / kWsKB;
-  const size_t digest_tiles = mask ? size_t(batch) * nqt * nkt : 0;
+  const size_t digest_tiles = mask && !have_digest ? size_t(batch) * nqt * nkt : 0;
   const size_t words_bytes = digest_tiles * 1024;
   const size_t summary_bytes = (digest_tiles + 255) / 256 * 256;
   uint8_t* scratch = nullptr;
@@ -717,8 +726,10 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   const uint8_t* qimg = have_img ? a.qimg : own;
   const uint8_t* kimg = have_img ? a.kimg : own + qimg_bytes;
   const uint8_t* vimg = have_img ? a.vimg : own + qimg_bytes + kimg_bytes;
-  uint32_t* words = reinterpret_cast<uint32_t*>(own + qimg_bytes + 2 * kimg_bytes);
-  uint8_t* summary = reinterpret_cast<uint8_t*>(words) + words_bytes;
+  uint32_t* own_words = reinterpret_cast<uint32_t*>(own + qimg_bytes + 2 * kimg_bytes);
+  uint8_t* own_summary = reinterpret_cast<uint8_t*>(own_words) + words_bytes;
+  const uint32_t* words = have_digest ? a.digest_words : own_words;
+  const uint8_t* summary = have_digest ? a.digest_summary : own_summary;
   int rc = TFX_OK;
   if (!have_img) {
     const uint64_t total = uint64_t(nbh) * lq * 16;
@@ -728,9 +739,9 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
                        a.v, own, own + qimg_bytes, own + qimg_bytes + kimg_bytes, a.length, lq,
                        lk, total, flags);
   }
-  if (rc == TFX_OK && mask)
+  if (rc == TFX_OK && mask && !have_digest)
     rc = launch_kernel(op, attn_keep_digest_kernel, dim3(nkt, nqt, batch), dim3(32), 0, stream, 1,
-                       a, nqt, nkt, words, summary);
+                       a, nqt, nkt, own_words, own_summary);
   if (rc == TFX_OK) {
     a.vflags = pre_flags ? pre_flags : flags;
     a.vflag_mode = 1;
@@ -740,9 +751,7 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
           kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kWsSmem));
       if (e2 != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(e2));
       return launch_kernel(op, kernel, grid, dim3(kWsThreads), kWsSmem, stream, 1, qimg, kimg,
-                           vimg, nkt,
-                           static_cast<const uint32_t*>(words),
-                           static_cast<const uint8_t*>(summary), a);
+                           vimg, nkt, words, summary, a);
     };
     switch ((mask ? 2 : 0) | (a.bias ? 1 : 0)) {
       case 0: rc = run(attn_ws_kernel<false, false>); break;
@@ -820,7 +829,7 @@ int attention_wait_timeouts(uint32_t* count) {
 int laya_prep(const char* op, const float* qkv, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t hidden, int64_t heads, int64_t length,
               int64_t batch, cudaStream_t stream, uint8_t* flags = nullptr,
-              uint8_t* const* img = nullptr) {
+              uint8_t* const* img = nullptr, bool late = false) {
   TFX_REQUIRE(hidden >= 0 && heads > 0 && length >= 0 && batch >= 0, op, "shape",
               "extents must be non-negative (heads positive)");
   TFX_REQUIRE(hidden % heads == 0, op, "hidden", "hidden must be a multiple of heads");
@@ -850,10 +859,13 @@ int laya_prep(const char* op, const float* qkv, const float* cos_t, const float*
   if (img) {
     const uint32_t nqt = uint32_t((length + kWsTQ - 1) / kWsTQ);
     const uint32_t nkt = uint32_t((length + kWsKB - 1) / kWsKB);
-    return launch_kernel(op, laya_prep_kernel<4, true>, dim3(grid), dim3(256), 0, stream, 1, qkv,
-                         cos_t, sin_t, qh, kh, vh, uint32_t(hidden), uint32_t(heads),
-                         uint32_t(length), uint32_t(hd), uint64_t(total), dc, dh, dl, flags,
-                         img[0], img[1], img[2], nqt, nkt);
+    auto run = [&](auto kernel) {
+      return launch_kernel(op, kernel, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t, sin_t,
+                           qh, kh, vh, uint32_t(hidden), uint32_t(heads), uint32_t(length),
+                           uint32_t(hd), uint64_t(total), dc, dh, dl, flags, img[0], img[1],
+                           img[2], nqt, nkt);
+    };
+    return late ? run(laya_prep_kernel<4, true, true>) : run(laya_prep_kernel<4, true>);
   }
   if (v4)
     return launch_kernel(op, laya_prep_kernel<4>, dim3(grid), dim3(256), 0, stream, 1, qkv, cos_t,
@@ -895,9 +907,15 @@ int jeff_prep(const char* op, const float* q, const float* k, const float* v,
 
 // img (optional, head_dim 64 with attn_tc_covers): q, k, v as tile images
 // instead of qh / kh / vh.
+AttnArgs attn_args(const float* qh, const float* kh, const float* vh, float* out,
+                   const tfx_attention_desc* d);
+
+// digest_words / digest_summary (optional): the keep / active digest,
+// computed before the call.
 int attention(const char* op, const float* qh, const float* kh, const float* vh, float* out,
               const tfx_attention_desc* d, cudaStream_t stream,
-              const uint8_t* pre_flags = nullptr, uint8_t* const* img = nullptr) {
+              const uint8_t* pre_flags = nullptr, uint8_t* const* img = nullptr,
+              const uint32_t* digest_words = nullptr, const uint8_t* digest_summary = nullptr) {
   TFX_REQUIRE(d, op, "desc", "null pointer");
   TFX_REQUIRE(d->batch >= 0 && d->heads >= 0 && d->length >= 0 && d->head_dim >= 0, op, "shape",
               "extents must be non-negative");
@@ -908,6 +926,21 @@ int attention(const char* op, const float* qh, const float* kh, const float* vh,
   TFX_REQUIRE(d->length < (int64_t(1) << 31) && d->heads < 65536 && d->batch < 65536, op,
               "shape", "too large");
   TFX_REQUIRE(d->head_dim <= 1024, op, "head_dim", "head_dim above 1024");
+  AttnArgs a = attn_args(qh, kh, vh, out, d);
+  if (img) {
+    a.qimg = img[0];
+    a.kimg = img[1];
+    a.vimg = img[2];
+    a.nqt = uint32_t((d->length + kWsTQ - 1) / kWsTQ);
+    a.nkt = uint32_t((d->length + kWsKB - 1) / kWsKB);
+  }
+  a.digest_words = digest_words;
+  a.digest_summary = digest_summary;
+  return attn_launch(op, a, uint32_t(d->batch), stream, pre_flags);
+}
+
+AttnArgs attn_args(const float* qh, const float* kh, const float* vh, float* out,
+                   const tfx_attention_desc* d) {
   AttnArgs a;
   a.q = qh;
   a.k = kh;
@@ -931,14 +964,7 @@ int attention(const char* op, const float* qh, const float* kh, const float* vh,
   a.valid_len = d->valid_len;
   a.vflags = nullptr;
   a.vflag_mode = 0;
-  if (img) {
-    a.qimg = img[0];
-    a.kimg = img[1];
-    a.vimg = img[2];
-    a.nqt = uint32_t((d->length + kWsTQ - 1) / kWsTQ);
-    a.nkt = uint32_t((d->length + kWsKB - 1) / kWsKB);
-  }
-  return attn_launch(op, a, uint32_t(d->batch), stream, pre_flags);
+  return a;
 }
 
 }  // namespace tfx
@@ -1039,20 +1065,37 @@ int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const fl
   const uint64_t lq = uint64_t((length + kWsTQ - 1) / kWsTQ) * kWsTQ;
   const uint64_t lk = uint64_t((length + kWsKB - 1) / kWsKB) * kWsKB;
   const size_t data_bytes = img ? nbh * (lq + 2 * lk) * 512 : size_t(3 * n) * 4;
+  // with the images, the keep digest (1 KB of words and a summary byte per
+  // (batch, query tile, key tile)) is computed first, overlapping the prep
+  const uint32_t nqt = uint32_t(lq / kWsTQ), nkt = uint32_t(lk / kWsKB);
+  const size_t dtiles = img ? size_t(batch) * nqt * nkt : 0;
+  const size_t words_bytes = dtiles * 1024, summary_bytes = (dtiles + 255) / 256 * 256;
   uint8_t* scratch = nullptr;
-  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), data_bytes + nbh, s);
-  uint8_t* flags = scratch + data_bytes;
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch),
+                                 data_bytes + words_bytes + summary_bytes + nbh, s);
+  uint32_t* words = reinterpret_cast<uint32_t*>(scratch + data_bytes);
+  uint8_t* summary = scratch + data_bytes + words_bytes;
+  uint8_t* flags = summary + summary_bytes;
   if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, nbh, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
+  tfx_attention_desc d;
+  tfx_attention_desc_init(&d, batch, heads, length, hd);
+  d.keep = keep;
   float* raw = reinterpret_cast<float*>(scratch);
   uint8_t* const images[3] = {scratch, scratch + nbh * lq * 512, scratch + nbh * (lq + lk) * 512};
-  int rc = img ? laya_prep(op, qkv, cos_table, sin_table, nullptr, nullptr, nullptr, hidden,
-                           heads, length, batch, s, flags, images)
-               : laya_prep(op, qkv, cos_table, sin_table, raw, raw + n, raw + 2 * n, hidden,
-                           heads, length, batch, s, flags);
+  int rc = TFX_OK;
+  if (img)
+    rc = launch_kernel(op, attn_keep_digest_kernel, dim3(nkt, nqt, unsigned(batch)), dim3(32), 0,
+                       s, 1, attn_args(nullptr, nullptr, nullptr, out, &d), nqt, nkt, words,
+                       summary);
+  if (rc == TFX_OK)
+    rc = img ? laya_prep(op, qkv, cos_table, sin_table, nullptr, nullptr, nullptr, hidden, heads,
+                         length, batch, s, flags, images, /*late=*/true)
+             : laya_prep(op, qkv, cos_table, sin_table, raw, raw + n, raw + 2 * n, hidden,
+                         heads, length, batch, s, flags);
   if (rc == TFX_OK && img && lq != uint64_t(length)) {  // rows past the sequence: 0
     const uint64_t total = nbh * (lq - uint64_t(length)) * 16;
     rc = launch_kernel(op, attn_img_pad_kernel, dim3(unsigned(std::min<uint64_t>(
@@ -1060,13 +1103,9 @@ int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep, const fl
                        dim3(256), 0, s, 1, images[0], images[1], images[2], uint32_t(length),
                        uint32_t(lq), uint32_t(lk), total);
   }
-  if (rc == TFX_OK) {
-    tfx_attention_desc d;
-    tfx_attention_desc_init(&d, batch, heads, length, hd);
-    d.keep = keep;
-    rc = img ? attention(op, nullptr, nullptr, nullptr, out, &d, s, flags, images)
+  if (rc == TFX_OK)
+    rc = img ? attention(op, nullptr, nullptr, nullptr, out, &d, s, flags, images, words, summary)
              : attention(op, raw, raw + n, raw + 2 * n, out, &d, s, flags);
-  }
   cudaFreeAsync(scratch, s);
   return rc;
 }

@@ -236,6 +236,9 @@ __global__ void __launch_bounds__(32) attn_keep_digest_kernel(AttnArgs a, uint32
                                                               uint32_t nkt, uint32_t* words,
                                                               uint8_t* summary) {
   pdl_enter();
+  // nothing that runs next reads the digest before its own wait: the Laya
+  // block's prep kernel (which does not use it) starts at once and overlaps
+  pdl_launch_dependents();
   const uint32_t kt = blockIdx.x, qt = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
   const uint64_t L = a.length;
   const uint32_t q0 = qt * kWsTQ, nq = min(uint32_t(kWsTQ), uint32_t(L) - q0);
