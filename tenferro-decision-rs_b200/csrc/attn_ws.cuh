@@ -31,12 +31,14 @@
 // from the summary row and its softmax threads load their words directly.
 //
 // Roles (12 warps):
-//   warp 0      bulk copies (Q once, K and V of each 64-key block into
-//               two-slot rings) and P V of column group 1 for every block;
+//   warp 0      bulk copies of V (a two-slot ring) and P V of column group 1
+//               for every block;
 //   warps 1-3   MMA issuers: issuer p computes S(j) and P V of column group
 //               0 of the blocks j = p mod 3 (both halves of P V run at once:
 //               one thread issues at most one MMA per ~100 cycles); S(j + 3)
-//               waits until both halves of P V(j) have read buffer p;
+//               waits until both halves of P V(j) have read buffer p; each
+//               issuer loads its own K tiles (Q once, by thread 0) into its
+//               own K slot as soon as its S has read the slot;
 //   warps 4-11  softmax: thread = (query row, column group g of 32 keys).
 //
 // TMEM (512 columns, one CTA per SM): block j (p = j % 3) has S, then P hi,
@@ -62,15 +64,16 @@ constexpr int kWsThreads = 384;
 constexpr uint32_t kWsIssuers = 3;          // MMA issuers (block j -> issuer j % 3)
 constexpr uint32_t kWsOffQlo = kWsQPlane;
 constexpr uint32_t kWsOffK = 2 * kWsQPlane;
-constexpr uint32_t kWsOffV = kWsOffK + 2 * kWsSlot;
+constexpr uint32_t kWsOffV = kWsOffK + 3 * kWsSlot;  // K: one slot per issuer
 constexpr uint32_t kWsSmem = kWsOffV + 2 * kWsSlot + 1024;  // + alignment slack
 constexpr float kWsRescale = 8.0f;          // natural-log headroom before m moves
 constexpr uint32_t kWsStage = 68;           // output staging row stride (floats)
 
 struct WsShared {
   uint64_t q_full;
-  uint64_t k_empty[2], v_empty[2];  // per K / V slot (block j -> slot j % 2)
-  uint64_t k_full[kWsIssuers], v_full[kWsIssuers], s_full[kWsIssuers];  // per issuer
+  uint64_t v_empty[2];  // per V slot (block j -> slot j % 2)
+  // per issuer (block j -> issuer and K slot j % 3)
+  uint64_t k_full[kWsIssuers], k_empty[kWsIssuers], v_full[kWsIssuers], s_full[kWsIssuers];
   uint64_t p_ready[kWsIssuers], o_done[kWsIssuers], drain[kWsIssuers + 1];
   uint32_t tmem_base;
   int abort;
@@ -321,12 +324,10 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
 
   if (tid == 0) {
     mbar_init(&sh.q_full, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&sh.k_empty[s], 1);
-      mbar_init(&sh.v_empty[s], 2);  // both halves of P V
-    }
+    for (int s = 0; s < 2; ++s) mbar_init(&sh.v_empty[s], 2);  // both halves of P V
     for (uint32_t q = 0; q < kWsIssuers; ++q) {
       mbar_init(&sh.k_full[q], 1);
+      mbar_init(&sh.k_empty[q], 1);
       mbar_init(&sh.v_full[q], 1);
       mbar_init(&sh.s_full[q], 1);
       mbar_init(&sh.p_ready[q], 256);
@@ -404,18 +405,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
   };
 
   if (warp == 0) {
-    // ---- bulk copies, and P V of column group 1 ----
+    // ---- V copies, and P V of column group 1 ----
     if (lane == 0) {
-      // block j goes to slot j % 2 and completes on the full barrier of its
-      // issuer j % 3 (each full barrier's waiters see its phases in order)
-      uint32_t kiss[kWsIssuers] = {0, 0, 0}, viss[kWsIssuers] = {0, 0, 0};
-      auto load_k = [&](uint32_t j) {
-        const uint32_t q = j % kWsIssuers;
-        mbar_arrive_expect_tx(&sh.k_full[q], kWsSlot);
-        bulk_load(base + kWsOffK + (j & 1) * kWsSlot,
-                  kimg + (uint64_t(bh) * nkt + kt0 + j) * kWsSlot, kWsSlot, &sh.k_full[q]);
-        ++kiss[q];
-      };
+      // V of block j goes to slot j % 2 and completes on the full barrier of
+      // its issuer j % 3 (each full barrier's waiters see its phases in order)
+      uint32_t viss[kWsIssuers] = {0, 0, 0};
       auto load_v = [&](uint32_t j) {
         const uint32_t q = j % kWsIssuers;
         mbar_arrive_expect_tx(&sh.v_full[q], kWsSlot);
@@ -423,17 +417,9 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
                   vimg + (uint64_t(bh) * nkt + kt0 + j) * kWsSlot, kWsSlot, &sh.v_full[q]);
         ++viss[q];
       };
-      for (uint32_t j = 0; j < 2 && j < nblk; ++j) {
-        load_k(j);
-        load_v(j);
-      }
+      for (uint32_t j = 0; j < 2 && j < nblk; ++j) load_v(j);
       for (uint32_t j = 0; j < nblk; ++j) {
         const uint32_t s = j & 1, q = j % kWsIssuers, use = j / kWsIssuers;
-        // K(j + 2) once S(j) has read slot s
-        if (j + 2 < nblk) {
-          if (!ws_wait(&sh.k_empty[s], (j >> 1) & 1, &sh)) break;
-          load_k(j + 2);
-        }
         // P V(j), group 1, beside the issuer's group 0
         if (!ws_wait(&sh.p_ready[q], use & 1, &sh) || !ws_wait(&sh.v_full[q], use & 1, &sh))
           break;
@@ -452,14 +438,12 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       mma_commit(&sh.drain[kWsIssuers]);
       mbar_wait_bounded(&sh.drain[kWsIssuers], 0, kTcWait);
       mbar_wait_bounded(&sh.q_full, 0, kTcWait);
-      for (uint32_t q = 0; q < kWsIssuers; ++q) {
-        if (kiss[q] > 0) mbar_wait_bounded(&sh.k_full[q], (kiss[q] - 1) & 1, kTcWait);
+      for (uint32_t q = 0; q < kWsIssuers; ++q)
         if (viss[q] > 0) mbar_wait_bounded(&sh.v_full[q], (viss[q] - 1) & 1, kTcWait);
-      }
     }
     __syncwarp();
   } else if (warp <= kWsIssuers) {
-    // ---- MMA issuer p: blocks j = p, p + 3, ... (S / P buffer p, K / V slot j % 2) ----
+    // ---- MMA issuer p: blocks j = p, p + 3, ... (S / P buffer p, K slot p, V slot j % 2) ----
     const uint32_t p = warp - 1;
     if (lane == 0 && nblk > p) {
       constexpr uint32_t id_s = idesc_tf32(kWsTQ, kWsKB);
@@ -468,11 +452,21 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
       const uint64_t dqh = smem_desc_sw128(smem_addr(qhi));
       const uint64_t dql = dqh + (kWsQPlane >> 4);
       const uint32_t ts = tm + 128 * p;
+      // this issuer's K slot p: K(j) of its blocks, each loaded by the issuer
+      // itself as soon as S of its previous block has read the slot
+      uint8_t* kslot = base + kWsOffK + p * kWsSlot;
+      const uint64_t dkh = smem_desc_sw128(smem_addr(kslot));
+      const uint64_t dkl = dkh + (kWsTile >> 4);
+      uint32_t kiss = 0;
+      auto load_k = [&](uint32_t j) {
+        mbar_arrive_expect_tx(&sh.k_full[p], kWsSlot);
+        bulk_load(kslot, kimg + (uint64_t(bh) * nkt + kt0 + j) * kWsSlot, kWsSlot, &sh.k_full[p]);
+        ++kiss;
+      };
+      load_k(p);
       bool ok = ws_wait(&sh.q_full, 0, &sh);
       for (uint32_t j = p; ok && j < nblk; j += kWsIssuers) {
         const uint32_t use = j / kWsIssuers, s = j & 1;
-        const uint64_t dkh = smem_desc_sw128(smem_addr(base + kWsOffK + s * kWsSlot));
-        const uint64_t dkl = dkh + (kWsTile >> 4);
         // buffer p is free once both halves of P V(j - 3) have read P(j - 3)
         // (group 1 comes from the copy thread)
         if (use > 0 && !ws_wait(&sh.o_done[p], (use - 1) & 1, &sh)) break;
@@ -488,7 +482,13 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
           mma_tf32_ss(ts, dql + oq, dkh + okk, id_s, 1);
         }
         mma_commit(&sh.s_full[p]);
-        mma_commit(&sh.k_empty[s]);  // the K slot is free once these have read it
+        mma_commit(&sh.k_empty[p]);
+        // the next K of this issuer once these MMAs have read the slot (this
+        // thread would wait for the softmax of block j now in any case)
+        if (j + kWsIssuers < nblk) {
+          if (!ws_wait(&sh.k_empty[p], use & 1, &sh)) break;
+          load_k(j + kWsIssuers);
+        }
         if (!ws_wait(&sh.p_ready[p], use & 1, &sh) || !ws_wait(&sh.v_full[p], use & 1, &sh))
           break;
         tc_fence_after();
@@ -496,9 +496,11 @@ __global__ void __launch_bounds__(kWsThreads, 1) attn_ws_kernel(
         mma_commit(&sh.o_done[p]);
         mma_commit(&sh.v_empty[s]);
       }
-      // every MMA this thread issued has completed before TMEM is freed
+      // every MMA this thread issued has completed, and the copies it issued
+      // have landed, before TMEM is freed and the CTA can exit
       mma_commit(&sh.drain[p]);
       mbar_wait_bounded(&sh.drain[p], 0, kTcWait);
+      if (kiss > 0) mbar_wait_bounded(&sh.k_full[p], (kiss - 1) & 1, kTcWait);
     }
     __syncwarp();
   } else {
