@@ -200,9 +200,10 @@ __global__ void __launch_bounds__(256) jeff_prep_kernel(
     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ qh,
     float* __restrict__ kh, float* __restrict__ vh, uint32_t length, uint32_t hd,
-    uint32_t rotary, float eps) {
+    uint32_t rotary, float eps, uint8_t* flags) {
   pdl_enter();
   extern __shared__ float tile[];  // [hd][33]
+  bool bad = false;  // a value the tensor-core path cannot take (flags)
   __shared__ float scale_s[32];
   const uint32_t tid = threadIdx.x, head = blockIdx.y, t0 = blockIdx.x * 32;
   const uint32_t half = rotary / 2;
@@ -248,9 +249,69 @@ __global__ void __launch_bounds__(256) jeff_prep_kernel(
     }
     for (uint32_t idx = tid; idx < hd * 32; idx += 256) {
       const uint32_t t = idx / hd, i = idx - t * hd;
-      if (t0 + t < length) dst[(uint64_t(head) * length + t0 + t) * hd + i] = tile[i * 33 + t];
+      if (t0 + t < length) {
+        const float x = tile[i * 33 + t];
+        bad |= !(fabsf(x) < 1.099511627776e12f);  // 2^40
+        dst[(uint64_t(head) * length + t0 + t) * hd + i] = x;
+      }
     }
     __syncthreads();
+  }
+  if (flags && __syncthreads_or(bad) && tid == 0) flags[head] = 1;
+}
+
+// ---- Jeff attention on the tensor cores ----------------------------------------------
+//
+// For head_dim a multiple of 32 and a length a multiple of 128, the Jeff block
+// runs as tensor-core GEMMs around the masked softmax: S_h = Q_h K_h^T (the
+// 3xTF32 GEMM, batched over heads), the causal / active softmax of S, O_h =
+// P_h V_h (the same GEMM on V_h transposed), then the gate. Heads holding a
+// value that is non-finite or at least 2^40 are redone by the f32 kernel
+// (whose arithmetic follows the reference's handling of such values); below
+// 2^40 every scaled score is below 2^84, far from the -1e30 the softmax gives
+// masked keys and from overflow.
+
+// keep[k] = (active[k] != 0); *first = the smallest such k (untouched when
+// none): query q has a kept key (causal) exactly when q >= *first.
+__global__ void __launch_bounds__(256) jeff_keep_kernel(const float* __restrict__ active,
+                                                        uint8_t* __restrict__ keep, int* first,
+                                                        uint32_t length) {
+  pdl_enter();
+  for (uint32_t k = blockIdx.x * blockDim.x + threadIdx.x; k < length;
+       k += gridDim.x * blockDim.x) {
+    const bool on = active[k] != 0.0f;
+    keep[k] = on;
+    if (on) atomicMin(first, int(k));
+  }
+}
+
+// dst[b][c][r] = src[b][r][c] (rows, cols multiples of 32; CTA = 32 x 32
+// tile through shared memory). GATE: the Jeff output, dst = 0 for rows
+// r < *first (no kept key) and src * sigmoid(gate[the dst index]) otherwise.
+template <bool GATE>
+__global__ void __launch_bounds__(256) jeff_transpose_kernel(const float* __restrict__ src,
+                                                             float* __restrict__ dst,
+                                                             uint32_t rows, uint32_t cols,
+                                                             const float* __restrict__ gate,
+                                                             const int* first) {
+  pdl_enter();
+  __shared__ float tile[32][33];
+  const uint32_t r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const uint64_t boff = uint64_t(blockIdx.z) * rows * cols;
+  for (uint32_t i = threadIdx.x; i < 1024; i += 256) {
+    const uint32_t r = i >> 5, c = i & 31;
+    tile[r][c] = src[boff + uint64_t(r0 + r) * cols + c0 + c];
+  }
+  __syncthreads();
+  const int kfirst = GATE ? *first : 0;
+  for (uint32_t i = threadIdx.x; i < 1024; i += 256) {
+    const uint32_t c = i >> 5, r = i & 31;
+    const uint64_t o = boff + uint64_t(c0 + c) * rows + r0 + r;
+    float v = tile[r][c];
+    if constexpr (GATE)
+      v = int(r0 + r) < kfirst ? 0.0f
+                               : __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gate[o]))));
+    dst[o] = v;
   }
 }
 
@@ -679,13 +740,17 @@ static_assert(kWsTQ == kTQ, "the grid tiles the queries by 128");
 // stream (the Laya prep kernel sets them). When a.qimg is set, the images
 // exist already (the Laya prep kernel wrote them, with pre_flags) and q, k,
 // v are not read. Returns 1 when the shape is not covered (nothing launched).
-bool attn_tc_covers(uint32_t hd, uint64_t rows, const DeviceInfo& dev) {
-  // TFX_ATTN_KERNEL=f32: the f32-pipe kernel for every head
+// TFX_ATTN_KERNEL=f32: the f32-pipe kernel for every head (read once).
+bool attn_f32_only() {
   static const bool f32_only = [] {
     const char* e = getenv("TFX_ATTN_KERNEL");
     return e && std::string(e) == "f32";
   }();
-  return !f32_only && hd == 64 && rows < (uint64_t(1) << 31) && kWsSmem <= size_t(dev.smem_optin);
+  return f32_only;
+}
+
+bool attn_tc_covers(uint32_t hd, uint64_t rows, const DeviceInfo& dev) {
+  return !attn_f32_only() && hd == 64 && rows < (uint64_t(1) << 31) && kWsSmem <= size_t(dev.smem_optin);
 }
 
 int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo& dev,
@@ -776,12 +841,13 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
   return rc;
 }
 
+// f32_only: skip the tensor-core kernel (a redo of flagged heads).
 int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t stream,
-                const uint8_t* pre_flags) {
+                const uint8_t* pre_flags, bool f32_only = false) {
   int st = TFX_OK;
   const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
-  {
+  if (!f32_only) {
     const int rc = attn_launch_tc(op, a, batch, dev, stream, pre_flags);
     if (rc != 1) return rc;
   }
@@ -881,7 +947,7 @@ int laya_prep(const char* op, const float* qkv, const float* cos_t, const float*
 int jeff_prep(const char* op, const float* q, const float* k, const float* v,
               const float* q_norm, const float* k_norm, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t length, int64_t heads, int64_t head_dim,
-              int64_t rotary_dim, float eps, cudaStream_t stream) {
+              int64_t rotary_dim, float eps, cudaStream_t stream, uint8_t* flags = nullptr) {
   TFX_REQUIRE(length >= 0 && heads >= 0 && head_dim >= 0, op, "shape",
               "extents must be non-negative");
   TFX_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0, op,
@@ -902,7 +968,7 @@ int jeff_prep(const char* op, const float* q, const float* k, const float* v,
   }
   return launch_kernel(op, jeff_prep_kernel, dim3(unsigned((length + 31) / 32), unsigned(heads)),
                        dim3(256), smem, stream, 1, q, k, v, q_norm, k_norm, cos_t, sin_t, qh, kh,
-                       vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps);
+                       vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps, flags);
 }
 
 // img (optional, head_dim 64 with attn_tc_covers): q, k, v as tile images
@@ -937,6 +1003,100 @@ int attention(const char* op, const float* qh, const float* kh, const float* vh,
   a.digest_words = digest_words;
   a.digest_summary = digest_summary;
   return attn_launch(op, a, uint32_t(d->batch), stream, pre_flags);
+}
+
+// The Jeff attention descriptor (fused.cu / lib.rs Jeff path): causal over the
+// active keys, empty rows 0, gated, out (hidden, length).
+tfx_attention_desc jeff_desc(const float* gate, const float* mask, int64_t length, int64_t heads,
+                             int64_t head_dim) {
+  tfx_attention_desc d;
+  tfx_attention_desc_init(&d, 1, heads, length, head_dim);
+  d.empty_rows = TFX_ATTN_EMPTY_ZERO;
+  d.causal = 1;
+  d.active = mask;
+  d.gate = gate;
+  d.out_tok = 1;
+  d.out_feat = length;
+  d.out_batch = 0;
+  return d;
+}
+
+// The Jeff block on the tensor cores (length % 128 == 0, head_dim % 32 == 0):
+// prep -> S_h = Q_h K_h^T -> causal / active softmax in place -> V_h^T ->
+// O_h = P_h V_h -> gate into (hidden, length); heads that prep flagged are
+// then redone by the f32 kernel. qkv: the 3 n floats of head-major scratch.
+int jeff_attention_tc(const char* op, float* qkv, const float* q, const float* k, const float* v,
+                      const float* gate, const float* q_norm, const float* k_norm,
+                      const float* mask, const float* cos_t, const float* sin_t, float* out,
+                      int64_t length, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                      float eps, cudaStream_t s) {
+  const int64_t n = length * heads * head_dim;
+  const int64_t nscore = heads * length * length;
+  // scratch: scores | V^T | O | keep bytes | first active key | head flags
+  const size_t keep_off = size_t(nscore + 2 * n) * 4;
+  const size_t first_off = keep_off + (size_t(length) + 255) / 256 * 256;
+  const size_t flags_off = first_off + 256;
+  uint8_t* work = nullptr;
+  cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&work),
+                                 flags_off + (size_t(heads) + 255) / 256 * 256, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  }
+  float* qh = qkv;
+  float* kh = qkv + n;
+  float* vh = qkv + 2 * n;
+  float* scores = reinterpret_cast<float*>(work);
+  float* vt = scores + nscore;
+  float* o = vt + n;
+  uint8_t* keep = work + keep_off;
+  int* first = reinterpret_cast<int*>(work + first_off);
+  uint8_t* flags = work + flags_off;
+  const uint32_t L = uint32_t(length), hd = uint32_t(head_dim), H = uint32_t(heads);
+  int rc = TFX_OK;
+  e = cudaMemsetAsync(first, 0x7F, 4, s);  // 0x7F7F7F7F: no active key yet
+  if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, size_t(heads), s);
+  if (e != cudaSuccess) rc = fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
+  if (rc == TFX_OK)
+    rc = jeff_prep(op, q, k, v, q_norm, k_norm, cos_t, sin_t, qh, kh, vh, length, heads,
+                   head_dim, rotary_dim, eps, s, flags);
+  if (rc == TFX_OK)
+    rc = launch_kernel(op, jeff_keep_kernel, dim3(std::min<uint32_t>((L + 255) / 256, 148)),
+                       dim3(256), 0, s, 1, mask, keep, first, L);
+  if (rc == TFX_OK) rc = gemm_batched_f32(op, qh, kh, scores, head_dim, length, heads * length,
+                                          length, s);
+  if (rc == TFX_OK) {
+    tfx_softmax_desc sd;
+    tfx_softmax_desc_init(&sd, 1, heads, length, length);
+    sd.scale = 1.0f / sqrtf(float(head_dim));
+    sd.semantics = TFX_SOFTMAX_FILL;
+    sd.causal = 1;
+    sd.keep = keep;
+    sd.keep_stride_b = 0;
+    sd.keep_stride_q = 0;
+    sd.keep_stride_k = 1;
+    rc = masked_softmax_rows(scores, scores, &sd, 0, heads * length, s);
+  }
+  const float* no_gate = nullptr;
+  const int* no_first = nullptr;
+  if (rc == TFX_OK)
+    rc = launch_kernel(op, jeff_transpose_kernel<false>, dim3(L / 32, hd / 32, H), dim3(256), 0,
+                       s, 1, vh, vt, L, hd, no_gate, no_first);
+  if (rc == TFX_OK)
+    rc = gemm_batched_f32(op, scores, vt, o, length, head_dim, heads * length, length, s);
+  if (rc == TFX_OK)
+    rc = launch_kernel(op, jeff_transpose_kernel<true>, dim3(L / 32, hd / 32, H), dim3(256), 0, s,
+                       1, o, out, L, hd, gate, static_cast<const int*>(first));
+  if (rc == TFX_OK) {
+    // flagged heads: the f32 kernel, which returns at once for the others
+    const tfx_attention_desc d = jeff_desc(gate, mask, length, heads, head_dim);
+    AttnArgs a = attn_args(qh, kh, vh, out, &d);
+    a.vflags = flags;
+    a.vflag_mode = 2;
+    rc = attn_launch(op, a, 1, s, nullptr, true);
+  }
+  cudaFreeAsync(work, s);
+  return rc;
 }
 
 AttnArgs attn_args(const float* qh, const float* kh, const float* vh, float* out,
@@ -1132,18 +1292,21 @@ int tfx_jeff_attention_f32(const float* q, const float* k, const float* v, const
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
+  // Tensor-core route (GEMM, masked softmax, GEMM): whole 128-token tiles,
+  // whole 32 x 32 transposition tiles, and scores of at most 2^30 values.
+  const bool tc = !attn_f32_only() && length % 128 == 0 && head_dim % 32 == 0 &&
+                  heads * length * length <= (int64_t(1) << 30) && aligned(gate, 4) &&
+                  aligned(mask, 4);
+  if (tc) {
+    const int rc = jeff_attention_tc(op, scratch, q, k, v, gate, q_norm, k_norm, mask, cos_table,
+                                     sin_table, out, length, heads, head_dim, rotary_dim, eps, s);
+    cudaFreeAsync(scratch, s);
+    return rc;
+  }
   int rc = jeff_prep(op, q, k, v, q_norm, k_norm, cos_table, sin_table, scratch, scratch + n,
                      scratch + 2 * n, length, heads, head_dim, rotary_dim, eps, s);
   if (rc == TFX_OK) {
-    tfx_attention_desc d;
-    tfx_attention_desc_init(&d, 1, heads, length, head_dim);
-    d.empty_rows = TFX_ATTN_EMPTY_ZERO;
-    d.causal = 1;
-    d.active = mask;
-    d.gate = gate;
-    d.out_tok = 1;
-    d.out_feat = length;
-    d.out_batch = 0;
+    const tfx_attention_desc d = jeff_desc(gate, mask, length, heads, head_dim);
     rc = attention(op, scratch, scratch + n, scratch + 2 * n, out, &d, s);
   }
   cudaFreeAsync(scratch, s);

@@ -93,7 +93,15 @@ struct GemmArgs {
   uint32_t inter;         // GeGLU: I, the row offset of the gate half
   uint32_t mtiles, ntiles;
   int vec4;               // every output row 16-byte aligned and nout % 4 == 0
+  // batched weights (bias + act only): tokens [b * batch_tokens, (b + 1) *
+  // batch_tokens) use weight rows [b * batch_wrows, ...); 0 = one weight
+  uint32_t batch_tokens, batch_wrows;
 };
+
+// First weight row of the batch that token t belongs to.
+__device__ __forceinline__ uint32_t batch_wrow(const GemmArgs& a, uint32_t t) {
+  return a.batch_tokens ? (t / a.batch_tokens) * a.batch_wrows : 0u;
+}
 
 __device__ __forceinline__ float tf32_rna(float v) {
   uint32_t r;
@@ -260,7 +268,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           row_w0 = int(n * (kBN / 2));
           row_w1 = int(a.inter + n * (kBN / 2));
         } else {
-          row_w0 = int(n * kBN);
+          row_w0 = int(batch_wrow(a, m * kBM) + n * kBN);
           row_w1 = row_w0 + kBN / 2;
         }
         for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
@@ -464,6 +472,7 @@ __global__ void __launch_bounds__(128) gemm_epi_simt_kernel(const float* __restr
   const uint32_t t = m * kBM + threadIdx.x;
   if (t >= a.length) return;
   const float* xt = x + uint64_t(t) * in_dim;
+  w += uint64_t(batch_wrow(a, t)) * in_dim;
   for (uint32_t o0 = blockIdx.y * 16; o0 < a.nout; o0 += gridDim.y * 16) {
     for (uint32_t j = o0; j < min(o0 + 16, a.nout); ++j) {
       auto proj = [&](uint32_t o) {
@@ -540,9 +549,11 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 
 // The shared host path. nproj = rows of the weight (2I or out_dim), nout =
 // outputs per token (I or out_dim).
+// batch_tokens > 0 (bias + act): batched weights, batch_tokens tokens (a
+// multiple of 128 dividing length) per batch of nout weight rows.
 int gemm_epilogue(const char* op, int epi, int act, const float* x, const float* w,
                   const float* bias, float* y, int64_t in_dim, int64_t nproj, int64_t nout,
-                  int64_t length, cudaStream_t stream) {
+                  int64_t length, cudaStream_t stream, int64_t batch_tokens = 0) {
   if (nout == 0 || length == 0) return TFX_OK;  // an empty output: a no-op, as the reference
   TFX_REQUIRE(x || in_dim == 0, op, "x", "null pointer");
   TFX_REQUIRE(w || in_dim == 0, op, "weight", "null pointer");
@@ -570,6 +581,13 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
                                        : (nout + kBN - 1) / kBN);
   a.vec4 = nout % 4 == 0 && aligned(y, 16);
+  if (batch_tokens > 0) {
+    TFX_REQUIRE(epi == kEpiBiasAct && batch_tokens % kBM == 0 && length % batch_tokens == 0 &&
+                    nproj == nout * (length / batch_tokens),
+                op, "batch", "batched weights need whole 128-token tiles per batch");
+    a.batch_tokens = uint32_t(batch_tokens);
+    a.batch_wrows = uint32_t(nout);
+  }
   TFX_REQUIRE(uint64_t(a.mtiles) * a.ntiles < (uint64_t(1) << 31), op, "shape",
               "too many tiles for one call");
   const uint64_t kp = round_up(size_t(in_dim), kBK);
@@ -581,7 +599,9 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   // can start at (GeGLU: I + 128 (ntiles - 1); bias + act: 256 ntiles - 128).
   const uint64_t xrows = uint64_t(a.mtiles) * kBM;
   const uint64_t wrows = epi == kEpiGeglu ? uint64_t(nproj) + kBN / 2
-                                          : uint64_t(a.ntiles) * kBN;
+                        : batch_tokens > 0
+                            ? uint64_t(nproj) - uint64_t(nout) + uint64_t(a.ntiles) * kBN
+                            : uint64_t(a.ntiles) * kBN;
   const size_t xbytes = round_up(kp * size_t(xrows) * 4, 1024);
   const size_t wbytes = round_up(kp * size_t(wrows) * 4, 1024);
   const size_t fbytes = round_up((size_t(a.mtiles) + 1) * 4, 1024);
@@ -645,6 +665,18 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
 }
 
 }  // namespace
+
+// y (nout, length) = W_b^T x over batches of batch_tokens tokens: token t uses
+// the weight rows of batch t / batch_tokens (weight: (in_dim, nout * batches)
+// column-major, batch b's rows [b * nout, (b + 1) * nout)). Same arithmetic as
+// tfx_gemm_bias_act_ff_f32 without bias and activation.
+int gemm_batched_f32(const char* op, const float* x, const float* w, float* y, int64_t in_dim,
+                     int64_t nout, int64_t length, int64_t batch_tokens, cudaStream_t stream) {
+  TFX_REQUIRE(in_dim >= 0 && nout >= 0 && length >= 0 && batch_tokens > 0, op, "shape",
+              "extents must be non-negative");
+  return gemm_epilogue(op, kEpiBiasAct, TFX_ACT_IDENTITY, x, w, nullptr, y, in_dim,
+                       nout * (length / batch_tokens), nout, length, stream, batch_tokens);
+}
 
 int gemm_wait_timeouts(uint32_t* count) {
   const cudaError_t err = cudaMemcpyFromSymbol(count, g_gemm_wait_timeouts, sizeof(uint32_t));

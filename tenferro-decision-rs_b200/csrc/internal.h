@@ -34,5 +34,9 @@ int attention_wait_timeouts(uint32_t* count);
 
 // gemm_epilogue.cu: the same count for the tensor-core GEMM-epilogue kernel.
 int gemm_wait_timeouts(uint32_t* count);
+// Batched y (nout, length) = W_b^T x: token t uses the weight rows of batch
+// t / batch_tokens (gemm_epilogue.cu).
+int gemm_batched_f32(const char* op, const float* x, const float* w, float* y, int64_t in_dim,
+                     int64_t nout, int64_t length, int64_t batch_tokens, cudaStream_t stream);
 
 }  // namespace tfx

@@ -159,6 +159,46 @@ def test_jeff_attention(orc, hd, rot, heads, L):
     assert np.all(got.reshape(w, L)[:, 0] == 0.0)
 
 
+# Lengths that are whole 128-token tiles take the tensor-core route (3xTF32
+# GEMMs around the masked softmax); the others the f32 kernel.
+@pytest.mark.parametrize("hd,rot,heads,L,big_v", [
+    (256, 64, 4, 512, False), (64, 16, 3, 384, False), (128, 32, 2, 256, True)])
+def test_jeff_attention_tensor_cores(orc, hd, rot, heads, L, big_v):
+    w = heads * hd
+    theta, eps = 1e7, 1e-6
+    q, k, v, g = (splitmix_normal(L * w, 0x7E4F0A40 + i + hd) for i in range(4))
+    qn = splitmix_normal(hd, 0x7E4F0A48, std=0.1)
+    kn = splitmix_normal(hd, 0x7E4F0A49, std=0.1)
+    mask = (splitmix_uniform(L, 0x7E4F0A4A, 0.0, 1.0) > 0.3).astype(np.float32)
+    mask[:3] = 0.0  # queries 0..2 see no key: their rows are 0
+    if big_v:
+        # a value of 2^41 in head 1's V: that head goes to the f32 kernel
+        v.reshape(w, L)[hd + 7, L // 2] = 2.0 ** 41  # (length, hidden) time-first
+    c, s = orc.rope_tables_powf_f32(theta, L, rot)
+    out = empty(L * w)
+    ins = [dev(t) for t in (q, k, v, g, qn, kn, mask, c, s)]
+    call("tfx_jeff_attention_f32", *[P(t) for t in ins], P(out), L, heads, hd, rot,
+         ctypes.c_float(eps), S())
+    got = host(out)
+    want = orc.jeff_full_attention_f32(q, k, v, g, qn, kn, mask, L, heads, hd, rot, theta, eps)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"jeff attention (tensor cores) hd={hd}")
+    assert np.all(got.reshape(w, L)[:, :3] == 0.0)
+
+
+def test_jeff_attention_no_active_key(orc):
+    hd, rot, heads, L = 64, 16, 2, 128
+    w = heads * hd
+    q, k, v, g = (splitmix_normal(L * w, 0x7E4F0A50 + i) for i in range(4))
+    qn, kn = splitmix_normal(hd, 0x7E4F0A58, std=0.1), splitmix_normal(hd, 0x7E4F0A59, std=0.1)
+    mask = np.zeros(L, np.float32)
+    c, s = orc.rope_tables_powf_f32(1e7, L, rot)
+    out = empty(L * w)
+    ins = [dev(t) for t in (q, k, v, g, qn, kn, mask, c, s)]
+    call("tfx_jeff_attention_f32", *[P(t) for t in ins], P(out), L, heads, hd, rot,
+         ctypes.c_float(1e-6), S())
+    assert np.all(host(out) == 0.0)
+
+
 def attention_f64(qh, kh, vh, B, H, L, hd, scale, bias=None, causal=False, active=None):
     """Double-precision restatement of the additive-bias path (fused.cu:239-306)."""
     q = qh.reshape(B, H, L, hd).astype(np.float64)
