@@ -200,10 +200,9 @@ __global__ void __launch_bounds__(256) jeff_prep_kernel(
     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ qh,
     float* __restrict__ kh, float* __restrict__ vh, uint32_t length, uint32_t hd,
-    uint32_t rotary, float eps, uint8_t* flags) {
+    uint32_t rotary, float eps) {
   pdl_enter();
   extern __shared__ float tile[];  // [hd][33]
-  bool bad = false;  // a value the tensor-core path cannot take (flags)
   __shared__ float scale_s[32];
   const uint32_t tid = threadIdx.x, head = blockIdx.y, t0 = blockIdx.x * 32;
   const uint32_t half = rotary / 2;
@@ -249,15 +248,10 @@ __global__ void __launch_bounds__(256) jeff_prep_kernel(
     }
     for (uint32_t idx = tid; idx < hd * 32; idx += 256) {
       const uint32_t t = idx / hd, i = idx - t * hd;
-      if (t0 + t < length) {
-        const float x = tile[i * 33 + t];
-        bad |= !(fabsf(x) < 1.099511627776e12f);  // 2^40
-        dst[(uint64_t(head) * length + t0 + t) * hd + i] = x;
-      }
+      if (t0 + t < length) dst[(uint64_t(head) * length + t0 + t) * hd + i] = tile[i * 33 + t];
     }
     __syncthreads();
   }
-  if (flags && __syncthreads_or(bad) && tid == 0) flags[head] = 1;
 }
 
 // ---- Jeff attention on the tensor cores ----------------------------------------------
@@ -270,6 +264,115 @@ __global__ void __launch_bounds__(256) jeff_prep_kernel(
 // (whose arithmetic follows the reference's handling of such values); below
 // 2^40 every scaled score is below 2^84, far from the -1e30 the softmax gives
 // masked keys and from overflow.
+
+// hi = tf32(x), lo = x - hi (exact, so hi + lo == x); a value beyond the
+// largest tf32 (or non-finite) stays whole in hi with lo = 0. bad: |x| >= 2^40
+// or non-finite (the head goes to the f32 kernel).
+__device__ __forceinline__ void jeff_split(float x, float* hi, float* lo, bool* bad) {
+  const bool ok = fabsf(x) < 3.4e38f;
+  *bad |= !(fabsf(x) < 1.099511627776e12f);  // 2^40
+  *hi = ok ? tf32_round_finite(x) : x;
+  *lo = ok ? __fsub_rn(x, *hi) : 0.0f;
+}
+
+// The Jeff prep for the tensor-core route, one (32-token, head, tensor) tile
+// per CTA (blockIdx.z: 0 q, 1 k, 2 v), with the arithmetic of jeff_prep_kernel
+// (bit-identical values). q and k are written as the hi / lo planes of the
+// score GEMM's operands, head-major [head][token][HD]; v head-major as it is
+// (for the f32 kernel) and as the hi / lo planes of V^T [head][channel][token]
+// (the P V GEMM's weight). flags[head] = 1 when a value of the head is
+// non-finite or at least 2^40. length % 32 == 0.
+template <int HD>
+__global__ void __launch_bounds__(256) jeff_prep_planes_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ q_norm, const float* __restrict__ k_norm,
+    const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ qhi,
+    float* __restrict__ qlo, float* __restrict__ khi, float* __restrict__ klo,
+    float* __restrict__ vh, float* __restrict__ vthi, float* __restrict__ vtlo, uint32_t length,
+    uint32_t rotary, float eps, uint8_t* flags) {
+  pdl_enter();
+  __shared__ float tile[HD * 33];
+  __shared__ float scale_s[32];
+  const uint32_t tid = threadIdx.x, head = blockIdx.y, t0 = blockIdx.x * 32, which = blockIdx.z;
+  const uint64_t feat = uint64_t(head) * HD;
+  const float* src = which == 0 ? q : which == 1 ? k : v;
+  bool bad = false;
+  // eight loads in flight per thread before their shared-memory stores
+#pragma unroll
+  for (uint32_t idx0 = tid; idx0 < HD * 32; idx0 += 256 * 8) {
+    float r[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t idx = idx0 + 256 * u, i = idx >> 5, t = idx & 31;
+      r[u] = src[t0 + t + uint64_t(length) * (feat + i)];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t idx = idx0 + 256 * u;
+      tile[(idx >> 5) * 33 + (idx & 31)] = r[u];
+    }
+  }
+  __syncthreads();
+  if (which == 2) {
+    // V^T planes: row (head, channel i), 32 consecutive tokens per warp
+#pragma unroll 4
+    for (uint32_t idx = tid; idx < HD * 32; idx += 256) {
+      const uint32_t i = idx >> 5, t = idx & 31;
+      float h, l;
+      jeff_split(tile[i * 33 + t], &h, &l, &bad);
+      const uint64_t o = (feat + i) * length + t0 + t;
+      vthi[o] = h;
+      vtlo[o] = l;
+    }
+#pragma unroll 4
+    for (uint32_t idx = tid; idx < HD * 32; idx += 256) {
+      const uint32_t t = idx / HD, i = idx % HD;
+      vh[(uint64_t(head) * length + t0 + t) * HD + i] = tile[i * 33 + t];
+    }
+  } else {
+    const float* w = which == 0 ? q_norm : k_norm;
+    if (tid < 32) {
+      float ms = 0.0f;
+#pragma unroll 16
+      for (uint32_t i = 0; i < HD; ++i) {
+        const float x = tile[i * 33 + tid];
+        ms = __fadd_rn(ms, __fmul_rn(x, x));
+      }
+      ms = __fdiv_rn(ms, float(HD));
+      scale_s[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (uint32_t idx = tid; idx < HD * 32; idx += 256) {
+      const uint32_t i = idx >> 5, t = idx & 31;
+      tile[i * 33 + t] =
+          __fmul_rn(tile[i * 33 + t], __fmul_rn(scale_s[t], __fadd_rn(1.0f, __ldg(w + i))));
+    }
+    __syncthreads();
+    const uint32_t half = rotary / 2;
+    for (uint32_t idx = tid; idx < half * 32; idx += 256) {
+      const uint32_t i = idx >> 5, t = idx & 31;
+      const float c = __ldg(cos_t + uint64_t(t0 + t) * half + i);
+      const float sn = __ldg(sin_t + uint64_t(t0 + t) * half + i);
+      const float a = tile[i * 33 + t], b = tile[(i + half) * 33 + t];
+      tile[i * 33 + t] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, sn));
+      tile[(i + half) * 33 + t] = __fadd_rn(__fmul_rn(a, sn), __fmul_rn(b, c));
+    }
+    __syncthreads();
+    float* dhi = which == 0 ? qhi : khi;
+    float* dlo = which == 0 ? qlo : klo;
+#pragma unroll 4
+    for (uint32_t idx = tid; idx < HD * 32; idx += 256) {
+      const uint32_t t = idx / HD, i = idx % HD;
+      float h, l;
+      jeff_split(tile[i * 33 + t], &h, &l, &bad);
+      const uint64_t o = (uint64_t(head) * length + t0 + t) * HD + i;
+      dhi[o] = h;
+      dlo[o] = l;
+    }
+  }
+  if (__syncthreads_or(bad) && tid == 0) flags[head] = 1;
+}
 
 // keep[k] = (active[k] != 0); *first = the smallest such k (untouched when
 // none): query q has a kept key (causal) exactly when q >= *first.
@@ -285,33 +388,108 @@ __global__ void __launch_bounds__(256) jeff_keep_kernel(const float* __restrict_
   }
 }
 
-// dst[b][c][r] = src[b][r][c] (rows, cols multiples of 32; CTA = 32 x 32
-// tile through shared memory). GATE: the Jeff output, dst = 0 for rows
-// r < *first (no kept key) and src * sigmoid(gate[the dst index]) otherwise.
-template <bool GATE>
-__global__ void __launch_bounds__(256) jeff_transpose_kernel(const float* __restrict__ src,
-                                                             float* __restrict__ dst,
-                                                             uint32_t rows, uint32_t cols,
-                                                             const float* __restrict__ gate,
-                                                             const int* first) {
+// The causal / active softmax of one score row per warp, written as the
+// hi / lo planes of the P V GEMM's x operand. Row = (head, query q) of
+// scores [head][q][key] (keys contiguous, only keys <= q read); keys [0, W),
+// W = 128 (q / 128 + 1), are written (the P V contraction of q's 128-query
+// tile stops there): p = exp(s scale - max) / sum over the kept keys (key <=
+// q and keep[key]), 0 for the others. Rows q < *first have no kept key and
+// are written as zeros (their output is 0).
+__global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
+    const float* __restrict__ scores, const uint8_t* __restrict__ keep, const int* first,
+    float* __restrict__ phi, float* __restrict__ plo, uint32_t length, uint32_t rows, float scale) {
   pdl_enter();
-  __shared__ float tile[32][33];
-  const uint32_t r0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
-  const uint64_t boff = uint64_t(blockIdx.z) * rows * cols;
-  for (uint32_t i = threadIdx.x; i < 1024; i += 256) {
-    const uint32_t r = i >> 5, c = i & 31;
-    tile[r][c] = src[boff + uint64_t(r0 + r) * cols + c0 + c];
+  const uint32_t lane = threadIdx.x & 31;
+  const uint32_t row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint32_t qi = row % length;
+  const uint32_t width = (qi / 128 + 1) * 128;
+  const float* srow = scores + uint64_t(row) * length;
+  float* hrow = phi + uint64_t(row) * length;
+  float* lrow = plo + uint64_t(row) * length;
+  if (int(qi) < __ldg(first)) {
+    const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (uint32_t c = 4 * lane; c < width; c += 128) {
+      *reinterpret_cast<float4*>(hrow + c) = z;
+      *reinterpret_cast<float4*>(lrow + c) = z;
+    }
+    return;
   }
-  __syncthreads();
-  const int kfirst = GATE ? *first : 0;
-  for (uint32_t i = threadIdx.x; i < 1024; i += 256) {
-    const uint32_t c = i >> 5, r = i & 31;
-    const uint64_t o = boff + uint64_t(c0 + c) * rows + r0 + r;
-    float v = tile[r][c];
-    if constexpr (GATE)
-      v = int(r0 + r) < kfirst ? 0.0f
-                               : __fmul_rn(v, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gate[o]))));
-    dst[o] = v;
+  // the scaled score of key c + j, -inf when not kept
+  auto scaled = [&](float4 sv, uint32_t kb, uint32_t c, float* v) {
+    const float x[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool kept = c + j <= qi && ((kb >> (8 * j)) & 0xFFu) != 0;
+      v[j] = kept ? __fmul_rn(x[j], scale) : -INFINITY;
+    }
+  };
+  float mx = -INFINITY;
+  for (uint32_t c = 4 * lane; c <= qi; c += 128) {
+    float v[4];
+    scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
+           __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
+    mx = fmaxf(mx, fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])));
+  }
+  mx = warp_max(mx);
+  float sum = 0.0f;
+  for (uint32_t c = 4 * lane; c <= qi; c += 128) {
+    float v[4];
+    scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
+           __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) sum = __fadd_rn(sum, expf(__fsub_rn(v[j], mx)));
+  }
+  sum = warp_sum(sum);
+  const float r = __fdiv_rn(1.0f, sum);
+  for (uint32_t c = 4 * lane; c < width; c += 128) {
+    float h[4] = {0.0f, 0.0f, 0.0f, 0.0f}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c <= qi) {
+      float v[4];
+      scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
+             __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pv = __fmul_rn(expf(__fsub_rn(v[j], mx)), r);
+        h[j] = tf32_round_finite(pv);
+        l[j] = __fsub_rn(pv, h[j]);
+      }
+    }
+    *reinterpret_cast<float4*>(hrow + c) = make_float4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<float4*>(lrow + c) = make_float4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+// The Jeff output, elementwise over out (hidden, length): the sum of the P V
+// GEMM's slots for this element (slot p at o + p * n, p < split.pieces(head,
+// t / 128), added in slot order), 0 for tokens t < *first (no kept key), then
+// times sigmoid(gate). Four consecutive tokens per thread (length % 128 == 0).
+__global__ void __launch_bounds__(256) jeff_gate_kernel(const float* __restrict__ o,
+                                                        const float* __restrict__ gate,
+                                                        float* __restrict__ out, const int* first,
+                                                        uint64_t n, uint32_t length,
+                                                        uint32_t head_elems, CausalKSplit split) {
+  pdl_enter();
+  const int kfirst = __ldg(first);
+  for (uint64_t i = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n;
+       i += uint64_t(gridDim.x) * blockDim.x * 4) {
+    const uint32_t t = uint32_t(i % length);
+    const uint32_t pieces = split.pieces(uint32_t(i / head_elems), t / 128);
+    float4 v = __ldg(reinterpret_cast<const float4*>(o + i));
+    for (uint32_t p = 1; p < pieces; ++p) {
+      const float4 w = __ldg(reinterpret_cast<const float4*>(o + i + p * n));
+      v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z),
+                      __fadd_rn(v.w, w.w));
+    }
+    const float4 g = ld_stream(reinterpret_cast<const float4*>(gate + i));
+    const float x[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    float y[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      y[j] = int(t) + j < kfirst
+                 ? 0.0f
+                 : __fmul_rn(x[j], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-gg[j]))));
+    *reinterpret_cast<float4*>(out + i) = make_float4(y[0], y[1], y[2], y[3]);
   }
 }
 
@@ -345,6 +523,9 @@ struct AttnArgs {
   // the mask digest, when computed before the call (attn_keep_digest_kernel)
   const uint32_t* digest_words = nullptr;
   const uint8_t* digest_summary = nullptr;
+  // q = q + q_lo and k = k + k_lo when set (hi / lo planes, same layout)
+  const float* q_lo = nullptr;
+  const float* k_lo = nullptr;
 };
 
 // Channels ch .. ch + 3 of row `row` of head bh of q (t = 0), k (1) or v (2):
@@ -370,7 +551,13 @@ __device__ __forceinline__ float4 attn_ld4(const AttnArgs& a, int t, uint64_t bh
                        __fadd_rn(h.w, l.w));
   }
   const float* src = t == 0 ? a.q : t == 1 ? a.k : a.v;
-  return ld_stream(reinterpret_cast<const float4*>(src + (bh * a.length + row) * a.hd + ch));
+  const uint64_t off = (bh * a.length + row) * a.hd + ch;
+  const float* lo = t == 0 ? a.q_lo : t == 1 ? a.k_lo : nullptr;
+  const float4 h = ld_stream(reinterpret_cast<const float4*>(src + off));
+  if (!lo) return h;
+  const float4 l = ld_stream(reinterpret_cast<const float4*>(lo + off));
+  return make_float4(__fadd_rn(h.x, l.x), __fadd_rn(h.y, l.y), __fadd_rn(h.z, l.z),
+                     __fadd_rn(h.w, l.w));
 }
 
 __device__ __forceinline__ bool routed_away(const AttnArgs& a, uint32_t bh) {
@@ -947,7 +1134,7 @@ int laya_prep(const char* op, const float* qkv, const float* cos_t, const float*
 int jeff_prep(const char* op, const float* q, const float* k, const float* v,
               const float* q_norm, const float* k_norm, const float* cos_t, const float* sin_t,
               float* qh, float* kh, float* vh, int64_t length, int64_t heads, int64_t head_dim,
-              int64_t rotary_dim, float eps, cudaStream_t stream, uint8_t* flags = nullptr) {
+              int64_t rotary_dim, float eps, cudaStream_t stream) {
   TFX_REQUIRE(length >= 0 && heads >= 0 && head_dim >= 0, op, "shape",
               "extents must be non-negative");
   TFX_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0, op,
@@ -968,7 +1155,7 @@ int jeff_prep(const char* op, const float* q, const float* k, const float* v,
   }
   return launch_kernel(op, jeff_prep_kernel, dim3(unsigned((length + 31) / 32), unsigned(heads)),
                        dim3(256), smem, stream, 1, q, k, v, q_norm, k_norm, cos_t, sin_t, qh, kh,
-                       vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps, flags);
+                       vh, uint32_t(length), uint32_t(head_dim), uint32_t(rotary_dim), eps);
 }
 
 // img (optional, head_dim 64 with attn_tc_covers): q, k, v as tile images
@@ -1025,15 +1212,21 @@ tfx_attention_desc jeff_desc(const float* gate, const float* mask, int64_t lengt
 // prep -> S_h = Q_h K_h^T -> causal / active softmax in place -> V_h^T ->
 // O_h = P_h V_h -> gate into (hidden, length); heads that prep flagged are
 // then redone by the f32 kernel. qkv: the 3 n floats of head-major scratch.
-int jeff_attention_tc(const char* op, float* qkv, const float* q, const float* k, const float* v,
+int jeff_attention_tc(const char* op, const float* q, const float* k, const float* v,
                       const float* gate, const float* q_norm, const float* k_norm,
                       const float* mask, const float* cos_t, const float* sin_t, float* out,
                       int64_t length, int64_t heads, int64_t head_dim, int64_t rotary_dim,
                       float eps, cudaStream_t s) {
   const int64_t n = length * heads * head_dim;
   const int64_t nscore = heads * length * length;
-  // scratch: scores | V^T | O | keep bytes | first active key | head flags
-  const size_t keep_off = size_t(nscore + 2 * n) * 4;
+  CausalKSplit split;
+  int rc = gemm_causal_k_split(heads * length, length, &split);
+  if (rc != TFX_OK) return rc;
+  const uint32_t slots = split.max_pieces(uint32_t(heads));
+  // scratch (floats): q hi | q lo | k hi | k lo | v | V^T hi | V^T lo |
+  // scores | P hi | P lo | O slots, then keep bytes | first active key | flags
+  const size_t floats = size_t(7 * n + 3 * nscore + int64_t(slots) * n);
+  const size_t keep_off = floats * 4;
   const size_t first_off = keep_off + (size_t(length) + 255) / 256 * 256;
   const size_t flags_off = first_off + 256;
   uint8_t* work = nullptr;
@@ -1043,54 +1236,76 @@ int jeff_attention_tc(const char* op, float* qkv, const float* q, const float* k
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
   }
-  float* qh = qkv;
-  float* kh = qkv + n;
-  float* vh = qkv + 2 * n;
-  float* scores = reinterpret_cast<float*>(work);
-  float* vt = scores + nscore;
-  float* o = vt + n;
+  float* f = reinterpret_cast<float*>(work);
+  float* qhi = f;
+  float* qlo = f + n;
+  float* khi = f + 2 * n;
+  float* klo = f + 3 * n;
+  float* vh = f + 4 * n;
+  float* vthi = f + 5 * n;
+  float* vtlo = f + 6 * n;
+  float* scores = f + 7 * n;
+  float* phi = scores + nscore;
+  float* plo = phi + nscore;
+  float* o = plo + nscore;
   uint8_t* keep = work + keep_off;
   int* first = reinterpret_cast<int*>(work + first_off);
   uint8_t* flags = work + flags_off;
   const uint32_t L = uint32_t(length), hd = uint32_t(head_dim), H = uint32_t(heads);
-  int rc = TFX_OK;
   e = cudaMemsetAsync(first, 0x7F, 4, s);  // 0x7F7F7F7F: no active key yet
   if (e == cudaSuccess) e = cudaMemsetAsync(flags, 0, size_t(heads), s);
   if (e != cudaSuccess) rc = fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
-  if (rc == TFX_OK)
-    rc = jeff_prep(op, q, k, v, q_norm, k_norm, cos_t, sin_t, qh, kh, vh, length, heads,
-                   head_dim, rotary_dim, eps, s, flags);
+  if (rc == TFX_OK) {
+    const dim3 grid(L / 32, H, 3);
+    auto prep = [&](auto kernel) {
+      return launch_kernel(op, kernel, grid, dim3(256), 0, s, 1, q, k, v, q_norm, k_norm, cos_t,
+                           sin_t, qhi, qlo, khi, klo, vh, vthi, vtlo, L, uint32_t(rotary_dim),
+                           eps, flags);
+    };
+    rc = hd == 256   ? prep(jeff_prep_planes_kernel<256>)
+         : hd == 128 ? prep(jeff_prep_planes_kernel<128>)
+                     : prep(jeff_prep_planes_kernel<64>);
+  }
   if (rc == TFX_OK)
     rc = launch_kernel(op, jeff_keep_kernel, dim3(std::min<uint32_t>((L + 255) / 256, 148)),
                        dim3(256), 0, s, 1, mask, keep, first, L);
-  if (rc == TFX_OK) rc = gemm_batched_f32(op, qh, kh, scores, head_dim, length, heads * length,
-                                          length, s);
+  // S = Q K^T per head; scores above the diagonal's 256-key tiles are never
+  // read and left unwritten
   if (rc == TFX_OK) {
-    tfx_softmax_desc sd;
-    tfx_softmax_desc_init(&sd, 1, heads, length, length);
-    sd.scale = 1.0f / sqrtf(float(head_dim));
-    sd.semantics = TFX_SOFTMAX_FILL;
-    sd.causal = 1;
-    sd.keep = keep;
-    sd.keep_stride_b = 0;
-    sd.keep_stride_q = 0;
-    sd.keep_stride_k = 1;
-    rc = masked_softmax_rows(scores, scores, &sd, 0, heads * length, s);
+    const float* planes[4] = {qhi, qlo, khi, klo};
+    rc = gemm_batched_f32(op, nullptr, nullptr, scores, head_dim, length, heads * length, length,
+                          s, 1, planes);
   }
-  const float* no_gate = nullptr;
-  const int* no_first = nullptr;
-  if (rc == TFX_OK)
-    rc = launch_kernel(op, jeff_transpose_kernel<false>, dim3(L / 32, hd / 32, H), dim3(256), 0,
-                       s, 1, vh, vt, L, hd, no_gate, no_first);
-  if (rc == TFX_OK)
-    rc = gemm_batched_f32(op, scores, vt, o, length, head_dim, heads * length, length, s);
-  if (rc == TFX_OK)
-    rc = launch_kernel(op, jeff_transpose_kernel<true>, dim3(L / 32, hd / 32, H), dim3(256), 0, s,
-                       1, o, out, L, hd, gate, static_cast<const int*>(first));
   if (rc == TFX_OK) {
-    // flagged heads: the f32 kernel, which returns at once for the others
+    const uint32_t rows = H * L;
+    rc = launch_kernel(op, jeff_softmax_planes_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, 1,
+                       static_cast<const float*>(scores), static_cast<const uint8_t*>(keep),
+                       static_cast<const int*>(first), phi, plo, L, rows,
+                       1.0f / sqrtf(float(head_dim)));
+  }
+  // O = P V per head, written (head, channel, token) into the split's slots
+  if (rc == TFX_OK) {
+    const float* planes[4] = {phi, plo, vthi, vtlo};
+    rc = gemm_batched_f32(op, nullptr, nullptr, o, length, head_dim, heads * length, length, s, 2,
+                          planes, 1);
+  }
+  if (rc == TFX_OK) {
+    int st = TFX_OK;
+    const DeviceInfo& dev = device_info(&st);
+    if (st != TFX_OK) rc = st;
+    const unsigned grid = unsigned(std::min<int64_t>((n / 4 + 255) / 256, int64_t(dev.sms) * 8));
+    if (rc == TFX_OK)
+      rc = launch_kernel(op, jeff_gate_kernel, dim3(grid), dim3(256), 0, s, 1,
+                         static_cast<const float*>(o), gate, out, static_cast<const int*>(first),
+                         uint64_t(n), L, hd * L, split);
+  }
+  if (rc == TFX_OK) {
+    // flagged heads: the f32 kernel (q, k as hi + lo), which returns at once
+    // for the others
     const tfx_attention_desc d = jeff_desc(gate, mask, length, heads, head_dim);
-    AttnArgs a = attn_args(qh, kh, vh, out, &d);
+    AttnArgs a = attn_args(qhi, khi, vh, out, &d);
+    a.q_lo = qlo;
+    a.k_lo = klo;
     a.vflags = flags;
     a.vflag_mode = 2;
     rc = attn_launch(op, a, 1, s, nullptr, true);
@@ -1286,22 +1501,27 @@ int tfx_jeff_attention_f32(const float* q, const float* k, const float* v, const
   int st = TFX_OK;
   device_info(&st);
   if (st != TFX_OK) return st;
+  // Tensor-core route (score GEMM, masked softmax, P V GEMM): whole 128-token
+  // tiles, head_dim 64, 128 or 256 (one GEMM tile), scores of at most 2^30
+  // values, 16-byte aligned gate and out. The prep checks come first.
+  const bool tc = !attn_f32_only() && length % 128 == 0 &&
+                  (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+                  heads * length * length <= (int64_t(1) << 30) && aligned(gate, 16) &&
+                  aligned(out, 16);
+  if (tc) {
+    TFX_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0, op,
+                "rotary_dim", "rotary_dim must be even and at most head_dim");
+    TFX_REQUIRE(q && k && v && q_norm && k_norm, op, "tensors", "null pointer");
+    TFX_REQUIRE(rotary_dim == 0 || (cos_table && sin_table), op, "tables", "null pointer");
+    TFX_REQUIRE(heads < 65536, op, "shape", "too large");
+    return jeff_attention_tc(op, q, k, v, gate, q_norm, k_norm, mask, cos_table, sin_table, out,
+                             length, heads, head_dim, rotary_dim, eps, s);
+  }
   float* scratch = nullptr;
   const cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch), size_t(3 * n) * 4, s);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return fail(TFX_ERR_CUDA, op, "scratch", cudaGetErrorString(e));
-  }
-  // Tensor-core route (GEMM, masked softmax, GEMM): whole 128-token tiles,
-  // whole 32 x 32 transposition tiles, and scores of at most 2^30 values.
-  const bool tc = !attn_f32_only() && length % 128 == 0 && head_dim % 32 == 0 &&
-                  heads * length * length <= (int64_t(1) << 30) && aligned(gate, 4) &&
-                  aligned(mask, 4);
-  if (tc) {
-    const int rc = jeff_attention_tc(op, scratch, q, k, v, gate, q_norm, k_norm, mask, cos_table,
-                                     sin_table, out, length, heads, head_dim, rotary_dim, eps, s);
-    cudaFreeAsync(scratch, s);
-    return rc;
   }
   int rc = jeff_prep(op, q, k, v, q_norm, k_norm, cos_table, sin_table, scratch, scratch + n,
                      scratch + 2 * n, length, heads, head_dim, rotary_dim, eps, s);

@@ -56,6 +56,7 @@
 #include <mutex>
 #include <string>
 
+#include "causal_tiles.cuh"
 #include "common.cuh"
 #include "internal.h"
 #include "tc.cuh"
@@ -96,7 +97,31 @@ struct GemmArgs {
   // batched weights (bias + act only): tokens [b * batch_tokens, (b + 1) *
   // batch_tokens) use weight rows [b * batch_wrows, ...); 0 = one weight
   uint32_t batch_tokens, batch_wrows;
+  // causal batches (batched, batch_tokens == nout or == in_dim; t_b = the
+  // token's index in its batch): kCausalOut: only outputs o <= t_b are wanted
+  // (only the live tiles are computed, the others left unwritten); kCausalK:
+  // x[t][i] = 0 for i > t_b (a tile contracts up to its last token; the
+  // chunks are split evenly over the CTAs, piece p of a tile writes slot p,
+  // y + p * slot_stride).
+  uint32_t causal;
+  uint32_t mb;         // 128-token tiles per batch (causal modes)
+  uint64_t items;      // tiles (kCausalOut: live tiles) dealt round robin
+  uint64_t slot_stride;
+  CausalKSplit split;  // kCausalK
+  // batched only: y of batch b is (nout, batch_tokens), token-contiguous:
+  // y[b * nout * batch_tokens + o * batch_tokens + t_b]
+  int out_t;
 };
+
+// A run of K stages [s0, s1) of tile (m, n) that one CTA computes, written
+// to output slot `slot`.
+struct GemmPiece {
+  uint32_t m, n, s0, s1, slot;
+  bool skip;  // a tile with a non-finite operand (the SIMT kernel's)
+};
+
+constexpr uint32_t kCausalOut = 1;
+constexpr uint32_t kCausalK = 2;
 
 // First weight row of the batch that token t belongs to.
 __device__ __forceinline__ uint32_t batch_wrow(const GemmArgs& a, uint32_t t) {
@@ -190,6 +215,57 @@ __device__ __forceinline__ bool tile_skipped(const GemmArgs& a, uint32_t m) {
   return __ldcg(a.flags + m) != 0u || __ldcg(a.flags + a.mtiles) != 0u;
 }
 
+// The CTA's first work item.
+__device__ __forceinline__ uint64_t first_item(const GemmArgs& a) {
+  return a.causal == kCausalK ? a.split.start(blockIdx.x) : uint64_t(blockIdx.x);
+}
+
+// The CTA's next piece of work from item i (advanced past it); false at the
+// end. Every role of the CTA walks the same sequence.
+template <int SK>
+__device__ __forceinline__ bool next_piece(const GemmArgs& a, uint32_t nst, uint64_t& i,
+                                           GemmPiece& p) {
+  if (a.causal == kCausalK) {
+    // 128-key chunks: kBM / SK stages each
+    const uint64_t end = a.split.start(blockIdx.x + 1);
+    if (i >= end) return false;
+    const uint32_t batch = uint32_t(i / a.split.per_batch);
+    const uint64_t r = i - uint64_t(batch) * a.split.per_batch;
+    const uint32_t lm = CausalKSplit::row_of(r);
+    const uint32_t c0 = uint32_t(r - CausalKSplit::prefix(lm));
+    const uint32_t c1 = uint32_t(min(uint64_t(lm) + 1, uint64_t(c0) + (end - i)));
+    p.m = batch * a.mb + lm;
+    p.n = 0;
+    p.s0 = c0 * (kBM / SK);
+    p.s1 = min(nst, c1 * (kBM / SK));
+    p.slot = blockIdx.x - a.split.owner(a.split.first(batch, lm));
+    p.skip = tile_skipped(a, p.m);
+    i += c1 - c0;
+    return true;
+  }
+  for (; i < a.items; i += gridDim.x) {
+    if (a.causal == kCausalOut) {
+      const uint64_t per = live_prefix(a.mb);
+      const uint32_t batch = uint32_t(i / per);
+      const uint64_t r = i - uint64_t(batch) * per;
+      const uint32_t lm = live_row(r);
+      p.m = batch * a.mb + lm;
+      p.n = uint32_t(r - live_prefix(lm));
+    } else {
+      p.m = uint32_t(i / a.ntiles);
+      p.n = uint32_t(i - uint64_t(p.m) * a.ntiles);
+    }
+    if (tile_skipped(a, p.m)) continue;
+    p.s0 = 0;
+    p.s1 = nst;
+    p.slot = 0;
+    p.skip = false;
+    i += gridDim.x;
+    return true;
+  }
+  return false;
+}
+
 template <int EPI, int ACT>
 __device__ __forceinline__ float epi_act(float v) {
   if constexpr (EPI == kEpiBiasAct && ACT == TFX_ACT_GELU_ERF) return math::gelu_mlx(v);
@@ -225,14 +301,12 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
   constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBBytes;
   constexpr uint32_t kSpf = FK / SK;  // stages per partial
   const uint32_t nst = a.nk * (kBK / SK);     // stages per tile
-  const uint32_t npart = (nst + kSpf - 1) / kSpf;  // partials per tile (the last may be short)
   extern __shared__ __align__(1024) uint8_t gemm_smem[];
   __shared__ GemmShared sh;
   pdl_enter();
   const uint32_t tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) &
                                              ~uintptr_t(1023));
-  const uint32_t ntiles_total = a.mtiles * a.ntiles;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -259,9 +333,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
-      for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
-        const uint32_t m = tile / a.ntiles, n = tile - m * a.ntiles;
-        if (tile_skipped(a, m)) continue;
+      uint64_t it = first_item(a);
+      GemmPiece pc;
+      while (ok && next_piece<SK>(a, nst, it, pc)) {
+        if (pc.skip) continue;
+        const uint32_t m = pc.m, n = pc.n;
         const int row_x = int(m * kBM);
         int row_w0, row_w1;
         if constexpr (EPI == kEpiGeglu) {
@@ -271,7 +347,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           row_w0 = int(batch_wrow(a, m * kBM) + n * kBN);
           row_w1 = row_w0 + kBN / 2;
         }
-        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
+        for (uint32_t kc = pc.s0; kc < pc.s1; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           if (use > 0 && !gemm_wait(&sh.empty[s], (use - 1) & 1, &sh)) {
             ok = false;
@@ -304,13 +380,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
       };
       uint32_t g = 0, pg = 0;  // stages and partials issued
       bool ok = true;
-      for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
-        const uint32_t m = tile / a.ntiles;
-        if (tile_skipped(a, m)) continue;
-        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
+      uint64_t it = first_item(a);
+      GemmPiece pc;
+      while (ok && next_piece<SK>(a, nst, it, pc)) {
+        if (pc.skip) continue;
+        for (uint32_t kc = pc.s0; kc < pc.s1; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           const uint32_t pb = pg & 1, puse = pg >> 1;
-          const bool first = kc % kSpf == 0;
+          const bool first = (kc - pc.s0) % kSpf == 0;
           if ((first && puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
               !gemm_wait(&sh.full[s], use & 1, &sh)) {
             ok = false;
@@ -331,7 +408,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
           for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x hi * w hi
             mma_tf32_ss(d, desc(ah + ks * 32), desc(bh + ks * 32), idesc, 1);
           mma_commit(&sh.empty[s]);  // the stage is free once these MMAs have read it
-          if (kc % kSpf == kSpf - 1 || kc + 1 == nst) {
+          if ((kc - pc.s0) % kSpf == kSpf - 1 || kc + 1 == pc.s1) {
             mma_commit(&sh.part_full[pb]);  // and the partial is complete
             ++pg;
           }
@@ -355,12 +432,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
     float2 acc2[64];  // 128 f32 sums, added two per instruction (FADD2)
     uint32_t g = 0;
     bool ok = true;
-    for (uint32_t tile = blockIdx.x; ok && tile < ntiles_total; tile += gridDim.x) {
-      const uint32_t m = tile / a.ntiles, n = tile - m * a.ntiles;
-      if (tile_skipped(a, m)) continue;
+    uint64_t it = first_item(a);
+    GemmPiece pc;
+    while (ok && next_piece<SK>(a, nst, it, pc)) {
+      const uint32_t m = pc.m, n = pc.n;
+      // a skipped piece (kCausalK) writes zeros: the SIMT kernel fills slot 0
+      const uint32_t tpart = pc.skip ? 0u : (pc.s1 - pc.s0 + kSpf - 1) / kSpf;
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc2[j] = make_float2(0.0f, 0.0f);
-      for (uint32_t kc = 0; kc < npart; ++kc, ++g) {
+      for (uint32_t kc = 0; kc < tpart; ++kc, ++g) {
         const uint32_t pb = g & 1, puse = g >> 1;
         bool got = true;
         if (lane == 0) got = gemm_wait(&sh.part_full[pb], puse & 1, &sh);
@@ -420,7 +500,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
         const uint32_t o0 = n * kBN + 128 * half;  // first output row of this thread
         if (o0 >= a.nout) continue;
         const uint32_t valid = min(128u, a.nout - o0);
-        float* yr = a.y + uint64_t(t) * a.nout + o0;
+        if (a.out_t) {  // identity epilogue; a warp stores 32 consecutive tokens
+          const uint32_t b = t / a.batch_tokens, tb = t - b * a.batch_tokens;
+          float* yc = a.y + uint64_t(pc.slot) * a.slot_stride +
+                      (uint64_t(b) * a.nout + o0) * a.batch_tokens + tb;
+#pragma unroll
+          for (int c = 0; c < 128; ++c)  // fully unrolled: acc stays in registers
+            if (uint32_t(c) < valid) yc[uint64_t(c) * a.batch_tokens] = acc[c];
+          continue;
+        }
+        float* yr = a.y + uint64_t(pc.slot) * a.slot_stride + uint64_t(t) * a.nout + o0;
 #pragma unroll
         for (int c = 0; c < 128; c += 4) {
           float v[4];
@@ -503,8 +592,9 @@ int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const 
                                    int(kGemmSmem));
   });
   if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
-  const uint32_t tiles = a.mtiles * a.ntiles;
-  const unsigned grid = unsigned(std::min<uint32_t>(tiles, uint32_t(dev.sms)));
+  const unsigned grid = a.causal == kCausalK
+                            ? a.split.grid
+                            : unsigned(std::min<uint64_t>(a.items, uint64_t(dev.sms)));
   return launch_kernel(op, kernel, dim3(grid), dim3(kGThreads), kGemmSmem, stream, 1, maps[0],
                        maps[1], maps[2], maps[3], a);
 }
@@ -551,12 +641,20 @@ size_t round_up(size_t v, size_t m) { return (v + m - 1) / m * m; }
 // outputs per token (I or out_dim).
 // batch_tokens > 0 (bias + act): batched weights, batch_tokens tokens (a
 // multiple of 128 dividing length) per batch of nout weight rows.
+// planes (optional, batched only): x and the weight already split, {x hi,
+// x lo, w hi, w lo}, row-major with in_dim (a multiple of 32) values per row:
+// no split pass, no SIMT pass (the caller routes non-finite values itself).
+// out_t: the token-contiguous batched output (GemmArgs::out_t).
 int gemm_epilogue(const char* op, int epi, int act, const float* x, const float* w,
                   const float* bias, float* y, int64_t in_dim, int64_t nproj, int64_t nout,
-                  int64_t length, cudaStream_t stream, int64_t batch_tokens = 0) {
+                  int64_t length, cudaStream_t stream, int64_t batch_tokens = 0,
+                  uint32_t causal = 0, const float* const* planes = nullptr, int out_t = 0) {
   if (nout == 0 || length == 0) return TFX_OK;  // an empty output: a no-op, as the reference
-  TFX_REQUIRE(x || in_dim == 0, op, "x", "null pointer");
-  TFX_REQUIRE(w || in_dim == 0, op, "weight", "null pointer");
+  TFX_REQUIRE(planes || x || in_dim == 0, op, "x", "null pointer");
+  TFX_REQUIRE(planes || w || in_dim == 0, op, "weight", "null pointer");
+  TFX_REQUIRE(!planes || (batch_tokens > 0 && in_dim > 0 && in_dim % kBK == 0 && planes[0] &&
+                          planes[1] && planes[2] && planes[3]),
+              op, "planes", "pre-split operands need a batched call and in_dim % 32 == 0");
   TFX_REQUIRE(y, op, "y", "null pointer");
   TFX_REQUIRE(in_dim < (int64_t(1) << 31) && nproj < (int64_t(1) << 30) &&
                   length < (int64_t(1) << 31),
@@ -581,12 +679,27 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
                                        : (nout + kBN - 1) / kBN);
   a.vec4 = nout % 4 == 0 && aligned(y, 16);
+  a.items = uint64_t(a.mtiles) * a.ntiles;
   if (batch_tokens > 0) {
     TFX_REQUIRE(epi == kEpiBiasAct && batch_tokens % kBM == 0 && length % batch_tokens == 0 &&
                     nproj == nout * (length / batch_tokens),
                 op, "batch", "batched weights need whole 128-token tiles per batch");
     a.batch_tokens = uint32_t(batch_tokens);
     a.batch_wrows = uint32_t(nout);
+    a.causal = causal;
+    a.out_t = out_t;
+    a.mb = uint32_t(batch_tokens / kBM);
+    const uint32_t batches = uint32_t(length / batch_tokens);
+    static_assert(kBN == 2 * kBM, "live score tiles assume 256-wide output tiles");
+    if (causal == kCausalOut) {
+      TFX_REQUIRE(nout == batch_tokens, op, "causal", "causal outputs need nout == batch_tokens");
+      a.items = uint64_t(batches) * live_prefix(a.mb);
+    } else if (causal == kCausalK) {
+      TFX_REQUIRE(in_dim == batch_tokens && nout <= kBN, op, "causal",
+                  "a causal contraction needs in_dim == batch_tokens and nout <= 256");
+      a.split = causal_k_split(batches, a.mb, uint32_t(dev.sms));
+      a.slot_stride = uint64_t(length) * uint64_t(nout);
+    }
   }
   TFX_REQUIRE(uint64_t(a.mtiles) * a.ntiles < (uint64_t(1) << 31), op, "shape",
               "too many tiles for one call");
@@ -602,8 +715,8 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
                         : batch_tokens > 0
                             ? uint64_t(nproj) - uint64_t(nout) + uint64_t(a.ntiles) * kBN
                             : uint64_t(a.ntiles) * kBN;
-  const size_t xbytes = round_up(kp * size_t(xrows) * 4, 1024);
-  const size_t wbytes = round_up(kp * size_t(wrows) * 4, 1024);
+  const size_t xbytes = planes ? 0 : round_up(kp * size_t(xrows) * 4, 1024);
+  const size_t wbytes = planes ? 0 : round_up(kp * size_t(wrows) * 4, 1024);
   const size_t fbytes = round_up((size_t(a.mtiles) + 1) * 4, 1024);
   uint8_t* scratch = nullptr;
   cudaError_t e = scratch_malloc(reinterpret_cast<void**>(&scratch),
@@ -636,6 +749,19 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
                               hi, lo, fl, shift);
   };
   CUtensorMap maps[4];
+  if (rc == TFX_OK && planes) {
+    // the caller's planes, at their own extents: rows past them load as zeros
+    std::string why;
+    for (int i = 0; rc == TFX_OK && i < 4; ++i) {
+      const uint64_t rows = i < 2 ? uint64_t(length) : uint64_t(nproj);
+      if (!encode_map_2d_f32(&maps[i], planes[i], kp, rows, kp, kBK, 128, &why, kBK * 4))
+        rc = fail(TFX_ERR_CUDA, op, "tensor map", why);
+    }
+    if (rc == TFX_OK)
+      rc = launch_tc_layout<kEpiBiasAct, TFX_ACT_IDENTITY, false>(op, maps, a, dev, stream);
+    cudaFreeAsync(scratch, stream);
+    return rc;
+  }
   if (rc == TFX_OK && !force_simt) {
     rc = prep(x, uint64_t(length), xrows, xh, xl, flags, 7);  // one flag per 128-token tile
     if (rc == TFX_OK) rc = prep(w, uint64_t(nproj), wrows, wh, wl, flags + a.mtiles, 31);
@@ -670,12 +796,26 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
 // the weight rows of batch t / batch_tokens (weight: (in_dim, nout * batches)
 // column-major, batch b's rows [b * nout, (b + 1) * nout)). Same arithmetic as
 // tfx_gemm_bias_act_ff_f32 without bias and activation.
+// The split of gemm_batched_f32's causal contraction (causal 2) on the
+// current device: y needs split.max_pieces(length / batch_tokens) slots.
+int gemm_causal_k_split(int64_t length, int64_t batch_tokens, CausalKSplit* split) {
+  int st = TFX_OK;
+  const DeviceInfo& dev = device_info(&st);
+  if (st != TFX_OK) return st;
+  *split = causal_k_split(uint32_t(length / batch_tokens), uint32_t(batch_tokens / kBM),
+                          uint32_t(dev.sms));
+  return TFX_OK;
+}
+
+// causal: 0, kCausalOut or kCausalK (GemmArgs).
 int gemm_batched_f32(const char* op, const float* x, const float* w, float* y, int64_t in_dim,
-                     int64_t nout, int64_t length, int64_t batch_tokens, cudaStream_t stream) {
-  TFX_REQUIRE(in_dim >= 0 && nout >= 0 && length >= 0 && batch_tokens > 0, op, "shape",
-              "extents must be non-negative");
+                     int64_t nout, int64_t length, int64_t batch_tokens, cudaStream_t stream,
+                     uint32_t causal, const float* const* planes, int out_t) {
+  TFX_REQUIRE(in_dim >= 0 && nout >= 0 && length >= 0 && batch_tokens > 0 && causal <= 2, op,
+              "shape", "extents must be non-negative");
   return gemm_epilogue(op, kEpiBiasAct, TFX_ACT_IDENTITY, x, w, nullptr, y, in_dim,
-                       nout * (length / batch_tokens), nout, length, stream, batch_tokens);
+                       nout * (length / batch_tokens), nout, length, stream, batch_tokens, causal,
+                       planes, out_t);
 }
 
 int gemm_wait_timeouts(uint32_t* count) {
