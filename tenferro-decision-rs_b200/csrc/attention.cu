@@ -388,13 +388,23 @@ __global__ void __launch_bounds__(256) jeff_keep_kernel(const float* __restrict_
   }
 }
 
+// exp(d) for d <= 0 as 2^(d log2 e) on the ex2 unit (relative error ~2^-22
+// plus |d| 2^-24 from the product; results below 2^-126 flush to 0).
+__device__ __forceinline__ float jeff_exp(float d) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(d, 1.4426950408889634f)));
+  return r;
+}
+
 // The causal / active softmax of one score row per warp, written as the
 // hi / lo planes of the P V GEMM's x operand. Row = (head, query q) of
 // scores [head][q][key] (keys contiguous, only keys <= q read); keys [0, W),
 // W = 128 (q / 128 + 1), are written (the P V contraction of q's 128-query
 // tile stops there): p = exp(s scale - max) / sum over the kept keys (key <=
-// q and keep[key]), 0 for the others. Rows q < *first have no kept key and
-// are written as zeros (their output is 0).
+// q and keep[key]), 0 for the others. Two passes over the row: a running
+// (max, sum) per lane, combined over the warp, then the probabilities (the
+// second read comes from cache). Rows q < *first have no kept key and are
+// written as zeros (their output is 0).
 __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
     const float* __restrict__ scores, const uint8_t* __restrict__ keep, const int* first,
     float* __restrict__ phi, float* __restrict__ plo, uint32_t length, uint32_t rows, float scale) {
@@ -415,8 +425,10 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
     }
     return;
   }
-  // the scaled score of key c + j, -inf when not kept
-  auto scaled = [&](float4 sv, uint32_t kb, uint32_t c, float* v) {
+  // the scaled scores of keys c .. c + 3, -inf when not kept
+  auto scaled = [&](uint32_t c, float* v) {
+    const float4 sv = __ldg(reinterpret_cast<const float4*>(srow + c));
+    const uint32_t kb = __ldg(reinterpret_cast<const uint32_t*>(keep + c));
     const float x[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -424,33 +436,35 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
       v[j] = kept ? __fmul_rn(x[j], scale) : -INFINITY;
     }
   };
-  float mx = -INFINITY;
+  float mx = -INFINITY, sum = 0.0f;
+#pragma unroll 4
   for (uint32_t c = 4 * lane; c <= qi; c += 128) {
     float v[4];
-    scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
-           __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
-    mx = fmaxf(mx, fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3])));
-  }
-  mx = warp_max(mx);
-  float sum = 0.0f;
-  for (uint32_t c = 4 * lane; c <= qi; c += 128) {
-    float v[4];
-    scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
-           __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
+    scaled(c, v);
+    const float m4 = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+    if (m4 > mx) {  // a new running max: rescale the lane's sum
+      sum = mx == -INFINITY ? 0.0f : __fmul_rn(sum, jeff_exp(__fsub_rn(mx, m4)));
+      mx = m4;
+    }
+    if (mx != -INFINITY) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) sum = __fadd_rn(sum, expf(__fsub_rn(v[j], mx)));
+      for (int j = 0; j < 4; ++j)
+        if (v[j] != -INFINITY) sum = __fadd_rn(sum, jeff_exp(__fsub_rn(v[j], mx)));
+    }
   }
+  const float m = warp_max(mx);  // finite: key *first <= q is kept
+  sum = mx == -INFINITY ? 0.0f : __fmul_rn(sum, jeff_exp(__fsub_rn(mx, m)));
   sum = warp_sum(sum);
   const float r = __fdiv_rn(1.0f, sum);
+#pragma unroll 2
   for (uint32_t c = 4 * lane; c < width; c += 128) {
     float h[4] = {0.0f, 0.0f, 0.0f, 0.0f}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (c <= qi) {
       float v[4];
-      scaled(__ldg(reinterpret_cast<const float4*>(srow + c)),
-             __ldg(reinterpret_cast<const uint32_t*>(keep + c)), c, v);
+      scaled(c, v);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float pv = __fmul_rn(expf(__fsub_rn(v[j], mx)), r);
+        const float pv = v[j] == -INFINITY ? 0.0f : __fmul_rn(jeff_exp(__fsub_rn(v[j], m)), r);
         h[j] = tf32_round_finite(pv);
         l[j] = __fsub_rn(pv, h[j]);
       }
@@ -463,23 +477,28 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
 // The Jeff output, elementwise over out (hidden, length): the sum of the P V
 // GEMM's slots for this element (slot p at o + p * n, p < split.pieces(head,
 // t / 128), added in slot order), 0 for tokens t < *first (no kept key), then
-// times sigmoid(gate). Four consecutive tokens per thread (length % 128 == 0).
+// times sigmoid(gate). One warp per 128 tokens of a feature row (one query
+// tile: one piece count per warp), four consecutive tokens per lane.
 __global__ void __launch_bounds__(256) jeff_gate_kernel(const float* __restrict__ o,
                                                         const float* __restrict__ gate,
                                                         float* __restrict__ out, const int* first,
-                                                        uint64_t n, uint32_t length,
-                                                        uint32_t head_elems, CausalKSplit split) {
+                                                        uint64_t n, uint32_t length, uint32_t hd,
+                                                        uint32_t nwarps, CausalKSplit split) {
   pdl_enter();
   const int kfirst = __ldg(first);
-  for (uint64_t i = (uint64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 4; i < n;
-       i += uint64_t(gridDim.x) * blockDim.x * 4) {
-    const uint32_t t = uint32_t(i % length);
-    const uint32_t pieces = split.pieces(uint32_t(i / head_elems), t / 128);
+  const uint32_t lane = threadIdx.x & 31, tiles = length / 128;
+  for (uint32_t w = blockIdx.x * 8 + (threadIdx.x >> 5); w < nwarps; w += gridDim.x * 8) {
+    const uint32_t f = w / tiles, lm = w - f * tiles;
+    uint32_t pieces = 0;
+    if (lane == 0) pieces = split.pieces(f / hd, lm);
+    pieces = __shfl_sync(0xffffffffu, pieces, 0);
+    const uint32_t t = lm * 128 + lane * 4;
+    const uint64_t i = uint64_t(f) * length + t;
     float4 v = __ldg(reinterpret_cast<const float4*>(o + i));
     for (uint32_t p = 1; p < pieces; ++p) {
-      const float4 w = __ldg(reinterpret_cast<const float4*>(o + i + p * n));
-      v = make_float4(__fadd_rn(v.x, w.x), __fadd_rn(v.y, w.y), __fadd_rn(v.z, w.z),
-                      __fadd_rn(v.w, w.w));
+      const float4 u = __ldg(reinterpret_cast<const float4*>(o + i + p * n));
+      v = make_float4(__fadd_rn(v.x, u.x), __fadd_rn(v.y, u.y), __fadd_rn(v.z, u.z),
+                      __fadd_rn(v.w, u.w));
     }
     const float4 g = ld_stream(reinterpret_cast<const float4*>(gate + i));
     const float x[4] = {v.x, v.y, v.z, v.w}, gg[4] = {g.x, g.y, g.z, g.w};
@@ -1293,11 +1312,12 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
     int st = TFX_OK;
     const DeviceInfo& dev = device_info(&st);
     if (st != TFX_OK) rc = st;
-    const unsigned grid = unsigned(std::min<int64_t>((n / 4 + 255) / 256, int64_t(dev.sms) * 8));
+    const uint32_t nwarps = uint32_t(n / 128);  // n < 2^32: H L <= 2^23, hd <= 256
+    const unsigned grid = std::min<unsigned>((nwarps + 7) / 8, unsigned(dev.sms) * 16);
     if (rc == TFX_OK)
       rc = launch_kernel(op, jeff_gate_kernel, dim3(grid), dim3(256), 0, s, 1,
                          static_cast<const float*>(o), gate, out, static_cast<const int*>(first),
-                         uint64_t(n), L, hd * L, split);
+                         uint64_t(n), L, hd, nwarps, split);
   }
   if (rc == TFX_OK) {
     // flagged heads: the f32 kernel (q, k as hi + lo), which returns at once

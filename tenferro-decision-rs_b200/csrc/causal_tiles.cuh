@@ -52,6 +52,8 @@ struct CausalKSplit {
   __host__ __device__ uint64_t start(uint32_t b) const { return uint64_t(b) * items / grid; }
   // The CTA whose run holds chunk i: the largest b with start(b) <= i.
   __host__ __device__ uint32_t owner(uint64_t i) const {
+    if (items * grid < (uint64_t(1) << 32))  // the usual case: 32-bit division
+      return (uint32_t(i + 1) * grid - 1) / uint32_t(items);
     return uint32_t(((i + 1) * grid - 1) / items);
   }
   __host__ __device__ uint64_t first(uint32_t batch, uint32_t lm) const {

@@ -162,7 +162,8 @@ def test_jeff_attention(orc, hd, rot, heads, L):
 # Lengths that are whole 128-token tiles take the tensor-core route (3xTF32
 # GEMMs around the masked softmax); the others the f32 kernel.
 @pytest.mark.parametrize("hd,rot,heads,L,big_v", [
-    (256, 64, 4, 512, False), (64, 16, 3, 384, False), (128, 32, 2, 256, True)])
+    (256, 64, 4, 512, False), (64, 16, 3, 384, False), (128, 32, 2, 256, True),
+    (64, 16, 1, 2176, False)])  # rows past 2048 keys: the softmax's multi-pass variant
 def test_jeff_attention_tensor_cores(orc, hd, rot, heads, L, big_v):
     w = heads * hd
     theta, eps = 1e7, 1e-6
