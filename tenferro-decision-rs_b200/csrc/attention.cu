@@ -278,18 +278,18 @@ __device__ __forceinline__ void jeff_split(float x, float* hi, float* lo, bool* 
 // The Jeff prep for the tensor-core route, one (32-token, head, tensor) tile
 // per CTA (blockIdx.z: 0 q, 1 k, 2 v), with the arithmetic of jeff_prep_kernel
 // (bit-identical values). q and k are written as the hi / lo planes of the
-// score GEMM's operands, head-major [head][token][HD]; v head-major as it is
-// (for the f32 kernel) and as the hi / lo planes of V^T [head][channel][token]
-// (the P V GEMM's weight). flags[head] = 1 when a value of the head is
-// non-finite or at least 2^40. length % 32 == 0.
+// score GEMM's operands, head-major [head][token][HD]; v as the hi / lo planes
+// of V^T [head][channel][token] (the P V GEMM's weight; hi + lo == v).
+// flags[head] = 1 when a value of the head is non-finite or at least 2^40.
+// length % 32 == 0.
 template <int HD>
 __global__ void __launch_bounds__(256) jeff_prep_planes_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ q_norm, const float* __restrict__ k_norm,
     const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ qhi,
     float* __restrict__ qlo, float* __restrict__ khi, float* __restrict__ klo,
-    float* __restrict__ vh, float* __restrict__ vthi, float* __restrict__ vtlo, uint32_t length,
-    uint32_t rotary, float eps, uint8_t* flags) {
+    float* __restrict__ vthi, float* __restrict__ vtlo, uint32_t length, uint32_t rotary, float eps,
+    uint8_t* flags) {
   pdl_enter();
   __shared__ float tile[HD * 33];
   __shared__ float scale_s[32];
@@ -323,11 +323,6 @@ __global__ void __launch_bounds__(256) jeff_prep_planes_kernel(
       const uint64_t o = (feat + i) * length + t0 + t;
       vthi[o] = h;
       vtlo[o] = l;
-    }
-#pragma unroll 4
-    for (uint32_t idx = tid; idx < HD * 32; idx += 256) {
-      const uint32_t t = idx / HD, i = idx % HD;
-      vh[(uint64_t(head) * length + t0 + t) * HD + i] = tile[i * 33 + t];
     }
   } else {
     const float* w = which == 0 ? q_norm : k_norm;
@@ -437,7 +432,7 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
     }
   };
   float mx = -INFINITY, sum = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
   for (uint32_t c = 4 * lane; c <= qi; c += 128) {
     float v[4];
     scaled(c, v);
@@ -456,7 +451,7 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
   sum = mx == -INFINITY ? 0.0f : __fmul_rn(sum, jeff_exp(__fsub_rn(mx, m)));
   sum = warp_sum(sum);
   const float r = __fdiv_rn(1.0f, sum);
-#pragma unroll 2
+#pragma unroll 4
   for (uint32_t c = 4 * lane; c < width; c += 128) {
     float h[4] = {0.0f, 0.0f, 0.0f, 0.0f}, l[4] = {0.0f, 0.0f, 0.0f, 0.0f};
     if (c <= qi) {
@@ -545,6 +540,9 @@ struct AttnArgs {
   // q = q + q_lo and k = k + k_lo when set (hi / lo planes, same layout)
   const float* q_lo = nullptr;
   const float* k_lo = nullptr;
+  // when set, v and v_lo are the hi / lo planes of V^T: channel c of key j of
+  // head bh at (bh * hd + c) * length + j
+  const float* v_lo = nullptr;
 };
 
 // Channels ch .. ch + 3 of row `row` of head bh of q (t = 0), k (1) or v (2):
@@ -570,6 +568,15 @@ __device__ __forceinline__ float4 attn_ld4(const AttnArgs& a, int t, uint64_t bh
                        __fadd_rn(h.w, l.w));
   }
   const float* src = t == 0 ? a.q : t == 1 ? a.k : a.v;
+  if (t == 2 && a.v_lo) {  // V^T planes: four channels, length apart
+    const uint64_t o = (bh * a.hd + ch) * a.length + row;
+    float x[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      x[i] = __fadd_rn(__ldg(a.v + o + uint64_t(i) * a.length),
+                       __ldg(a.v_lo + o + uint64_t(i) * a.length));
+    return make_float4(x[0], x[1], x[2], x[3]);
+  }
   const uint64_t off = (bh * a.length + row) * a.hd + ch;
   const float* lo = t == 0 ? a.q_lo : t == 1 ? a.k_lo : nullptr;
   const float4 h = ld_stream(reinterpret_cast<const float4*>(src + off));
@@ -1242,9 +1249,9 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
   int rc = gemm_causal_k_split(heads * length, length, &split);
   if (rc != TFX_OK) return rc;
   const uint32_t slots = split.max_pieces(uint32_t(heads));
-  // scratch (floats): q hi | q lo | k hi | k lo | v | V^T hi | V^T lo |
-  // scores | P hi | P lo | O slots, then keep bytes | first active key | flags
-  const size_t floats = size_t(7 * n + 3 * nscore + int64_t(slots) * n);
+  // scratch (floats): q hi | q lo | k hi | k lo | V^T hi | V^T lo | scores |
+  // P hi | P lo | O slots, then keep bytes | first active key | flags
+  const size_t floats = size_t(6 * n + 3 * nscore + int64_t(slots) * n);
   const size_t keep_off = floats * 4;
   const size_t first_off = keep_off + (size_t(length) + 255) / 256 * 256;
   const size_t flags_off = first_off + 256;
@@ -1260,10 +1267,9 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
   float* qlo = f + n;
   float* khi = f + 2 * n;
   float* klo = f + 3 * n;
-  float* vh = f + 4 * n;
-  float* vthi = f + 5 * n;
-  float* vtlo = f + 6 * n;
-  float* scores = f + 7 * n;
+  float* vthi = f + 4 * n;
+  float* vtlo = f + 5 * n;
+  float* scores = f + 6 * n;
   float* phi = scores + nscore;
   float* plo = phi + nscore;
   float* o = plo + nscore;
@@ -1278,8 +1284,8 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
     const dim3 grid(L / 32, H, 3);
     auto prep = [&](auto kernel) {
       return launch_kernel(op, kernel, grid, dim3(256), 0, s, 1, q, k, v, q_norm, k_norm, cos_t,
-                           sin_t, qhi, qlo, khi, klo, vh, vthi, vtlo, L, uint32_t(rotary_dim),
-                           eps, flags);
+                           sin_t, qhi, qlo, khi, klo, vthi, vtlo, L, uint32_t(rotary_dim), eps,
+                           flags);
     };
     rc = hd == 256   ? prep(jeff_prep_planes_kernel<256>)
          : hd == 128 ? prep(jeff_prep_planes_kernel<128>)
@@ -1320,12 +1326,13 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
                          uint64_t(n), L, hd, nwarps, split);
   }
   if (rc == TFX_OK) {
-    // flagged heads: the f32 kernel (q, k as hi + lo), which returns at once
-    // for the others
+    // flagged heads: the f32 kernel (q, k as hi + lo, v from the V^T planes),
+    // which returns at once for the others
     const tfx_attention_desc d = jeff_desc(gate, mask, length, heads, head_dim);
-    AttnArgs a = attn_args(qhi, khi, vh, out, &d);
+    AttnArgs a = attn_args(qhi, khi, vthi, out, &d);
     a.q_lo = qlo;
     a.k_lo = klo;
+    a.v_lo = vtlo;
     a.vflags = flags;
     a.vflag_mode = 2;
     rc = attn_launch(op, a, 1, s, nullptr, true);

@@ -602,22 +602,30 @@ int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const 
 // Partial length of the tensor-core kernel: 0 = one partial per 32 values of K
 // (default), 1 = per 64 (2 % faster on the configs[1] projection, error still
 // below the reference's sequential sum: max 1.3e-7 of sum|x w| against 0.75e-7
-// and the reference's 3.6e-7). TFX_GEMM_STAGES = k32 / k32f64 selects one for
-// tuning runs. (Four stages of K 16 with 64-byte swizzle were measured 5 %
-// slower: the MMA pipe, not the copy latency, bounds the kernel.)
+// and the reference's 3.6e-7), 2 = four stages of K 16 (64-byte swizzle),
+// one partial per 32. TFX_GEMM_STAGES = k32 / k32f64 / k16 selects one for
+// tuning runs. (K 16 stages were measured 5 % slower on the configs[1]
+// projection: the MMA pipe, not the copy latency, bounds that kernel.)
 int gemm_stage_layout() {
   static const int v = [] {
     const char* e = getenv("TFX_GEMM_STAGES");
-    return e && std::string(e) == "k32f64" ? 1 : 0;
+    if (!e) return 0;
+    const std::string s(e);
+    return s == "k32f64" ? 1 : s == "k16" ? 2 : 0;
   }();
   return v;
 }
 
+// K values per stage (the inner extent of every TMA box).
+int gemm_stage_k() { return gemm_stage_layout() == 2 ? 16 : 32; }
+
 template <int EPI, int ACT, bool BIAS>
 int launch_tc_layout(const char* op, const CUtensorMap* maps, const GemmArgs& a,
                      const DeviceInfo& dev, cudaStream_t stream) {
-  return gemm_stage_layout() == 1 ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
-                                  : launch_tc<EPI, ACT, BIAS, 32, 32>(op, maps, a, dev, stream);
+  const int layout = gemm_stage_layout();
+  return layout == 1   ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
+         : layout == 2 ? launch_tc<EPI, ACT, BIAS, 16, 32>(op, maps, a, dev, stream)
+                       : launch_tc<EPI, ACT, BIAS, 32, 32>(op, maps, a, dev, stream);
 }
 
 template <int EPI, int ACT>
@@ -754,7 +762,8 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
     std::string why;
     for (int i = 0; rc == TFX_OK && i < 4; ++i) {
       const uint64_t rows = i < 2 ? uint64_t(length) : uint64_t(nproj);
-      if (!encode_map_2d_f32(&maps[i], planes[i], kp, rows, kp, kBK, 128, &why, kBK * 4))
+      if (!encode_map_2d_f32(&maps[i], planes[i], kp, rows, kp, uint32_t(gemm_stage_k()), 128,
+                             &why, gemm_stage_k() * 4))
         rc = fail(TFX_ERR_CUDA, op, "tensor map", why);
     }
     if (rc == TFX_OK)
@@ -769,7 +778,8 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
     const float* bases[4] = {xh, xl, wh, wl};
     for (int i = 0; rc == TFX_OK && i < 4; ++i) {
       const uint64_t rows = i < 2 ? xrows : wrows;
-      if (!encode_map_2d_f32(&maps[i], bases[i], kp, rows, kp, kBK, 128, &why, kBK * 4))
+      if (!encode_map_2d_f32(&maps[i], bases[i], kp, rows, kp, uint32_t(gemm_stage_k()), 128,
+                             &why, gemm_stage_k() * 4))
         rc = fail(TFX_ERR_CUDA, op, "tensor map", why);
     }
   }
