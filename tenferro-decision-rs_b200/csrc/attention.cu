@@ -86,6 +86,9 @@ __device__ __forceinline__ void img_split4(float4 x, float4* hi, float4* lo, boo
 // the mask digest, which waited for everything before it and let this grid
 // start at once; this grid reads nothing the digest writes, and waiting at the
 // end makes its completion imply the digest's for the attention that follows.
+// LATE also lets the attention grid launch as soon as every CTA of this one
+// has started (the attention waits for this grid's completion before it reads
+// anything).
 template <int VEC, bool IMG = false, bool LATE = false>
 __global__ void __launch_bounds__(256) laya_prep_kernel(
     const float* __restrict__ qkv, const float* __restrict__ cos_t,
@@ -95,6 +98,7 @@ __global__ void __launch_bounds__(256) laya_prep_kernel(
     uint8_t* __restrict__ qimg, uint8_t* __restrict__ kimg, uint8_t* __restrict__ vimg,
     uint32_t nqt, uint32_t nkt) {
   if constexpr (!LATE) pdl_enter();
+  if constexpr (LATE) pdl_launch_dependents();
   const uint32_t half = hd / 2;
   for (uint64_t n = blockIdx.x * uint64_t(blockDim.x) + threadIdx.x; n < total;
        n += uint64_t(gridDim.x) * blockDim.x) {
@@ -678,188 +682,193 @@ __global__ void __launch_bounds__(256) attn_flash_kernel(AttnArgs a) {
   __shared__ int vbad;
   pdl_enter();
   const uint32_t tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const uint32_t q0 = blockIdx.x * kQT, head = blockIdx.y, b = blockIdx.z;
+  const uint32_t head = blockIdx.y, b = blockIdx.z;
   if (routed_away(a, b * a.heads + head)) return;
-  const uint32_t L = a.length;
-  const uint32_t nq = min(uint32_t(kQT), L - q0);
-  const uint64_t bh = uint64_t(b) * a.heads + head;
-  int64_t lo, hi;
-  analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
-  if (a.keep && lo < hi) keep_narrow(a, b, q0, nq, &lo, &hi, red);
+  // query tiles q0 = 64 blockIdx.x, then gridDim.x tiles further on (a grid
+  // of one tile per head runs them all)
+  for (uint32_t q0 = blockIdx.x * kQT; q0 < a.length; q0 += gridDim.x * kQT) {
+    const uint32_t L = a.length;
+    const uint32_t nq = min(uint32_t(kQT), L - q0);
+    const uint64_t bh = uint64_t(b) * a.heads + head;
+    int64_t lo, hi;
+    analytic_range(a, q0, q0 + nq - 1, &lo, &hi);
+    if (a.keep && lo < hi) keep_narrow(a, b, q0, nq, &lo, &hi, red);
 
-  for (uint32_t idx = tid; idx < kQT * HD / 4; idx += 256) {
-    const uint32_t qq = idx % kQT, h4 = idx / kQT;
-    float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (qq < nq) val = attn_ld4(a, 0, bh, q0 + qq, 4 * h4);
-    Qt[(4 * h4 + 0) * kQT + qq] = val.x;
-    Qt[(4 * h4 + 1) * kQT + qq] = val.y;
-    Qt[(4 * h4 + 2) * kQT + qq] = val.z;
-    Qt[(4 * h4 + 3) * kQT + qq] = val.w;
-  }
-
-  float o[4][DJ][4];
-  float m[4], l[4];
-  bool inf_row[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.0f;
-    inf_row[i] = false;
-#pragma unroll
-    for (int j = 0; j < DJ; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[i][j][e] = 0.0f;
-  }
-
-  const int64_t kb_first = lo / KB * KB;
-  for (int64_t kb0 = kb_first; kb0 < hi; kb0 += KB) {
-    if (tid == 0) vbad = 0;
-    __syncthreads();  // the previous block's reads of K, V, P are done
-    for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
-      const uint32_t kk = idx % KB, h4 = idx / KB;
+    for (uint32_t idx = tid; idx < kQT * HD / 4; idx += 256) {
+      const uint32_t qq = idx % kQT, h4 = idx / kQT;
       float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (kb0 + kk < L)
-        val = attn_ld4(a, 1, bh, uint32_t(kb0 + kk), 4 * h4);
-      Kt[(4 * h4 + 0) * KB + kk] = val.x;
-      Kt[(4 * h4 + 1) * KB + kk] = val.y;
-      Kt[(4 * h4 + 2) * KB + kk] = val.z;
-      Kt[(4 * h4 + 3) * KB + kk] = val.w;
-    }
-    bool bad = false;
-    for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
-      const uint32_t kk = idx / (HD / 4), h4 = idx % (HD / 4);
-      float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (kb0 + kk < L)
-        val = attn_ld4(a, 2, bh, uint32_t(kb0 + kk), 4 * h4);
-      bad |= !(fabsf(val.x) < INFINITY && fabsf(val.y) < INFINITY && fabsf(val.z) < INFINITY &&
-               fabsf(val.w) < INFINITY);
-      *reinterpret_cast<float4*>(Vs + kk * HD + 4 * h4) = val;
-    }
-    if (bad) vbad = 1;
-    __syncthreads();
-
-    // scores of queries 4ty+i against keys KT*tx+j
-    float s[4][KT];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-      for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
-#pragma unroll 8
-    for (int h = 0; h < HD; ++h) {
-      const float4 q4 = *reinterpret_cast<const float4*>(Qt + h * kQT + 4 * ty);
-      float kv[KT];
-      if constexpr (KT == 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(Kt + h * KB + 4 * tx);
-        kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
-      } else {
-        const float2 k2 = *reinterpret_cast<const float2*>(Kt + h * KB + 2 * tx);
-        kv[0] = k2.x; kv[1] = k2.y;
-      }
-      const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < KT; ++j) s[i][j] = __fmaf_rn(qv[i], kv[j], s[i][j]);
+      if (qq < nq) val = attn_ld4(a, 0, bh, q0 + qq, 4 * h4);
+      Qt[(4 * h4 + 0) * kQT + qq] = val.x;
+      Qt[(4 * h4 + 1) * kQT + qq] = val.y;
+      Qt[(4 * h4 + 2) * kQT + qq] = val.z;
+      Qt[(4 * h4 + 3) * kQT + qq] = val.w;
     }
 
-    // mask, scale, online softmax
-#pragma unroll
+    float o[4][DJ][4];
+    float m[4], l[4];
+    bool inf_row[4];
+  #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int64_t qi = int64_t(q0) + 4 * ty + i;
-      float mb = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < KT; ++j) {
-        const int64_t kj = kb0 + KT * tx + j;
-        float sc = -INFINITY;
-        if (qi < L && kj >= lo && kj < hi && key_kept(a, b, qi, kj)) {
-          sc = __fmul_rn(s[i][j], a.scale);
-          if (a.bias) sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kj) + uint64_t(L) * b)]);
-          if (sc == INFINITY) inf_row[i] = true;
-          if (!(fabsf(sc) < INFINITY)) sc = -INFINITY;  // NaN / inf: contributes nothing
-        }
-        s[i][j] = sc;
-        mb = fmaxf(mb, sc);
-      }
-#pragma unroll
-      for (int d = 1; d < 16; d <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, d));
-      const float mn = fmaxf(m[i], mb);
-      float corr = 1.0f, ps = 0.0f;
-      if (mn != -INFINITY) {
-        corr = expf(__fsub_rn(m[i], mn));
-#pragma unroll
-        for (int j = 0; j < KT; ++j) {
-          const float p = s[i][j] == -INFINITY ? 0.0f : expf(__fsub_rn(s[i][j], mn));
-          s[i][j] = p;
-          ps = __fadd_rn(ps, p);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
-      }
-#pragma unroll
-      for (int d = 1; d < 16; d <<= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, d));
-      m[i] = mn;
-      l[i] = __fmaf_rn(l[i], corr, ps);
-#pragma unroll
+      m[i] = -INFINITY;
+      l[i] = 0.0f;
+      inf_row[i] = false;
+  #pragma unroll
       for (int j = 0; j < DJ; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[i][j][e] = __fmul_rn(o[i][j][e], corr);
-      if constexpr (KT == 4) {
-        *reinterpret_cast<float4*>(Ps + (4 * ty + i) * PS + 4 * tx) =
-            make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
-      } else {
-        *reinterpret_cast<float2*>(Ps + (4 * ty + i) * PS + 2 * tx) = make_float2(s[i][0], s[i][1]);
-      }
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) o[i][j][e] = 0.0f;
     }
-    __syncthreads();
 
-    // O += P V (keys whose p is 0 are skipped when V holds a non-finite value)
-    const bool guard = vbad != 0;
-#pragma unroll 2
-    for (int k4 = 0; k4 < KB; k4 += 4) {
-      float p[4][4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float4 t = *reinterpret_cast<const float4*>(Ps + (4 * ty + i) * PS + k4);
-        p[i][0] = t.x; p[i][1] = t.y; p[i][2] = t.z; p[i][3] = t.w;
+    const int64_t kb_first = lo / KB * KB;
+    for (int64_t kb0 = kb_first; kb0 < hi; kb0 += KB) {
+      if (tid == 0) vbad = 0;
+      __syncthreads();  // the previous block's reads of K, V, P are done
+      for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
+        const uint32_t kk = idx % KB, h4 = idx / KB;
+        float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (kb0 + kk < L)
+          val = attn_ld4(a, 1, bh, uint32_t(kb0 + kk), 4 * h4);
+        Kt[(4 * h4 + 0) * KB + kk] = val.x;
+        Kt[(4 * h4 + 1) * KB + kk] = val.y;
+        Kt[(4 * h4 + 2) * KB + kk] = val.z;
+        Kt[(4 * h4 + 3) * KB + kk] = val.w;
       }
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-        for (int j = 0; j < DJ; ++j) {
-          const float4 vv = *reinterpret_cast<const float4*>(Vs + (k4 + kk) * HD + 64 * j + 4 * tx);
-          const float ve[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            if (guard && p[i][kk] == 0.0f) continue;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) o[i][j][e] = __fmaf_rn(p[i][kk], ve[e], o[i][j][e]);
+      bool bad = false;
+      for (uint32_t idx = tid; idx < KB * HD / 4; idx += 256) {
+        const uint32_t kk = idx / (HD / 4), h4 = idx % (HD / 4);
+        float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (kb0 + kk < L)
+          val = attn_ld4(a, 2, bh, uint32_t(kb0 + kk), 4 * h4);
+        bad |= !(fabsf(val.x) < INFINITY && fabsf(val.y) < INFINITY && fabsf(val.z) < INFINITY &&
+                 fabsf(val.w) < INFINITY);
+        *reinterpret_cast<float4*>(Vs + kk * HD + 4 * h4) = val;
+      }
+      if (bad) vbad = 1;
+      __syncthreads();
+
+      // scores of queries 4ty+i against keys KT*tx+j
+      float s[4][KT];
+  #pragma unroll
+      for (int i = 0; i < 4; ++i)
+  #pragma unroll
+        for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
+  #pragma unroll 8
+      for (int h = 0; h < HD; ++h) {
+        const float4 q4 = *reinterpret_cast<const float4*>(Qt + h * kQT + 4 * ty);
+        float kv[KT];
+        if constexpr (KT == 4) {
+          const float4 k4 = *reinterpret_cast<const float4*>(Kt + h * KB + 4 * tx);
+          kv[0] = k4.x; kv[1] = k4.y; kv[2] = k4.z; kv[3] = k4.w;
+        } else {
+          const float2 k2 = *reinterpret_cast<const float2*>(Kt + h * KB + 2 * tx);
+          kv[0] = k2.x; kv[1] = k2.y;
+        }
+        const float qv[4] = {q4.x, q4.y, q4.z, q4.w};
+  #pragma unroll
+        for (int i = 0; i < 4; ++i)
+  #pragma unroll
+          for (int j = 0; j < KT; ++j) s[i][j] = __fmaf_rn(qv[i], kv[j], s[i][j]);
+      }
+
+      // mask, scale, online softmax
+  #pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t qi = int64_t(q0) + 4 * ty + i;
+        float mb = -INFINITY;
+  #pragma unroll
+        for (int j = 0; j < KT; ++j) {
+          const int64_t kj = kb0 + KT * tx + j;
+          float sc = -INFINITY;
+          if (qi < L && kj >= lo && kj < hi && key_kept(a, b, qi, kj)) {
+            sc = __fmul_rn(s[i][j], a.scale);
+            if (a.bias) sc = __fadd_rn(sc, a.bias[uint64_t(qi) + uint64_t(L) * (uint64_t(kj) + uint64_t(L) * b)]);
+            if (sc == INFINITY) inf_row[i] = true;
+            if (!(fabsf(sc) < INFINITY)) sc = -INFINITY;  // NaN / inf: contributes nothing
+          }
+          s[i][j] = sc;
+          mb = fmaxf(mb, sc);
+        }
+  #pragma unroll
+        for (int d = 1; d < 16; d <<= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, d));
+        const float mn = fmaxf(m[i], mb);
+        float corr = 1.0f, ps = 0.0f;
+        if (mn != -INFINITY) {
+          corr = expf(__fsub_rn(m[i], mn));
+  #pragma unroll
+          for (int j = 0; j < KT; ++j) {
+            const float p = s[i][j] == -INFINITY ? 0.0f : expf(__fsub_rn(s[i][j], mn));
+            s[i][j] = p;
+            ps = __fadd_rn(ps, p);
+          }
+        } else {
+  #pragma unroll
+          for (int j = 0; j < KT; ++j) s[i][j] = 0.0f;
+        }
+  #pragma unroll
+        for (int d = 1; d < 16; d <<= 1) ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, d));
+        m[i] = mn;
+        l[i] = __fmaf_rn(l[i], corr, ps);
+  #pragma unroll
+        for (int j = 0; j < DJ; ++j)
+  #pragma unroll
+          for (int e = 0; e < 4; ++e) o[i][j][e] = __fmul_rn(o[i][j][e], corr);
+        if constexpr (KT == 4) {
+          *reinterpret_cast<float4*>(Ps + (4 * ty + i) * PS + 4 * tx) =
+              make_float4(s[i][0], s[i][1], s[i][2], s[i][3]);
+        } else {
+          *reinterpret_cast<float2*>(Ps + (4 * ty + i) * PS + 2 * tx) = make_float2(s[i][0], s[i][1]);
+        }
+      }
+      __syncthreads();
+
+      // O += P V (keys whose p is 0 are skipped when V holds a non-finite value)
+      const bool guard = vbad != 0;
+  #pragma unroll 2
+      for (int k4 = 0; k4 < KB; k4 += 4) {
+        float p[4][4];
+  #pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 t = *reinterpret_cast<const float4*>(Ps + (4 * ty + i) * PS + k4);
+          p[i][0] = t.x; p[i][1] = t.y; p[i][2] = t.z; p[i][3] = t.w;
+        }
+  #pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+  #pragma unroll
+          for (int j = 0; j < DJ; ++j) {
+            const float4 vv = *reinterpret_cast<const float4*>(Vs + (k4 + kk) * HD + 64 * j + 4 * tx);
+            const float ve[4] = {vv.x, vv.y, vv.z, vv.w};
+  #pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              if (guard && p[i][kk] == 0.0f) continue;
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) o[i][j][e] = __fmaf_rn(p[i][kk], ve[e], o[i][j][e]);
+            }
           }
         }
       }
     }
-  }
 
-  // a +inf score seen by any of the 16 lanes of a row empties the whole row
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int d = 1; d < 16; d <<= 1)
-      inf_row[i] = (__shfl_xor_sync(0xffffffffu, int(inf_row[i]), d) != 0) || inf_row[i];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t qi = q0 + 4 * ty + i;
-    if (qi >= L) continue;
-    const bool empty = l[i] == 0.0f || inf_row[i];
-    const float ev = a.empty_nan ? NAN : 0.0f;
-#pragma unroll
-    for (int j = 0; j < DJ; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t d = 64 * j + 4 * tx + e;
-        const float val = empty ? ev : __fdiv_rn(o[i][j][e], l[i]);
-        store_out(a, b, qi, uint64_t(head) * HD + d, val);
-      }
+    // a +inf score seen by any of the 16 lanes of a row empties the whole row
+  #pragma unroll
+    for (int i = 0; i < 4; ++i)
+  #pragma unroll
+      for (int d = 1; d < 16; d <<= 1)
+        inf_row[i] = (__shfl_xor_sync(0xffffffffu, int(inf_row[i]), d) != 0) || inf_row[i];
+  #pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t qi = q0 + 4 * ty + i;
+      if (qi >= L) continue;
+      const bool empty = l[i] == 0.0f || inf_row[i];
+      const float ev = a.empty_nan ? NAN : 0.0f;
+  #pragma unroll
+      for (int j = 0; j < DJ; ++j)
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t d = 64 * j + 4 * tx + e;
+          const float val = empty ? ev : __fdiv_rn(o[i][j][e], l[i]);
+          store_out(a, b, qi, uint64_t(head) * HD + d, val);
+        }
+    }
+    __syncthreads();  // the shared tiles are reused by the next query tile
   }
 }
 
@@ -1045,9 +1054,10 @@ int attn_launch_tc(const char* op, AttnArgs a, uint32_t batch, const DeviceInfo&
     const size_t fsmem = size_t(64 * 64 * 3 + 64 * 68) * 4;
     const cudaError_t fe = cudaFuncSetAttribute(
         attn_flash_kernel<64, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(fsmem));
+    // one CTA per head, looping over the query tiles: the usual call has no
+    // flagged head, and a small grid that returns at once costs least
     rc = fe != cudaSuccess ? fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(fe))
-                           : launch_kernel(op, attn_flash_kernel<64, 64>,
-                                           dim3((a.length + kQT - 1) / kQT, a.heads, batch),
+                           : launch_kernel(op, attn_flash_kernel<64, 64>, dim3(1, a.heads, batch),
                                            dim3(256), fsmem, stream, 1, a);
   }
   cudaFreeAsync(scratch, stream);
@@ -1065,7 +1075,8 @@ int attn_launch(const char* op, const AttnArgs& a, uint32_t batch, cudaStream_t 
     if (rc != 1) return rc;
   }
   const bool vec = aligned(a.q, 16) && aligned(a.k, 16) && aligned(a.v, 16);
-  const dim3 grid((a.length + kQT - 1) / kQT, a.heads, batch);
+  // a redo of flagged heads: one CTA per head looping over the query tiles
+  const dim3 grid(f32_only ? 1u : (a.length + kQT - 1) / kQT, a.heads, batch);
   auto flash = [&](auto kernel, int hd, int kb) -> int {
     const size_t smem = size_t(hd * kQT + hd * kb + kb * hd + kQT * (kb + 4)) * 4;
     if (smem > size_t(dev.smem_optin)) return 1;
