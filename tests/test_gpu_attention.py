@@ -186,6 +186,33 @@ def test_jeff_attention_tensor_cores(orc, hd, rot, heads, L, big_v):
     assert np.all(got.reshape(w, L)[:, :3] == 0.0)
 
 
+def test_jeff_attention_tensor_cores_nonfinite(orc):
+    """Non-finite inputs on the tensor-core route: the heads holding them go to
+    the f32 kernel (the reference's rules: non-finite scores contribute
+    nothing, a NaN in V of a key whose probability is 0 does not leak), the
+    others stay on the GEMMs; everything matches the oracle, NaN for NaN."""
+    hd, rot, heads, L = 64, 16, 4, 256
+    w = heads * hd
+    q, k, v, g = (splitmix_normal(L * w, 0x7E4F0A60 + i) for i in range(4))
+    qn, kn = splitmix_normal(hd, 0x7E4F0A68, std=0.1), splitmix_normal(hd, 0x7E4F0A69, std=0.1)
+    mask = (splitmix_uniform(L, 0x7E4F0A6A, 0.0, 1.0) > 0.25).astype(np.float32)
+    mask[0] = 1.0
+    mask[3] = 0.0
+    # (length, hidden) time-first: element (t, f) at t + L f
+    q.reshape(w, L)[0 * hd + 5, 40] = np.inf        # head 0: one query token
+    k.reshape(w, L)[1 * hd + 9, 70] = np.nan        # head 1: one key token
+    v.reshape(w, L)[2 * hd + 2, 3] = np.nan         # head 2: a masked key's V
+    c, s = orc.rope_tables_powf_f32(1e7, L, rot)
+    out = empty(L * w)
+    ins = [dev(t) for t in (q, k, v, g, qn, kn, mask, c, s)]
+    call("tfx_jeff_attention_f32", *[P(t) for t in ins], P(out), L, heads, hd, rot,
+         ctypes.c_float(1e-6), S())
+    got = host(out)
+    want = orc.jeff_full_attention_f32(q, k, v, g, qn, kn, mask, L, heads, hd, rot, 1e7, 1e-6)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, "jeff attention (tensor cores), non-finite")
+    assert np.isfinite(got.reshape(w, L)[2 * hd:3 * hd]).all()  # the masked NaN did not leak
+
+
 def test_jeff_attention_no_active_key(orc):
     hd, rot, heads, L = 64, 16, 2, 128
     w = heads * hd
