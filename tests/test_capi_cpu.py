@@ -164,6 +164,19 @@ def test_session_chunk_plan_invariants(tmp_path):
     assert res.returncode == 0 and "bad=0" in res.stdout, res.stdout
 
 
+def test_causal_tile_enumeration(tmp_path):
+    """The batched GEMM's causal schedules (causal_tiles.cuh, host-compiled):
+    live score tiles and the even split-K of the probability-times-value
+    contraction cover every unit once, with pieces and slots in order."""
+    exe = tmp_path / "causal_tiles_test"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-Wall", "-Werror", "-I",
+                    os.path.join(ROOT, "tenferro-decision-rs_b200", "csrc"),
+                    os.path.join(ROOT, "tests", "native", "causal_tiles_test.cpp"), "-o", str(exe)],
+                   check=True)
+    res = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert res.returncode == 0 and "bad=0" in res.stdout, res.stdout
+
+
 # Entry points whose arguments are all checked before any CUDA call: with every
 # pointer NULL (the required data pointers among them) and every extent 8 the
 # call must fail as invalid argument (a null pointer, or a shape the op cannot
