@@ -213,6 +213,33 @@ def test_jeff_attention_tensor_cores_nonfinite(orc):
     assert np.isfinite(got.reshape(w, L)[2 * hd:3 * hd]).all()  # the masked NaN did not leak
 
 
+@pytest.mark.parametrize("rot,misalign", [(0, False), (32, True)])
+def test_jeff_attention_tc_edges(orc, rot, misalign):
+    """Rotary width 0 (no tables) on the tensor-core route, and an output /
+    gate that is not 16-byte aligned (the f32 route takes the call)."""
+    hd, heads, L = 128, 2, 256
+    w = heads * hd
+    q, k, v, g = (splitmix_normal(L * w, 0x7E4F0A70 + i + rot) for i in range(4))
+    qn, kn = splitmix_normal(hd, 0x7E4F0A78, std=0.1), splitmix_normal(hd, 0x7E4F0A79, std=0.1)
+    mask = (splitmix_uniform(L, 0x7E4F0A7A, 0.0, 1.0) > 0.2).astype(np.float32)
+    mask[0] = 1.0
+    want = orc.jeff_full_attention_f32(q, k, v, g, qn, kn, mask, L, heads, hd, rot, 1e7, 1e-6)
+    if rot:
+        c, s = orc.rope_tables_powf_f32(1e7, L, rot)
+        cd, sd = dev(c), dev(s)
+    else:
+        cd = sd = None
+    off = 1 if misalign else 0  # one float off the 16-byte grid
+    gd = dev(g, off)
+    out = empty(L * w, offset_elems=off)
+    ins = [dev(t) for t in (q, k, v)]
+    qnd, knd, md = dev(qn), dev(kn), dev(mask)
+    call("tfx_jeff_attention_f32", *[P(t) for t in ins], P(gd), P(qnd), P(knd), P(md),
+         P(cd), P(sd), P(out), L, heads, hd, rot, ctypes.c_float(1e-6), S())
+    got = host(out)
+    assert_close(got, want, F32_RTOL, F32_ATOL_REL, f"jeff attention rot={rot} misalign={misalign}")
+
+
 def test_jeff_attention_no_active_key(orc):
     hd, rot, heads, L = 64, 16, 2, 128
     w = heads * hd
