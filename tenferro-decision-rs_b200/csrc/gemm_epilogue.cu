@@ -273,6 +273,82 @@ __device__ __forceinline__ float epi_act(float v) {
   else return v;
 }
 
+// The epilogue of one thread: token t's 128 sums in acc for output tile n,
+// column half `half` (GeGLU: 64 values and their 64 gates), with bias,
+// activation or GeGLU, stored into output slot `slot` (split contractions).
+template <int EPI, int ACT, bool BIAS>
+__device__ __forceinline__ void epi_store(const GemmArgs& a, uint32_t t, uint32_t n, uint32_t half,
+                                          uint32_t slot, float* acc) {
+  if constexpr (EPI == kEpiGeglu) {
+    const uint32_t j0 = n * (kBN / 2) + 64 * half;  // first output row of this thread
+    if (j0 >= a.nout) return;
+    const uint32_t valid = min(64u, a.nout - j0);
+    if constexpr (BIAS) {
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (uint32_t(j) < valid) {
+          acc[j] = __fadd_rn(acc[j], __ldg(a.bias + j0 + j));
+          acc[64 + j] = __fadd_rn(acc[64 + j], __ldg(a.bias + a.inter + j0 + j));
+        }
+    }
+    float* yr = a.y + uint64_t(t) * a.nout + j0;
+#pragma unroll
+    for (int c = 0; c < 64; c += 4) {
+      const float2 g0 = math::gelu_mlx2(make_float2(acc[c], acc[c + 1]));
+      const float2 g1 = math::gelu_mlx2(make_float2(acc[c + 2], acc[c + 3]));
+      const float4 o = make_float4(__fmul_rn(g0.x, acc[64 + c]), __fmul_rn(g0.y, acc[65 + c]),
+                                   __fmul_rn(g1.x, acc[66 + c]), __fmul_rn(g1.y, acc[67 + c]));
+      if (a.vec4 && uint32_t(c) + 4 <= valid) {
+        *reinterpret_cast<float4*>(yr + c) = o;
+      } else {
+        if (uint32_t(c) < valid) yr[c] = o.x;
+        if (uint32_t(c) + 1 < valid) yr[c + 1] = o.y;
+        if (uint32_t(c) + 2 < valid) yr[c + 2] = o.z;
+        if (uint32_t(c) + 3 < valid) yr[c + 3] = o.w;
+      }
+    }
+  } else {
+    const uint32_t o0 = n * kBN + 128 * half;  // first output row of this thread
+    if (o0 >= a.nout) return;
+    const uint32_t valid = min(128u, a.nout - o0);
+    if (a.out_t) {  // identity epilogue; a warp stores 32 consecutive tokens
+      const uint32_t b = t / a.batch_tokens, tb = t - b * a.batch_tokens;
+      float* yc = a.y + uint64_t(slot) * a.slot_stride +
+                  (uint64_t(b) * a.nout + o0) * a.batch_tokens + tb;
+#pragma unroll
+      for (int c = 0; c < 128; ++c)  // fully unrolled: acc stays in registers
+        if (uint32_t(c) < valid) yc[uint64_t(c) * a.batch_tokens] = acc[c];
+      return;
+    }
+    float* yr = a.y + uint64_t(slot) * a.slot_stride + uint64_t(t) * a.nout + o0;
+#pragma unroll
+    for (int c = 0; c < 128; c += 4) {
+      float v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[j] = acc[c + j];
+        if constexpr (BIAS)
+          if (uint32_t(c + j) < valid) v[j] = __fadd_rn(v[j], __ldg(a.bias + o0 + c + j));
+      }
+      if constexpr (ACT == TFX_ACT_GELU_ERF) {
+        const float2 g0 = math::gelu_mlx2(make_float2(v[0], v[1]));
+        const float2 g1 = math::gelu_mlx2(make_float2(v[2], v[3]));
+        v[0] = g0.x; v[1] = g0.y; v[2] = g1.x; v[3] = g1.y;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = epi_act<EPI, ACT>(v[j]);
+      }
+      if (a.vec4 && uint32_t(c) + 4 <= valid) {
+        *reinterpret_cast<float4*>(yr + c) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (uint32_t(c + j) < valid) yr[c + j] = v[j];
+      }
+    }
+  }
+}
+
 // Accumulation. The tensor cores' f32 accumulation is not IEEE: each MMA
 // aligns the accumulator and its products to the largest exponent and keeps
 // about 22 bits below it (measured: an accumulator fed all 288 MMAs of a
@@ -468,74 +544,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
       if (!ok) break;
       const uint32_t t = m * kBM + row;
       if (t >= a.length) continue;
-      if constexpr (EPI == kEpiGeglu) {
-        const uint32_t j0 = n * (kBN / 2) + 64 * half;  // first output row of this thread
-        if (j0 >= a.nout) continue;
-        const uint32_t valid = min(64u, a.nout - j0);
-        if constexpr (BIAS) {
-#pragma unroll
-          for (int j = 0; j < 64; ++j)
-            if (uint32_t(j) < valid) {
-              acc[j] = __fadd_rn(acc[j], __ldg(a.bias + j0 + j));
-              acc[64 + j] = __fadd_rn(acc[64 + j], __ldg(a.bias + a.inter + j0 + j));
-            }
-        }
-        float* yr = a.y + uint64_t(t) * a.nout + j0;
-#pragma unroll
-        for (int c = 0; c < 64; c += 4) {
-          const float2 g0 = math::gelu_mlx2(make_float2(acc[c], acc[c + 1]));
-          const float2 g1 = math::gelu_mlx2(make_float2(acc[c + 2], acc[c + 3]));
-          const float4 o = make_float4(__fmul_rn(g0.x, acc[64 + c]), __fmul_rn(g0.y, acc[65 + c]),
-                                       __fmul_rn(g1.x, acc[66 + c]), __fmul_rn(g1.y, acc[67 + c]));
-          if (a.vec4 && uint32_t(c) + 4 <= valid) {
-            *reinterpret_cast<float4*>(yr + c) = o;
-          } else {
-            if (uint32_t(c) < valid) yr[c] = o.x;
-            if (uint32_t(c) + 1 < valid) yr[c + 1] = o.y;
-            if (uint32_t(c) + 2 < valid) yr[c + 2] = o.z;
-            if (uint32_t(c) + 3 < valid) yr[c + 3] = o.w;
-          }
-        }
-      } else {
-        const uint32_t o0 = n * kBN + 128 * half;  // first output row of this thread
-        if (o0 >= a.nout) continue;
-        const uint32_t valid = min(128u, a.nout - o0);
-        if (a.out_t) {  // identity epilogue; a warp stores 32 consecutive tokens
-          const uint32_t b = t / a.batch_tokens, tb = t - b * a.batch_tokens;
-          float* yc = a.y + uint64_t(pc.slot) * a.slot_stride +
-                      (uint64_t(b) * a.nout + o0) * a.batch_tokens + tb;
-#pragma unroll
-          for (int c = 0; c < 128; ++c)  // fully unrolled: acc stays in registers
-            if (uint32_t(c) < valid) yc[uint64_t(c) * a.batch_tokens] = acc[c];
-          continue;
-        }
-        float* yr = a.y + uint64_t(pc.slot) * a.slot_stride + uint64_t(t) * a.nout + o0;
-#pragma unroll
-        for (int c = 0; c < 128; c += 4) {
-          float v[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            v[j] = acc[c + j];
-            if constexpr (BIAS)
-              if (uint32_t(c + j) < valid) v[j] = __fadd_rn(v[j], __ldg(a.bias + o0 + c + j));
-          }
-          if constexpr (ACT == TFX_ACT_GELU_ERF) {
-            const float2 g0 = math::gelu_mlx2(make_float2(v[0], v[1]));
-            const float2 g1 = math::gelu_mlx2(make_float2(v[2], v[3]));
-            v[0] = g0.x; v[1] = g0.y; v[2] = g1.x; v[3] = g1.y;
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) v[j] = epi_act<EPI, ACT>(v[j]);
-          }
-          if (a.vec4 && uint32_t(c) + 4 <= valid) {
-            *reinterpret_cast<float4*>(yr + c) = make_float4(v[0], v[1], v[2], v[3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              if (uint32_t(c + j) < valid) yr[c + j] = v[j];
-          }
-        }
-      }
+      epi_store<EPI, ACT, BIAS>(a, t, n, half, pc.slot, acc);
     }
   }
   tc_fence_before();
@@ -578,6 +587,8 @@ __global__ void __launch_bounds__(128) gemm_epi_simt_kernel(const float* __restr
   }
 }
 
+#include "gemm_pair.cuh"
+
 // ---- host ----------------------------------------------------------------------------
 
 template <int EPI, int ACT, bool BIAS, int SK, int FK>
@@ -619,9 +630,41 @@ int gemm_stage_layout() {
 // K values per stage (the inner extent of every TMA box).
 int gemm_stage_k() { return gemm_stage_layout() == 2 ? 16 : 32; }
 
+// Non-batched calls run on CTA pairs (gemm_pair_tc_kernel: 153.7 -> 143.6 us on
+// the configs[1] GeGLU projection, tensor pipe 66 -> 71 % active);
+// TFX_GEMM_PAIR=0 keeps them on one CTA per tile (tuning runs, and the tests
+// of that kernel).
+bool gemm_pair_mode() {
+  static const bool v = [] {
+    const char* e = getenv("TFX_GEMM_PAIR");
+    return !(e && std::string(e) == "0");
+  }();
+  return v;
+}
+
+template <int EPI, int ACT, bool BIAS>
+int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, const DeviceInfo& dev,
+                cudaStream_t stream) {
+  auto kernel = gemm_pair_tc_kernel<EPI, ACT, BIAS>;
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  const int di = dev.device & 63;
+  std::call_once(once[di], [&] {
+    err[di] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   int(kGemmSmem));
+  });
+  if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
+  const uint64_t pairs = uint64_t((a.mtiles + 1) / 2) * a.ntiles;
+  const unsigned npairs = unsigned(std::min<uint64_t>(pairs, uint64_t(dev.sms / 2)));
+  return launch_kernel(op, kernel, dim3(2 * npairs), dim3(kGThreads), kGemmSmem, stream, 2,
+                       maps[0], maps[1], maps[2], maps[3], a);
+}
+
 template <int EPI, int ACT, bool BIAS>
 int launch_tc_layout(const char* op, const CUtensorMap* maps, const GemmArgs& a,
                      const DeviceInfo& dev, cudaStream_t stream) {
+  if (gemm_pair_mode() && a.batch_tokens == 0 && dev.sms >= 2)
+    return launch_pair<EPI, ACT, BIAS>(op, maps, a, dev, stream);
   const int layout = gemm_stage_layout();
   return layout == 1   ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
          : layout == 2 ? launch_tc<EPI, ACT, BIAS, 16, 32>(op, maps, a, dev, stream)

@@ -116,3 +116,13 @@ def test_attention_f32_variant():
                           "no:cacheprovider", os.path.join(ROOT, "tests", "test_gpu_attention.py")],
                          env=env, capture_output=True, text=True, timeout=900, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+
+
+def test_gemm_one_cta_variant():
+    """The GEMM-epilogue tests again on the one-CTA tensor-core kernel
+    (TFX_GEMM_PAIR=0; the default runs non-batched calls on CTA pairs)."""
+    env = dict(os.environ, TFX_GEMM_PAIR="0")
+    res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p",
+                          "no:cacheprovider", os.path.join(ROOT, "tests", "test_gpu_gemm_epilogue.py")],
+                         env=env, capture_output=True, text=True, timeout=900, cwd=ROOT)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
