@@ -610,19 +610,20 @@ int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const 
                        maps[1], maps[2], maps[3], a);
 }
 
-// Partial length of the tensor-core kernel: 0 = one partial per 32 values of K
-// (default), 1 = per 64 (2 % faster on the configs[1] projection, error still
-// below the reference's sequential sum: max 1.3e-7 of sum|x w| against 0.75e-7
-// and the reference's 3.6e-7), 2 = four stages of K 16 (64-byte swizzle),
-// one partial per 32. TFX_GEMM_STAGES = k32 / k32f64 / k16 selects one for
-// tuning runs. (K 16 stages were measured 5 % slower on the configs[1]
-// projection: the MMA pipe, not the copy latency, bounds that kernel.)
+// Partial length of the tensor-core kernels. One partial per 32 values of K
+// is the most accurate; per 64 is faster (one CTA: 2 %, CTA pairs: 3 %, 143.9
+// -> 139.3 us on the configs[1] projection) with the error still below the
+// reference's sequential sum (max 1.3e-7 of sum|x w| against 0.75e-7, and the
+// reference's 3.6e-7). Default (0): the pair kernel per 64, the one-CTA
+// kernel per 32. TFX_GEMM_STAGES = k32 (3: both per 32), k32f64 (1: both per
+// 64), k16 (2: four stages of K 16 with 64-byte swizzle on one CTA, measured
+// 5 % slower there: the MMA pipe, not the copy latency, bounds it).
 int gemm_stage_layout() {
   static const int v = [] {
     const char* e = getenv("TFX_GEMM_STAGES");
     if (!e) return 0;
     const std::string s(e);
-    return s == "k32f64" ? 1 : s == "k16" ? 2 : 0;
+    return s == "k32f64" ? 1 : s == "k16" ? 2 : s == "k32" ? 3 : 0;
   }();
   return v;
 }
@@ -630,7 +631,7 @@ int gemm_stage_layout() {
 // K values per stage (the inner extent of every TMA box).
 int gemm_stage_k() { return gemm_stage_layout() == 2 ? 16 : 32; }
 
-// Non-batched calls run on CTA pairs (gemm_pair_tc_kernel: 153.7 -> 143.6 us on
+// Non-batched calls run on CTA pairs (gemm_pair_tc_kernel: 153.7 -> 139.3 us on
 // the configs[1] GeGLU projection, tensor pipe 66 -> 71 % active);
 // TFX_GEMM_PAIR=0 keeps them on one CTA per tile (tuning runs, and the tests
 // of that kernel).
@@ -642,10 +643,10 @@ bool gemm_pair_mode() {
   return v;
 }
 
-template <int EPI, int ACT, bool BIAS>
+template <int EPI, int ACT, bool BIAS, int FK>
 int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, const DeviceInfo& dev,
                 cudaStream_t stream) {
-  auto kernel = gemm_pair_tc_kernel<EPI, ACT, BIAS>;
+  auto kernel = gemm_pair_tc_kernel<EPI, ACT, BIAS, FK>;
   static std::once_flag once[64];
   static cudaError_t err[64];
   const int di = dev.device & 63;
@@ -663,9 +664,10 @@ int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, cons
 template <int EPI, int ACT, bool BIAS>
 int launch_tc_layout(const char* op, const CUtensorMap* maps, const GemmArgs& a,
                      const DeviceInfo& dev, cudaStream_t stream) {
-  if (gemm_pair_mode() && a.batch_tokens == 0 && dev.sms >= 2)
-    return launch_pair<EPI, ACT, BIAS>(op, maps, a, dev, stream);
   const int layout = gemm_stage_layout();
+  if (gemm_pair_mode() && a.batch_tokens == 0 && dev.sms >= 2)
+    return layout == 0 || layout == 1 ? launch_pair<EPI, ACT, BIAS, 64>(op, maps, a, dev, stream)
+                                      : launch_pair<EPI, ACT, BIAS, 32>(op, maps, a, dev, stream);
   return layout == 1   ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
          : layout == 2 ? launch_tc<EPI, ACT, BIAS, 16, 32>(op, maps, a, dev, stream)
                        : launch_tc<EPI, ACT, BIAS, 32, 32>(op, maps, a, dev, stream);

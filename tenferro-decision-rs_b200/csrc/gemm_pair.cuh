@@ -89,7 +89,8 @@ __device__ __forceinline__ void pair_arrive_leader(uint64_t* bar) {
 
 // Non-batched calls only (GeGLU and bias + act); tiles with non-finite operands
 // are computed here too and then overwritten by the SIMT kernel.
-template <int EPI, int ACT, bool BIAS>
+// FK: K values per partial (32 or 64: one or two stages between drains).
+template <int EPI, int ACT, bool BIAS, int FK>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
     const __grid_constant__ CUtensorMap xh_map, const __grid_constant__ CUtensorMap xl_map,
     const __grid_constant__ CUtensorMap wh_map, const __grid_constant__ CUtensorMap wl_map,
@@ -100,7 +101,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
   constexpr uint32_t kBHalf = (kBN / 2) * SK * 4;        // 128 output rows x 32 (16 KB)
   constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBHalf;  // 64 KB
   static_assert(kStages * kStageBytes + 1024 <= kGemmSmem, "stage ring");
+  constexpr uint32_t kSpf = FK / SK;  // stages per partial
+  static_assert(FK % SK == 0, "partial length");
   const uint32_t nst = a.nk;  // K chunks of 32
+  const uint32_t npart = (nst + kSpf - 1) / kSpf;  // partials per tile
   extern __shared__ __align__(1024) uint8_t gemm_smem[];
   __shared__ GemmShared sh;
   pdl_enter();
@@ -171,10 +175,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
       uint32_t g = 0, pg = 0;
       bool ok = true;
       for (uint32_t tile = pair; ok && tile < total; tile += npairs) {
-        for (uint32_t kc = 0; kc < nst; ++kc, ++g, ++pg) {  // a partial per stage
+        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           const uint32_t pb = pg & 1, puse = pg >> 1;
-          if ((puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
+          const bool first = kc % kSpf == 0;
+          if ((first && puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
               !gemm_wait(&sh.full[s], use & 1, &sh)) {
             ok = false;
             break;
@@ -186,7 +191,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
 #pragma unroll
           for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x hi * w lo (starts the partial)
             pair_mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bl + ks * 32),
-                             idesc, ks != 0);
+                             idesc, !first || ks != 0);
 #pragma unroll
           for (uint32_t ks = 0; ks < SK / 8; ++ks)  // x lo * w hi
             pair_mma_tf32_ss(d, smem_desc_sw128(al + ks * 32), smem_desc_sw128(bh + ks * 32),
@@ -196,7 +201,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
             pair_mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bh + ks * 32),
                              idesc, 1);
           pair_commit_both(&sh.empty[s]);
-          pair_commit_both(&sh.part_full[pb]);
+          if (kc % kSpf == kSpf - 1 || kc + 1 == nst) {
+            pair_commit_both(&sh.part_full[pb]);
+            ++pg;
+          }
         }
       }
       pair_commit_own(&sh.drain);
@@ -218,7 +226,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
       const uint32_t pm = tile / a.ntiles, n = tile - pm * a.ntiles;
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc2[j] = make_float2(0.0f, 0.0f);
-      for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
+      for (uint32_t kc = 0; kc < npart; ++kc, ++g) {
         const uint32_t pb = g & 1, puse = g >> 1;
         bool got = true;
         if (lane == 0) got = gemm_wait(&sh.part_full[pb], puse & 1, &sh);
