@@ -398,21 +398,22 @@ __device__ __forceinline__ float jeff_exp(float d) {
 // The causal / active softmax of one score row per warp, written as the
 // hi / lo planes of the P V GEMM's x operand. Row = (head, query q) of
 // scores [head][q][key] (keys contiguous, only keys <= q read); keys [0, W),
-// W = 128 (q / 128 + 1), are written (the P V contraction of q's 128-query
-// tile stops there): p = exp(s scale - max) / sum over the kept keys (key <=
+// W = rt (q / rt + 1), are written (the P V contraction of q's rt-query tile
+// row stops there; rt = 128, or 256 when that GEMM runs on CTA pairs): p = exp(s scale - max) / sum over the kept keys (key <=
 // q and keep[key]), 0 for the others. Two passes over the row: a running
 // (max, sum) per lane, combined over the warp, then the probabilities (the
 // second read comes from cache). Rows q < *first have no kept key and are
 // written as zeros (their output is 0).
 __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
     const float* __restrict__ scores, const uint8_t* __restrict__ keep, const int* first,
-    float* __restrict__ phi, float* __restrict__ plo, uint32_t length, uint32_t rows, float scale) {
+    float* __restrict__ phi, float* __restrict__ plo, uint32_t length, uint32_t rows, float scale,
+    uint32_t rt) {
   pdl_enter();
   const uint32_t lane = threadIdx.x & 31;
   const uint32_t row = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (row >= rows) return;
   const uint32_t qi = row % length;
-  const uint32_t width = (qi / 128 + 1) * 128;
+  const uint32_t width = (qi / rt + 1) * rt;
   const float* srow = scores + uint64_t(row) * length;
   float* hrow = phi + uint64_t(row) * length;
   float* lrow = plo + uint64_t(row) * length;
@@ -475,7 +476,7 @@ __global__ void __launch_bounds__(256) jeff_softmax_planes_kernel(
 
 // The Jeff output, elementwise over out (hidden, length): the sum of the P V
 // GEMM's slots for this element (slot p at o + p * n, p < split.pieces(head,
-// t / 128), added in slot order), 0 for tokens t < *first (no kept key), then
+// t / split.row_tokens), added in slot order), 0 for tokens t < *first (no kept key), then
 // times sigmoid(gate). One warp per 128 tokens of a feature row (one query
 // tile: one piece count per warp), four consecutive tokens per lane.
 __global__ void __launch_bounds__(256) jeff_gate_kernel(const float* __restrict__ o,
@@ -489,7 +490,7 @@ __global__ void __launch_bounds__(256) jeff_gate_kernel(const float* __restrict_
   for (uint32_t w = blockIdx.x * 8 + (threadIdx.x >> 5); w < nwarps; w += gridDim.x * 8) {
     const uint32_t f = w / tiles, lm = w - f * tiles;
     uint32_t pieces = 0;
-    if (lane == 0) pieces = split.pieces(f / hd, lm);
+    if (lane == 0) pieces = split.pieces(f / hd, lm * 128 / split.row_tokens);
     pieces = __shfl_sync(0xffffffffu, pieces, 0);
     const uint32_t t = lm * 128 + lane * 4;
     const uint64_t i = uint64_t(f) * length + t;
@@ -1317,7 +1318,7 @@ int jeff_attention_tc(const char* op, const float* q, const float* k, const floa
     rc = launch_kernel(op, jeff_softmax_planes_kernel, dim3((rows + 7) / 8), dim3(256), 0, s, 1,
                        static_cast<const float*>(scores), static_cast<const uint8_t*>(keep),
                        static_cast<const int*>(first), phi, plo, L, rows,
-                       1.0f / sqrtf(float(head_dim)));
+                       1.0f / sqrtf(float(head_dim)), split.row_tokens);
   }
   // O = P V per head, written (head, channel, token) into the split's slots
   if (rc == TFX_OK) {

@@ -7,7 +7,8 @@
 //    tiles n <= lm / 2 only. Live tiles are numbered batch by batch, lm by lm;
 //    tile lm starts at live_prefix(lm).
 //  * P V (causal on the contraction): tile lm contracts over keys < 128 (lm +
-//    1), i.e. lm + 1 chunks of 128 keys. The chunks of all tiles, numbered
+//    1), i.e. lm + 1 chunks of 128 keys. On CTA pairs the rows are 256 tokens
+//    and the chunks 256 keys, with the same triangle. The chunks of all tiles, numbered
 //    batch by batch, lm by lm, are split into contiguous runs, one per CTA
 //    (CTA b owns chunks [start(b), start(b + 1))), so every CTA gets the same
 //    amount of MMA work whatever the tile lengths. A tile whose chunks span
@@ -36,7 +37,8 @@ __host__ __device__ __forceinline__ uint32_t live_row(uint64_t r) {
 }
 
 struct CausalKSplit {
-  uint32_t mb;         // 128-token tiles per batch
+  uint32_t mb;         // token tiles per batch (rows of the triangle)
+  uint32_t row_tokens; // tokens per tile row and keys per chunk: 128, or 256 on CTA pairs
   uint32_t grid;       // CTAs
   uint64_t per_batch;  // chunks per batch: mb (mb + 1) / 2
   uint64_t items;      // chunks in all
@@ -76,10 +78,13 @@ struct CausalKSplit {
   }
 };
 
-// The split for `batches` batches of mb tiles over at most `sms` CTAs.
-inline CausalKSplit causal_k_split(uint32_t batches, uint32_t mb, uint32_t sms) {
+// The split for `batches` batches of mb tile rows of row_tokens tokens over
+// at most `sms` CTAs (or CTA pairs).
+inline CausalKSplit causal_k_split(uint32_t batches, uint32_t mb, uint32_t sms,
+                                   uint32_t row_tokens = 128) {
   CausalKSplit s;
   s.mb = mb;
+  s.row_tokens = row_tokens;
   s.per_batch = uint64_t(mb) * (mb + 1) / 2;
   s.items = s.per_batch * batches;
   s.grid = uint32_t(s.items < sms ? s.items : sms);

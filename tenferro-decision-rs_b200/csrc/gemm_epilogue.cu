@@ -111,6 +111,9 @@ struct GemmArgs {
   // batched only: y of batch b is (nout, batch_tokens), token-contiguous:
   // y[b * nout * batch_tokens + o * batch_tokens + t_b]
   int out_t;
+  // the call runs on CTA pairs (gemm_pair_tc_kernel): items and the causal
+  // schedules count 256-token pair rows
+  int pair;
 };
 
 // A run of K stages [s0, s1) of tile (m, n) that one CTA computes, written
@@ -643,6 +646,12 @@ bool gemm_pair_mode() {
   return v;
 }
 
+// A call runs on CTA pairs when pair mode is on and its batches (if any)
+// are whole 256-token pair rows.
+bool gemm_pair_call(int64_t batch_tokens, const DeviceInfo& dev) {
+  return gemm_pair_mode() && dev.sms >= 2 && (batch_tokens == 0 || batch_tokens % (2 * kBM) == 0);
+}
+
 template <int EPI, int ACT, bool BIAS, int FK>
 int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, const DeviceInfo& dev,
                 cudaStream_t stream) {
@@ -655,8 +664,9 @@ int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, cons
                                    int(kGemmSmem));
   });
   if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
-  const uint64_t pairs = uint64_t((a.mtiles + 1) / 2) * a.ntiles;
-  const unsigned npairs = unsigned(std::min<uint64_t>(pairs, uint64_t(dev.sms / 2)));
+  const unsigned npairs = a.causal == kCausalK
+                             ? a.split.grid
+                             : unsigned(std::min<uint64_t>(a.items, uint64_t(dev.sms / 2)));
   return launch_kernel(op, kernel, dim3(2 * npairs), dim3(kGThreads), kGemmSmem, stream, 2,
                        maps[0], maps[1], maps[2], maps[3], a);
 }
@@ -665,7 +675,7 @@ template <int EPI, int ACT, bool BIAS>
 int launch_tc_layout(const char* op, const CUtensorMap* maps, const GemmArgs& a,
                      const DeviceInfo& dev, cudaStream_t stream) {
   const int layout = gemm_stage_layout();
-  if (gemm_pair_mode() && a.batch_tokens == 0 && dev.sms >= 2)
+  if (a.pair)
     return layout == 0 || layout == 1 ? launch_pair<EPI, ACT, BIAS, 64>(op, maps, a, dev, stream)
                                       : launch_pair<EPI, ACT, BIAS, 32>(op, maps, a, dev, stream);
   return layout == 1   ? launch_tc<EPI, ACT, BIAS, 32, 64>(op, maps, a, dev, stream)
@@ -732,7 +742,8 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
                                        : (nout + kBN - 1) / kBN);
   a.vec4 = nout % 4 == 0 && aligned(y, 16);
-  a.items = uint64_t(a.mtiles) * a.ntiles;
+  a.pair = gemm_pair_call(batch_tokens, dev) ? 1 : 0;
+  a.items = uint64_t(a.pair ? (a.mtiles + 1) / 2 : a.mtiles) * a.ntiles;
   if (batch_tokens > 0) {
     TFX_REQUIRE(epi == kEpiBiasAct && batch_tokens % kBM == 0 && length % batch_tokens == 0 &&
                     nproj == nout * (length / batch_tokens),
@@ -746,11 +757,13 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
     static_assert(kBN == 2 * kBM, "live score tiles assume 256-wide output tiles");
     if (causal == kCausalOut) {
       TFX_REQUIRE(nout == batch_tokens, op, "causal", "causal outputs need nout == batch_tokens");
-      a.items = uint64_t(batches) * live_prefix(a.mb);
+      a.items = uint64_t(batches) *
+                (a.pair ? CausalKSplit::prefix(a.mb / 2) : live_prefix(a.mb));
     } else if (causal == kCausalK) {
       TFX_REQUIRE(in_dim == batch_tokens && nout <= kBN, op, "causal",
                   "a causal contraction needs in_dim == batch_tokens and nout <= 256");
-      a.split = causal_k_split(batches, a.mb, uint32_t(dev.sms));
+      a.split = a.pair ? causal_k_split(batches, a.mb / 2, uint32_t(dev.sms / 2), 2 * kBM)
+                       : causal_k_split(batches, a.mb, uint32_t(dev.sms));
       a.slot_stride = uint64_t(length) * uint64_t(nout);
     }
   }
@@ -857,8 +870,10 @@ int gemm_causal_k_split(int64_t length, int64_t batch_tokens, CausalKSplit* spli
   int st = TFX_OK;
   const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
-  *split = causal_k_split(uint32_t(length / batch_tokens), uint32_t(batch_tokens / kBM),
-                          uint32_t(dev.sms));
+  const uint32_t batches = uint32_t(length / batch_tokens), mb = uint32_t(batch_tokens / kBM);
+  *split = gemm_pair_call(batch_tokens, dev)
+               ? causal_k_split(batches, mb / 2, uint32_t(dev.sms / 2), 2 * kBM)
+               : causal_k_split(batches, mb, uint32_t(dev.sms));
   return TFX_OK;
 }
 

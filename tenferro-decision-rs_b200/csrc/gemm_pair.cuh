@@ -87,8 +87,56 @@ __device__ __forceinline__ void pair_arrive_leader(uint64_t* bar) {
       : "memory");
 }
 
-// Non-batched calls only (GeGLU and bias + act); tiles with non-finite operands
-// are computed here too and then overwritten by the SIMT kernel.
+// The pair's next piece of work from item i (advanced past it); false at the
+// end. Pair tile rows are 256 tokens (two 128-token tiles). Non-batched and
+// batched calls without a causal schedule: pair tiles dealt round robin;
+// kCausalOut (batch_tokens == nout): pair row r of a batch needs the 256-wide
+// output tiles n <= r, numbered as a triangle; kCausalK (in_dim ==
+// batch_tokens): pair row r contracts over 256 (r + 1) keys, in chunks of 256
+// keys (8 stages) split evenly over the pairs (a.split, row_tokens 256).
+__device__ __forceinline__ bool next_pair_piece(const GemmArgs& a, uint32_t nst, uint32_t pair,
+                                                uint32_t npairs, uint64_t& i, GemmPiece& p) {
+  constexpr uint32_t kChunkStages = 8;  // 256 keys of 32
+  if (a.causal == kCausalK) {
+    const uint64_t end = a.split.start(pair + 1);
+    if (i >= end) return false;
+    const uint32_t batch = uint32_t(i / a.split.per_batch);
+    const uint64_t r = i - uint64_t(batch) * a.split.per_batch;
+    const uint32_t pr = CausalKSplit::row_of(r);
+    const uint32_t c0 = uint32_t(r - CausalKSplit::prefix(pr));
+    const uint32_t c1 = uint32_t(min(uint64_t(pr) + 1, uint64_t(c0) + (end - i)));
+    p.m = batch * a.split.mb + pr;  // pair row
+    p.n = 0;
+    p.s0 = c0 * kChunkStages;
+    p.s1 = min(nst, c1 * kChunkStages);
+    p.slot = pair - a.split.owner(a.split.first(batch, pr));
+    p.skip = false;
+    i += c1 - c0;
+    return true;
+  }
+  if (i >= a.items) return false;
+  if (a.causal == kCausalOut) {
+    const uint32_t rows = a.mb / 2;  // pair rows per batch
+    const uint64_t per = CausalKSplit::prefix(rows);
+    const uint32_t batch = uint32_t(i / per);
+    const uint64_t r = i - uint64_t(batch) * per;
+    const uint32_t pr = CausalKSplit::row_of(r);
+    p.m = batch * rows + pr;
+    p.n = uint32_t(r - CausalKSplit::prefix(pr));
+  } else {
+    p.m = uint32_t(i / a.ntiles);
+    p.n = uint32_t(i - uint64_t(p.m) * a.ntiles);
+  }
+  p.s0 = 0;
+  p.s1 = nst;
+  p.slot = 0;
+  p.skip = false;
+  i += npairs;
+  return true;
+}
+
+// Tiles with non-finite operands are computed here too and then overwritten by
+// the SIMT kernel (calls with pre-split operands have none).
 // FK: K values per partial (32 or 64: one or two stages between drains).
 template <int EPI, int ACT, bool BIAS, int FK>
 __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
@@ -104,7 +152,6 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
   constexpr uint32_t kSpf = FK / SK;  // stages per partial
   static_assert(FK % SK == 0, "partial length");
   const uint32_t nst = a.nk;  // K chunks of 32
-  const uint32_t npart = (nst + kSpf - 1) / kSpf;  // partials per tile
   extern __shared__ __align__(1024) uint8_t gemm_smem[];
   __shared__ GemmShared sh;
   pdl_enter();
@@ -113,8 +160,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
   const uint32_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gemm_smem) + 1023) &
                                              ~uintptr_t(1023));
-  const uint32_t mpairs = (a.mtiles + 1) / 2;
-  const uint32_t total = mpairs * a.ntiles;
+  const uint64_t first = a.causal == kCausalK ? a.split.start(pair) : uint64_t(pair);
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -141,12 +187,15 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
     if (lane == 0) {
       uint32_t g = 0;
       bool ok = true;
-      for (uint32_t tile = pair; ok && tile < total; tile += npairs) {
-        const uint32_t pm = tile / a.ntiles, n = tile - pm * a.ntiles;
+      uint64_t it = first;
+      GemmPiece pc;
+      while (ok && next_pair_piece(a, nst, pair, npairs, it, pc)) {
+        const uint32_t pm = pc.m, n = pc.n;
         const int row_x = int((2 * pm + rank) * kBM);
-        const int row_w = EPI == kEpiGeglu ? int(rank * a.inter + n * (kBN / 2))
-                                           : int(n * kBN + rank * (kBN / 2));
-        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
+        const int row_w = EPI == kEpiGeglu
+                              ? int(rank * a.inter + n * (kBN / 2))
+                              : int(batch_wrow(a, 2 * pm * kBM) + n * kBN + rank * (kBN / 2));
+        for (uint32_t kc = pc.s0; kc < pc.s1; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           if (use > 0 && !gemm_wait(&sh.empty[s], (use - 1) & 1, &sh)) {
             ok = false;
@@ -174,11 +223,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
       constexpr uint32_t idesc = idesc_tf32(2 * kBM, kBN);
       uint32_t g = 0, pg = 0;
       bool ok = true;
-      for (uint32_t tile = pair; ok && tile < total; tile += npairs) {
-        for (uint32_t kc = 0; kc < nst; ++kc, ++g) {
+      uint64_t it = first;
+      GemmPiece pc;
+      while (ok && next_pair_piece(a, nst, pair, npairs, it, pc)) {
+        for (uint32_t kc = pc.s0; kc < pc.s1; ++kc, ++g) {
           const uint32_t s = g % kStages, use = g / kStages;
           const uint32_t pb = pg & 1, puse = pg >> 1;
-          const bool first = kc % kSpf == 0;
+          const bool first = (kc - pc.s0) % kSpf == 0;
           if ((first && puse > 0 && !gemm_wait(&sh.part_empty[pb], (puse - 1) & 1, &sh)) ||
               !gemm_wait(&sh.full[s], use & 1, &sh)) {
             ok = false;
@@ -201,7 +252,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
             pair_mma_tf32_ss(d, smem_desc_sw128(ah + ks * 32), smem_desc_sw128(bh + ks * 32),
                              idesc, 1);
           pair_commit_both(&sh.empty[s]);
-          if (kc % kSpf == kSpf - 1 || kc + 1 == nst) {
+          if ((kc - pc.s0) % kSpf == kSpf - 1 || kc + 1 == pc.s1) {
             pair_commit_both(&sh.part_full[pb]);
             ++pg;
           }
@@ -222,11 +273,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
     float2 acc2[64];
     uint32_t g = 0;
     bool ok = true;
-    for (uint32_t tile = pair; ok && tile < total; tile += npairs) {
-      const uint32_t pm = tile / a.ntiles, n = tile - pm * a.ntiles;
+    uint64_t it = first;
+    GemmPiece pc;
+    while (ok && next_pair_piece(a, nst, pair, npairs, it, pc)) {
+      const uint32_t pm = pc.m, n = pc.n;
+      const uint32_t tpart = (pc.s1 - pc.s0 + kSpf - 1) / kSpf;
 #pragma unroll
       for (int j = 0; j < 64; ++j) acc2[j] = make_float2(0.0f, 0.0f);
-      for (uint32_t kc = 0; kc < npart; ++kc, ++g) {
+      for (uint32_t kc = 0; kc < tpart; ++kc, ++g) {
         const uint32_t pb = g & 1, puse = g >> 1;
         bool got = true;
         if (lane == 0) got = gemm_wait(&sh.part_full[pb], puse & 1, &sh);
@@ -252,7 +306,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
       if (!ok) break;
       const uint32_t t = (2 * pm + rank) * kBM + row;
       if (t >= a.length) continue;
-      epi_store<EPI, ACT, BIAS>(a, t, n, half, 0, reinterpret_cast<float*>(acc2));
+      epi_store<EPI, ACT, BIAS>(a, t, n, half, pc.slot, reinterpret_cast<float*>(acc2));
     }
   }
   tc_fence_before();

@@ -35,11 +35,15 @@ int main() {
     if (live_prefix(lm + 1) - live_prefix(lm) != (128 * lm + 127) / 256 + 1) ++bad;
 
   int cases = 0;
+  // cs: 32-key stages per chunk -- 4 (128-token rows, one CTA per tile) or 8
+  // (256-token pair rows on CTA pairs)
+  for (uint32_t cs : {4u, 8u})
   for (uint32_t batches : {1u, 2u, 3u, 8u, 16u, 64u})
     for (uint32_t mb : {1u, 2u, 3u, 5u, 16u, 33u, 64u})
-      for (uint32_t sms : {1u, 7u, 148u, 1000u}) {
-        const CausalKSplit sp = causal_k_split(batches, mb, sms);
-        const uint32_t nst = 4 * mb;  // 32-key stages of a batch's contraction
+      for (uint32_t sms : {1u, 7u, 74u, 148u, 1000u}) {
+        const CausalKSplit sp = causal_k_split(batches, mb, sms, 32 * cs);
+        if (sp.row_tokens != 32 * cs) ++bad;
+        const uint32_t nst = cs * mb;  // 32-key stages of a batch's contraction
         std::map<std::pair<uint32_t, uint32_t>, std::vector<std::pair<uint32_t, uint32_t>>> tiles;
         std::vector<int> covered(sp.items, 0);
         for (uint32_t b = 0; b < sp.grid; ++b) {
@@ -53,7 +57,7 @@ int main() {
             const uint32_t c1 =
                 uint32_t(std::min<uint64_t>(uint64_t(lm) + 1, uint64_t(c0) + (end - i)));
             const uint32_t slot = b - sp.owner(sp.first(batch, lm));
-            const uint32_t s0 = c0 * 4, s1 = std::min(nst, c1 * 4);
+            const uint32_t s0 = c0 * cs, s1 = std::min(nst, c1 * cs);
             if (s1 <= s0) ++bad;
             for (uint64_t k = i; k < i + (c1 - c0); ++k) covered[k]++;
             tiles[{batch, lm}].push_back({slot, s1 - s0});
@@ -71,7 +75,7 @@ int main() {
             if (kv.second[p].first != p) ++bad;
             stages += kv.second[p].second;
           }
-          if (stages != 4 * (kv.first.second + 1)) ++bad;
+          if (stages != cs * (kv.first.second + 1)) ++bad;
         }
         if (tiles.size() != size_t(batches) * mb) ++bad;
         ++cases;
