@@ -119,10 +119,13 @@ def test_attention_f32_variant():
 
 
 def test_gemm_one_cta_variant():
-    """The GEMM-epilogue tests again on the one-CTA tensor-core kernel
-    (TFX_GEMM_PAIR=0; the default runs non-batched calls on CTA pairs)."""
+    """The GEMM-epilogue and Jeff attention tests again on the one-CTA
+    tensor-core GEMM (TFX_GEMM_PAIR=0; by default calls whose batches are whole
+    256-token rows run on CTA pairs)."""
     env = dict(os.environ, TFX_GEMM_PAIR="0")
     res = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p",
-                          "no:cacheprovider", os.path.join(ROOT, "tests", "test_gpu_gemm_epilogue.py")],
+                          "no:cacheprovider", "-k", "gemm or jeff",
+                          os.path.join(ROOT, "tests", "test_gpu_gemm_epilogue.py"),
+                          os.path.join(ROOT, "tests", "test_gpu_attention.py")],
                          env=env, capture_output=True, text=True, timeout=900, cwd=ROOT)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
