@@ -163,7 +163,8 @@ def test_jeff_attention(orc, hd, rot, heads, L):
 # GEMMs around the masked softmax); the others the f32 kernel.
 @pytest.mark.parametrize("hd,rot,heads,L,big_v", [
     (256, 64, 4, 512, False), (64, 16, 3, 384, False), (128, 32, 2, 256, True),
-    (64, 16, 1, 2176, False)])  # rows past 2048 keys: the softmax's multi-pass variant
+    (64, 16, 1, 2176, False),   # rows past 2048 keys; an odd number of 128-token tiles
+    (64, 16, 1, 4224, False)])  # a long single head: 33 tiles, many slots per tile
 def test_jeff_attention_tensor_cores(orc, hd, rot, heads, L, big_v):
     w = heads * hd
     theta, eps = 1e7, 1e-6
