@@ -742,7 +742,10 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
   a.ntiles = uint32_t(epi == kEpiGeglu ? (nout + kBN / 2 - 1) / (kBN / 2)
                                        : (nout + kBN - 1) / kBN);
   a.vec4 = nout % 4 == 0 && aligned(y, 16);
-  a.pair = gemm_pair_call(batch_tokens, dev) ? 1 : 0;
+  // (a split contraction with the split pass stays on one CTA per tile: there
+  // the SIMT kernel's slot-0 result for a flagged tile relies on the tile's
+  // other pieces being written as zeros, which only the one-CTA kernel does)
+  a.pair = gemm_pair_call(batch_tokens, dev) && !(causal == kCausalK && !planes) ? 1 : 0;
   a.items = uint64_t(a.pair ? (a.mtiles + 1) / 2 : a.mtiles) * a.ntiles;
   if (batch_tokens > 0) {
     TFX_REQUIRE(epi == kEpiBiasAct && batch_tokens % kBM == 0 && length % batch_tokens == 0 &&
@@ -870,6 +873,8 @@ int gemm_causal_k_split(int64_t length, int64_t batch_tokens, CausalKSplit* spli
   int st = TFX_OK;
   const DeviceInfo& dev = device_info(&st);
   if (st != TFX_OK) return st;
+  // (the split of a call with pre-split operands, the only kind that runs a
+  // split contraction on CTA pairs)
   const uint32_t batches = uint32_t(length / batch_tokens), mb = uint32_t(batch_tokens / kBM);
   *split = gemm_pair_call(batch_tokens, dev)
                ? causal_k_split(batches, mb / 2, uint32_t(dev.sms / 2), 2 * kBM)

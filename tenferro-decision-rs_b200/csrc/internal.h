@@ -47,7 +47,8 @@ int gemm_wait_timeouts(uint32_t* count);
 int gemm_batched_f32(const char* op, const float* x, const float* w, float* y, int64_t in_dim,
                      int64_t nout, int64_t length, int64_t batch_tokens, cudaStream_t stream,
                      uint32_t causal = 0, const float* const* planes = nullptr, int out_t = 0);
-// The split causal 2 uses for these extents on the current device.
+// The split causal 2 uses for these extents on the current device, for a call
+// with pre-split operands (planes).
 int gemm_causal_k_split(int64_t length, int64_t batch_tokens, CausalKSplit* split);
 
 }  // namespace tfx
