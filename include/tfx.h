@@ -389,9 +389,10 @@ TFX_API int tfx_laya_attention_block_f32(const float* qkv, const uint8_t* keep,
  * (length, width) like q); all-masked rows are 0. out (length, heads*head_dim)
  * column-major. Scratch from the library's stream-ordered pool: with length a
  * multiple of 128, head_dim 64 / 128 / 256, heads*length^2 <= 2^30 and 16-byte
- * aligned gate and out, the tensor-core route (about (7 + s) n + 2 heads
- * length^2 floats, n = length*heads*head_dim, s = the most CTAs one 128-query
- * tile's P V contraction is split over: 3 at 8 heads x 2048 tokens);
+ * aligned gate and out, the tensor-core route (about (6 + s) n + 3 heads
+ * length^2 floats, n = length*heads*head_dim, s = the most CTAs (or CTA
+ * pairs) one query tile's P V contraction is split over: 3 at 8 heads x 2048
+ * tokens);
  * otherwise 3 n floats. */
 TFX_API int tfx_jeff_attention_f32(const float* q, const float* k, const float* v,
                                    const float* gate, const float* q_norm, const float* k_norm,
