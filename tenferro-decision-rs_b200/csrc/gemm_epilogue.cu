@@ -81,6 +81,9 @@ constexpr int kMaxStages = 4;
 // Shared memory: the stage ring holds 192 KB whatever the stage width (two
 // stages of K 32, or four of K 16), plus alignment slack.
 constexpr size_t kGemmSmem = size_t(2) * (2 * kBM + 2 * kBN) * kBK * 4 + 1024;
+// + a 32 x 32 staging tile per epilogue warp (stage_rows)
+constexpr size_t kGemmStage = size_t(kEpiWarps) * 32 * 32 * 4;
+constexpr size_t kGemmSmemAll = kGemmSmem + kGemmStage;
 constexpr long long kGemmWait = 1LL << 31;  // ~1 s at B200 clocks
 constexpr float kSplitLimit = 1152921504606846976.0f;  // 2^60
 
@@ -114,6 +117,9 @@ struct GemmArgs {
   // the call runs on CTA pairs (gemm_pair_tc_kernel): items and the causal
   // schedules count 256-token pair rows
   int pair;
+  // identity epilogue into row-major y: each warp's 32 token rows go out
+  // through a shared-memory tile, 32 consecutive outputs of one row per store
+  int stage_rows;
 };
 
 // A run of K stages [s0, s1) of tile (m, n) that one CTA computes, written
@@ -352,6 +358,28 @@ __device__ __forceinline__ void epi_store(const GemmArgs& a, uint32_t t, uint32_
   }
 }
 
+// The identity epilogue of a warp's 32 token rows t0 .. t0 + 31 (lane = row),
+// 128 outputs each from o0, into row-major y: staged through the warp's 32 x
+// 32 shared tile (element (row r, column j) at r * 32 + (j ^ r): no bank
+// conflicts either way) so that every store writes 32 consecutive outputs of
+// one row, instead of 32 rows' 16 bytes each.
+__device__ __forceinline__ void epi_store_staged(const GemmArgs& a, uint32_t t0, uint32_t lane,
+                                                 uint32_t o0, uint32_t slot, const float* acc,
+                                                 float* stage) {
+  const uint32_t valid = min(128u, a.nout - o0);
+  float* yb = a.y + uint64_t(slot) * a.slot_stride + uint64_t(t0) * a.nout + o0;
+#pragma unroll
+  for (int c = 0; c < 128; c += 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stage[lane * 32 + (uint32_t(j) ^ lane)] = acc[c + j];
+    __syncwarp();
+    if (uint32_t(c) + lane < valid)
+      for (uint32_t r = 0; r < 32; ++r)
+        if (t0 + r < a.length) yb[uint64_t(r) * a.nout + c + lane] = stage[r * 32 + (lane ^ r)];
+    __syncwarp();
+  }
+}
+
 // Accumulation. The tensor cores' f32 accumulation is not IEEE: each MMA
 // aligns the accumulator and its products to the largest exponent and keeps
 // about 22 bits below it (measured: an accumulator fed all 288 MMAs of a
@@ -545,6 +573,16 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_epi_tc_kernel(
       }
       float* acc = reinterpret_cast<float*>(acc2);
       if (!ok) break;
+      if constexpr (EPI == kEpiBiasAct && ACT == TFX_ACT_IDENTITY && !BIAS) {
+        if (a.stage_rows) {  // the whole warp, rows past the length included
+          const uint32_t o0 = n * kBN + 128 * half;
+          if (o0 < a.nout)
+            epi_store_staged(a, m * kBM + q * 32, lane, o0, pc.slot, acc,
+                             reinterpret_cast<float*>(base + size_t(kStages) * kStageBytes) +
+                                 (warp - 2) * 1024);
+          continue;
+        }
+      }
       const uint32_t t = m * kBM + row;
       if (t >= a.length) continue;
       epi_store<EPI, ACT, BIAS>(a, t, n, half, pc.slot, acc);
@@ -603,13 +641,13 @@ int launch_tc(const char* op, const CUtensorMap* maps, const GemmArgs& a, const 
   const int di = dev.device & 63;
   std::call_once(once[di], [&] {
     err[di] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(kGemmSmem));
+                                   int(kGemmSmemAll));
   });
   if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
   const unsigned grid = a.causal == kCausalK
                             ? a.split.grid
                             : unsigned(std::min<uint64_t>(a.items, uint64_t(dev.sms)));
-  return launch_kernel(op, kernel, dim3(grid), dim3(kGThreads), kGemmSmem, stream, 1, maps[0],
+  return launch_kernel(op, kernel, dim3(grid), dim3(kGThreads), kGemmSmemAll, stream, 1, maps[0],
                        maps[1], maps[2], maps[3], a);
 }
 
@@ -646,6 +684,16 @@ bool gemm_pair_mode() {
   return v;
 }
 
+// TFX_GEMM_STAGE_ROWS=0: the row-major identity epilogue stores straight from
+// registers (32 rows' 16 bytes per store) instead of through the staging tile.
+bool gemm_stage_rows() {
+  static const bool v = [] {
+    const char* e = getenv("TFX_GEMM_STAGE_ROWS");
+    return !(e && std::string(e) == "0");
+  }();
+  return v;
+}
+
 // A call runs on CTA pairs when pair mode is on and its batches (if any)
 // are whole 256-token pair rows.
 bool gemm_pair_call(int64_t batch_tokens, const DeviceInfo& dev) {
@@ -661,13 +709,13 @@ int launch_pair(const char* op, const CUtensorMap* maps, const GemmArgs& a, cons
   const int di = dev.device & 63;
   std::call_once(once[di], [&] {
     err[di] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   int(kGemmSmem));
+                                   int(kGemmSmemAll));
   });
   if (err[di] != cudaSuccess) return fail(TFX_ERR_CUDA, op, "launch", cudaGetErrorString(err[di]));
   const unsigned npairs = a.causal == kCausalK
                              ? a.split.grid
                              : unsigned(std::min<uint64_t>(a.items, uint64_t(dev.sms / 2)));
-  return launch_kernel(op, kernel, dim3(2 * npairs), dim3(kGThreads), kGemmSmem, stream, 2,
+  return launch_kernel(op, kernel, dim3(2 * npairs), dim3(kGThreads), kGemmSmemAll, stream, 2,
                        maps[0], maps[1], maps[2], maps[3], a);
 }
 
@@ -755,6 +803,7 @@ int gemm_epilogue(const char* op, int epi, int act, const float* x, const float*
     a.batch_wrows = uint32_t(nout);
     a.causal = causal;
     a.out_t = out_t;
+    a.stage_rows = out_t || !gemm_stage_rows() ? 0 : 1;
     a.mb = uint32_t(batch_tokens / kBM);
     const uint32_t batches = uint32_t(length / batch_tokens);
     static_assert(kBN == 2 * kBM, "live score tiles assume 256-wide output tiles");

@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
   constexpr uint32_t kBHalf = (kBN / 2) * SK * 4;        // 128 output rows x 32 (16 KB)
   constexpr uint32_t kStageBytes = 2 * kABytes + 2 * kBHalf;  // 64 KB
   static_assert(kStages * kStageBytes + 1024 <= kGemmSmem, "stage ring");
+  static_assert(kGemmSmemAll <= 227 * 1024, "stage ring + staging tiles");
   constexpr uint32_t kSpf = FK / SK;  // stages per partial
   static_assert(FK % SK == 0, "partial length");
   const uint32_t nst = a.nk;  // K chunks of 32
@@ -304,6 +305,17 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_pair_tc_kernel(
         if (lane == 0) pair_arrive_leader(&sh.part_empty[pb]);
       }
       if (!ok) break;
+      if constexpr (EPI == kEpiBiasAct && ACT == TFX_ACT_IDENTITY && !BIAS) {
+        if (a.stage_rows) {  // the whole warp, rows past the length included
+          const uint32_t o0 = n * kBN + 128 * half;
+          if (o0 < a.nout)
+            epi_store_staged(a, (2 * pm + rank) * kBM + q * 32, lane, o0, pc.slot,
+                             reinterpret_cast<const float*>(acc2),
+                             reinterpret_cast<float*>(base + size_t(kStages) * kStageBytes) +
+                                 (warp - 2) * 1024);
+          continue;
+        }
+      }
       const uint32_t t = (2 * pm + rank) * kBM + row;
       if (t >= a.length) continue;
       epi_store<EPI, ACT, BIAS>(a, t, n, half, pc.slot, reinterpret_cast<float*>(acc2));
